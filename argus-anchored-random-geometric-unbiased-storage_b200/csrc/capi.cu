@@ -1,0 +1,40 @@
+// Status codes, error text and version of the C ABI (include/argus_b200.h).
+#include <stdio.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace {
+thread_local char g_last_error[512] = "";
+}
+
+int argus_set_error(int status, const char* msg) {
+    snprintf(g_last_error, sizeof(g_last_error), "%s", msg ? msg : "");
+    return status;
+}
+
+int argus_set_cuda_error(cudaError_t e) {
+    snprintf(g_last_error, sizeof(g_last_error), "CUDA error %d: %s", (int)e, cudaGetErrorString(e));
+    return ARGUS_ERR_CUDA;
+}
+
+extern "C" {
+
+const char* argus_status_string(int status) {
+    switch (status) {
+        case ARGUS_OK: return "ok";
+        case ARGUS_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case ARGUS_ERR_MISALIGNED: return "misaligned pointer or stride";
+        case ARGUS_ERR_CUDA: return "CUDA error";
+        case ARGUS_ERR_UNSUPPORTED: return "unsupported shape";
+        case ARGUS_ERR_TIMEOUT: return "device-side wait timed out";
+        case ARGUS_ERR_CAPACITY: return "request exceeds a fixed-size buffer";
+        default: return "unknown status";
+    }
+}
+
+const char* argus_last_error(void) { return g_last_error; }
+
+int argus_version(void) { return 100; /* 0.1.0 */ }
+
+}  // extern "C"
