@@ -1,0 +1,791 @@
+// Mixed-tier paged decode attention for sm_100a, fused with the dequantization of every tier.
+//
+// Replaces the dequantize -> concatenate -> dense softmax path of
+// PagedDynamicKVCache.inplace_paged_attention (core/memory_manager.py:1317-1447) and the
+// reconstruct-then-SDPA path (get_all_keys_values + transformers' attention).
+//
+// Work decomposition: one CTA per (split, batch*kv_head, query group of 8).  The CTA's four warps
+// each stream their own chunks of compressed tiles (<= 16 tokens each) from HBM into a private
+// two-stage shared-memory ring with cp.async.bulk (TMA bulk copies) completed on an mbarrier.
+// A warp rebuilds each staged tile in registers as the exact fp16 values the reference's
+// dequantizers produce (fp16(fp16(u*s) + min), fp16(q*s), +-s) and feeds them to mma.sync m16n8k16:
+//   S^T[16 tokens x 8 queries] = K[16 x D] . Q^T        (tokens on M, queries on N)
+//   O^T[D x 8 queries]        += V^T[D x 16] . P^T      (P = unnormalised softmax weights, fp16)
+// A token/dim permutation lets each thread turn whole packed bytes into fragments:
+//   K (A operand) thread (g, t) holds tokens 2g, 2g+1 and dims t*D/4 .. t*D/4 + D/4 - 1;
+//   V (A operand) thread (g, t) holds tokens 4t .. 4t+3 and dims g*D/8 .. g*D/8 + D/8 - 1.
+// The score tile is moved into the PV operand layout with movmatrix (8x8 transpose).  Online
+// softmax runs in the log2 domain; warps merge in shared memory; splits merge in a second kernel
+// (log-sum-exp combine).
+#include "common.cuh"
+
+namespace argus {
+namespace da {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 2;
+constexpr int kMaxTiles = 16;
+constexpr int kQ = 8;                       // queries per CTA (mma N)
+constexpr long long kSpinLimit = 1ll << 26; // bounded mbarrier waits
+
+__device__ int g_status = 0;
+
+__host__ __device__ constexpr int stage_bytes(int D) {
+    return (64 * D + 128) > 9216 ? ((64 * D + 128 + 127) / 128) * 128 : 9216;
+}
+__host__ __device__ constexpr int tier_bits(int tier) {
+    return tier == ARGUS_TIER_FP16 ? 16 : (tier == ARGUS_TIER_INT4 ? 4 : (tier == ARGUS_TIER_INT2 ? 2 : (tier == ARGUS_TIER_1BIT ? 1 : 8)));
+}
+__host__ __device__ constexpr int tier_per(int tier) {
+    return tier == ARGUS_TIER_INT4 ? 2 : (tier == ARGUS_TIER_INT2 ? 4 : (tier == ARGUS_TIER_1BIT ? 8 : 1));
+}
+__host__ __device__ constexpr bool tier_scaled(int tier) { return tier != ARGUS_TIER_FP16; }
+__host__ __device__ constexpr bool tier_min(int tier) { return tier == ARGUS_TIER_INT4 || tier == ARGUS_TIER_INT2; }
+// payload bytes of a full 16-token tile of K (or V)
+__host__ __device__ constexpr int tile_payload(int tier, int D) { return 16 * D * tier_bits(tier) / 8; }
+__host__ __device__ constexpr int tile_stage_bytes(int tier, int D) {
+    return 2 * tile_payload(tier, D) + 64 + (tier_min(tier) ? 64 : 0);
+}
+__host__ __device__ constexpr int chunk_tiles(int tier, int D) {
+    return (stage_bytes(D) / tile_stage_bytes(tier, D)) > kMaxTiles ? kMaxTiles : (stage_bytes(D) / tile_stage_bytes(tier, D));
+}
+
+struct Params {
+    argus_kv_arena arenas[ARGUS_MAX_ARENAS];
+    const argus_kv_tile* tiles;
+    const argus_kv_chunk* chunks;
+    const int32_t* split_chunk0;
+    const __half* q;
+    __half* out;
+    float* lse;
+    float* part_o;    // [B*Hkv*NQG][S][8][D]
+    float* part_lse;  // [B*Hkv*NQG][S][8]
+    int B, Hkv, G, qlen, S, nqg;
+    float scale_log2;
+};
+
+// ------------------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false after kSpinLimit polls (the caller records a timeout and stops).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
+    for (long long i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, phase)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(m), "r"(o));  // (a & m) | o
+    return r;
+}
+__device__ __forceinline__ uint32_t lop_and_xor(uint32_t a, uint32_t m, uint32_t x) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(m), "r"(x));  // (a & m) ^ x
+    return r;
+}
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Loads BYTES (a multiple of 4) of shared memory into u32 registers with the widest vectors.
+template <int BYTES>
+__device__ __forceinline__ void lds(const unsigned char* p, uint32_t* r) {
+    if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+        for (int i = 0; i < BYTES / 16; ++i) {
+            uint4 v = *reinterpret_cast<const uint4*>(p + 16 * i);
+            r[4 * i] = v.x; r[4 * i + 1] = v.y; r[4 * i + 2] = v.z; r[4 * i + 3] = v.w;
+        }
+    } else if constexpr (BYTES % 8 == 0) {
+#pragma unroll
+        for (int i = 0; i < BYTES / 8; ++i) {
+            uint2 v = *reinterpret_cast<const uint2*>(p + 8 * i);
+            r[2 * i] = v.x; r[2 * i + 1] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < BYTES / 4; ++i) r[i] = *reinterpret_cast<const uint32_t*>(p + 4 * i);
+    }
+}
+
+// Loads BYTES (>= 2, even) into u32 registers; a 2-byte span lands zero-extended in r[0].
+template <int BYTES>
+__device__ __forceinline__ void lds_small(const unsigned char* p, uint32_t* r) {
+    if constexpr (BYTES >= 4) {
+        lds<BYTES>(p, r);
+    } else {
+        r[0] = *reinterpret_cast<const uint16_t*>(p);
+    }
+}
+
+constexpr uint32_t kMagic1024 = 0x64006400u;  // fp16 1024.0 in both halves: 1024 + u for u in 0..1023
+constexpr uint32_t kMagic1152 = 0x64806480u;  // 1024 + 128 (bias of sign-flipped int8 codes)
+constexpr float kFmaScaleLimit = 63.96875f;   // 1024 * s stays finite in fp16 below this
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+// (~a & m) ^ c: the sign bit of c flipped where the bit of a is clear (1-bit tier: b ? s : -s)
+__device__ __forceinline__ uint32_t lop_sign(uint32_t a, uint32_t m, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xA6;" : "=r"(r) : "r"(a), "r"(m), "r"(c));
+    return r;
+}
+
+// Exact dequantization of unsigned codes held as (1024 + u) in fp16 halves:
+//   fp16(fp16(u * s) + mn).  Fast form: fp16(u * s) = fma((1024 + u), s, -1024 s) with one rounding,
+//   exact while 1024 s is finite; otherwise subtract the bias and multiply (two roundings-free steps).
+template <bool FAST, bool MIN>
+__device__ __forceinline__ uint32_t deq_u(uint32_t biased, __half2 s, __half2 ns1024, __half2 mn) {
+    __half2 v;
+    if constexpr (FAST) {
+        v = __hfma2(u2h(biased), s, ns1024);
+    } else {
+        v = __hmul2_rn(__hsub2(u2h(biased), u2h(kMagic1024)), s);
+    }
+    if constexpr (MIN) v = __hadd2_rn(v, mn);
+    return h2u(v);
+}
+
+// Per-token dequantization parameters of one operand, as half2 pairs.
+struct TokScale {
+    __half2 s[2], ns[2], mn[2];  // scale, -1024*scale, min for the two half2 token pairs
+};
+
+// ------------------------------------------------------------------------ K fragments (QK^T)
+// a[c][0..3] for k-chunk c: (token 2g, dims 4c..4c+1), (token 2g+1, same), (token 2g, 4c+2..3),
+// (token 2g+1, 4c+2..3), dims relative to this thread's span t*D/4.  Values are the reference's
+// fp16 dequantization, bit for bit.  ts.s[0] is token 2g broadcast, ts.s[1] token 2g+1.
+template <int D, int TIER, bool FAST>
+__device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4, const TokScale& ts,
+                                        uint32_t (&a)[D / 16][4]) {
+    constexpr int KC = D / 16;
+    if constexpr (TIER == ARGUS_TIER_FP16) {
+        uint32_t ra[D / 8], rb[D / 8];
+        lds<D / 2>(kp + (2 * g4) * D * 2 + t4 * (D / 2), ra);
+        lds<D / 2>(kp + (2 * g4 + 1) * D * 2 + t4 * (D / 2), rb);
+#pragma unroll
+        for (int c = 0; c < KC; ++c) { a[c][0] = ra[2 * c]; a[c][1] = rb[2 * c]; a[c][2] = ra[2 * c + 1]; a[c][3] = rb[2 * c + 1]; }
+    } else if constexpr (TIER == ARGUS_TIER_INT8 || TIER == ARGUS_TIER_FP8SIM) {
+        uint32_t ra[KC], rb[KC];
+        lds<D / 4>(kp + (2 * g4) * D + t4 * (D / 4), ra);
+        lds<D / 4>(kp + (2 * g4 + 1) * D + t4 * (D / 4), rb);
+#pragma unroll
+        for (int c = 0; c < KC; ++c) {
+            const uint32_t wa = ra[c] ^ 0x80808080u, wb = rb[c] ^ 0x80808080u;
+            // fp16(q * s): exact code (bias removed) times the token's scale
+            a[c][0] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7170), kMagic1152)), ts.s[0]));
+            a[c][2] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7372), kMagic1152)), ts.s[0]));
+            a[c][1] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7170), kMagic1152)), ts.s[1]));
+            a[c][3] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7372), kMagic1152)), ts.s[1]));
+        }
+    } else if constexpr (TIER == ARGUS_TIER_INT4 || TIER == ARGUS_TIER_INT2) {
+        constexpr uint32_t M = TIER == ARGUS_TIER_INT4 ? 0x000F000Fu : 0x00030003u;
+        uint32_t r[KC];
+        int shA, shB;
+        if constexpr (TIER == ARGUS_TIER_INT4) {
+            lds<D / 4>(kp + g4 * D + t4 * (D / 4), r);
+            shA = 0; shB = 4;
+        } else {
+            lds<D / 4>(kp + (g4 >> 1) * D + t4 * (D / 4), r);
+            shA = 4 * (g4 & 1); shB = shA + 2;
+        }
+#pragma unroll
+        for (int c = 0; c < KC; ++c) {
+            const uint32_t x01 = prmt(r[c], 0u, 0x4140), x23 = prmt(r[c], 0u, 0x4342);
+            a[c][0] = deq_u<FAST, true>(lop_and_or(x01 >> shA, M, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
+            a[c][1] = deq_u<FAST, true>(lop_and_or(x01 >> shB, M, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+            a[c][2] = deq_u<FAST, true>(lop_and_or(x23 >> shA, M, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
+            a[c][3] = deq_u<FAST, true>(lop_and_or(x23 >> shB, M, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+        }
+    } else {  // 1-bit: b ? +s : -s, the sign bit taken from the packed bit moved to bit 15 / 31
+        uint32_t r[KC];
+        lds<D / 4>(kp + (g4 >> 2) * D + t4 * (D / 4), r);
+        const int k = 2 * (g4 & 3);
+        const uint32_t sA = h2u(ts.s[0]), sB = h2u(ts.s[1]);
+#pragma unroll
+        for (int c = 0; c < KC; ++c) {
+            const uint32_t x01 = prmt(r[c], 0u, 0x4140), x23 = prmt(r[c], 0u, 0x4342);
+            a[c][0] = lop_sign(x01 << (15 - k), 0x80008000u, sA);
+            a[c][1] = lop_sign(x01 << (14 - k), 0x80008000u, sB);
+            a[c][2] = lop_sign(x23 << (15 - k), 0x80008000u, sA);
+            a[c][3] = lop_sign(x23 << (14 - k), 0x80008000u, sB);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------ V fragments (PV)
+// a[t][0..3] for m-tile t: (dim 2t, tokens 4u,4u+2), (dim 2t+1, tokens 4u,4u+2),
+// (dim 2t, tokens 4u+1,4u+3), (dim 2t+1, tokens 4u+1,4u+3); u = t4, dims relative to g*D/8.
+// ts.s[0] = (s_4u, s_4u+2), ts.s[1] = (s_4u+1, s_4u+3).  Exact fp16 dequantized values.
+template <int D, int TIER, bool FAST>
+__device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4, const TokScale& ts,
+                                        uint32_t (&a)[D / 16][4]) {
+    constexpr int KC = D / 16;
+    constexpr int W = (D / 8 + 3) / 4;
+    if constexpr (TIER == ARGUS_TIER_FP16) {
+        uint32_t r0[KC], r1[KC], r2[KC], r3[KC];
+        const unsigned char* base = vp + (4 * t4) * D * 2 + g4 * (D / 4);
+        lds_small<D / 4>(base, r0);
+        lds_small<D / 4>(base + D * 2, r1);
+        lds_small<D / 4>(base + 2 * D * 2, r2);
+        lds_small<D / 4>(base + 3 * D * 2, r3);
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            a[t][0] = prmt(r0[t], r2[t], 0x5410);
+            a[t][1] = prmt(r0[t], r2[t], 0x7632);
+            a[t][2] = prmt(r1[t], r3[t], 0x5410);
+            a[t][3] = prmt(r1[t], r3[t], 0x7632);
+        }
+    } else if constexpr (TIER == ARGUS_TIER_INT8 || TIER == ARGUS_TIER_FP8SIM) {
+        uint32_t r0[W], r1[W], r2[W], r3[W];
+        const unsigned char* base = vp + (4 * t4) * D + g4 * (D / 8);
+        lds_small<D / 8>(base, r0);
+        lds_small<D / 8>(base + D, r1);
+        lds_small<D / 8>(base + 2 * D, r2);
+        lds_small<D / 8>(base + 3 * D, r3);
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            const int w = t >> 1, e0 = 2 * (t & 1);
+            const uint32_t sel = e0 | ((4 + e0) << 4) | ((e0 + 1) << 8) | ((5 + e0) << 12);
+            const uint32_t y02 = prmt(r0[w], r2[w], sel) ^ 0x80808080u;  // (tok 4u d0, tok 4u+2 d0, .. d1, .. d1)
+            const uint32_t y13 = prmt(r1[w], r3[w], sel) ^ 0x80808080u;
+            a[t][0] = h2u(__hmul2_rn(u2h(hsub2u(prmt(y02, kMagic1024, 0x7170), kMagic1152)), ts.s[0]));
+            a[t][1] = h2u(__hmul2_rn(u2h(hsub2u(prmt(y02, kMagic1024, 0x7372), kMagic1152)), ts.s[0]));
+            a[t][2] = h2u(__hmul2_rn(u2h(hsub2u(prmt(y13, kMagic1024, 0x7170), kMagic1152)), ts.s[1]));
+            a[t][3] = h2u(__hmul2_rn(u2h(hsub2u(prmt(y13, kMagic1024, 0x7372), kMagic1152)), ts.s[1]));
+        }
+    } else if constexpr (TIER == ARGUS_TIER_INT4) {
+        uint32_t ra[W], rb[W];
+        const unsigned char* base = vp + (2 * t4) * D + g4 * (D / 8);
+        lds_small<D / 8>(base, ra);   // pair row 2u: tokens 4u (lo), 4u+1 (hi)
+        lds_small<D / 8>(base + D, rb);  // pair row 2u+1: tokens 4u+2 (lo), 4u+3 (hi)
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            const int w = t >> 1, e0 = 2 * (t & 1);
+            const uint32_t y0 = prmt(ra[w], rb[w], e0 | ((4 + e0) << 8));              // (A.d0, -, B.d0, -)
+            const uint32_t y1 = prmt(ra[w], rb[w], (e0 + 1) | ((5 + e0) << 8));        // (A.d1, -, B.d1, -)
+            a[t][0] = deq_u<FAST, true>(lop_and_or(y0, 0x000F000Fu, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
+            a[t][2] = deq_u<FAST, true>(lop_and_or(y0 >> 4, 0x000F000Fu, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+            a[t][1] = deq_u<FAST, true>(lop_and_or(y1, 0x000F000Fu, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
+            a[t][3] = deq_u<FAST, true>(lop_and_or(y1 >> 4, 0x000F000Fu, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+        }
+    } else if constexpr (TIER == ARGUS_TIER_INT2) {
+        uint32_t r[W];
+        lds_small<D / 8>(vp + t4 * D + g4 * (D / 8), r);  // tokens 4u+i in bits 2i..2i+1
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            const int w = t >> 1, e0 = 2 * (t & 1);
+            const uint32_t rs = r[w] >> 4;  // bits 4..7 of each byte moved down
+            const uint32_t y0 = prmt(r[w], rs, e0 | ((4 + e0) << 8));             // (d0 bits0-3, -, d0 bits4-7, -)
+            const uint32_t y1 = prmt(r[w], rs, (e0 + 1) | ((5 + e0) << 8));
+            a[t][0] = deq_u<FAST, true>(lop_and_or(y0, 0x00030003u, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
+            a[t][2] = deq_u<FAST, true>(lop_and_or(y0 >> 2, 0x00030003u, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+            a[t][1] = deq_u<FAST, true>(lop_and_or(y1, 0x00030003u, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
+            a[t][3] = deq_u<FAST, true>(lop_and_or(y1 >> 2, 0x00030003u, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+        }
+    } else {  // 1-bit: tokens 4u+i sit in bit k0+i of row u/2, k0 = 4(u&1)
+        uint32_t r[W];
+        lds_small<D / 8>(vp + (t4 >> 1) * D + g4 * (D / 8), r);
+        const int k0 = 4 * (t4 & 1);
+        const uint32_t s02 = h2u(ts.s[0]), s13 = h2u(ts.s[1]);
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            const int w = t >> 1, e0 = 2 * (t & 1);
+            const uint32_t rs = r[w] >> 2;  // bit k0+2 moved to k0
+            const uint32_t y0 = prmt(r[w], rs, e0 | ((4 + e0) << 8));
+            const uint32_t y1 = prmt(r[w], rs, (e0 + 1) | ((5 + e0) << 8));
+            a[t][0] = lop_sign(y0 << (15 - k0), 0x80008000u, s02);  // tokens 4u, 4u+2
+            a[t][2] = lop_sign(y0 << (14 - k0), 0x80008000u, s13);  // tokens 4u+1, 4u+3
+            a[t][1] = lop_sign(y1 << (15 - k0), 0x80008000u, s02);
+            a[t][3] = lop_sign(y1 << (14 - k0), 0x80008000u, s13);
+        }
+    }
+}
+
+struct SoftmaxState {
+    float m[2];  // running max (log2 domain) for queries 2t, 2t+1
+    float l[2];  // this thread's partial sum of weights
+};
+
+__device__ __forceinline__ __half2 load_h2(const __half* p) { return *reinterpret_cast<const __half2*>(p); }
+
+// Processes one staged tile: exact dequantization into fragments, scores, online softmax, PV.
+template <int D, int TIER>
+__device__ __forceinline__ void process_tile(const unsigned char* kp, const unsigned char* vp, const __half* ks,
+                                             const __half* vs, const __half* km, const __half* vm, int ntok, int g4,
+                                             int t4, const uint32_t (&qf)[D / 16][2], float scale_log2,
+                                             SoftmaxState& st, float (&o)[D / 16][4]) {
+    constexpr int KC = D / 16;
+    const int tokA = 2 * g4, tokB = 2 * g4 + 1;
+    const bool va = tokA < ntok, vb = tokB < ntok;
+    // ---- per-token parameters (K: tokens 2g, 2g+1; V: tokens 4u..4u+3)
+    TokScale tk, tv;
+    bool fast = true;
+    if constexpr (TIER != ARGUS_TIER_FP16) {
+        const __half2 k2 = load_h2(ks + tokA);
+        tk.s[0] = __low2half2(k2);
+        tk.s[1] = __high2half2(k2);
+        const uint2 v4 = *reinterpret_cast<const uint2*>(vs + 4 * t4);
+        tv.s[0] = u2h(prmt(v4.x, v4.y, 0x5410));
+        tv.s[1] = u2h(prmt(v4.x, v4.y, 0x7632));
+        if constexpr (tier_min(TIER)) {
+            const __half2 m2 = load_h2(km + tokA);
+            tk.mn[0] = __low2half2(m2);
+            tk.mn[1] = __high2half2(m2);
+            const uint2 w4 = *reinterpret_cast<const uint2*>(vm + 4 * t4);
+            tv.mn[0] = u2h(prmt(w4.x, w4.y, 0x5410));
+            tv.mn[1] = u2h(prmt(w4.x, w4.y, 0x7632));
+            const __half2 lim = __float2half2_rn(kFmaScaleLimit);
+            const bool ok = __hbge2(lim, k2) && __hbge2(lim, tv.s[0]) && __hbge2(lim, tv.s[1]);
+            fast = __all_sync(0xffffffffu, ok);
+            const __half2 n1024 = __float2half2_rn(-1024.0f);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) { tk.ns[i] = __hmul2(tk.s[i], n1024); tv.ns[i] = __hmul2(tv.s[i], n1024); }
+        }
+    }
+    // ---- S^T = K . Q^T
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+        uint32_t a[KC][4];
+        if (fast) k_frags<D, TIER, true>(kp, g4, t4, tk, a);
+        else k_frags<D, TIER, false>(kp, g4, t4, tk, a);
+#pragma unroll
+        for (int c = 0; c < KC; ++c) mma16816(s, a[c], qf[c][0], qf[c][1]);
+    }
+    float x[4] = {s[0] * scale_log2, s[1] * scale_log2, s[2] * scale_log2, s[3] * scale_log2};
+    if (!va) { x[0] = -INFINITY; x[1] = -INFINITY; }
+    if (!vb) { x[2] = -INFINITY; x[3] = -INFINITY; }
+    // ---- online softmax (queries 2t4 -> index 0, 2t4+1 -> index 1)
+    float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float n0 = fmaxf(st.m[0], mx0), n1 = fmaxf(st.m[1], mx1);
+    if (n0 > st.m[0] || n1 > st.m[1]) {
+        const float f0 = exp2f(st.m[0] - n0), f1 = exp2f(st.m[1] - n1);  // -inf - finite -> 0
+#pragma unroll
+        for (int t = 0; t < KC; ++t) { o[t][0] *= f0; o[t][2] *= f0; o[t][1] *= f1; o[t][3] *= f1; }
+        st.l[0] *= f0; st.l[1] *= f1;
+        st.m[0] = n0; st.m[1] = n1;
+    }
+    const float b0 = (st.m[0] == -INFINITY) ? 0.f : st.m[0];
+    const float b1 = (st.m[1] == -INFINITY) ? 0.f : st.m[1];
+    const float p0 = exp2f(x[0] - b0), p1 = exp2f(x[1] - b1), p2 = exp2f(x[2] - b0), p3 = exp2f(x[3] - b1);
+    st.l[0] += p0 + p2;
+    st.l[1] += p1 + p3;
+    const uint32_t b01 = movmatrix_t(pack_half2(p0, p1));  // mma rows 0..7 (tokens 2g)
+    const uint32_t b23 = movmatrix_t(pack_half2(p2, p3));  // mma rows 8..15 (tokens 2g+1)
+    // ---- O^T += V^T . P^T
+    uint32_t av[KC][4];
+    if (fast) v_frags<D, TIER, true>(vp, g4, t4, tv, av);
+    else v_frags<D, TIER, false>(vp, g4, t4, tv, av);
+    if (ntok < 16) {
+        // tokens past the tile's end may hold non-finite garbage: zero their V values
+        const uint32_t m01 = (4 * t4 < ntok ? 0x0000FFFFu : 0u) | (4 * t4 + 2 < ntok ? 0xFFFF0000u : 0u);
+        const uint32_t m23 = (4 * t4 + 1 < ntok ? 0x0000FFFFu : 0u) | (4 * t4 + 3 < ntok ? 0xFFFF0000u : 0u);
+#pragma unroll
+        for (int t = 0; t < KC; ++t) { av[t][0] &= m01; av[t][1] &= m01; av[t][2] &= m23; av[t][3] &= m23; }
+    }
+#pragma unroll
+    for (int t = 0; t < KC; ++t) mma16816(o[t], av[t], b01, b23);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_constant__ Params p) {
+    constexpr int KC = D / 16;
+    constexpr int STAGE = stage_bytes(D);
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t mbar[kWarps][kStages];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g4 = lane >> 2, t4 = lane & 3;
+    const int split = blockIdx.x, bh = blockIdx.y, qg = blockIdx.z;
+    const int b = bh / p.Hkv, h = bh - b * p.Hkv;
+    const int NQ = p.G * p.qlen;
+    unsigned char* wbuf = smem + (size_t)warp * kStages * STAGE;
+
+    // ---- Q^T fragments (query qg*8 + g4, dims t4*D/4 ..) and per-query sums
+    uint32_t qf[KC][2];
+    {
+        const int n = qg * kQ + g4;
+        if (n < NQ) {
+            const int gi = n / p.qlen, qi = n - gi * p.qlen;
+            const __half* qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
+#pragma unroll
+            for (int c = 0; c < KC; ++c) {
+                qf[c][0] = *reinterpret_cast<const uint32_t*>(qrow + 4 * c);
+                qf[c][1] = *reinterpret_cast<const uint32_t*>(qrow + 4 * c + 2);
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < KC; ++c) { qf[c][0] = 0u; qf[c][1] = 0u; }
+        }
+    }
+
+    SoftmaxState st;
+    st.m[0] = st.m[1] = -INFINITY;
+    st.l[0] = st.l[1] = 0.f;
+    float o[KC][4];
+#pragma unroll
+    for (int t = 0; t < KC; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+
+    const int c_begin = p.split_chunk0[split], c_end = p.split_chunk0[split + 1];
+    const int first = c_begin + warp;
+    const int n_my = first < c_end ? (c_end - first + kWarps - 1) / kWarps : 0;
+
+    if (lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) mbar_init(&mbar[warp][s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    // Issue the bulk copies of chunk j of this warp into stage j % kStages (lane 0).
+    auto issue = [&](int j) {
+        const argus_kv_chunk ch = p.chunks[first + j * kWarps];
+        const argus_kv_arena& ar = p.arenas[ch.arena];
+        const int tier = ar.tier;
+        const int per = tier_per(tier);
+        const int row_bytes = D * tier_bits(tier) / 8 * per;  // bytes of one packed row
+        const int PB = tile_payload(tier, D);
+        const int n = ch.ntiles;
+        unsigned char* dst = wbuf + (j % kStages) * STAGE;
+        uint64_t* bar = &mbar[warp][j % kStages];
+        uint32_t total = 0;
+        for (int i = 0; i < n; ++i) {
+            const argus_kv_tile tl = p.tiles[ch.tile0 + i];
+            const int prow = (tl.ntok + per - 1) / per;
+            total += 2u * prow * row_bytes;
+            if (tier != ARGUS_TIER_FP16) total += 2u * (((tl.ntok * 2) + 15) & ~15) * (tier_min(tier) ? 2 : 1);
+        }
+        fence_proxy_async();
+        mbar_expect_tx(bar, total);
+        for (int i = 0; i < n; ++i) {
+            const argus_kv_tile tl = p.tiles[ch.tile0 + i];
+            const int prow = (tl.ntok + per - 1) / per;
+            const int64_t off = (int64_t)tl.slot * ar.slot_stride + (int64_t)bh * ar.bh_stride +
+                                (int64_t)(tl.tok0 / per) * row_bytes;
+            bulk_g2s(dst + i * PB, static_cast<const unsigned char*>(ar.k) + off, prow * row_bytes, bar);
+            bulk_g2s(dst + (n + i) * PB, static_cast<const unsigned char*>(ar.v) + off, prow * row_bytes, bar);
+            if (tier != ARGUS_TIER_FP16) {
+                const int64_t so = (int64_t)tl.slot * ar.scale_slot_stride + (int64_t)bh * ar.scale_bh_stride + tl.tok0;
+                const uint32_t sb = ((tl.ntok * 2) + 15) & ~15;
+                unsigned char* sbase = dst + 2 * n * PB;
+                bulk_g2s(sbase + 32 * i, ar.k_scale + so, sb, bar);
+                bulk_g2s(sbase + 32 * (n + i), ar.v_scale + so, sb, bar);
+                if (tier_min(tier)) {
+                    bulk_g2s(sbase + 32 * (2 * n + i), ar.k_min + so, sb, bar);
+                    bulk_g2s(sbase + 32 * (3 * n + i), ar.v_min + so, sb, bar);
+                }
+            }
+        }
+    };
+
+    if (lane == 0) {
+        for (int j = 0; j < kStages && j < n_my; ++j) issue(j);
+    }
+    __syncwarp();
+
+    bool failed = false;
+    for (int j = 0; j < n_my; ++j) {
+        const int stage = j % kStages;
+        if (!mbar_wait(&mbar[warp][stage], (uint32_t)((j / kStages) & 1))) {
+            failed = true;
+            break;
+        }
+        const argus_kv_chunk ch = p.chunks[first + j * kWarps];
+        const int tier = p.arenas[ch.arena].tier;
+        const unsigned char* sb = wbuf + stage * STAGE;
+        const int n = ch.ntiles;
+        switch (tier) {
+#define ARGUS_TILE_CASE(T)                                                                                      \
+    case T: {                                                                                                   \
+        constexpr int PB = tile_payload(T, D);                                                                  \
+        const __half* sbase = reinterpret_cast<const __half*>(sb + 2 * n * PB);                                 \
+        for (int i = 0; i < n; ++i) {                                                                           \
+            const int ntok = p.tiles[ch.tile0 + i].ntok;                                                        \
+            process_tile<D, T>(sb + i * PB, sb + (n + i) * PB, sbase + 16 * i, sbase + 16 * (n + i),            \
+                               sbase + 16 * (2 * n + i), sbase + 16 * (3 * n + i), ntok, g4, t4, qf,            \
+                               p.scale_log2, st, o);                                                            \
+        }                                                                                                       \
+        break;                                                                                                  \
+    }
+            ARGUS_TILE_CASE(ARGUS_TIER_FP16)
+            ARGUS_TILE_CASE(ARGUS_TIER_FP8SIM)
+            ARGUS_TILE_CASE(ARGUS_TIER_INT8)
+            ARGUS_TILE_CASE(ARGUS_TIER_INT4)
+            ARGUS_TILE_CASE(ARGUS_TIER_INT2)
+            ARGUS_TILE_CASE(ARGUS_TIER_1BIT)
+#undef ARGUS_TILE_CASE
+            default: break;
+        }
+        __syncwarp();
+        if (lane == 0 && j + kStages < n_my) issue(j + kStages);
+        __syncwarp();
+    }
+    if (failed) {
+        if (lane == 0) atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
+        // let copies still in flight land before the shared memory is released (bounded again)
+        for (int s = 0; s < kStages; ++s) (void)mbar_wait(&mbar[warp][s], 0u);
+    }
+
+    // ---- finish this warp: reduce l over the 8 token lanes
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        st.l[0] += __shfl_xor_sync(0xffffffffu, st.l[0], off);
+        st.l[1] += __shfl_xor_sync(0xffffffffu, st.l[1], off);
+    }
+    __syncthreads();  // all warps are done with their stages: reuse shared memory for the merge
+
+    // merge buffer: per warp m[8], l[8], O[8][D]
+    float* mw = reinterpret_cast<float*>(smem);
+    float* lw = mw + kWarps * kQ;
+    float* ow = lw + kWarps * kQ;
+    if (g4 == 0) {
+        mw[warp * kQ + 2 * t4] = st.m[0];
+        mw[warp * kQ + 2 * t4 + 1] = st.m[1];
+        lw[warp * kQ + 2 * t4] = st.l[0];
+        lw[warp * kQ + 2 * t4 + 1] = st.l[1];
+    }
+    {
+        const int dbase = g4 * (D / 8);
+        float* o0 = ow + ((size_t)warp * kQ + 2 * t4) * D + dbase;
+        float* o1 = o0 + D;
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            o0[2 * t] = o[t][0];
+            o0[2 * t + 1] = o[t][2];
+            o1[2 * t] = o[t][1];
+            o1[2 * t + 1] = o[t][3];
+        }
+    }
+    __syncthreads();
+
+    const int64_t grp = ((int64_t)bh * p.nqg + qg);
+    for (int e = threadIdx.x; e < kQ * D; e += kThreads) {
+        const int n = e / D, d = e - n * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mw[w * kQ + n]);
+        float L = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float f = exp2f(mw[w * kQ + n] - M);
+                L += f * lw[w * kQ + n];
+                acc += f * ow[((size_t)w * kQ + n) * D + d];
+            }
+        }
+        const int ng = qg * kQ + n;
+        if (p.S == 1) {
+            if (ng < NQ) {
+                const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
+                const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
+                p.out[row * D + d] = __float2half_rn(L > 0.f ? acc / L : 0.f);
+                if (p.lse && d == 0) p.lse[row] = (L > 0.f) ? (M + log2f(L)) * 0.69314718055994530942f : -INFINITY;
+            }
+        } else {
+            float* po = p.part_o + ((grp * p.S + split) * kQ + n) * D;
+            po[d] = L > 0.f ? acc / L : 0.f;
+            if (d == 0) p.part_lse[(grp * p.S + split) * kQ + n] = (L > 0.f) ? M + log2f(L) : -INFINITY;
+        }
+    }
+}
+
+// Merges the split partials: out = sum_s 2^(lse_s - LSE) O_s, LSE = log2 sum_s 2^lse_s.
+template <int D>
+__global__ void combine_kernel(const __grid_constant__ Params p) {
+    const int64_t grp = blockIdx.x;  // (b*Hkv + h) * nqg + qg
+    const int qg = (int)(grp % p.nqg);
+    const int64_t bh = grp / p.nqg;
+    const int b = (int)(bh / p.Hkv), h = (int)(bh - (int64_t)b * p.Hkv);
+    const int NQ = p.G * p.qlen;
+    for (int e = threadIdx.x; e < kQ * D; e += blockDim.x) {
+        const int n = e / D, d = e - n * D;
+        const int ng = qg * kQ + n;
+        if (ng >= NQ) continue;
+        const float* pl = p.part_lse + grp * p.S * kQ + n;
+        float M = -INFINITY;
+        for (int s = 0; s < p.S; ++s) M = fmaxf(M, pl[s * kQ]);
+        float W = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+            for (int s = 0; s < p.S; ++s) {
+                const float w = exp2f(pl[s * kQ] - M);
+                W += w;
+                acc += w * p.part_o[((grp * p.S + s) * kQ + n) * D + d];
+            }
+        }
+        const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
+        const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
+        p.out[row * D + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
+        if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
+    }
+}
+
+template <int D>
+int launch(const Params& prm, int n_splits, cudaStream_t st) {
+    const size_t smem = (size_t)kWarps * kStages * stage_bytes(D);
+    static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kWarps * kStages * stage_bytes(D),
+                  "merge buffer must fit in the stage memory");
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    dim3 grid(n_splits, prm.B * prm.Hkv, prm.nqg);
+    decode_attn_kernel<D><<<grid, kThreads, smem, st>>>(prm);
+    ARGUS_CHECK_LAUNCH();
+    if (n_splits > 1) {
+        combine_kernel<D><<<(unsigned)((int64_t)prm.B * prm.Hkv * prm.nqg), 256, 0, st>>>(prm);
+        ARGUS_CHECK_LAUNCH();
+    }
+    return ARGUS_OK;
+}
+
+}  // namespace da
+}  // namespace argus
+
+using namespace argus;
+
+extern "C" {
+
+int argus_decode_attention_chunk_tiles(int tier, int head_dim) {
+    if (tier < 0 || tier > ARGUS_TIER_1BIT) return 0;
+    switch (head_dim) {
+        case 16: return da::chunk_tiles(tier, 16);
+        case 32: return da::chunk_tiles(tier, 32);
+        case 64: return da::chunk_tiles(tier, 64);
+        case 128: return da::chunk_tiles(tier, 128);
+        case 256: return da::chunk_tiles(tier, 256);
+        default: return 0;
+    }
+}
+
+int64_t argus_decode_attention_workspace_size(const argus_attn_shape* s) {
+    if (!s || s->n_splits <= 1) return 0;
+    const int64_t nqg = (s->group * (int64_t)s->q_len + da::kQ - 1) / da::kQ;
+    const int64_t groups = (int64_t)s->batch * s->heads_kv * nqg;
+    return groups * s->n_splits * da::kQ * ((int64_t)s->head_dim + 1) * (int64_t)sizeof(float) + 256;
+}
+
+int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_tile* tiles,
+                           const argus_kv_chunk* chunks, const int32_t* split_chunk0, const uint16_t* q, uint16_t* out,
+                           float* lse, void* workspace, argus_stream_t stream) {
+    if (!s || !arenas || !split_chunk0 || !q || !out)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    if (s->batch <= 0 || s->heads_kv <= 0 || s->group <= 0 || s->q_len <= 0 || s->n_splits <= 0)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "non-positive size");
+    if (s->n_arenas <= 0 || s->n_arenas > ARGUS_MAX_ARENAS)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "arena count out of range");
+    if (s->n_chunks > 0 && (!tiles || !chunks)) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null tile table");
+    if ((int64_t)s->batch * s->heads_kv > 65535) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "B*H_kv above 65535");
+    const int D = s->head_dim;
+    if (D != 16 && D != 32 && D != 64 && D != 128 && D != 256)
+        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "head_dim must be 16, 32, 64, 128 or 256");
+    if (!argus_aligned(q, 16) || !argus_aligned(out, 16)) return argus_set_error(ARGUS_ERR_MISALIGNED, "q/out alignment");
+    da::Params prm;
+    memset(&prm, 0, sizeof(prm));
+    for (int i = 0; i < s->n_arenas; ++i) {
+        const argus_kv_arena& a = arenas[i];
+        if (a.tier < ARGUS_TIER_FP16 || a.tier > ARGUS_TIER_1BIT)
+            return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad arena tier");
+        if (!a.k || !a.v) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null arena payload");
+        if (!argus_aligned(a.k, 16) || !argus_aligned(a.v, 16) || (a.slot_stride % 16) || (a.bh_stride % 16))
+            return argus_set_error(ARGUS_ERR_MISALIGNED, "arena payload must be 16-byte aligned");
+        if (a.tier != ARGUS_TIER_FP16) {
+            if (!a.k_scale || !a.v_scale) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null arena scales");
+            if (!argus_aligned(a.k_scale, 16) || !argus_aligned(a.v_scale, 16) || (a.scale_slot_stride % 8) ||
+                (a.scale_bh_stride % 8))
+                return argus_set_error(ARGUS_ERR_MISALIGNED, "arena scales must be 16-byte aligned");
+            if (da::tier_min(a.tier) && (!a.k_min || !a.v_min || !argus_aligned(a.k_min, 16) || !argus_aligned(a.v_min, 16)))
+                return argus_set_error(ARGUS_ERR_MISALIGNED, "arena mins must be non-null and 16-byte aligned");
+        }
+        prm.arenas[i] = a;
+    }
+    prm.tiles = tiles;
+    prm.chunks = chunks;
+    prm.split_chunk0 = split_chunk0;
+    prm.q = reinterpret_cast<const __half*>(q);
+    prm.out = reinterpret_cast<__half*>(out);
+    prm.lse = lse;
+    prm.B = s->batch;
+    prm.Hkv = s->heads_kv;
+    prm.G = s->group;
+    prm.qlen = s->q_len;
+    prm.S = s->n_splits;
+    prm.nqg = (s->group * s->q_len + da::kQ - 1) / da::kQ;
+    if (prm.nqg > 65535) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "too many query groups");
+    prm.scale_log2 = s->scale * 1.4426950408889634f;
+    if (s->n_splits > 1) {
+        if (!workspace || !argus_aligned(workspace, 16))
+            return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "split-K needs a 16-byte aligned workspace");
+        const int64_t groups = (int64_t)prm.B * prm.Hkv * prm.nqg;
+        prm.part_o = reinterpret_cast<float*>(workspace);
+        prm.part_lse = prm.part_o + groups * s->n_splits * da::kQ * D;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (D) {
+        case 16: return da::launch<16>(prm, s->n_splits, st);
+        case 32: return da::launch<32>(prm, s->n_splits, st);
+        case 64: return da::launch<64>(prm, s->n_splits, st);
+        case 128: return da::launch<128>(prm, s->n_splits, st);
+        default: return da::launch<256>(prm, s->n_splits, st);
+    }
+}
+
+int argus_device_status(int* status, argus_stream_t stream) {
+    if (!status) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null status");
+    int v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, da::g_status, sizeof(int), 0, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(da::g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    *status = v;
+    return ARGUS_OK;
+}
+
+}  // extern "C"

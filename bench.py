@@ -1,0 +1,354 @@
+"""Benchmark: mixed-tier paged decode attention, KV tokens/s and HBM GB/s against the roofline.
+
+Workload (one decode step = one attention pass over the whole cache of one layer):
+Llama-3-8B-shaped layer, batch 8 per GPU, 32 query heads, 8 KV heads, head_dim 128, context
+32,768 tokens in 16-token pages, tiers by age (newest to oldest): FP16 1024 tokens, simulated-FP8
+3072, INT8 4096, INT4 8192, INT2 8192, 1-bit 8192.  K/V are seeded N(0,1) fp16 quantized by the
+tier codecs; queries N(0,1)/sqrt(128); softmax scale 1/sqrt(128).  The compressed cache is
+280.8 MB per GPU, larger than the 126 MB L2, so every step streams it from HBM.
+
+Multi-GPU: one process per GPU (torchrun); each rank holds its own batch of 8 sequences (batch
+sharding: no exchange in the data path), so per-GPU work is fixed ("weak" scaling) and `value`
+is the whole-job KV tokens/s (ranks x 8 x 32768 / max-over-ranks step time).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the CPU restatement of the reference's path (dequantize every page, then
+softmax attention over the reconstructed K/V; argus_cache core/memory_manager.py:1157-1315 +
+1424-1430) on the host cores, on a bounded sample (one sequence, all KV heads, full context).
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "argus-anchored-random-geometric-unbiased-storage_b200")
+for _p in (ROOT, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode-attn KV tokens/s/GPU & HBM GB/s vs roofline (mixed tiers), 1/2/4/8 B200"
+UNIT = "KV tokens/s"
+B, HQ, HKV, D, P = 8, 32, 8, 128, 16
+L = 32768
+SPLIT = [("one_bit", 8192), ("int2", 8192), ("int4", 8192), ("int8", 4096), ("fp8", 3072), ("fp16", 1024)]
+WORKLOAD = "llama3-8b-layer-mixed-tier-decode"
+
+
+def config(parallelism):
+    return {"workload": WORKLOAD, "batch_per_gpu": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+            "context": L, "page_size": P, "tiers_oldest_first": dict(SPLIT),
+            "l2": "inputs larger than L2 (280.8 MB compressed per GPU vs 126 MB L2), no flush",
+            "parallelism": parallelism}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "decode_attention_llama8b.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------------------ workload
+def build_cache(device, seed):
+    import torch
+
+    from argus_b200 import attention as A
+    from argus_b200.core import quantization as Q
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    arenas, pages = [], []
+    for tier, ntok in SPLIT:
+        n = ntok // P
+        k = torch.randn(n, B, HKV, P, D, device=device, generator=g).half()
+        v = torch.randn(n, B, HKV, P, D, device=device, generator=g).half()
+        if tier == "fp16":
+            a = A.KVArena.from_pools(A.TIER_FP16, k, v)
+        elif tier in ("int8", "fp8"):
+            f = Q.quantize_to_int8 if tier == "int8" else Q.quantize_to_fp8_simulated
+            (kq, ks), (vq, vs) = f(k), f(v)
+            a = A.KVArena.from_pools(A.TIER_NAMES[tier], kq, vq, ks, vs)
+        elif tier in ("int4", "int2"):
+            f = Q.quantize_to_int4_packed if tier == "int4" else Q.quantize_to_int2_packed
+            (kp, ks, km), (vp, vs, vm) = f(k), f(v)
+            a = A.KVArena.from_pools(A.TIER_NAMES[tier], kp, vp, ks, vs, km, vm)
+        else:
+            (kp, ks), (vp, vs) = Q.quantize_to_1bit_packed(k), Q.quantize_to_1bit_packed(v)
+            a = A.KVArena.from_pools(A.TIER_1BIT, kp, vp, ks, vs)
+        del k, v
+        ai = len(arenas)
+        arenas.append(a)
+        pages += [(ai, j, P) for j in range(n)]
+    torch.cuda.synchronize(device)
+    plan = A.AttentionPlan(arenas, pages, batch=B, heads_kv=HKV, group=HQ // HKV, head_dim=D)
+    q = (torch.randn(B, HQ, 1, D, device=device, generator=g) / math.sqrt(D)).half()
+    return plan, q
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.25)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------- CPU reference arm
+def cpu_reference_step(pages_np, q_np, threads):
+    """One sequence of the workload through the CPU restatement of the reference's path: every
+    page dequantized (oracle, bit-exact with the reference's codecs), then softmax attention over
+    the reconstructed K/V per GQA group."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+    import torch
+
+    import oracle
+
+    def deq(item):
+        tier, pg = item
+        return oracle.page_kv(tier, pg)
+
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        kv = list(ex.map(deq, pages_np))
+    K = torch.from_numpy(np.concatenate([k for k, _ in kv], axis=2)).float()
+    V = torch.from_numpy(np.concatenate([v for _, v in kv], axis=2)).float()
+    q = torch.from_numpy(q_np).float()  # [1, HQ, 1, D]
+    g = HQ // HKV
+    qg = q.view(1, HKV, g, D)
+    w = torch.matmul(qg, K.transpose(-1, -2)) / math.sqrt(D)
+    p = torch.softmax(w, dim=-1)
+    return torch.matmul(p, V)
+
+
+def cpu_sample(seed=0):
+    """Host copies of one sequence's pages (b = 0, all KV heads, full context)."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(seed)
+    pages = []
+    for tier, ntok in SPLIT:
+        for _ in range(ntok // P):
+            k = rng.standard_normal((1, HKV, P, D), dtype=np.float32).astype(np.float16)
+            v = rng.standard_normal((1, HKV, P, D), dtype=np.float32).astype(np.float16)
+            if tier == "fp16":
+                pg = {"key": k, "value": v}
+            elif tier in ("fp8", "int8"):
+                f = oracle.quantize_to_int8 if tier == "int8" else oracle.quantize_to_fp8_simulated
+                pg = dict(zip(("key_q", "key_scales"), f(k)))
+                pg.update(zip(("value_q", "value_scales"), f(v)))
+            elif tier in ("int4", "int2"):
+                f = oracle.quantize_to_int4_packed if tier == "int4" else oracle.quantize_to_int2_packed
+                pg = dict(zip(("key_packed", "key_scales", "key_min"), f(k)))
+                pg.update(zip(("value_packed", "value_scales", "value_min"), f(v)))
+            else:
+                pg = dict(zip(("key_packed", "key_scales"), oracle.quantize_to_1bit_packed(k)))
+                pg.update(zip(("value_packed", "value_scales"), oracle.quantize_to_1bit_packed(v)))
+            pages.append((tier, pg))
+    q = (rng.standard_normal((1, HQ, 1, D)) / math.sqrt(D)).astype(np.float16)
+    return pages, q
+
+
+def time_cpu(steps, warmup, threads):
+    import torch
+
+    torch.set_num_threads(threads)
+    pages, q = cpu_sample()
+    for _ in range(warmup):
+        cpu_reference_step(pages, q, threads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_reference_step(pages, q, threads)
+    dt = (time.perf_counter() - t0) / steps
+    return L / dt, dt
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    value, dt = time_cpu(args.steps, args.warmup, threads)
+    sample = f"1 sequence x {HKV} KV heads x {L} tokens per step (one of the {B} sequences of the workload)"
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": config(f"cpu, {threads} host threads"),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    plan, q = build_cache(device, seed=1234 + rank)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # device-resident timing
+    for _ in range(args.warmup):
+        plan.run(q)
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
+    with ClockSampler(smi_index) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            plan.run(q)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end-to-end through the public API: q from pinned host memory, output back to host, per step
+    q_host = q.cpu().pin_memory()
+    o_host = torch.empty_like(q_host).pin_memory()
+    q_dev = torch.empty_like(q)
+    for _ in range(args.warmup):
+        q_dev.copy_(q_host, non_blocking=True)
+        o_host.copy_(plan.run(q_dev), non_blocking=True)
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        o_host.copy_(plan.run(q_dev), non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    if rank != 0:
+        return
+    tokens = world * B * L
+    hbm, peak_kind = peaks()
+    achieved = plan.compressed_bytes / (ms * 1e-3) / 1e9
+    launches_per_step = 1 + (1 if plan.n_splits > 1 else 0)
+    line = {"metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": config(f"batch-sharded x{world}" if world > 1 else "single GPU"),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_kind": peak_kind, "traffic": traffic_from_profile(),
+                         "algorithmic_bytes_per_launch": plan.compressed_bytes,
+                         "timed": "decode kernel + split combine kernel, CUDA events"},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": q.numel() * 2,
+                    "d2h_bytes_per_step": q.numel() * 2, "path": "AttentionPlan.run with pinned host q/out"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+            "splits": plan.n_splits}
+    if not args.no_cpu_baseline:
+        cpu_steps = 2
+        value, dt = time_cpu(cpu_steps, 1, os.cpu_count() or 1)
+        line["cpu_baseline"] = {"value": value, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": f"1 sequence x {HKV} KV heads x {L} tokens, {cpu_steps} timed steps"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -108,6 +108,98 @@ int argus_isolate_outliers(const uint16_t* x, int64_t n_rows, int D, float sigma
 int argus_jl_apply(const uint16_t* A, const uint16_t* X, int64_t batch, int M, int K, int N, uint16_t* C,
                    argus_stream_t stream);
 
+/* ------------------------------------------------------------------- mixed-tier decode attention */
+
+/* Storage tiers of a KV arena. */
+enum argus_tier {
+    ARGUS_TIER_FP16 = 0,   /* fp16 values; no scales */
+    ARGUS_TIER_FP8SIM = 1, /* int8 codes (simulated-FP8 wraparound), fp16 scale per token */
+    ARGUS_TIER_INT8 = 2,   /* int8 codes, fp16 scale per token */
+    ARGUS_TIER_INT4 = 3,   /* 2 tokens per byte, fp16 scale + min per token */
+    ARGUS_TIER_INT2 = 4,   /* 4 tokens per byte, fp16 scale + min per token */
+    ARGUS_TIER_1BIT = 5    /* 8 tokens per byte (sign), fp16 scale per token */
+};
+
+/* One storage arena: a tier pool (pages stored as [slot][B][H_kv][packed rows][D]) or an fp16
+ * [B][H_kv][L][D] tensor viewed as 16-token slots.  The K (or V) payload of page `slot` for batch
+ * b and KV head h starts at  k + slot*slot_stride + (b*H_kv + h)*bh_stride  (bytes) and its
+ * per-token scales/mins at  k_scale + slot*scale_slot_stride + (b*H_kv + h)*scale_bh_stride
+ * (fp16 elements).  Payload rows (one packed row = `per` tokens x D) are contiguous.  All
+ * pointers and byte strides must be 16-byte aligned. */
+typedef struct argus_kv_arena {
+    int32_t tier;
+    int32_t reserved;
+    const void* k;
+    const void* v;
+    const uint16_t* k_scale;
+    const uint16_t* v_scale;
+    const uint16_t* k_min;
+    const uint16_t* v_min;
+    int64_t slot_stride;
+    int64_t bh_stride;
+    int64_t scale_slot_stride;
+    int64_t scale_bh_stride;
+} argus_kv_arena;
+
+/* One tile of up to 16 consecutive tokens inside one page of one arena, in attention order. */
+typedef struct argus_kv_tile {
+    int32_t slot;  /* page slot within the arena */
+    uint16_t tok0; /* first token of the tile within its page (a multiple of 16) */
+    uint8_t arena; /* index into the arena array */
+    uint8_t ntok;  /* tokens in the tile, 1..16 */
+} argus_kv_tile;
+
+/* A run of consecutive tiles of one arena that is staged into shared memory as one unit. */
+typedef struct argus_kv_chunk {
+    int32_t tile0;
+    uint8_t ntiles;
+    uint8_t arena;
+    uint16_t reserved;
+} argus_kv_chunk;
+
+#define ARGUS_MAX_ARENAS 8
+
+/* Geometry of one decode-attention call. */
+typedef struct argus_attn_shape {
+    int32_t batch;      /* B */
+    int32_t heads_kv;   /* H_kv */
+    int32_t group;      /* query heads per KV head (H_q / H_kv) */
+    int32_t q_len;      /* query tokens per sequence (all attend to every cached token) */
+    int32_t head_dim;   /* D: 16, 32, 64, 128 or 256 */
+    int32_t n_splits;   /* split-K partitions of the chunk list */
+    int32_t n_arenas;
+    int32_t n_chunks;
+    float scale;        /* softmax scale (1/sqrt(D) by default in the reference) */
+    int32_t reserved;
+} argus_attn_shape;
+
+/* Bytes of scratch argus_decode_attention needs for split-K partials (0 when n_splits == 1). */
+int64_t argus_decode_attention_workspace_size(const argus_attn_shape* shape);
+
+/* Chunk capacity: the largest number of tiles of `tier` that one staged chunk may hold for
+ * head dim D (the chunk list passed to argus_decode_attention must respect it). */
+int argus_decode_attention_chunk_tiles(int tier, int head_dim);
+
+/* Decode attention over a paged KV cache held in mixed tiers, fused with the dequantization:
+ * out = softmax(q K^T * scale) V for every query token, K/V read straight from the compressed
+ * pages.  q: [B][H_q][q_len][D] fp16 (H_q = H_kv * group), out: same shape fp16, lse: optional
+ * [B][H_q][q_len] fp32 natural-log sum-exp.  The chunk list covers the cached tokens in any order;
+ * split_chunk0[s] .. split_chunk0[s+1] are the chunks of split s (n_splits + 1 entries, device).
+ * tiles, chunks and split_chunk0 are device arrays; arenas is a host array copied into the launch.
+ * workspace: device scratch of argus_decode_attention_workspace_size bytes (may be null when
+ * n_splits == 1).
+ * Replaces PagedDynamicKVCache.inplace_paged_attention, core/memory_manager.py:1317-1447 (its
+ * dequantize-concatenate-softmax part), and the reconstruct-then-SDPA path of
+ * get_all_keys_values + transformers' attention (core/memory_manager.py:1157-1315,
+ * models/attention_wrapper.py:87-88), which it matches within fp32-accumulation tolerance. */
+int argus_decode_attention(const argus_attn_shape* shape, const argus_kv_arena* arenas, const argus_kv_tile* tiles,
+                           const argus_kv_chunk* chunks, const int32_t* split_chunk0, const uint16_t* q,
+                           uint16_t* out, float* lse, void* workspace, argus_stream_t stream);
+
+/* Reads (and clears) the device-side status word that bounded waits in the kernels set on a
+ * timeout; writes ARGUS_OK or ARGUS_ERR_TIMEOUT to *status after synchronising `stream`. */
+int argus_device_status(int* status, argus_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,112 @@
+"""GPU parity of the fused mixed-tier decode attention (through the C ABI).
+
+Bar: within 2e-3 max-abs of the exact (float64) softmax attention over the K/V the reference
+reconstructs from the same pages (which the oracle reproduces bit for bit); and within 2e-3 plus
+the reference's own fp16 rounding of the reference's fp16 reconstruct-then-SDPA output."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import attn_util as U
+
+pytestmark = pytest.mark.gpu
+ATOL = 2e-3
+
+
+def run_plan(pages, B, Hkv, G, D, q, n_splits=None, scale=None):
+    from argus_b200 import attention as A
+    arenas, plist = U.arenas_from_pages(pages)
+    plan = A.AttentionPlan(arenas, plist, batch=B, heads_kv=Hkv, group=G, head_dim=D, q_len=q.shape[2],
+                           n_splits=n_splits)
+    out = plan.run(torch.from_numpy(q).cuda(), scale=scale)
+    torch.cuda.synchronize()
+    assert A.device_status() == 0
+    return out.cpu().numpy().astype(np.float64), plan
+
+
+@pytest.mark.parametrize("case", ["mixed", "peaky"])
+@pytest.mark.parametrize("n_splits", [1, 3])
+def test_golden_cases(golden, case, n_splits):
+    z = golden("attention")
+    B, Hq, Hkv, D, P, L = (int(v) for v in z[f"{case}/meta"])
+    pages = U.golden_pages(z, case)
+    out, _ = run_plan(pages, B, Hkv, Hq // Hkv, D, z[f"{case}/q"], n_splits=n_splits)
+    f64 = z[f"{case}/out_f64"]
+    ref16 = z[f"{case}/out_ref16"].astype(np.float64)
+    assert np.abs(out - f64).max() < ATOL
+    assert (np.abs(out - ref16) <= np.abs(f64 - ref16) + ATOL).all()
+
+
+SHAPES = [
+    # B, Hkv, G, D, P, q_len, tiers
+    (2, 2, 4, 128, 16, 1, [("one_bit", 64), ("int2", 64), ("int4", 64), ("int8", 32), ("fp8", 32), ("fp16", 48)]),
+    (1, 4, 8, 64, 16, 1, [("int8", 128), ("fp16", 32)]),
+    (1, 2, 1, 128, 16, 1, [("int4", 32), ("int2", 32), ("fp16", 16)]),
+    (1, 1, 4, 16, 8, 1, [("one_bit", 16), ("int2", 16), ("int4", 16), ("int8", 8), ("fp8", 8), ("fp16", 8)]),
+    (2, 2, 2, 64, 32, 2, [("one_bit", 64), ("int4", 64), ("fp16", 32)]),
+    (1, 1, 16, 128, 16, 1, [("int8", 32), ("fp16", 16)]),
+    (1, 2, 4, 32, 16, 3, [("int2", 48), ("fp8", 32), ("fp16", 16)]),
+    (1, 1, 4, 256, 16, 1, [("int4", 32), ("one_bit", 32), ("fp16", 16)]),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"B{s[0]}H{s[1]}G{s[2]}D{s[3]}P{s[4]}q{s[5]}")
+@pytest.mark.parametrize("n_splits", [1, None])
+def test_random_mixed_tiers(shape, n_splits):
+    B, Hkv, G, D, P, qlen, tiers = shape
+    rng = np.random.default_rng(hash(shape[:6]) % 2**32)
+    pages = U.random_pages(rng, tiers, B, Hkv, D, P)
+    q = rng.standard_normal((B, Hkv * G, qlen, D)).astype(np.float16)
+    out, plan = run_plan(pages, B, Hkv, G, D, q, n_splits=n_splits)
+    K, V = U.reference_kv(pages)
+    ref = U.f64_attention(q, K, V)
+    err = np.abs(out - ref).max()
+    assert err < ATOL, err
+
+
+def test_partial_fp16_tiles_and_custom_scale():
+    """An fp16 staging buffer whose length is not a multiple of 16 (garbage beyond it must not
+    leak), plus a non-default softmax scale."""
+    from argus_b200 import attention as A
+    rng = np.random.default_rng(7)
+    B, Hkv, G, D = 2, 2, 4, 64
+    Lbuf, cap = 21, 32
+    kb = torch.full((B, Hkv, cap, D), float("nan"), dtype=torch.float16, device="cuda")
+    vb = torch.full((B, Hkv, cap, D), float("inf"), dtype=torch.float16, device="cuda")
+    kr = rng.standard_normal((B, Hkv, Lbuf, D)).astype(np.float16)
+    vr = rng.standard_normal((B, Hkv, Lbuf, D)).astype(np.float16)
+    kb[:, :, :Lbuf] = torch.from_numpy(kr).cuda()
+    vb[:, :, :Lbuf] = torch.from_numpy(vr).cuda()
+    pages = U.random_pages(rng, [("int4", 32)], B, Hkv, D, 16)
+    arenas, plist = U.arenas_from_pages(pages)
+    arenas.append(A.KVArena.from_fp16(kb, vb))
+    plist += [(len(arenas) - 1, 0, 16), (len(arenas) - 1, 1, Lbuf - 16)]
+    q = rng.standard_normal((B, Hkv * G, 1, D)).astype(np.float16)
+    plan = A.AttentionPlan(arenas, plist, batch=B, heads_kv=Hkv, group=G, head_dim=D)
+    out = plan.run(torch.from_numpy(q).cuda(), scale=0.3).cpu().numpy().astype(np.float64)
+    K, V = U.reference_kv(pages)
+    K = np.concatenate([K, kr], axis=2)
+    V = np.concatenate([V, vr], axis=2)
+    ref = U.f64_attention(q, K, V, scale=0.3)
+    assert np.isfinite(out).all()
+    assert np.abs(out - ref).max() < ATOL
+
+
+def test_lse_output():
+    from argus_b200 import attention as A
+    rng = np.random.default_rng(3)
+    B, Hkv, G, D = 1, 2, 4, 128
+    pages = U.random_pages(rng, [("int8", 64), ("fp16", 32)], B, Hkv, D, 16)
+    arenas, plist = U.arenas_from_pages(pages)
+    q = rng.standard_normal((B, Hkv * G, 1, D)).astype(np.float16)
+    for ns in (1, 4):
+        plan = A.AttentionPlan(arenas, plist, batch=B, heads_kv=Hkv, group=G, head_dim=D, n_splits=ns)
+        lse = torch.empty(B, Hkv * G, 1, dtype=torch.float32, device="cuda")
+        plan.run(torch.from_numpy(q).cuda(), lse=lse)
+        K, V = U.reference_kv(pages)
+        Kr = np.repeat(K.astype(np.float64), G, axis=1)
+        w = np.einsum("bhqd,bhkd->bhqk", q.astype(np.float64), Kr) / math.sqrt(D)
+        ref = np.log(np.exp(w - w.max(-1, keepdims=True)).sum(-1)) + w.max(-1)
+        assert np.abs(lse.cpu().numpy() - ref).max() < 1e-3
