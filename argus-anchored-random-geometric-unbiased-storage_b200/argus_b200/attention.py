@@ -1,12 +1,17 @@
 """Host side of the fused mixed-tier decode attention (libargus_b200 argus_decode_attention).
 
-A KV cache is described by up to eight *arenas* (a tier pool laid out [slot][B][H_kv][rows][D],
-or an fp16 [B][H_kv][L][D] tensor) and a list of *pages* in attention order, each page being
-(arena, slot, tokens).  An AttentionPlan turns the page list into the kernel's device tables:
-16-token tiles, chunks of tiles staged together (sized per tier so each chunk is ~9 KB of
-compressed data) and split-K partitions balanced by an estimated cost.  A plan is reusable
-across decode steps while the page list is unchanged; its launch only reads device pointers,
-so it can be captured in a CUDA graph.
+KV storage is a set of *arenas* (at most eight per call):
+  * record arenas, one per tier pool: a byte buffer [B*H_kv][slots][record] where a record holds
+    one page of one (batch, kv_head): [K payload][V payload][K scales][V scales][K mins][V mins].
+    Consecutive slots of one (b, h) are contiguous, so a run of small pages is staged into shared
+    memory with a single TMA bulk copy.  The reference's page tensors (key_q, key_scales, ...) are
+    strided views into the records (KVArena.view);
+  * split fp16 arenas: a pair of [B, H_kv, L, D] fp16 tensors (sinks, anchors, the staging buffer).
+A *page list* in attention order ((arena, slot, tokens) triples; attention is order-free, so the
+list is best given in slot order) becomes an AttentionPlan: chunks of up to 16 tiles of 16 tokens
+staged together (~9 KB of compressed data each) and split-K partitions balanced by estimated cost,
+sized so the grid fills the GPU in one wave.  A plan is reusable across decode steps while the page
+list is unchanged; its launch only reads device pointers, so it can be captured in a CUDA graph.
 """
 import ctypes
 import math
@@ -17,23 +22,30 @@ import torch
 from . import _lib
 
 TIER_FP16, TIER_FP8SIM, TIER_INT8, TIER_INT4, TIER_INT2, TIER_1BIT = range(6)
+LAYOUT_RECORD, LAYOUT_SPLIT_FP16 = 0, 1
 TIER_NAMES = {"fp16": TIER_FP16, "fp8": TIER_FP8SIM, "int8": TIER_INT8, "int4": TIER_INT4, "int2": TIER_INT2,
               "one_bit": TIER_1BIT}
 TIER_BITS = {TIER_FP16: 16, TIER_FP8SIM: 8, TIER_INT8: 8, TIER_INT4: 4, TIER_INT2: 2, TIER_1BIT: 1}
 TIER_PER = {TIER_FP16: 1, TIER_FP8SIM: 1, TIER_INT8: 1, TIER_INT4: 2, TIER_INT2: 4, TIER_1BIT: 8}
+TIER_PAYLOAD_DTYPE = {TIER_FP16: torch.float16, TIER_FP8SIM: torch.int8, TIER_INT8: torch.int8,
+                      TIER_INT4: torch.uint8, TIER_INT2: torch.uint8, TIER_1BIT: torch.uint8}
 MAX_ARENAS = 8
 NUM_SMS = 148
+CTAS_PER_SM = 3
 # C-ABI entry points bound in this module (with structure-typed arguments)
 BOUND_SYMBOLS = ("argus_decode_attention", "argus_decode_attention_workspace_size",
-                 "argus_decode_attention_chunk_tiles", "argus_device_status")
+                 "argus_decode_attention_chunk_tiles", "argus_record_bytes", "argus_device_status")
 
 
 class ArenaC(ctypes.Structure):
-    _fields_ = [("tier", ctypes.c_int32), ("reserved", ctypes.c_int32), ("k", ctypes.c_void_p),
-                ("v", ctypes.c_void_p), ("k_scale", ctypes.c_void_p), ("v_scale", ctypes.c_void_p),
-                ("k_min", ctypes.c_void_p), ("v_min", ctypes.c_void_p), ("slot_stride", ctypes.c_int64),
-                ("bh_stride", ctypes.c_int64), ("scale_slot_stride", ctypes.c_int64),
-                ("scale_bh_stride", ctypes.c_int64)]
+    _fields_ = [("tier", ctypes.c_int32), ("layout", ctypes.c_int32), ("k", ctypes.c_void_p),
+                ("v", ctypes.c_void_p), ("bh_stride", ctypes.c_int64), ("record_bytes", ctypes.c_int32),
+                ("page_tokens", ctypes.c_int32)]
+
+
+class ChunkC(ctypes.Structure):
+    _fields_ = [("slot0", ctypes.c_int32), ("tok0", ctypes.c_uint16), ("arena", ctypes.c_uint8),
+                ("ntiles", ctypes.c_uint8), ("ntok_last", ctypes.c_uint8), ("reserved", ctypes.c_uint8 * 3)]
 
 
 class ShapeC(ctypes.Structure):
@@ -43,57 +55,93 @@ class ShapeC(ctypes.Structure):
                 ("reserved", ctypes.c_int32)]
 
 
+assert ctypes.sizeof(ChunkC) == 12
+
+
 def _bind():
     L = _lib.lib()
     if not getattr(L, "_argus_attn_bound", False):
         L.argus_decode_attention.argtypes = [ctypes.POINTER(ShapeC), ctypes.POINTER(ArenaC), ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+                                             ctypes.c_void_p, ctypes.c_void_p]
         L.argus_decode_attention.restype = ctypes.c_int
         L.argus_decode_attention_workspace_size.argtypes = [ctypes.POINTER(ShapeC)]
         L.argus_decode_attention_workspace_size.restype = ctypes.c_int64
-        L.argus_decode_attention_chunk_tiles.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.argus_decode_attention_chunk_tiles.argtypes = [ctypes.c_int] * 4
         L.argus_decode_attention_chunk_tiles.restype = ctypes.c_int
+        L.argus_record_bytes.argtypes = [ctypes.c_int] * 3
+        L.argus_record_bytes.restype = ctypes.c_int
         L.argus_device_status.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
         L.argus_device_status.restype = ctypes.c_int
         L._argus_attn_bound = True
     return L
 
 
+def record_bytes(tier, page_tokens, head_dim):
+    return _bind().argus_record_bytes(tier, page_tokens, head_dim)
+
+
 class KVArena:
-    """One storage arena.  Tensors are kept referenced so their memory outlives the plan."""
+    """One storage arena (see the module docstring).  Tensors are kept referenced so their memory
+    outlives any plan that points at them."""
 
-    def __init__(self, tier, k, v, k_scale=None, v_scale=None, k_min=None, v_min=None, *, slot_stride,
-                 bh_stride, scale_slot_stride=0, scale_bh_stride=0, page_tokens):
-        self.tier = tier
+    def __init__(self, tier, layout, k, v=None, *, bh_stride, record_bytes=0, page_tokens, head_dim, batch,
+                 heads, slots):
+        self.tier, self.layout = tier, layout
         self.k, self.v = k, v
-        self.k_scale, self.v_scale, self.k_min, self.v_min = k_scale, v_scale, k_min, v_min
-        self.slot_stride, self.bh_stride = int(slot_stride), int(bh_stride)
-        self.scale_slot_stride, self.scale_bh_stride = int(scale_slot_stride), int(scale_bh_stride)
-        self.page_tokens = int(page_tokens)
+        self.bh_stride, self.record_bytes, self.page_tokens = int(bh_stride), int(record_bytes), int(page_tokens)
+        self.D, self.B, self.H, self.slots = int(head_dim), int(batch), int(heads), int(slots)
 
+    # ---------------------------------------------------------------- record arenas
     @classmethod
-    def from_pools(cls, tier, k, v, k_scale=None, v_scale=None, k_min=None, v_min=None):
-        """Pools shaped like the reference's: payload [slots, B, H, rows, D] (rows = P / per),
-        scales/mins [slots, B, H, P, 1].  Each slot's [rows, D] block must be contiguous."""
-        for t in (k, v):
-            _lib.require_cuda(t, "pool")
-            if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
-                raise ValueError("pool pages must have contiguous [rows, D] blocks")
-        es = k.element_size()
-        rows = k.shape[-2]
-        P = rows * TIER_PER[tier]
-        if k.stride() != v.stride():
-            raise ValueError("K and V pools must share a layout")
-        kw = dict(slot_stride=k.stride(0) * es, bh_stride=k.stride(2) * es, page_tokens=P)
-        if k.stride(1) != k.shape[2] * k.stride(2):
-            raise ValueError("pool batch/head dims must be contiguous ([B][H] blocks)")
-        if tier != TIER_FP16:
-            if k_scale.stride() != v_scale.stride() or k_scale.stride(1) != k_scale.shape[2] * k_scale.stride(2):
-                raise ValueError("scale pools must share a contiguous [B][H] layout")
-            kw.update(scale_slot_stride=k_scale.stride(0), scale_bh_stride=k_scale.stride(2))
-        return cls(tier, k, v, k_scale, v_scale, k_min, v_min, **kw)
+    def allocate(cls, tier, batch, heads, slots, page_tokens, head_dim, device="cuda"):
+        """A zero-filled record arena for `slots` pages of `page_tokens` tokens."""
+        rec = record_bytes(tier, page_tokens, head_dim)
+        if rec <= 0 or rec % 16:
+            raise ValueError(f"no record layout for tier {tier}, page {page_tokens}, head_dim {head_dim}")
+        buf = torch.zeros(batch * heads, slots, rec, dtype=torch.uint8, device=device)
+        return cls(tier, LAYOUT_RECORD, buf, None, bh_stride=slots * rec, record_bytes=rec, page_tokens=page_tokens,
+                   head_dim=head_dim, batch=batch, heads=heads, slots=slots)
 
+    def _offsets(self):
+        P, D, tier = self.page_tokens, self.D, self.tier
+        pb = P * D * TIER_BITS[tier] // 8
+        return {"k": 0, "v": pb, "ks": 2 * pb, "vs": 2 * pb + 2 * P, "km": 2 * pb + 4 * P, "vm": 2 * pb + 6 * P}
+
+    def view(self, part, slot, n=None):
+        """The reference-shaped tensor of one record component for page `slot` ([B, H, rows, D] payload
+        or [B, H, P, 1] fp16 scales/mins), or of n consecutive pages with a leading page dim."""
+        assert self.layout == LAYOUT_RECORD
+        off = self._offsets()[part]
+        rec, S, H, B, D, P = self.record_bytes, self.slots, self.H, self.B, self.D, self.page_tokens
+        if part in ("k", "v"):
+            dt = TIER_PAYLOAD_DTYPE[self.tier]
+            es = torch.tensor([], dtype=dt).element_size()
+            rows = P // TIER_PER[self.tier]
+            base = self.k.view(dt) if es == 1 else self.k.view(torch.float16)
+            size, stride = [B, H, rows, D], [H * S * rec // es, S * rec // es, D, 1]
+        else:
+            es = 2
+            base = self.k.view(torch.float16)
+            size, stride = [B, H, P, 1], [H * S * rec // 2, S * rec // 2, 1, 1]
+        if n is not None:
+            size, stride = [n] + size, [rec // es] + stride
+        return torch.as_strided(base, size, stride, (slot * rec + off) // es)
+
+    def write_pages(self, slot0, k, v, k_scale=None, v_scale=None, k_min=None, v_min=None):
+        """Copies n pages ([n, B, H, rows, D] payloads, [n, B, H, P, 1] scales/mins) into slots
+        slot0 .. slot0+n-1."""
+        n = k.shape[0]
+        self.view("k", slot0, n).copy_(k)
+        self.view("v", slot0, n).copy_(v)
+        if self.tier != TIER_FP16:
+            self.view("ks", slot0, n).copy_(k_scale)
+            self.view("vs", slot0, n).copy_(v_scale)
+        if self.tier in (TIER_INT4, TIER_INT2):
+            self.view("km", slot0, n).copy_(k_min)
+            self.view("vm", slot0, n).copy_(v_min)
+
+    # ---------------------------------------------------------------- split fp16 arenas
     @classmethod
     def from_fp16(cls, k, v):
         """An fp16 [B, H, L, D] tensor pair (sinks, anchors, the staging buffer) as an arena whose
@@ -105,24 +153,23 @@ class KVArena:
             raise ValueError("fp16 arena tensors must have contiguous [L, D] rows and equal strides")
         if k.stride(0) != k.shape[1] * k.stride(1):
             raise ValueError("fp16 arena [B][H] blocks must be contiguous")
-        D = k.shape[-1]
-        return cls(TIER_FP16, k, v, slot_stride=16 * D * 2, bh_stride=k.stride(1) * 2, page_tokens=16)
+        B, H, L, D = k.shape
+        return cls(TIER_FP16, LAYOUT_SPLIT_FP16, k, v, bh_stride=k.stride(1) * 2, page_tokens=16, head_dim=D,
+                   batch=B, heads=H, slots=(L + 15) // 16)
 
     def c_struct(self):
-        ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
-        return ArenaC(self.tier, 0, ptr(self.k), ptr(self.v), ptr(self.k_scale), ptr(self.v_scale), ptr(self.k_min),
-                      ptr(self.v_min), self.slot_stride, self.bh_stride, self.scale_slot_stride, self.scale_bh_stride)
+        return ArenaC(self.tier, self.layout, self.k.data_ptr(), self.v.data_ptr() if self.v is not None else None,
+                      self.bh_stride, self.record_bytes, self.page_tokens)
 
 
-def chunk_tiles(tier, head_dim):
-    return _bind().argus_decode_attention_chunk_tiles(tier, head_dim)
+def chunk_capacity(arena, head_dim):
+    return _bind().argus_decode_attention_chunk_tiles(arena.tier, arena.layout, arena.page_tokens, head_dim)
 
 
 def _tile_cost(tier, head_dim, ntok):
     """Estimated cost of one tile for split balancing: compressed bytes (K+V, scales) plus a
     per-token term for dequantization and the two contractions."""
-    bits = TIER_BITS[tier]
-    payload = 2 * ntok * head_dim * bits / 8
+    payload = 2 * ntok * head_dim * TIER_BITS[tier] / 8
     meta = 0 if tier == TIER_FP16 else (2 * 2 * ntok * (2 if tier in (TIER_INT4, TIER_INT2) else 1))
     return payload + meta + 24.0 * ntok * head_dim / 128
 
@@ -130,8 +177,8 @@ def _tile_cost(tier, head_dim, ntok):
 class AttentionPlan:
     """Device tables for one page list.
 
-    pages: sequence of (arena_index, slot, n_tokens) in attention order; n_tokens <= the
-    arena's page size (partial pages only for fp16 arenas)."""
+    pages: sequence of (arena_index, slot, n_tokens).  Record pages of <= 16 tokens must be full;
+    longer record pages and split-fp16 slots may end short."""
 
     def __init__(self, arenas, pages, *, batch, heads_kv, group, head_dim, q_len=1, n_splits=None, device=None):
         if not 0 < len(arenas) <= MAX_ARENAS:
@@ -139,45 +186,67 @@ class AttentionPlan:
         self.arenas = list(arenas)
         self.B, self.Hkv, self.G, self.D, self.qlen = int(batch), int(heads_kv), int(group), int(head_dim), int(q_len)
         self.device = device or self.arenas[0].k.device
-        L = _bind()
-        caps = {a.tier: L.argus_decode_attention_chunk_tiles(a.tier, self.D) for a in self.arenas}
-        if min(caps.values()) <= 0:
+        caps = [chunk_capacity(a, self.D) for a in self.arenas]
+        if min(caps) <= 0:
             raise ValueError(f"head_dim {self.D} is not supported")
-        # tiles
-        tiles, tcost, tarena = [], [], []
+        chunks, ccost = [], []
+        cur = None  # open chunk: [slot0, tok0, arena, ntiles, ntok_last, next_slot]
+        total_tokens = 0
+
+        def close():
+            nonlocal cur
+            if cur is not None:
+                chunks.append(tuple(cur[:5]))
+                cur = None
+
         for ai, slot, ntok in pages:
-            a = self.arenas[ai]
+            ntok = int(ntok)
             if ntok <= 0:
                 continue
-            if a.tier != TIER_FP16 and ntok % 8:
-                raise ValueError("quantized pages hold a multiple of 8 tokens")
-            for t0 in range(0, ntok, 16):
-                n = min(16, ntok - t0)
-                tiles.append((slot, t0, ai, n))
-                tcost.append(_tile_cost(a.tier, self.D, n))
-                tarena.append(ai)
-        self.n_tokens = int(sum(t[3] for t in tiles))
-        # chunks: runs of one arena, at most the tier's chunk capacity
-        chunks, ccost = [], []
-        i = 0
-        while i < len(tiles):
-            ai = tarena[i]
-            cap = caps[self.arenas[ai].tier]
-            j = i
-            while j < len(tiles) and j - i < cap and tarena[j] == ai:
-                j += 1
-            chunks.append((i, j - i, ai))
-            ccost.append(sum(tcost[i:j]))
-            i = j
+            a = self.arenas[ai]
+            total_tokens += ntok
+            if a.layout == LAYOUT_RECORD and a.page_tokens <= 16:
+                if ntok != a.page_tokens:
+                    raise ValueError("record pages of <= 16 tokens must be full")
+                if cur is not None and cur[2] == ai and cur[5] == slot and cur[3] < caps[ai]:
+                    cur[3] += 1
+                    cur[5] += 1
+                else:
+                    close()
+                    cur = [slot, 0, ai, 1, ntok, slot + 1]
+            elif a.layout == LAYOUT_RECORD:
+                close()
+                if a.tier != TIER_FP16 and ntok % 8:
+                    raise ValueError("quantized pages hold a multiple of 8 tokens")
+                ntiles_page = (ntok + 15) // 16
+                for t0 in range(0, ntiles_page, caps[ai]):
+                    nt = min(caps[ai], ntiles_page - t0)
+                    last = ntok - 16 * (t0 + nt - 1)
+                    chunks.append((slot, 16 * t0, ai, nt, min(16, last)))
+            else:  # split fp16: slot = 16-token block
+                if ntok > 16:
+                    raise ValueError("split fp16 slots hold at most 16 tokens")
+                if cur is not None and cur[2] == ai and cur[5] == slot and cur[3] < caps[ai] and cur[4] == 16:
+                    cur[3] += 1
+                    cur[4] = ntok
+                    cur[5] += 1
+                else:
+                    close()
+                    cur = [slot, 0, ai, 1, ntok, slot + 1]
+        close()
+        self.n_tokens = total_tokens
+        for slot, tok0, ai, nt, last in chunks:
+            a = self.arenas[ai]
+            toks = 16 * (nt - 1) + last if not (a.layout == LAYOUT_RECORD and a.page_tokens <= 16) else nt * last
+            ccost.append(_tile_cost(a.tier, self.D, toks))
         self.n_chunks = len(chunks)
         nqg = (self.G * self.qlen + 7) // 8
         groups = self.B * self.Hkv * nqg
         if n_splits is None:
-            # about three CTAs per SM in one wave, at least one chunk per warp
-            n_splits = max(1, min(math.ceil(3 * NUM_SMS / groups), max(1, self.n_chunks // 4)))
+            # as many splits as fill one wave of CTAs, with at least ~2 chunks per warp
+            n_splits = max(1, min(NUM_SMS * CTAS_PER_SM // groups, max(1, self.n_chunks // 8)))
         n_splits = max(1, min(int(n_splits), max(1, self.n_chunks)))
         self.n_splits = n_splits
-        # split boundaries at equal cumulative cost
         if self.n_chunks:
             cum = np.concatenate([[0.0], np.cumsum(ccost)])
             targets = cum[-1] * np.arange(n_splits + 1) / n_splits
@@ -186,34 +255,29 @@ class AttentionPlan:
             bounds = np.maximum.accumulate(bounds)
         else:
             bounds = np.zeros(n_splits + 1, np.int32)
-        # device tables
-        t = np.zeros((max(1, len(tiles)), 2), np.int32)
-        for k, (slot, t0, ai, n) in enumerate(tiles):
-            t[k, 0] = slot
-            t[k, 1] = (t0 & 0xFFFF) | (ai << 16) | (n << 24)
-        c = np.zeros((max(1, len(chunks)), 2), np.int32)
-        for k, (t0, nt, ai) in enumerate(chunks):
-            c[k, 0] = t0
-            c[k, 1] = nt | (ai << 8)
-        self.tiles_dev = torch.from_numpy(t).to(self.device)
-        self.chunks_dev = torch.from_numpy(c).to(self.device)
+        arr = (ChunkC * max(1, len(chunks)))()
+        for i, (slot, tok0, ai, nt, last) in enumerate(chunks):
+            arr[i] = ChunkC(slot, tok0, ai, nt, last)
+        raw = np.frombuffer(bytes(arr), dtype=np.uint8).copy()
+        self.chunks_dev = torch.from_numpy(raw).to(self.device)
         self.splits_dev = torch.from_numpy(bounds.astype(np.int32)).to(self.device)
         self._arena_c = (ArenaC * MAX_ARENAS)(*[a.c_struct() for a in self.arenas])
         self._shape = ShapeC(self.B, self.Hkv, self.G, self.qlen, self.D, n_splits, len(self.arenas), self.n_chunks,
                              1.0 / math.sqrt(self.D), 0)
-        ws = L.argus_decode_attention_workspace_size(ctypes.byref(self._shape))
+        ws = _bind().argus_decode_attention_workspace_size(ctypes.byref(self._shape))
         self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=self.device) if ws > 0 else None
-        self.compressed_bytes = self._algorithmic_bytes(tiles)
+        self.chunks = chunks
+        self.compressed_bytes = self._algorithmic_bytes(pages)
 
-    def _algorithmic_bytes(self, tiles):
+    def _algorithmic_bytes(self, pages):
         """Compressed bytes one launch must read: K+V payload and per-token scales/mins over all
         (batch, kv_head) pairs."""
         total = 0
-        for slot, t0, ai, n in tiles:
+        for ai, slot, n in pages:
             tier = self.arenas[ai].tier
-            total += 2 * n * self.D * TIER_BITS[tier] // 8
+            total += 2 * int(n) * self.D * TIER_BITS[tier] // 8
             if tier != TIER_FP16:
-                total += 2 * 2 * n * (2 if tier in (TIER_INT4, TIER_INT2) else 1)
+                total += 2 * 2 * int(n) * (2 if tier in (TIER_INT4, TIER_INT2) else 1)
         return total * self.B * self.Hkv
 
     def run(self, q, scale=None, out=None, lse=None, stream=None):
@@ -230,9 +294,9 @@ class AttentionPlan:
         self._shape.scale = float(1.0 / math.sqrt(self.D) if scale is None else scale)
         st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
         L = _bind()
-        rc = L.argus_decode_attention(ctypes.byref(self._shape), self._arena_c, self.tiles_dev.data_ptr(),
-                                      self.chunks_dev.data_ptr(), self.splits_dev.data_ptr(), q.data_ptr(),
-                                      out.data_ptr(), lse.data_ptr() if lse is not None else None,
+        rc = L.argus_decode_attention(ctypes.byref(self._shape), self._arena_c, self.chunks_dev.data_ptr(),
+                                      self.splits_dev.data_ptr(), q.data_ptr(), out.data_ptr(),
+                                      lse.data_ptr() if lse is not None else None,
                                       self.workspace.data_ptr() if self.workspace is not None else None,
                                       ctypes.c_void_p(st))
         if rc != 0:
@@ -260,27 +324,28 @@ def smoke_check():
     torch.manual_seed(0)
     B, Hkv, G, D, P = 1, 2, 4, 128, 16
     dev = "cuda:0"
-    kv = {name: (torch.randn(1, B, Hkv, P, D, device=dev).half(), torch.randn(1, B, Hkv, P, D, device=dev).half())
-          for name in ("fp16", "int8", "int4", "one_bit")}
-    arenas = [KVArena.from_pools(TIER_FP16, kv["fp16"][0], kv["fp16"][1])]
-    refs = [(kv["fp16"][0][0].cpu().numpy(), kv["fp16"][1][0].cpu().numpy())]
-    for name, tier in (("int8", TIER_INT8), ("int4", TIER_INT4), ("one_bit", TIER_1BIT)):
-        k, v = kv[name]
-        if tier == TIER_INT8:
+    arenas, refs = [], []
+    for tier in (TIER_FP16, TIER_INT8, TIER_INT4, TIER_1BIT):
+        k = torch.randn(1, B, Hkv, P, D, device=dev).half()
+        v = torch.randn(1, B, Hkv, P, D, device=dev).half()
+        a = KVArena.allocate(tier, B, Hkv, 1, P, D, dev)
+        kn, vn = k[0].cpu().numpy(), v[0].cpu().numpy()
+        if tier == TIER_FP16:
+            a.write_pages(0, k, v)
+            refs.append((kn, vn))
+        elif tier == TIER_INT8:
             (kq, ks), (vq, vs) = Q.quantize_to_int8(k), Q.quantize_to_int8(v)
-            arenas.append(KVArena.from_pools(tier, kq, vq, ks, vs))
-            refs.append((oracle.dequantize_from_int8(kq[0].cpu().numpy(), ks[0].cpu().numpy()),
-                         oracle.dequantize_from_int8(vq[0].cpu().numpy(), vs[0].cpu().numpy())))
+            a.write_pages(0, kq, vq, ks, vs)
+            refs.append(tuple(oracle.dequantize_from_int8(*oracle.quantize_to_int8(x)) for x in (kn, vn)))
         elif tier == TIER_INT4:
             (kp, ks, km), (vp, vs, vm) = Q.quantize_to_int4_packed(k), Q.quantize_to_int4_packed(v)
-            arenas.append(KVArena.from_pools(tier, kp, vp, ks, vs, km, vm))
-            refs.append((oracle.dequantize_from_int4_packed(kp[0].cpu().numpy(), ks[0].cpu().numpy(), km[0].cpu().numpy()),
-                         oracle.dequantize_from_int4_packed(vp[0].cpu().numpy(), vs[0].cpu().numpy(), vm[0].cpu().numpy())))
+            a.write_pages(0, kp, vp, ks, vs, km, vm)
+            refs.append(tuple(oracle.dequantize_from_int4_packed(*oracle.quantize_to_int4_packed(x)) for x in (kn, vn)))
         else:
             (kp, ks), (vp, vs) = Q.quantize_to_1bit_packed(k), Q.quantize_to_1bit_packed(v)
-            arenas.append(KVArena.from_pools(tier, kp, vp, ks, vs))
-            refs.append((oracle.dequantize_from_1bit_packed(kp[0].cpu().numpy(), ks[0].cpu().numpy()),
-                         oracle.dequantize_from_1bit_packed(vp[0].cpu().numpy(), vs[0].cpu().numpy())))
+            a.write_pages(0, kp, vp, ks, vs)
+            refs.append(tuple(oracle.dequantize_from_1bit_packed(*oracle.quantize_to_1bit_packed(x)) for x in (kn, vn)))
+        arenas.append(a)
     plan = AttentionPlan(arenas, [(i, 0, P) for i in range(len(arenas))], batch=B, heads_kv=Hkv, group=G,
                          head_dim=D, n_splits=2)
     q = torch.randn(B, Hkv * G, 1, D, device=dev).half()

@@ -34,26 +34,37 @@ __device__ int g_status = 0;
 __host__ __device__ constexpr int stage_bytes(int D) {
     return (64 * D + 128) > 9216 ? ((64 * D + 128 + 127) / 128) * 128 : 9216;
 }
+// Shared memory past the last stage that fragment loads of short (8-token) pages may touch.
+__host__ __device__ constexpr int stage_slack(int D) { return 16 * D; }
 __host__ __device__ constexpr int tier_bits(int tier) {
     return tier == ARGUS_TIER_FP16 ? 16 : (tier == ARGUS_TIER_INT4 ? 4 : (tier == ARGUS_TIER_INT2 ? 2 : (tier == ARGUS_TIER_1BIT ? 1 : 8)));
 }
-__host__ __device__ constexpr int tier_per(int tier) {
-    return tier == ARGUS_TIER_INT4 ? 2 : (tier == ARGUS_TIER_INT2 ? 4 : (tier == ARGUS_TIER_1BIT ? 8 : 1));
+__host__ __device__ constexpr int tier_log2per(int tier) {
+    return tier == ARGUS_TIER_INT4 ? 1 : (tier == ARGUS_TIER_INT2 ? 2 : (tier == ARGUS_TIER_1BIT ? 3 : 0));
 }
 __host__ __device__ constexpr bool tier_scaled(int tier) { return tier != ARGUS_TIER_FP16; }
 __host__ __device__ constexpr bool tier_min(int tier) { return tier == ARGUS_TIER_INT4 || tier == ARGUS_TIER_INT2; }
-// payload bytes of a full 16-token tile of K (or V)
-__host__ __device__ constexpr int tile_payload(int tier, int D) { return 16 * D * tier_bits(tier) / 8; }
-__host__ __device__ constexpr int tile_stage_bytes(int tier, int D) {
-    return 2 * tile_payload(tier, D) + 64 + (tier_min(tier) ? 64 : 0);
+// bytes of one packed row (`per` tokens x D)
+__host__ __device__ constexpr int row_bytes(int tier, int D) { return tier == ARGUS_TIER_FP16 ? 2 * D : D; }
+// payload bytes of `tokens` tokens of K (or V)
+__host__ __device__ constexpr int payload_bytes(int tier, int tokens, int D) { return tokens * D * tier_bits(tier) / 8; }
+// bytes of one record: [K][V][K scales][V scales][K mins][V mins]
+__host__ __device__ constexpr int record_bytes(int tier, int P, int D) {
+    return 2 * payload_bytes(tier, P, D) + (tier_scaled(tier) ? 4 * P : 0) + (tier_min(tier) ? 4 * P : 0);
 }
-__host__ __device__ constexpr int chunk_tiles(int tier, int D) {
-    return (stage_bytes(D) / tile_stage_bytes(tier, D)) > kMaxTiles ? kMaxTiles : (stage_bytes(D) / tile_stage_bytes(tier, D));
+// staged bytes of one 16-token tile when tiles are not whole records
+__host__ __device__ constexpr int tile_stage_bytes(int tier, int D) {
+    return 2 * payload_bytes(tier, 16, D) + (tier_scaled(tier) ? 64 : 0) + (tier_min(tier) ? 64 : 0);
+}
+__host__ __device__ constexpr bool whole_records(int layout, int P) { return layout == ARGUS_LAYOUT_RECORD && P <= 16; }
+__host__ __device__ constexpr int chunk_tiles(int tier, int layout, int P, int D) {
+    return whole_records(layout, P)
+               ? ((stage_bytes(D) / record_bytes(tier, P, D)) > kMaxTiles ? kMaxTiles : (stage_bytes(D) / record_bytes(tier, P, D)))
+               : ((stage_bytes(D) / tile_stage_bytes(tier, D)) > kMaxTiles ? kMaxTiles : (stage_bytes(D) / tile_stage_bytes(tier, D)));
 }
 
 struct Params {
     argus_kv_arena arenas[ARGUS_MAX_ARENAS];
-    const argus_kv_tile* tiles;
     const argus_kv_chunk* chunks;
     const int32_t* split_chunk0;
     const __half* q;
@@ -64,6 +75,43 @@ struct Params {
     int B, Hkv, G, qlen, S, nqg;
     float scale_log2;
 };
+
+// Where the pieces of tile i of a staged chunk sit in shared memory (uniform across the warp).
+struct ChunkView {
+    int k_off, v_off, ks_off, vs_off, km_off, vm_off;
+    int pstride, sstride;  // bytes between consecutive tiles: payload, scales
+    int ntok_full;         // tokens in every tile but the last
+};
+
+template <int D>
+__device__ __forceinline__ ChunkView chunk_view(const argus_kv_arena& ar, int n) {
+    ChunkView cv;
+    const int tier = ar.tier;
+    if (whole_records(ar.layout, ar.page_tokens)) {
+        const int P = ar.page_tokens;
+        const int pb = payload_bytes(tier, P, D);
+        cv.k_off = 0;
+        cv.v_off = pb;
+        cv.ks_off = 2 * pb;
+        cv.vs_off = 2 * pb + 2 * P;
+        cv.km_off = 2 * pb + 4 * P;
+        cv.vm_off = 2 * pb + 6 * P;
+        cv.pstride = cv.sstride = ar.record_bytes;
+        cv.ntok_full = P;
+    } else {
+        const int pb = payload_bytes(tier, 16, D);
+        cv.k_off = 0;
+        cv.v_off = n * pb;
+        cv.ks_off = 2 * n * pb;
+        cv.vs_off = cv.ks_off + 32 * n;
+        cv.km_off = cv.ks_off + 64 * n;
+        cv.vm_off = cv.ks_off + 96 * n;
+        cv.pstride = pb;
+        cv.sstride = 32;
+        cv.ntok_full = 16;
+    }
+    return cv;
+}
 
 // ------------------------------------------------------------------------------ PTX helpers
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -394,8 +442,15 @@ __device__ __forceinline__ void process_tile(const unsigned char* kp, const unsi
         uint32_t a[KC][4];
         if (fast) k_frags<D, TIER, true>(kp, g4, t4, tk, a);
         else k_frags<D, TIER, false>(kp, g4, t4, tk, a);
+        // two independent accumulation chains halve the dependent-MMA latency
+        float s2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < KC; ++c) mma16816(s, a[c], qf[c][0], qf[c][1]);
+        for (int c = 0; c < KC; c += 2) {
+            mma16816(s, a[c], qf[c][0], qf[c][1]);
+            if (c + 1 < KC) mma16816(s2, a[c + 1], qf[c + 1][0], qf[c + 1][1]);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[e] += s2[e];
     }
     float x[4] = {s[0] * scale_log2, s[1] * scale_log2, s[2] * scale_log2, s[3] * scale_log2};
     if (!va) { x[0] = -INFINITY; x[1] = -INFINITY; }
@@ -487,42 +542,49 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
     }
     __syncwarp();
 
-    // Issue the bulk copies of chunk j of this warp into stage j % kStages (lane 0).
+    // Issue the bulk copies of chunk j of this warp into stage j % kStages (lane 0 only).
     auto issue = [&](int j) {
         const argus_kv_chunk ch = p.chunks[first + j * kWarps];
         const argus_kv_arena& ar = p.arenas[ch.arena];
-        const int tier = ar.tier;
-        const int per = tier_per(tier);
-        const int row_bytes = D * tier_bits(tier) / 8 * per;  // bytes of one packed row
-        const int PB = tile_payload(tier, D);
-        const int n = ch.ntiles;
+        const int tier = ar.tier, n = ch.ntiles, P = ar.page_tokens;
         unsigned char* dst = wbuf + (j % kStages) * STAGE;
         uint64_t* bar = &mbar[warp][j % kStages];
-        uint32_t total = 0;
-        for (int i = 0; i < n; ++i) {
-            const argus_kv_tile tl = p.tiles[ch.tile0 + i];
-            const int prow = (tl.ntok + per - 1) / per;
-            total += 2u * prow * row_bytes;
-            if (tier != ARGUS_TIER_FP16) total += 2u * (((tl.ntok * 2) + 15) & ~15) * (tier_min(tier) ? 2 : 1);
-        }
+        const unsigned char* blk = static_cast<const unsigned char*>(ar.k) + (int64_t)bh * ar.bh_stride;
         fence_proxy_async();
-        mbar_expect_tx(bar, total);
-        for (int i = 0; i < n; ++i) {
-            const argus_kv_tile tl = p.tiles[ch.tile0 + i];
-            const int prow = (tl.ntok + per - 1) / per;
-            const int64_t off = (int64_t)tl.slot * ar.slot_stride + (int64_t)bh * ar.bh_stride +
-                                (int64_t)(tl.tok0 / per) * row_bytes;
-            bulk_g2s(dst + i * PB, static_cast<const unsigned char*>(ar.k) + off, prow * row_bytes, bar);
-            bulk_g2s(dst + (n + i) * PB, static_cast<const unsigned char*>(ar.v) + off, prow * row_bytes, bar);
-            if (tier != ARGUS_TIER_FP16) {
-                const int64_t so = (int64_t)tl.slot * ar.scale_slot_stride + (int64_t)bh * ar.scale_bh_stride + tl.tok0;
-                const uint32_t sb = ((tl.ntok * 2) + 15) & ~15;
-                unsigned char* sbase = dst + 2 * n * PB;
-                bulk_g2s(sbase + 32 * i, ar.k_scale + so, sb, bar);
-                bulk_g2s(sbase + 32 * (n + i), ar.v_scale + so, sb, bar);
-                if (tier_min(tier)) {
-                    bulk_g2s(sbase + 32 * (2 * n + i), ar.k_min + so, sb, bar);
-                    bulk_g2s(sbase + 32 * (3 * n + i), ar.v_min + so, sb, bar);
+        if (whole_records(ar.layout, P)) {
+            // n consecutive records of this (b, h): one contiguous copy
+            const uint32_t bytes = (uint32_t)n * (uint32_t)ar.record_bytes;
+            mbar_expect_tx(bar, bytes);
+            bulk_g2s(dst, blk + (int64_t)ch.slot0 * ar.record_bytes, bytes, bar);
+        } else {
+            const int ntok = 16 * (n - 1) + ch.ntok_last;
+            const int lp = tier_log2per(tier);
+            const int rb = row_bytes(tier, D);
+            const uint32_t pbytes = (uint32_t)(((ntok + (1 << lp) - 1) >> lp) * rb);
+            const int pb16 = payload_bytes(tier, 16, D);
+            const uint32_t sbytes = (uint32_t)((ntok * 2 + 15) & ~15);
+            uint32_t total = 2 * pbytes;
+            if (tier_scaled(tier)) total += 2 * sbytes * (tier_min(tier) ? 2 : 1);
+            mbar_expect_tx(bar, total);
+            if (ar.layout == ARGUS_LAYOUT_SPLIT_FP16) {
+                const int64_t off = (int64_t)bh * ar.bh_stride + (int64_t)ch.slot0 * 32 * D;
+                bulk_g2s(dst, static_cast<const unsigned char*>(ar.k) + off, pbytes, bar);
+                bulk_g2s(dst + n * pb16, static_cast<const unsigned char*>(ar.v) + off, pbytes, bar);
+            } else {
+                const unsigned char* rec = blk + (int64_t)ch.slot0 * ar.record_bytes;
+                const int pbP = payload_bytes(tier, P, D);
+                const int64_t roff = (int64_t)(ch.tok0 >> lp) * rb;
+                bulk_g2s(dst, rec + roff, pbytes, bar);
+                bulk_g2s(dst + n * pb16, rec + pbP + roff, pbytes, bar);
+                if (tier_scaled(tier)) {
+                    const unsigned char* sc = rec + 2 * pbP + 2 * ch.tok0;
+                    unsigned char* sd = dst + 2 * n * pb16;
+                    bulk_g2s(sd, sc, sbytes, bar);
+                    bulk_g2s(sd + 32 * n, sc + 2 * P, sbytes, bar);
+                    if (tier_min(tier)) {
+                        bulk_g2s(sd + 64 * n, sc + 4 * P, sbytes, bar);
+                        bulk_g2s(sd + 96 * n, sc + 6 * P, sbytes, bar);
+                    }
                 }
             }
         }
@@ -541,21 +603,24 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
             break;
         }
         const argus_kv_chunk ch = p.chunks[first + j * kWarps];
-        const int tier = p.arenas[ch.arena].tier;
-        const unsigned char* sb = wbuf + stage * STAGE;
+        const argus_kv_arena& ar = p.arenas[ch.arena];
         const int n = ch.ntiles;
-        switch (tier) {
-#define ARGUS_TILE_CASE(T)                                                                                      \
-    case T: {                                                                                                   \
-        constexpr int PB = tile_payload(T, D);                                                                  \
-        const __half* sbase = reinterpret_cast<const __half*>(sb + 2 * n * PB);                                 \
-        for (int i = 0; i < n; ++i) {                                                                           \
-            const int ntok = p.tiles[ch.tile0 + i].ntok;                                                        \
-            process_tile<D, T>(sb + i * PB, sb + (n + i) * PB, sbase + 16 * i, sbase + 16 * (n + i),            \
-                               sbase + 16 * (2 * n + i), sbase + 16 * (3 * n + i), ntok, g4, t4, qf,            \
-                               p.scale_log2, st, o);                                                            \
-        }                                                                                                       \
-        break;                                                                                                  \
+        const ChunkView cv = chunk_view<D>(ar, n);
+        const unsigned char* sb = wbuf + stage * STAGE;
+        switch (ar.tier) {
+#define ARGUS_TILE_CASE(T)                                                                                        \
+    case T: {                                                                                                     \
+        for (int i = 0; i < n; ++i) {                                                                             \
+            const int ntok = (i == n - 1) ? ch.ntok_last : cv.ntok_full;                                          \
+            const int po = i * cv.pstride, so = i * cv.sstride;                                                   \
+            process_tile<D, T>(sb + cv.k_off + po, sb + cv.v_off + po,                                            \
+                               reinterpret_cast<const __half*>(sb + cv.ks_off + so),                              \
+                               reinterpret_cast<const __half*>(sb + cv.vs_off + so),                              \
+                               reinterpret_cast<const __half*>(sb + cv.km_off + so),                              \
+                               reinterpret_cast<const __half*>(sb + cv.vm_off + so), ntok, g4, t4, qf,            \
+                               p.scale_log2, st, o);                                                              \
+        }                                                                                                         \
+        break;                                                                                                    \
     }
             ARGUS_TILE_CASE(ARGUS_TIER_FP16)
             ARGUS_TILE_CASE(ARGUS_TIER_FP8SIM)
@@ -671,7 +736,7 @@ __global__ void combine_kernel(const __grid_constant__ Params p) {
 
 template <int D>
 int launch(const Params& prm, int n_splits, cudaStream_t st) {
-    const size_t smem = (size_t)kWarps * kStages * stage_bytes(D);
+    const size_t smem = (size_t)kWarps * kStages * stage_bytes(D) + stage_slack(D);
     static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kWarps * kStages * stage_bytes(D),
                   "merge buffer must fit in the stage memory");
     cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -691,18 +756,21 @@ int launch(const Params& prm, int n_splits, cudaStream_t st) {
 
 using namespace argus;
 
+namespace {
+bool valid_head_dim(int D) { return D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
+}  // namespace
+
 extern "C" {
 
-int argus_decode_attention_chunk_tiles(int tier, int head_dim) {
-    if (tier < 0 || tier > ARGUS_TIER_1BIT) return 0;
-    switch (head_dim) {
-        case 16: return da::chunk_tiles(tier, 16);
-        case 32: return da::chunk_tiles(tier, 32);
-        case 64: return da::chunk_tiles(tier, 64);
-        case 128: return da::chunk_tiles(tier, 128);
-        case 256: return da::chunk_tiles(tier, 256);
-        default: return 0;
-    }
+int argus_record_bytes(int tier, int page_tokens, int head_dim) {
+    if (tier < ARGUS_TIER_FP16 || tier > ARGUS_TIER_1BIT || page_tokens <= 0 || head_dim <= 0) return 0;
+    return da::record_bytes(tier, page_tokens, head_dim);
+}
+
+int argus_decode_attention_chunk_tiles(int tier, int layout, int page_tokens, int head_dim) {
+    if (tier < ARGUS_TIER_FP16 || tier > ARGUS_TIER_1BIT || !valid_head_dim(head_dim) || page_tokens <= 0) return 0;
+    if (layout != ARGUS_LAYOUT_RECORD && layout != ARGUS_LAYOUT_SPLIT_FP16) return 0;
+    return da::chunk_tiles(tier, layout, page_tokens, head_dim);
 }
 
 int64_t argus_decode_attention_workspace_size(const argus_attn_shape* s) {
@@ -712,20 +780,19 @@ int64_t argus_decode_attention_workspace_size(const argus_attn_shape* s) {
     return groups * s->n_splits * da::kQ * ((int64_t)s->head_dim + 1) * (int64_t)sizeof(float) + 256;
 }
 
-int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_tile* tiles,
-                           const argus_kv_chunk* chunks, const int32_t* split_chunk0, const uint16_t* q, uint16_t* out,
-                           float* lse, void* workspace, argus_stream_t stream) {
+int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
+                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, void* workspace,
+                           argus_stream_t stream) {
     if (!s || !arenas || !split_chunk0 || !q || !out)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
     if (s->batch <= 0 || s->heads_kv <= 0 || s->group <= 0 || s->q_len <= 0 || s->n_splits <= 0)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "non-positive size");
     if (s->n_arenas <= 0 || s->n_arenas > ARGUS_MAX_ARENAS)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "arena count out of range");
-    if (s->n_chunks > 0 && (!tiles || !chunks)) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null tile table");
+    if (s->n_chunks > 0 && !chunks) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null chunk table");
     if ((int64_t)s->batch * s->heads_kv > 65535) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "B*H_kv above 65535");
     const int D = s->head_dim;
-    if (D != 16 && D != 32 && D != 64 && D != 128 && D != 256)
-        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "head_dim must be 16, 32, 64, 128 or 256");
+    if (!valid_head_dim(D)) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "head_dim must be 16, 32, 64, 128 or 256");
     if (!argus_aligned(q, 16) || !argus_aligned(out, 16)) return argus_set_error(ARGUS_ERR_MISALIGNED, "q/out alignment");
     da::Params prm;
     memset(&prm, 0, sizeof(prm));
@@ -733,20 +800,24 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
         const argus_kv_arena& a = arenas[i];
         if (a.tier < ARGUS_TIER_FP16 || a.tier > ARGUS_TIER_1BIT)
             return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad arena tier");
-        if (!a.k || !a.v) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null arena payload");
-        if (!argus_aligned(a.k, 16) || !argus_aligned(a.v, 16) || (a.slot_stride % 16) || (a.bh_stride % 16))
-            return argus_set_error(ARGUS_ERR_MISALIGNED, "arena payload must be 16-byte aligned");
-        if (a.tier != ARGUS_TIER_FP16) {
-            if (!a.k_scale || !a.v_scale) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null arena scales");
-            if (!argus_aligned(a.k_scale, 16) || !argus_aligned(a.v_scale, 16) || (a.scale_slot_stride % 8) ||
-                (a.scale_bh_stride % 8))
-                return argus_set_error(ARGUS_ERR_MISALIGNED, "arena scales must be 16-byte aligned");
-            if (da::tier_min(a.tier) && (!a.k_min || !a.v_min || !argus_aligned(a.k_min, 16) || !argus_aligned(a.v_min, 16)))
-                return argus_set_error(ARGUS_ERR_MISALIGNED, "arena mins must be non-null and 16-byte aligned");
+        if (!a.k || !argus_aligned(a.k, 16) || (a.bh_stride % 16))
+            return argus_set_error(ARGUS_ERR_MISALIGNED, "arena base and (b,h) stride must be 16-byte aligned");
+        if (a.page_tokens <= 0 || a.page_tokens > 65535)
+            return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad page_tokens");
+        if (a.layout == ARGUS_LAYOUT_RECORD) {
+            if (a.tier != ARGUS_TIER_FP16 && (a.page_tokens % 8))
+                return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "quantized pages hold a multiple of 8 tokens");
+            if (a.record_bytes != da::record_bytes(a.tier, a.page_tokens, D))
+                return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "record_bytes does not match tier/page/head_dim");
+            if (a.record_bytes % 16) return argus_set_error(ARGUS_ERR_MISALIGNED, "record size not a multiple of 16");
+        } else if (a.layout == ARGUS_LAYOUT_SPLIT_FP16) {
+            if (a.tier != ARGUS_TIER_FP16 || !a.v || !argus_aligned(a.v, 16) || a.page_tokens != 16)
+                return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "split layout is fp16 K/V tensors in 16-token slots");
+        } else {
+            return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad arena layout");
         }
         prm.arenas[i] = a;
     }
-    prm.tiles = tiles;
     prm.chunks = chunks;
     prm.split_chunk0 = split_chunk0;
     prm.q = reinterpret_cast<const __half*>(q);

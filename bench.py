@@ -81,19 +81,20 @@ def build_cache(device, seed):
         n = ntok // P
         k = torch.randn(n, B, HKV, P, D, device=device, generator=g).half()
         v = torch.randn(n, B, HKV, P, D, device=device, generator=g).half()
+        a = A.KVArena.allocate(A.TIER_NAMES[tier], B, HKV, n, P, D, device)
         if tier == "fp16":
-            a = A.KVArena.from_pools(A.TIER_FP16, k, v)
+            a.write_pages(0, k, v)
         elif tier in ("int8", "fp8"):
             f = Q.quantize_to_int8 if tier == "int8" else Q.quantize_to_fp8_simulated
             (kq, ks), (vq, vs) = f(k), f(v)
-            a = A.KVArena.from_pools(A.TIER_NAMES[tier], kq, vq, ks, vs)
+            a.write_pages(0, kq, vq, ks, vs)
         elif tier in ("int4", "int2"):
             f = Q.quantize_to_int4_packed if tier == "int4" else Q.quantize_to_int2_packed
             (kp, ks, km), (vp, vs, vm) = f(k), f(v)
-            a = A.KVArena.from_pools(A.TIER_NAMES[tier], kp, vp, ks, vs, km, vm)
+            a.write_pages(0, kp, vp, ks, vs, km, vm)
         else:
             (kp, ks), (vp, vs) = Q.quantize_to_1bit_packed(k), Q.quantize_to_1bit_packed(v)
-            a = A.KVArena.from_pools(A.TIER_1BIT, kp, vp, ks, vs)
+            a.write_pages(0, kp, vp, ks, vs)
         del k, v
         ai = len(arenas)
         arenas.append(a)

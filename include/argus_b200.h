@@ -120,41 +120,40 @@ enum argus_tier {
     ARGUS_TIER_1BIT = 5    /* 8 tokens per byte (sign), fp16 scale per token */
 };
 
-/* One storage arena: a tier pool (pages stored as [slot][B][H_kv][packed rows][D]) or an fp16
- * [B][H_kv][L][D] tensor viewed as 16-token slots.  The K (or V) payload of page `slot` for batch
- * b and KV head h starts at  k + slot*slot_stride + (b*H_kv + h)*bh_stride  (bytes) and its
- * per-token scales/mins at  k_scale + slot*scale_slot_stride + (b*H_kv + h)*scale_bh_stride
- * (fp16 elements).  Payload rows (one packed row = `per` tokens x D) are contiguous.  All
- * pointers and byte strides must be 16-byte aligned. */
+/* Arena layouts. */
+enum argus_layout {
+    /* One record per (batch*kv_head, slot): [K payload][V payload][K scales][V scales][K mins][V mins],
+     * record r of (b, h) at  base + (b*H_kv + h)*bh_stride + slot*record_bytes.  Payload = page_tokens/per
+     * packed rows of D bytes (fp16: page_tokens rows of 2D bytes); scales/mins = page_tokens fp16 each. */
+    ARGUS_LAYOUT_RECORD = 0,
+    /* Separate fp16 K and V tensors [B][H_kv][L][D] (sinks, anchors, the staging buffer); slot j is
+     * tokens 16j .. 16j+15, at  k + (b*H_kv + h)*bh_stride + j*16*D*2. */
+    ARGUS_LAYOUT_SPLIT_FP16 = 1
+};
+
+/* One storage arena.  All pointers and byte strides must be 16-byte aligned. */
 typedef struct argus_kv_arena {
-    int32_t tier;
-    int32_t reserved;
-    const void* k;
-    const void* v;
-    const uint16_t* k_scale;
-    const uint16_t* v_scale;
-    const uint16_t* k_min;
-    const uint16_t* v_min;
-    int64_t slot_stride;
-    int64_t bh_stride;
-    int64_t scale_slot_stride;
-    int64_t scale_bh_stride;
+    int32_t tier;         /* argus_tier; ARGUS_TIER_FP16 for the split layout */
+    int32_t layout;       /* argus_layout */
+    const void* k;        /* record base, or the K tensor */
+    const void* v;        /* the V tensor (split layout); unused for records */
+    int64_t bh_stride;    /* bytes between consecutive (b, h) blocks */
+    int32_t record_bytes; /* bytes per record (record layout) */
+    int32_t page_tokens;  /* tokens per slot: page size for records, 16 for the split layout */
 } argus_kv_arena;
 
-/* One tile of up to 16 consecutive tokens inside one page of one arena, in attention order. */
-typedef struct argus_kv_tile {
-    int32_t slot;  /* page slot within the arena */
-    uint16_t tok0; /* first token of the tile within its page (a multiple of 16) */
-    uint8_t arena; /* index into the arena array */
-    uint8_t ntok;  /* tokens in the tile, 1..16 */
-} argus_kv_tile;
-
-/* A run of consecutive tiles of one arena that is staged into shared memory as one unit. */
+/* A run of up to 16 consecutive 16-token tiles of one arena, staged as one unit:
+ *   page_tokens <= 16 (records): tiles are the slots slot0 .. slot0+ntiles-1, one page each;
+ *   page_tokens  > 16 (records): tiles are tokens tok0 .. tok0+16*ntiles-1 of slot slot0;
+ *   split layout: tiles are the 16-token slots slot0 .. slot0+ntiles-1.
+ * The last tile holds ntok_last tokens (1..16; a multiple of 8 for quantized tiers). */
 typedef struct argus_kv_chunk {
-    int32_t tile0;
-    uint8_t ntiles;
+    int32_t slot0;
+    uint16_t tok0;
     uint8_t arena;
-    uint16_t reserved;
+    uint8_t ntiles;
+    uint8_t ntok_last;
+    uint8_t reserved[3];
 } argus_kv_chunk;
 
 #define ARGUS_MAX_ARENAS 8
@@ -176,25 +175,29 @@ typedef struct argus_attn_shape {
 /* Bytes of scratch argus_decode_attention needs for split-K partials (0 when n_splits == 1). */
 int64_t argus_decode_attention_workspace_size(const argus_attn_shape* shape);
 
-/* Chunk capacity: the largest number of tiles of `tier` that one staged chunk may hold for
- * head dim D (the chunk list passed to argus_decode_attention must respect it). */
-int argus_decode_attention_chunk_tiles(int tier, int head_dim);
+/* Chunk capacity: the largest number of tiles of an arena that one staged chunk may hold for
+ * head dim D (the chunk list passed to argus_decode_attention must respect it); page_tokens and
+ * layout as in argus_kv_arena. */
+int argus_decode_attention_chunk_tiles(int tier, int layout, int page_tokens, int head_dim);
+
+/* Bytes of one record of the record layout for a tier, page size and head dim. */
+int argus_record_bytes(int tier, int page_tokens, int head_dim);
 
 /* Decode attention over a paged KV cache held in mixed tiers, fused with the dequantization:
  * out = softmax(q K^T * scale) V for every query token, K/V read straight from the compressed
  * pages.  q: [B][H_q][q_len][D] fp16 (H_q = H_kv * group), out: same shape fp16, lse: optional
  * [B][H_q][q_len] fp32 natural-log sum-exp.  The chunk list covers the cached tokens in any order;
  * split_chunk0[s] .. split_chunk0[s+1] are the chunks of split s (n_splits + 1 entries, device).
- * tiles, chunks and split_chunk0 are device arrays; arenas is a host array copied into the launch.
+ * chunks and split_chunk0 are device arrays; arenas is a host array copied into the launch.
  * workspace: device scratch of argus_decode_attention_workspace_size bytes (may be null when
  * n_splits == 1).
  * Replaces PagedDynamicKVCache.inplace_paged_attention, core/memory_manager.py:1317-1447 (its
  * dequantize-concatenate-softmax part), and the reconstruct-then-SDPA path of
  * get_all_keys_values + transformers' attention (core/memory_manager.py:1157-1315,
  * models/attention_wrapper.py:87-88), which it matches within fp32-accumulation tolerance. */
-int argus_decode_attention(const argus_attn_shape* shape, const argus_kv_arena* arenas, const argus_kv_tile* tiles,
-                           const argus_kv_chunk* chunks, const int32_t* split_chunk0, const uint16_t* q,
-                           uint16_t* out, float* lse, void* workspace, argus_stream_t stream);
+int argus_decode_attention(const argus_attn_shape* shape, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
+                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, void* workspace,
+                           argus_stream_t stream);
 
 /* Reads (and clears) the device-side status word that bounded waits in the kernels set on a
  * timeout; writes ARGUS_OK or ARGUS_ERR_TIMEOUT to *status after synchronising `stream`. */

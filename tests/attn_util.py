@@ -27,7 +27,7 @@ def golden_pages(z, case):
 
 
 def arenas_from_pages(pages, device="cuda"):
-    """Stacks each tier's pages into reference-shaped pools and returns (arenas, page list)."""
+    """Writes each tier's pages into a record arena and returns (arenas, page list)."""
     from argus_b200 import attention as A
 
     tier_id = {"fp16": A.TIER_FP16, "fp8": A.TIER_FP8SIM, "int8": A.TIER_INT8, "int4": A.TIER_INT4,
@@ -38,20 +38,22 @@ def arenas_from_pages(pages, device="cuda"):
             continue
         lst = pages[tier]
         stack = lambda key: torch.from_numpy(np.stack([p[key] for p in lst])).to(device)  # noqa: E731
+        first = lst[0]["key"] if tier == "fp16" else lst[0]["key_scales"]
+        B, H, P = first.shape[0], first.shape[1], first.shape[2]
+        D = (lst[0]["key"] if tier == "fp16" else lst[0].get("key_q", lst[0].get("key_packed"))).shape[-1]
+        a = A.KVArena.allocate(tier_id[tier], B, H, len(lst), P, D, device)
         if tier == "fp16":
-            a = A.KVArena.from_pools(A.TIER_FP16, stack("key"), stack("value"))
+            a.write_pages(0, stack("key"), stack("value"))
         elif tier in ("fp8", "int8"):
-            a = A.KVArena.from_pools(tier_id[tier], stack("key_q"), stack("value_q"), stack("key_scales"),
-                                     stack("value_scales"))
+            a.write_pages(0, stack("key_q"), stack("value_q"), stack("key_scales"), stack("value_scales"))
         elif tier in ("int4", "int2"):
-            a = A.KVArena.from_pools(tier_id[tier], stack("key_packed"), stack("value_packed"), stack("key_scales"),
-                                     stack("value_scales"), stack("key_min"), stack("value_min"))
+            a.write_pages(0, stack("key_packed"), stack("value_packed"), stack("key_scales"), stack("value_scales"),
+                          stack("key_min"), stack("value_min"))
         else:
-            a = A.KVArena.from_pools(tier_id[tier], stack("key_packed"), stack("value_packed"), stack("key_scales"),
-                                     stack("value_scales"))
+            a.write_pages(0, stack("key_packed"), stack("value_packed"), stack("key_scales"), stack("value_scales"))
         ai = len(arenas)
         arenas.append(a)
-        plist += [(ai, j, a.page_tokens) for j in range(len(lst))]
+        plist += [(ai, j, P) for j in range(len(lst))]
     return arenas, plist
 
 

@@ -49,6 +49,10 @@ SHAPES = [
     (1, 1, 16, 128, 16, 1, [("int8", 32), ("fp16", 16)]),
     (1, 2, 4, 32, 16, 3, [("int2", 48), ("fp8", 32), ("fp16", 16)]),
     (1, 1, 4, 256, 16, 1, [("int4", 32), ("one_bit", 32), ("fp16", 16)]),
+    # pages larger than a tile (records staged tile by tile) and 8-token pages
+    (1, 2, 4, 128, 64, 1, [("one_bit", 128), ("int2", 64), ("int4", 128), ("int8", 64), ("fp8", 64), ("fp16", 64)]),
+    (2, 1, 4, 64, 8, 1, [("one_bit", 32), ("int2", 32), ("int4", 32), ("int8", 16), ("fp8", 16), ("fp16", 16)]),
+    (1, 1, 8, 128, 48, 2, [("int4", 96), ("fp16", 48)]),
 ]
 
 
