@@ -396,36 +396,40 @@ __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4,
 }
 
 struct SoftmaxState {
-    float m[2];  // running max (log2 domain) for queries 2t, 2t+1
+    float m[2];  // reference max (log2 domain) for queries 2t, 2t+1; weights are 2^(x - m)
     float l[2];  // this thread's partial sum of weights
 };
 
+// Lazy rescaling: the reference max only moves when a score exceeds it by more than this (log2
+// units), so weights stay <= 2^8 (exact range for fp16 P) and rescales of O are rare.
+constexpr float kRescaleSlack = 8.0f;
+
 __device__ __forceinline__ __half2 load_h2(const __half* p) { return *reinterpret_cast<const __half2*>(p); }
 
-// Processes one staged tile: exact dequantization into fragments, scores, online softmax, PV.
-template <int D, int TIER>
-__device__ __forceinline__ void process_tile(const unsigned char* kp, const unsigned char* vp, const __half* ks,
-                                             const __half* vs, const __half* km, const __half* vm, int ntok, int g4,
-                                             int t4, const uint32_t (&qf)[D / 16][2], float scale_log2,
-                                             SoftmaxState& st, float (&o)[D / 16][4]) {
-    constexpr int KC = D / 16;
-    const int tokA = 2 * g4, tokB = 2 * g4 + 1;
-    const bool va = tokA < ntok, vb = tokB < ntok;
-    // ---- per-token parameters (K: tokens 2g, 2g+1; V: tokens 4u..4u+3)
-    TokScale tk, tv;
-    bool fast = true;
+// Pointers of one staged tile.
+struct TilePtr {
+    const unsigned char* k;
+    const unsigned char* v;
+    const __half *ks, *vs, *km, *vm;
+    int ntok;
+};
+
+template <int TIER>
+__device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t4, TokScale& tk, TokScale& tv,
+                                                bool& fast) {
+    fast = true;
     if constexpr (TIER != ARGUS_TIER_FP16) {
-        const __half2 k2 = load_h2(ks + tokA);
+        const __half2 k2 = load_h2(tp.ks + 2 * g4);
         tk.s[0] = __low2half2(k2);
         tk.s[1] = __high2half2(k2);
-        const uint2 v4 = *reinterpret_cast<const uint2*>(vs + 4 * t4);
+        const uint2 v4 = *reinterpret_cast<const uint2*>(tp.vs + 4 * t4);
         tv.s[0] = u2h(prmt(v4.x, v4.y, 0x5410));
         tv.s[1] = u2h(prmt(v4.x, v4.y, 0x7632));
         if constexpr (tier_min(TIER)) {
-            const __half2 m2 = load_h2(km + tokA);
+            const __half2 m2 = load_h2(tp.km + 2 * g4);
             tk.mn[0] = __low2half2(m2);
             tk.mn[1] = __high2half2(m2);
-            const uint2 w4 = *reinterpret_cast<const uint2*>(vm + 4 * t4);
+            const uint2 w4 = *reinterpret_cast<const uint2*>(tp.vm + 4 * t4);
             tv.mn[0] = u2h(prmt(w4.x, w4.y, 0x5410));
             tv.mn[1] = u2h(prmt(w4.x, w4.y, 0x7632));
             const __half2 lim = __float2half2_rn(kFmaScaleLimit);
@@ -436,60 +440,112 @@ __device__ __forceinline__ void process_tile(const unsigned char* kp, const unsi
             for (int i = 0; i < 2; ++i) { tk.ns[i] = __hmul2(tk.s[i], n1024); tv.ns[i] = __hmul2(tv.s[i], n1024); }
         }
     }
-    // ---- S^T = K . Q^T
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-        uint32_t a[KC][4];
-        if (fast) k_frags<D, TIER, true>(kp, g4, t4, tk, a);
-        else k_frags<D, TIER, false>(kp, g4, t4, tk, a);
-        // two independent accumulation chains halve the dependent-MMA latency
-        float s2[4] = {0.f, 0.f, 0.f, 0.f};
+}
+
+// Rare path (a scale >= 64 or NaN in the tile): dequantize without the fma shortcut.
+template <int D, int TIER>
+__device__ __forceinline__ void k_frags_slow(const unsigned char* kp, int g4, int t4, const TokScale& ts,
+                                          uint32_t (&a)[D / 16][4]) {
+    k_frags<D, TIER, false>(kp, g4, t4, ts, a);
+}
+template <int D, int TIER>
+__device__ __forceinline__ void v_frags_slow(const unsigned char* vp, int g4, int t4, const TokScale& ts,
+                                          uint32_t (&a)[D / 16][4]) {
+    v_frags<D, TIER, false>(vp, g4, t4, ts, a);
+}
+
+// Scores of one tile in the log2 domain: x[0..3] = (token 2g, query 2t), (2g, 2t+1), (2g+1, 2t),
+// (2g+1, 2t+1); tokens past the tile's end are -inf.
+template <int D, int TIER>
+__device__ __forceinline__ void tile_scores(const TilePtr& tp, int g4, int t4, const TokScale& tk, bool fast,
+                                            const uint32_t (&qf)[D / 16][2], float scale_log2, float (&x)[4]) {
+    constexpr int KC = D / 16;
+    uint32_t a[KC][4];
+    if (fast) k_frags<D, TIER, true>(tp.k, g4, t4, tk, a);
+    else k_frags_slow<D, TIER>(tp.k, g4, t4, tk, a);
+    float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < KC; c += 2) {
-            mma16816(s, a[c], qf[c][0], qf[c][1]);
-            if (c + 1 < KC) mma16816(s2, a[c + 1], qf[c + 1][0], qf[c + 1][1]);
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s[e] += s2[e];
+    for (int c = 0; c < KC; c += 2) {
+        mma16816(s, a[c], qf[c][0], qf[c][1]);
+        if (c + 1 < KC) mma16816(s2, a[c + 1], qf[c + 1][0], qf[c + 1][1]);
     }
-    float x[4] = {s[0] * scale_log2, s[1] * scale_log2, s[2] * scale_log2, s[3] * scale_log2};
-    if (!va) { x[0] = -INFINITY; x[1] = -INFINITY; }
-    if (!vb) { x[2] = -INFINITY; x[3] = -INFINITY; }
-    // ---- online softmax (queries 2t4 -> index 0, 2t4+1 -> index 1)
-    float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+    const bool va = 2 * g4 < tp.ntok, vb = 2 * g4 + 1 < tp.ntok;
+    x[0] = va ? (s[0] + s2[0]) * scale_log2 : -INFINITY;
+    x[1] = va ? (s[1] + s2[1]) * scale_log2 : -INFINITY;
+    x[2] = vb ? (s[2] + s2[2]) * scale_log2 : -INFINITY;
+    x[3] = vb ? (s[3] + s2[3]) * scale_log2 : -INFINITY;
+}
+
+// O^T += V^T . P^T for one tile, P given as the two movmatrix-transposed fp16 fragments.
+template <int D, int TIER>
+__device__ __forceinline__ void tile_pv(const TilePtr& tp, int g4, int t4, const TokScale& tv, bool fast,
+                                        uint32_t b01, uint32_t b23, float (&o)[D / 16][4]) {
+    constexpr int KC = D / 16;
+    uint32_t av[KC][4];
+    if (fast) v_frags<D, TIER, true>(tp.v, g4, t4, tv, av);
+    else v_frags_slow<D, TIER>(tp.v, g4, t4, tv, av);
+    if (tp.ntok < 16) {
+        // tokens past the tile's end may hold non-finite garbage: zero their V values
+        const int nt = tp.ntok;
+        const uint32_t m01 = (4 * t4 < nt ? 0x0000FFFFu : 0u) | (4 * t4 + 2 < nt ? 0xFFFF0000u : 0u);
+        const uint32_t m23 = (4 * t4 + 1 < nt ? 0x0000FFFFu : 0u) | (4 * t4 + 3 < nt ? 0xFFFF0000u : 0u);
+#pragma unroll
+        for (int t = 0; t < KC; ++t) { av[t][0] &= m01; av[t][1] &= m01; av[t][2] &= m23; av[t][3] &= m23; }
+    }
+#pragma unroll
+    for (int t = 0; t < KC; ++t) mma16816(o[t], av[t], b01, b23);
+}
+
+// Online softmax over NT tiles' scores at once: one max reduction and at most one rescale.
+template <int KC, int NT>
+__device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxState& st, float (&o)[KC][4],
+                                               uint32_t (&b01)[NT], uint32_t (&b23)[NT]) {
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NT; ++i) { mx0 = fmaxf(mx0, fmaxf(x[i][0], x[i][2])); mx1 = fmaxf(mx1, fmaxf(x[i][1], x[i][3])); }
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
     }
-    const float n0 = fmaxf(st.m[0], mx0), n1 = fmaxf(st.m[1], mx1);
-    if (n0 > st.m[0] || n1 > st.m[1]) {
+    if (mx0 > st.m[0] + kRescaleSlack || mx1 > st.m[1] + kRescaleSlack) {
+        const float n0 = fmaxf(st.m[0], mx0), n1 = fmaxf(st.m[1], mx1);
         const float f0 = exp2f(st.m[0] - n0), f1 = exp2f(st.m[1] - n1);  // -inf - finite -> 0
 #pragma unroll
         for (int t = 0; t < KC; ++t) { o[t][0] *= f0; o[t][2] *= f0; o[t][1] *= f1; o[t][3] *= f1; }
         st.l[0] *= f0; st.l[1] *= f1;
         st.m[0] = n0; st.m[1] = n1;
     }
-    const float b0 = (st.m[0] == -INFINITY) ? 0.f : st.m[0];
-    const float b1 = (st.m[1] == -INFINITY) ? 0.f : st.m[1];
-    const float p0 = exp2f(x[0] - b0), p1 = exp2f(x[1] - b1), p2 = exp2f(x[2] - b0), p3 = exp2f(x[3] - b1);
-    st.l[0] += p0 + p2;
-    st.l[1] += p1 + p3;
-    const uint32_t b01 = movmatrix_t(pack_half2(p0, p1));  // mma rows 0..7 (tokens 2g)
-    const uint32_t b23 = movmatrix_t(pack_half2(p2, p3));  // mma rows 8..15 (tokens 2g+1)
-    // ---- O^T += V^T . P^T
-    uint32_t av[KC][4];
-    if (fast) v_frags<D, TIER, true>(vp, g4, t4, tv, av);
-    else v_frags<D, TIER, false>(vp, g4, t4, tv, av);
-    if (ntok < 16) {
-        // tokens past the tile's end may hold non-finite garbage: zero their V values
-        const uint32_t m01 = (4 * t4 < ntok ? 0x0000FFFFu : 0u) | (4 * t4 + 2 < ntok ? 0xFFFF0000u : 0u);
-        const uint32_t m23 = (4 * t4 + 1 < ntok ? 0x0000FFFFu : 0u) | (4 * t4 + 3 < ntok ? 0xFFFF0000u : 0u);
+    const float m0 = (st.m[0] == -INFINITY) ? 0.f : st.m[0];
+    const float m1 = (st.m[1] == -INFINITY) ? 0.f : st.m[1];
 #pragma unroll
-        for (int t = 0; t < KC; ++t) { av[t][0] &= m01; av[t][1] &= m01; av[t][2] &= m23; av[t][3] &= m23; }
+    for (int i = 0; i < NT; ++i) {
+        const float p0 = exp2f(x[i][0] - m0), p1 = exp2f(x[i][1] - m1);
+        const float p2 = exp2f(x[i][2] - m0), p3 = exp2f(x[i][3] - m1);
+        st.l[0] += p0 + p2;
+        st.l[1] += p1 + p3;
+        b01[i] = movmatrix_t(pack_half2(p0, p1));  // mma rows 0..7 (tokens 2g)
+        b23[i] = movmatrix_t(pack_half2(p2, p3));  // mma rows 8..15 (tokens 2g+1)
     }
-#pragma unroll
-    for (int t = 0; t < KC; ++t) mma16816(o[t], av[t], b01, b23);
+}
+
+// Processes tiles i0 and (if pair) i0+1 of a staged chunk with interleaved independent work.
+template <int D, int TIER, bool PAIR>
+__device__ __forceinline__ void process_tiles(const TilePtr& ta, const TilePtr& tb, int g4, int t4,
+                                              const uint32_t (&qf)[D / 16][2], float scale_log2, SoftmaxState& st,
+                                              float (&o)[D / 16][4]) {
+    constexpr int NT = PAIR ? 2 : 1;
+    TokScale tk[NT], tv[NT];
+    bool fast[NT];
+    float x[NT][4];
+    load_tok_scales<TIER>(ta, g4, t4, tk[0], tv[0], fast[0]);
+    if constexpr (PAIR) load_tok_scales<TIER>(tb, g4, t4, tk[NT - 1], tv[NT - 1], fast[NT - 1]);
+    tile_scores<D, TIER>(ta, g4, t4, tk[0], fast[0], qf, scale_log2, x[0]);
+    if constexpr (PAIR) tile_scores<D, TIER>(tb, g4, t4, tk[NT - 1], fast[NT - 1], qf, scale_log2, x[NT - 1]);
+    uint32_t b01[NT], b23[NT];
+    softmax_update<D / 16, NT>(x, st, o, b01, b23);
+    tile_pv<D, TIER>(ta, g4, t4, tv[0], fast[0], b01[0], b23[0], o);
+    if constexpr (PAIR) tile_pv<D, TIER>(tb, g4, t4, tv[NT - 1], fast[NT - 1], b01[NT - 1], b23[NT - 1], o);
 }
 
 template <int D>
@@ -610,15 +666,27 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
         switch (ar.tier) {
 #define ARGUS_TILE_CASE(T)                                                                                        \
     case T: {                                                                                                     \
-        for (int i = 0; i < n; ++i) {                                                                             \
-            const int ntok = (i == n - 1) ? ch.ntok_last : cv.ntok_full;                                          \
+        auto tile = [&](int i) {                                                                                  \
+            TilePtr tp;                                                                                           \
             const int po = i * cv.pstride, so = i * cv.sstride;                                                   \
-            process_tile<D, T>(sb + cv.k_off + po, sb + cv.v_off + po,                                            \
-                               reinterpret_cast<const __half*>(sb + cv.ks_off + so),                              \
-                               reinterpret_cast<const __half*>(sb + cv.vs_off + so),                              \
-                               reinterpret_cast<const __half*>(sb + cv.km_off + so),                              \
-                               reinterpret_cast<const __half*>(sb + cv.vm_off + so), ntok, g4, t4, qf,            \
-                               p.scale_log2, st, o);                                                              \
+            tp.k = sb + cv.k_off + po;                                                                            \
+            tp.v = sb + cv.v_off + po;                                                                            \
+            tp.ks = reinterpret_cast<const __half*>(sb + cv.ks_off + so);                                         \
+            tp.vs = reinterpret_cast<const __half*>(sb + cv.vs_off + so);                                         \
+            tp.km = reinterpret_cast<const __half*>(sb + cv.km_off + so);                                         \
+            tp.vm = reinterpret_cast<const __half*>(sb + cv.vm_off + so);                                         \
+            tp.ntok = (i == n - 1) ? ch.ntok_last : cv.ntok_full;                                                 \
+            return tp;                                                                                            \
+        };                                                                                                        \
+        int i = 0;                                                                                                \
+        /* pairs of tiles for ILP; at D = 256 the pair would not fit in registers */                           \
+        for (; D <= 128 && i + 1 < n; i += 2) {                                                                   \
+            const TilePtr ta = tile(i), tb = tile(i + 1);                                                         \
+            process_tiles<D, T, true>(ta, tb, g4, t4, qf, p.scale_log2, st, o);                                   \
+        }                                                                                                         \
+        for (; i < n; ++i) {                                                                                      \
+            const TilePtr ta = tile(i);                                                                           \
+            process_tiles<D, T, false>(ta, ta, g4, t4, qf, p.scale_log2, st, o);                                  \
         }                                                                                                         \
         break;                                                                                                    \
     }
