@@ -402,7 +402,13 @@ struct SoftmaxState {
 
 // Lazy rescaling: the reference max only moves when a score exceeds it by more than this (log2
 // units), so weights stay <= 2^8 (exact range for fp16 P) and rescales of O are rare.
-constexpr float kRescaleSlack = 8.0f;
+#ifndef ARGUS_DA_RESCALE_SLACK
+#define ARGUS_DA_RESCALE_SLACK 8.0f
+#endif
+constexpr float kRescaleSlack = ARGUS_DA_RESCALE_SLACK;
+#ifndef ARGUS_DA_PAIR
+#define ARGUS_DA_PAIR 0
+#endif
 
 __device__ __forceinline__ __half2 load_h2(const __half* p) { return *reinterpret_cast<const __half2*>(p); }
 
@@ -679,8 +685,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
             return tp;                                                                                            \
         };                                                                                                        \
         int i = 0;                                                                                                \
-        /* pairs of tiles for ILP; at D = 256 the pair would not fit in registers */                           \
-        for (; D <= 128 && i + 1 < n; i += 2) {                                                                   \
+        /* tile pairs (ARGUS_DA_PAIR=1) measured slower on B200: register pressure; D = 256 never pairs */      \
+        for (; ARGUS_DA_PAIR && D <= 128 && i + 1 < n; i += 2) {                                                                   \
             const TilePtr ta = tile(i), tb = tile(i + 1);                                                         \
             process_tiles<D, T, true>(ta, tb, g4, t4, qf, p.scale_log2, st, o);                                   \
         }                                                                                                         \
