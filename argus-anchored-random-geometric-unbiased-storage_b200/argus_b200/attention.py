@@ -52,7 +52,9 @@ class ShapeC(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("heads_kv", ctypes.c_int32), ("group", ctypes.c_int32),
                 ("q_len", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("n_splits", ctypes.c_int32),
                 ("n_arenas", ctypes.c_int32), ("n_chunks", ctypes.c_int32), ("scale", ctypes.c_float),
-                ("reserved", ctypes.c_int32)]
+                ("flags", ctypes.c_int32)]
+
+ATTN_PRECISE_PV = 1
 
 
 assert ctypes.sizeof(ChunkC) == 12
@@ -179,7 +181,8 @@ class AttentionPlan:
     pages: sequence of (arena_index, slot, n_tokens).  Record pages of <= 16 tokens must be full;
     longer record pages and split-fp16 slots may end short."""
 
-    def __init__(self, arenas, pages, *, batch, heads_kv, group, head_dim, q_len=1, n_splits=None, device=None):
+    def __init__(self, arenas, pages, *, batch, heads_kv, group, head_dim, q_len=1, n_splits=None, device=None,
+                 precise_pv=False):
         if not 0 < len(arenas) <= MAX_ARENAS:
             raise ValueError(f"1..{MAX_ARENAS} arenas supported")
         self.arenas = list(arenas)
@@ -262,7 +265,7 @@ class AttentionPlan:
         self.splits_dev = torch.from_numpy(bounds.astype(np.int32)).to(self.device)
         self._arena_c = (ArenaC * MAX_ARENAS)(*[a.c_struct() for a in self.arenas])
         self._shape = ShapeC(self.B, self.Hkv, self.G, self.qlen, self.D, n_splits, len(self.arenas), self.n_chunks,
-                             1.0 / math.sqrt(self.D), 0)
+                             1.0 / math.sqrt(self.D), ATTN_PRECISE_PV if precise_pv else 0)
         ws = _bind().argus_decode_attention_workspace_size(ctypes.byref(self._shape))
         self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=self.device) if ws > 0 else None
         self.chunks = chunks

@@ -10,7 +10,8 @@
 // A warp rebuilds each staged tile in registers as the exact fp16 values the reference's
 // dequantizers produce (fp16(fp16(u*s) + min), fp16(q*s), +-s) and feeds them to mma.sync m16n8k16:
 //   S^T[16 tokens x 8 queries] = K[16 x D] . Q^T        (tokens on M, queries on N)
-//   O^T[D x 8 queries]        += V^T[D x 16] . P^T      (P = unnormalised softmax weights, fp16)
+//   O^T[D x 8 queries]        += V^T[D x 16] . P^T      (P = unnormalised softmax weights as an
+//                                                        fp16 hi + lo pair, two MMAs)
 // A token/dim permutation lets each thread turn whole packed bytes into fragments:
 //   K (A operand) thread (g, t) holds tokens 2g, 2g+1 and dims t*D/4 .. t*D/4 + D/4 - 1;
 //   V (A operand) thread (g, t) holds tokens 4t .. 4t+3 and dims g*D/8 .. g*D/8 + D/8 - 1.
@@ -213,7 +214,6 @@ __device__ __forceinline__ void lds_small(const unsigned char* p, uint32_t* r) {
 
 constexpr uint32_t kMagic1024 = 0x64006400u;  // fp16 1024.0 in both halves: 1024 + u for u in 0..1023
 constexpr uint32_t kMagic1152 = 0x64806480u;  // 1024 + 128 (bias of sign-flipped int8 codes)
-constexpr float kFmaScaleLimit = 63.96875f;   // 1024 * s stays finite in fp16 below this
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
@@ -224,31 +224,38 @@ __device__ __forceinline__ uint32_t lop_sign(uint32_t a, uint32_t m, uint32_t c)
     return r;
 }
 
-// Exact dequantization of unsigned codes held as (1024 + u) in fp16 halves:
-//   fp16(fp16(u * s) + mn).  Fast form: fp16(u * s) = fma((1024 + u), s, -1024 s) with one rounding,
-//   exact while 1024 s is finite; otherwise subtract the bias and multiply (two roundings-free steps).
-template <bool FAST, bool MIN>
-__device__ __forceinline__ uint32_t deq_u(uint32_t biased, __half2 s, __half2 ns1024, __half2 mn) {
-    __half2 v;
-    if constexpr (FAST) {
-        v = __hfma2(u2h(biased), s, ns1024);
-    } else {
-        v = __hmul2_rn(__hsub2(u2h(biased), u2h(kMagic1024)), s);
-    }
-    if constexpr (MIN) v = __hadd2_rn(v, mn);
-    return h2u(v);
+// Exact dequantization of unsigned codes held as (1024 + u) in fp16 halves: fp16(fp16(u*s) + mn).
+// r = fma(1024 + u, s*2^-k, -s*2^(10-k)) is fp16(u*s)*2^-k with a single rounding (the addend is
+// exact, and for k = 10 the scaled product stays a normal number), then fma(r, 2^k, mn) =
+// fp16(fp16(u*s) + mn).  k = 0 for s < 64, k = 10 above, so every finite scale is exact.
+__device__ __forceinline__ uint32_t deq_u(uint32_t biased, __half2 b, __half2 c, __half2 f, __half2 mn) {
+    return h2u(__hfma2(__hfma2(u2h(biased), b, c), f, mn));
 }
 
-// Per-token dequantization parameters of one operand, as half2 pairs.
+// Per-token dequantization parameters of one operand, as half2 pairs over two tokens.
 struct TokScale {
-    __half2 s[2], ns[2], mn[2];  // scale, -1024*scale, min for the two half2 token pairs
+    __half2 s[2];   // scale
+    __half2 b[2];   // s * 2^-k
+    __half2 c[2];   // -s * 2^(10-k)
+    __half2 f[2];   // 2^k
+    __half2 mn[2];  // min
 };
+
+// Fills b, c, f from s: k = 10 where s >= 64 (so -1024*s would overflow fp16), else 0.
+__device__ __forceinline__ void scale_terms(TokScale& t, int i) {
+    const __half2 big = __hge2(t.s[i], __float2half2_rn(64.0f));  // 1.0 where s >= 64
+    const __half2 kf = __hfma2(big, __float2half2_rn(1023.0f), __float2half2_rn(1.0f));  // 2^k: 1 or 1024
+    const __half2 ik = __hfma2(big, __float2half2_rn(-0.9990234375f), __float2half2_rn(1.0f));  // 2^-k
+    t.f[i] = kf;
+    t.b[i] = __hmul2(t.s[i], ik);
+    t.c[i] = __hmul2(__hneg2(t.s[i]), __hmul2(__float2half2_rn(1024.0f), ik));
+}
 
 // ------------------------------------------------------------------------ K fragments (QK^T)
 // a[c][0..3] for k-chunk c: (token 2g, dims 4c..4c+1), (token 2g+1, same), (token 2g, 4c+2..3),
 // (token 2g+1, 4c+2..3), dims relative to this thread's span t*D/4.  Values are the reference's
 // fp16 dequantization, bit for bit.  ts.s[0] is token 2g broadcast, ts.s[1] token 2g+1.
-template <int D, int TIER, bool FAST>
+template <int D, int TIER>
 __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4, const TokScale& ts,
                                         uint32_t (&a)[D / 16][4]) {
     constexpr int KC = D / 16;
@@ -285,10 +292,10 @@ __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4,
 #pragma unroll
         for (int c = 0; c < KC; ++c) {
             const uint32_t x01 = prmt(r[c], 0u, 0x4140), x23 = prmt(r[c], 0u, 0x4342);
-            a[c][0] = deq_u<FAST, true>(lop_and_or(x01 >> shA, M, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
-            a[c][1] = deq_u<FAST, true>(lop_and_or(x01 >> shB, M, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
-            a[c][2] = deq_u<FAST, true>(lop_and_or(x23 >> shA, M, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
-            a[c][3] = deq_u<FAST, true>(lop_and_or(x23 >> shB, M, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+            a[c][0] = deq_u(lop_and_or(x01 >> shA, M, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[c][1] = deq_u(lop_and_or(x01 >> shB, M, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            a[c][2] = deq_u(lop_and_or(x23 >> shA, M, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[c][3] = deq_u(lop_and_or(x23 >> shB, M, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
         }
     } else {  // 1-bit: b ? +s : -s, the sign bit taken from the packed bit moved to bit 15 / 31
         uint32_t r[KC];
@@ -310,7 +317,7 @@ __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4,
 // a[t][0..3] for m-tile t: (dim 2t, tokens 4u,4u+2), (dim 2t+1, tokens 4u,4u+2),
 // (dim 2t, tokens 4u+1,4u+3), (dim 2t+1, tokens 4u+1,4u+3); u = t4, dims relative to g*D/8.
 // ts.s[0] = (s_4u, s_4u+2), ts.s[1] = (s_4u+1, s_4u+3).  Exact fp16 dequantized values.
-template <int D, int TIER, bool FAST>
+template <int D, int TIER>
 __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4, const TokScale& ts,
                                         uint32_t (&a)[D / 16][4]) {
     constexpr int KC = D / 16;
@@ -357,10 +364,10 @@ __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4,
             const int w = t >> 1, e0 = 2 * (t & 1);
             const uint32_t y0 = prmt(ra[w], rb[w], e0 | ((4 + e0) << 8));              // (A.d0, -, B.d0, -)
             const uint32_t y1 = prmt(ra[w], rb[w], (e0 + 1) | ((5 + e0) << 8));        // (A.d1, -, B.d1, -)
-            a[t][0] = deq_u<FAST, true>(lop_and_or(y0, 0x000F000Fu, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
-            a[t][2] = deq_u<FAST, true>(lop_and_or(y0 >> 4, 0x000F000Fu, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
-            a[t][1] = deq_u<FAST, true>(lop_and_or(y1, 0x000F000Fu, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
-            a[t][3] = deq_u<FAST, true>(lop_and_or(y1 >> 4, 0x000F000Fu, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+            a[t][0] = deq_u(lop_and_or(y0, 0x000F000Fu, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][2] = deq_u(lop_and_or(y0 >> 4, 0x000F000Fu, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            a[t][1] = deq_u(lop_and_or(y1, 0x000F000Fu, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][3] = deq_u(lop_and_or(y1 >> 4, 0x000F000Fu, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
         }
     } else if constexpr (TIER == ARGUS_TIER_INT2) {
         uint32_t r[W];
@@ -371,10 +378,10 @@ __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4,
             const uint32_t rs = r[w] >> 4;  // bits 4..7 of each byte moved down
             const uint32_t y0 = prmt(r[w], rs, e0 | ((4 + e0) << 8));             // (d0 bits0-3, -, d0 bits4-7, -)
             const uint32_t y1 = prmt(r[w], rs, (e0 + 1) | ((5 + e0) << 8));
-            a[t][0] = deq_u<FAST, true>(lop_and_or(y0, 0x00030003u, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
-            a[t][2] = deq_u<FAST, true>(lop_and_or(y0 >> 2, 0x00030003u, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
-            a[t][1] = deq_u<FAST, true>(lop_and_or(y1, 0x00030003u, kMagic1024), ts.s[0], ts.ns[0], ts.mn[0]);
-            a[t][3] = deq_u<FAST, true>(lop_and_or(y1 >> 2, 0x00030003u, kMagic1024), ts.s[1], ts.ns[1], ts.mn[1]);
+            a[t][0] = deq_u(lop_and_or(y0, 0x00030003u, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][2] = deq_u(lop_and_or(y0 >> 2, 0x00030003u, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            a[t][1] = deq_u(lop_and_or(y1, 0x00030003u, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][3] = deq_u(lop_and_or(y1 >> 2, 0x00030003u, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
         }
     } else {  // 1-bit: tokens 4u+i sit in bit k0+i of row u/2, k0 = 4(u&1)
         uint32_t r[W];
@@ -421,9 +428,7 @@ struct TilePtr {
 };
 
 template <int TIER>
-__device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t4, TokScale& tk, TokScale& tv,
-                                                bool& fast) {
-    fast = true;
+__device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t4, TokScale& tk, TokScale& tv) {
     if constexpr (TIER != ARGUS_TIER_FP16) {
         const __half2 k2 = load_h2(tp.ks + 2 * g4);
         tk.s[0] = __low2half2(k2);
@@ -438,37 +443,20 @@ __device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t
             const uint2 w4 = *reinterpret_cast<const uint2*>(tp.vm + 4 * t4);
             tv.mn[0] = u2h(prmt(w4.x, w4.y, 0x5410));
             tv.mn[1] = u2h(prmt(w4.x, w4.y, 0x7632));
-            const __half2 lim = __float2half2_rn(kFmaScaleLimit);
-            const bool ok = __hbge2(lim, k2) && __hbge2(lim, tv.s[0]) && __hbge2(lim, tv.s[1]);
-            fast = __all_sync(0xffffffffu, ok);
-            const __half2 n1024 = __float2half2_rn(-1024.0f);
 #pragma unroll
-            for (int i = 0; i < 2; ++i) { tk.ns[i] = __hmul2(tk.s[i], n1024); tv.ns[i] = __hmul2(tv.s[i], n1024); }
+            for (int i = 0; i < 2; ++i) { scale_terms(tk, i); scale_terms(tv, i); }
         }
     }
-}
-
-// Rare path (a scale >= 64 or NaN in the tile): dequantize without the fma shortcut.
-template <int D, int TIER>
-__device__ __forceinline__ void k_frags_slow(const unsigned char* kp, int g4, int t4, const TokScale& ts,
-                                          uint32_t (&a)[D / 16][4]) {
-    k_frags<D, TIER, false>(kp, g4, t4, ts, a);
-}
-template <int D, int TIER>
-__device__ __forceinline__ void v_frags_slow(const unsigned char* vp, int g4, int t4, const TokScale& ts,
-                                          uint32_t (&a)[D / 16][4]) {
-    v_frags<D, TIER, false>(vp, g4, t4, ts, a);
 }
 
 // Scores of one tile in the log2 domain: x[0..3] = (token 2g, query 2t), (2g, 2t+1), (2g+1, 2t),
 // (2g+1, 2t+1); tokens past the tile's end are -inf.
 template <int D, int TIER>
-__device__ __forceinline__ void tile_scores(const TilePtr& tp, int g4, int t4, const TokScale& tk, bool fast,
+__device__ __forceinline__ void tile_scores(const TilePtr& tp, int g4, int t4, const TokScale& tk,
                                             const uint32_t (&qf)[D / 16][2], float scale_log2, float (&x)[4]) {
     constexpr int KC = D / 16;
     uint32_t a[KC][4];
-    if (fast) k_frags<D, TIER, true>(tp.k, g4, t4, tk, a);
-    else k_frags_slow<D, TIER>(tp.k, g4, t4, tk, a);
+    k_frags<D, TIER>(tp.k, g4, t4, tk, a);
     float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < KC; c += 2) {
@@ -483,13 +471,12 @@ __device__ __forceinline__ void tile_scores(const TilePtr& tp, int g4, int t4, c
 }
 
 // O^T += V^T . P^T for one tile, P given as the two movmatrix-transposed fp16 fragments.
-template <int D, int TIER>
-__device__ __forceinline__ void tile_pv(const TilePtr& tp, int g4, int t4, const TokScale& tv, bool fast,
-                                        uint32_t b01, uint32_t b23, float (&o)[D / 16][4]) {
+template <int D, int TIER, bool PRECISE>
+__device__ __forceinline__ void tile_pv(const TilePtr& tp, int g4, int t4, const TokScale& tv, uint32_t b01,
+                                        uint32_t b23, uint32_t c01, uint32_t c23, float (&o)[D / 16][4]) {
     constexpr int KC = D / 16;
     uint32_t av[KC][4];
-    if (fast) v_frags<D, TIER, true>(tp.v, g4, t4, tv, av);
-    else v_frags_slow<D, TIER>(tp.v, g4, t4, tv, av);
+    v_frags<D, TIER>(tp.v, g4, t4, tv, av);
     if (tp.ntok < 16) {
         // tokens past the tile's end may hold non-finite garbage: zero their V values
         const int nt = tp.ntok;
@@ -499,13 +486,19 @@ __device__ __forceinline__ void tile_pv(const TilePtr& tp, int g4, int t4, const
         for (int t = 0; t < KC; ++t) { av[t][0] &= m01; av[t][1] &= m01; av[t][2] &= m23; av[t][3] &= m23; }
     }
 #pragma unroll
-    for (int t = 0; t < KC; ++t) mma16816(o[t], av[t], b01, b23);
+    for (int t = 0; t < KC; ++t) {
+        mma16816(o[t], av[t], b01, b23);
+        if constexpr (PRECISE) mma16816(o[t], av[t], c01, c23);
+    }
 }
 
-// Online softmax over NT tiles' scores at once: one max reduction and at most one rescale.
-template <int KC, int NT>
+// Online softmax over NT tiles' scores at once: one max reduction and at most one rescale.  The
+// weights go to the PV contraction as two fp16 fragments, p = hi + lo (lo = fp16(p - hi)), so the
+// product keeps ~22 bits of the fp32 weight instead of fp16's 11.
+template <int KC, int NT, bool PRECISE>
 __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxState& st, float (&o)[KC][4],
-                                               uint32_t (&b01)[NT], uint32_t (&b23)[NT]) {
+                                               uint32_t (&b01)[NT], uint32_t (&b23)[NT], uint32_t (&c01)[NT],
+                                               uint32_t (&c23)[NT]) {
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int i = 0; i < NT; ++i) { mx0 = fmaxf(mx0, fmaxf(x[i][0], x[i][2])); mx1 = fmaxf(mx1, fmaxf(x[i][1], x[i][3])); }
@@ -530,31 +523,37 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
         const float p2 = exp2f(x[i][2] - m0), p3 = exp2f(x[i][3] - m1);
         st.l[0] += p0 + p2;
         st.l[1] += p1 + p3;
-        b01[i] = movmatrix_t(pack_half2(p0, p1));  // mma rows 0..7 (tokens 2g)
-        b23[i] = movmatrix_t(pack_half2(p2, p3));  // mma rows 8..15 (tokens 2g+1)
+        const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        b01[i] = movmatrix_t(h2u(h01));  // mma rows 0..7 (tokens 2g)
+        b23[i] = movmatrix_t(h2u(h23));  // mma rows 8..15 (tokens 2g+1)
+        if constexpr (PRECISE) {
+            c01[i] = movmatrix_t(pack_half2(p0 - f01.x, p1 - f01.y));
+            c23[i] = movmatrix_t(pack_half2(p2 - f23.x, p3 - f23.y));
+        }
     }
 }
 
 // Processes tiles i0 and (if pair) i0+1 of a staged chunk with interleaved independent work.
-template <int D, int TIER, bool PAIR>
+template <int D, int TIER, bool PAIR, bool PRECISE>
 __device__ __forceinline__ void process_tiles(const TilePtr& ta, const TilePtr& tb, int g4, int t4,
                                               const uint32_t (&qf)[D / 16][2], float scale_log2, SoftmaxState& st,
                                               float (&o)[D / 16][4]) {
     constexpr int NT = PAIR ? 2 : 1;
     TokScale tk[NT], tv[NT];
-    bool fast[NT];
     float x[NT][4];
-    load_tok_scales<TIER>(ta, g4, t4, tk[0], tv[0], fast[0]);
-    if constexpr (PAIR) load_tok_scales<TIER>(tb, g4, t4, tk[NT - 1], tv[NT - 1], fast[NT - 1]);
-    tile_scores<D, TIER>(ta, g4, t4, tk[0], fast[0], qf, scale_log2, x[0]);
-    if constexpr (PAIR) tile_scores<D, TIER>(tb, g4, t4, tk[NT - 1], fast[NT - 1], qf, scale_log2, x[NT - 1]);
-    uint32_t b01[NT], b23[NT];
-    softmax_update<D / 16, NT>(x, st, o, b01, b23);
-    tile_pv<D, TIER>(ta, g4, t4, tv[0], fast[0], b01[0], b23[0], o);
-    if constexpr (PAIR) tile_pv<D, TIER>(tb, g4, t4, tv[NT - 1], fast[NT - 1], b01[NT - 1], b23[NT - 1], o);
+    load_tok_scales<TIER>(ta, g4, t4, tk[0], tv[0]);
+    if constexpr (PAIR) load_tok_scales<TIER>(tb, g4, t4, tk[NT - 1], tv[NT - 1]);
+    tile_scores<D, TIER>(ta, g4, t4, tk[0], qf, scale_log2, x[0]);
+    if constexpr (PAIR) tile_scores<D, TIER>(tb, g4, t4, tk[NT - 1], qf, scale_log2, x[NT - 1]);
+    uint32_t b01[NT], b23[NT], c01[NT], c23[NT];
+    softmax_update<D / 16, NT, PRECISE>(x, st, o, b01, b23, c01, c23);
+    tile_pv<D, TIER, PRECISE>(ta, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
+    if constexpr (PAIR)
+        tile_pv<D, TIER, PRECISE>(tb, g4, t4, tv[NT - 1], b01[NT - 1], b23[NT - 1], c01[NT - 1], c23[NT - 1], o);
 }
 
-template <int D>
+template <int D, bool PRECISE>
 __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_constant__ Params p) {
     constexpr int KC = D / 16;
     constexpr int STAGE = stage_bytes(D);
@@ -688,11 +687,11 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
         /* tile pairs (ARGUS_DA_PAIR=1) measured slower on B200: register pressure; D = 256 never pairs */      \
         for (; ARGUS_DA_PAIR && D <= 128 && i + 1 < n; i += 2) {                                                                   \
             const TilePtr ta = tile(i), tb = tile(i + 1);                                                         \
-            process_tiles<D, T, true>(ta, tb, g4, t4, qf, p.scale_log2, st, o);                                   \
+            process_tiles<D, T, true, PRECISE>(ta, tb, g4, t4, qf, p.scale_log2, st, o);                          \
         }                                                                                                         \
         for (; i < n; ++i) {                                                                                      \
             const TilePtr ta = tile(i);                                                                           \
-            process_tiles<D, T, false>(ta, ta, g4, t4, qf, p.scale_log2, st, o);                                  \
+            process_tiles<D, T, false, PRECISE>(ta, ta, g4, t4, qf, p.scale_log2, st, o);                         \
         }                                                                                                         \
         break;                                                                                                    \
     }
@@ -809,14 +808,15 @@ __global__ void combine_kernel(const __grid_constant__ Params p) {
 }
 
 template <int D>
-int launch(const Params& prm, int n_splits, cudaStream_t st) {
+int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
     const size_t smem = (size_t)kWarps * kStages * stage_bytes(D) + stage_slack(D);
     static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kWarps * kStages * stage_bytes(D),
                   "merge buffer must fit in the stage memory");
-    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kern = precise ? decode_attn_kernel<D, true> : decode_attn_kernel<D, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
     dim3 grid(n_splits, prm.B * prm.Hkv, prm.nqg);
-    decode_attn_kernel<D><<<grid, kThreads, smem, st>>>(prm);
+    kern<<<grid, kThreads, smem, st>>>(prm);
     ARGUS_CHECK_LAUNCH();
     if (n_splits > 1) {
         combine_kernel<D><<<(unsigned)((int64_t)prm.B * prm.Hkv * prm.nqg), 256, 0, st>>>(prm);
@@ -913,12 +913,13 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
         prm.part_lse = prm.part_o + groups * s->n_splits * da::kQ * D;
     }
     cudaStream_t st = (cudaStream_t)stream;
+    const bool precise = (s->flags & ARGUS_ATTN_PRECISE_PV) != 0;
     switch (D) {
-        case 16: return da::launch<16>(prm, s->n_splits, st);
-        case 32: return da::launch<32>(prm, s->n_splits, st);
-        case 64: return da::launch<64>(prm, s->n_splits, st);
-        case 128: return da::launch<128>(prm, s->n_splits, st);
-        default: return da::launch<256>(prm, s->n_splits, st);
+        case 16: return da::launch<16>(prm, s->n_splits, precise, st);
+        case 32: return da::launch<32>(prm, s->n_splits, precise, st);
+        case 64: return da::launch<64>(prm, s->n_splits, precise, st);
+        case 128: return da::launch<128>(prm, s->n_splits, precise, st);
+        default: return da::launch<256>(prm, s->n_splits, precise, st);
     }
 }
 

@@ -169,8 +169,12 @@ typedef struct argus_attn_shape {
     int32_t n_arenas;
     int32_t n_chunks;
     float scale;        /* softmax scale (1/sqrt(D) by default in the reference) */
-    int32_t reserved;
+    int32_t flags;      /* ARGUS_ATTN_* bits */
 } argus_attn_shape;
+
+/* argus_attn_shape.flags: feed the softmax weights to the V contraction as an fp16 hi + lo pair
+ * (two MMAs), keeping ~22 bits of each weight instead of fp16's 11; costs ~12% at head_dim 128. */
+#define ARGUS_ATTN_PRECISE_PV 1
 
 /* Bytes of scratch argus_decode_attention needs for split-K partials (0 when n_splits == 1). */
 int64_t argus_decode_attention_workspace_size(const argus_attn_shape* shape);
