@@ -40,6 +40,9 @@ SIGNATURES = {
     "argus_pack_1bit_signs": [_p, _i64, _i32, _p, _p],
     "argus_isolate_outliers": [_p, _i64, _i32, _f32, _p, _p, _p, _p],
     "argus_jl_apply": [_p, _p, _i64, _i32, _i32, _i32, _p, _p],
+    "argus_memcpy_async": [_p, _p, _i64, _p],
+    "argus_scatter_coo": [_p, _i64, _i64, _i32, _i32, _i32, _i32, _p, _p, _i64, _p],
+    "argus_outliers_to_coo": [_p, _p, _i32, _i32, _i32, _i32, _p, _p, _i64, _p, _p],
 }
 
 
@@ -92,6 +95,10 @@ def call(name, *args):
 
 def stream_handle(device=None):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def ptr_stream(stream):
+    return ctypes.c_void_p(stream.cuda_stream)
 
 
 def ptr(t):

@@ -65,7 +65,7 @@ def _bind():
     if not getattr(L, "_argus_attn_bound", False):
         L.argus_decode_attention.argtypes = [ctypes.POINTER(ShapeC), ctypes.POINTER(ArenaC), ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                                             ctypes.c_void_p, ctypes.c_void_p]
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.argus_decode_attention.restype = ctypes.c_int
         L.argus_decode_attention_workspace_size.argtypes = [ctypes.POINTER(ShapeC)]
         L.argus_decode_attention_workspace_size.restype = ctypes.c_int64
@@ -282,8 +282,13 @@ class AttentionPlan:
                 total += 2 * 2 * int(n) * (2 if tier in (TIER_INT4, TIER_INT2) else 1)
         return total * self.B * self.Hkv
 
-    def run(self, q, scale=None, out=None, lse=None, stream=None):
-        """q: [B, H_q, q_len, D] fp16 on the plan's device.  Returns out (and fills lse if given)."""
+    def tile_lse_shape(self):
+        nqg = (self.G * self.qlen + 7) // 8
+        return (self.B * self.Hkv * nqg, max(1, self.n_chunks), 16, 8)
+
+    def run(self, q, scale=None, out=None, lse=None, stream=None, tile_lse=None):
+        """q: [B, H_q, q_len, D] fp16 on the plan's device.  Returns out (and fills lse, and the
+        per-tile log2-sum-exp tile_lse of shape tile_lse_shape(), if given)."""
         _lib.require_cuda(q, "q")
         if q.dtype != torch.float16:
             raise TypeError("q must be float16")
@@ -299,6 +304,7 @@ class AttentionPlan:
         rc = L.argus_decode_attention(ctypes.byref(self._shape), self._arena_c, self.chunks_dev.data_ptr(),
                                       self.splits_dev.data_ptr(), q.data_ptr(), out.data_ptr(),
                                       lse.data_ptr() if lse is not None else None,
+                                      tile_lse.data_ptr() if tile_lse is not None else None,
                                       self.workspace.data_ptr() if self.workspace is not None else None,
                                       ctypes.c_void_p(st))
         if rc != 0:

@@ -1,0 +1,96 @@
+"""HuggingFace cache adapter with the reference's surface (argus_cache/models/attention_wrapper.py:12-173).
+
+One PagedDynamicKVCache per layer, created lazily on the first update() with the reference's
+auto-adaptive tier budgets (low-precision key dtypes get shorter FP16/FP8 stages and longer
+heavily-compressed ones, attention_wrapper.py:49-79).  update() pushes the new tokens (page
+formation and the fused demotion cascade run on the GPU) and returns the full K/V rebuilt by the
+page kernels, which is what transformers' attention consumes (attention_wrapper.py:87-88).
+"""
+import torch
+
+from ..core.memory_manager import PagedDynamicKVCache
+
+try:
+    from transformers.cache_utils import Cache
+except ImportError:  # transformers absent: a bare base class keeps the adapter importable
+    class Cache:
+        def __init__(self, *args, **kwargs):
+            pass
+
+
+class PagedDynamicQuantizedCache(Cache):
+    def __init__(self, page_size=4096, max_active_pages=2, max_fp8_pages=2, max_int8_pages=2, max_int4_pages=2,
+                 max_int2_pages=2, max_one_bit_pages=2, sink_tokens=4, threshold_sigma=3.0):
+        try:
+            super().__init__(layers=[])
+        except TypeError:
+            super().__init__()
+        self.page_size = page_size
+        self.max_active_pages = max_active_pages
+        self.max_fp8_pages = max_fp8_pages
+        self.max_int8_pages = max_int8_pages
+        self.max_int4_pages = max_int4_pages
+        self.max_int2_pages = max_int2_pages
+        self.max_one_bit_pages = max_one_bit_pages
+        self.sink_tokens = sink_tokens
+        self.threshold_sigma = threshold_sigma
+        self.layer_caches = {}
+
+    def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int, cache_kwargs=None):
+        if layer_idx not in self.layer_caches:
+            if key_states.dtype in (torch.float32, torch.float16, torch.bfloat16):
+                budgets = (self.max_active_pages, self.max_fp8_pages, self.max_int8_pages, self.max_int4_pages,
+                           self.max_int2_pages, self.max_one_bit_pages)
+            else:
+                budgets = (max(1, self.max_active_pages // 2), 1, self.max_int8_pages,
+                           max(1, self.max_int4_pages * 2), max(1, self.max_int2_pages * 2),
+                           max(1, self.max_one_bit_pages * 2))
+            self.layer_caches[layer_idx] = PagedDynamicKVCache(
+                page_size=self.page_size, max_active_pages=budgets[0], max_fp8_pages=budgets[1],
+                max_int8_pages=budgets[2], max_int4_pages=budgets[3], max_int2_pages=budgets[4],
+                max_one_bit_pages=budgets[5], sink_tokens=self.sink_tokens, threshold_sigma=self.threshold_sigma)
+        cache = self.layer_caches[layer_idx]
+        is_anchor = cache_kwargs.get("is_anchor") if cache_kwargs is not None else None
+        cache.push_new_tokens(key_states, value_states, is_anchor=is_anchor)
+        return cache.get_all_keys_values()
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        if layer_idx not in self.layer_caches:
+            return 0
+        c = self.layer_caches[layer_idx]
+        n = 0
+        if c.sink_k is not None:
+            n += c.sink_k.shape[-2]
+        if c.anchor_k is not None:
+            n += c.anchor_k.shape[-2]
+        pages = (len(c.active_pages) + len(c.fp8_pages) + len(c.int8_pages) + len(c.int4_pages) + len(c.int2_pages)
+                 + len(c.one_bit_pages) + len(c.jl_pages))
+        n += pages * c.page_size
+        if c.k_buffer is not None:
+            n += c.k_buffer.shape[-2]
+        return n
+
+    def get_usable_length(self, seq_len: int, layer_idx: int = 0) -> int:
+        return self.get_seq_length(layer_idx)
+
+    def get_vram_usage(self) -> int:
+        return sum(c.get_vram_usage() for c in self.layer_caches.values())
+
+    def speculate_and_prefetch(self, attn_weights=None):
+        for c in self.layer_caches.values():
+            c.speculate_and_prefetch(attn_weights)
+
+    def swap_out_to_host(self):
+        for c in self.layer_caches.values():
+            c.swap_out_to_host()
+
+    def swap_in_to_device(self, device="cuda"):
+        for c in self.layer_caches.values():
+            c.swap_in_to_device(device)
+
+    @property
+    def is_swapped_out(self) -> bool:
+        return any(c.is_swapped_out for c in self.layer_caches.values()) if self.layer_caches else False
+
+    def reset(self):
+        self.layer_caches.clear()

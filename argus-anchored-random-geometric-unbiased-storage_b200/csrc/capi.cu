@@ -38,3 +38,10 @@ const char* argus_last_error(void) { return g_last_error; }
 int argus_version(void) { return 100; /* 0.1.0 */ }
 
 }  // extern "C"
+
+extern "C" int argus_memcpy_async(void* dst, const void* src, int64_t bytes, argus_stream_t stream) {
+    if (bytes < 0 || (bytes > 0 && (!dst || !src))) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad copy");
+    if (bytes == 0) return ARGUS_OK;
+    cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, (cudaStream_t)stream);
+    return e == cudaSuccess ? ARGUS_OK : argus_set_cuda_error(e);
+}

@@ -1,31 +1,46 @@
 // Quantize/pack and unpack/dequantize kernels for ARGUS's storage tiers, bit-exact against the
 // reference's CPU arithmetic (argus_cache 0.1.8, core/quantization.py, core/triton_kernels.py CPU
-// path, core/memory_manager.py:89-113).
+// path, core/memory_manager.py:89-113, :944-1155).
 //
 // Arithmetic model: every torch op on fp16 data is an fp32 op rounded to fp16 (rh); divisions use
-// the IEEE-rounded fp32 divide so rh(x / s) equals the reference's fp16 quotient.  The
-// per-token reductions (amax, min, max) are order-free; mean|x| (1-bit scale, outlier threshold)
-// follows ATen's cascade_sum order: 8 fp32 lanes, 4 interleaved accumulators, 4 cascade levels,
-// lanes combined 0..7 in order, then / D in fp32.
+// the IEEE-rounded fp32 divide so rh(x / s) equals the reference's fp16 quotient.  The per-token
+// reductions (amax, min, max) are order-free; mean|x| (1-bit scale, outlier threshold) follows
+// ATen's cascade_sum order: 8 fp32 lanes, 4 interleaved accumulators, 4 cascade levels, lanes
+// combined 0..7 in order, then / D in fp32.
 //
-// HBM layout: [n_rows][D] fp16 rows (D contiguous), packed payload [n_rows/per][D] bytes, per-row
-// fp16 scale/min.  The quantizers stage a tile of rows in shared memory (row stride padded by 16 B
-// so 8-lane row groups hit distinct banks), reduce each row with 8 lanes, then emit 4 output bytes
-// per thread; the dequantizers are register-only, 8 columns per thread, 16-byte stores.
+// Row layouts.  A tensor is a set of groups of `group_rows` token rows of D values (a flat
+// [n_rows][D] tensor is one group; a page of a record arena is B*H_kv groups, one per (b, h),
+// `group_stride` bytes apart).  Packed tiers store `per` consecutive rows of a group in one
+// D-byte packed row; scales/mins are one fp16 per row.  The kernels stage a tile of rows of one
+// group in shared memory (decoded from any tier), reduce each row with 8 lanes, then emit 4 output
+// bytes per thread, so one kernel both quantizes fp16 and re-quantizes a page from one tier into
+// another (the fused demotion of the cascade).
 #include "common.cuh"
 
 namespace argus {
 
-enum QuantMode { Q_INT8 = 0, Q_FP8SIM = 1, Q_INT4 = 2, Q_INT2 = 3, Q_SIGN1 = 4, Q_OUTLIER = 5 };
+enum QuantMode { Q_INT8 = 0, Q_FP8SIM = 1, Q_INT4 = 2, Q_INT2 = 3, Q_SIGN1 = 4, Q_OUTLIER = 5, Q_FP16 = 6 };
 
-template <int MODE>
-struct ModeTraits;
-template <> struct ModeTraits<Q_INT8>    { static constexpr int per = 1; };
-template <> struct ModeTraits<Q_FP8SIM>  { static constexpr int per = 1; };
-template <> struct ModeTraits<Q_INT4>    { static constexpr int per = 2; };
-template <> struct ModeTraits<Q_INT2>    { static constexpr int per = 4; };
-template <> struct ModeTraits<Q_SIGN1>   { static constexpr int per = 8; };
-template <> struct ModeTraits<Q_OUTLIER> { static constexpr int per = 1; };
+__host__ __device__ constexpr int mode_per(int m) { return m == Q_INT4 ? 2 : (m == Q_INT2 ? 4 : (m == Q_SIGN1 ? 8 : 1)); }
+__host__ __device__ constexpr int tier_mode(int tier) {
+    return tier == ARGUS_TIER_FP16 ? Q_FP16
+         : tier == ARGUS_TIER_FP8SIM ? Q_FP8SIM
+         : tier == ARGUS_TIER_INT8 ? Q_INT8
+         : tier == ARGUS_TIER_INT4 ? Q_INT4
+         : tier == ARGUS_TIER_INT2 ? Q_INT2 : Q_SIGN1;
+}
+
+// Addressing of one operand: row t of group g sits at
+//   payload + g*group_stride + ((row0 + t) / per) * row_bytes      (bytes)
+//   scales/mins + g*sgroup_stride + row0 + t                       (fp16 elements)
+struct Rows {
+    unsigned char* payload;
+    __half* scales;
+    __half* mins;
+    int64_t group_stride;
+    int64_t sgroup_stride;
+    int row0;
+};
 
 constexpr int kQuantThreads = 256;
 constexpr int kRowLanes = 8;  // threads that cooperate on one row's statistics
@@ -87,40 +102,97 @@ __device__ __forceinline__ float cascade_combine(float mine) {
     return total;
 }
 
-// abs of fp16 bits with NaN/Inf cleaned to +0 (isolate_outliers' cleanse step).
+// NaN/Inf cleaned to +0 (isolate_outliers' cleanse step).
 __device__ __forceinline__ __half clean_nan_inf(__half h) {
     unsigned short b = __half_as_ushort(h);
     return ((b & 0x7c00u) == 0x7c00u) ? __ushort_as_half(0) : h;
 }
 
-template <int MODE>
+// ------------------------------------------------------------------------------ decoding
+// Decodes 8 consecutive columns (c8*8 ..) of the `per` rows held by packed row `pr` of group g
+// (rows pr*per .. relative to row0) into out[i][0..7] for i < per.  Exact reference dequantization.
+template <int SRC>
+__device__ __forceinline__ void decode8(const Rows& s, int64_t g, int pr, int c8, int D, __half (&out)[8][8]) {
+    constexpr int per = mode_per(SRC);
+    const int t0 = pr * per;  // first row of the packed row, relative to row0
+    if constexpr (SRC == Q_FP16) {
+        const unsigned char* rp = s.payload + g * s.group_stride + (int64_t)(s.row0 + t0) * D * 2;
+        *reinterpret_cast<uint4*>(out[0]) = *reinterpret_cast<const uint4*>(rp + c8 * 16);
+    } else {
+        const unsigned char* rp = s.payload + g * s.group_stride + (int64_t)((s.row0 + t0) / per) * D;
+        const uint2 raw = *reinterpret_cast<const uint2*>(rp + c8 * 8);
+        const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
+        const __half* sp = s.scales + g * s.sgroup_stride + s.row0 + t0;
+        if constexpr (SRC == Q_INT8 || SRC == Q_FP8SIM) {
+            const __half2 s2 = __half2half2(sp[0]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __half2 v = __hmul2_rn(__halves2half2(__short2half_rn((int8_t)b[2 * e]), __short2half_rn((int8_t)b[2 * e + 1])), s2);
+                out[0][2 * e] = __low2half(v);
+                out[0][2 * e + 1] = __high2half(v);
+            }
+        } else if constexpr (SRC == Q_INT4 || SRC == Q_INT2) {
+            constexpr int BITS = 8 / per;
+            constexpr uint32_t m = (1u << BITS) - 1u;
+            const __half* mp = s.mins + g * s.sgroup_stride + s.row0 + t0;
+#pragma unroll
+            for (int i = 0; i < per; ++i) {
+                const __half2 s2 = __half2half2(sp[i]), m2 = __half2half2(mp[i]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const __half2 u = __halves2half2(__uint2half_rn((b[2 * e] >> (BITS * i)) & m),
+                                                     __uint2half_rn((b[2 * e + 1] >> (BITS * i)) & m));
+                    const __half2 v = __hadd2_rn(__hmul2_rn(u, s2), m2);
+                    out[i][2 * e] = __low2half(v);
+                    out[i][2 * e + 1] = __high2half(v);
+                }
+            }
+        } else {  // 1-bit: exactly +s or -s
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const __half sv = sp[i], nv = __hneg(sv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) out[i][e] = ((b[e] >> i) & 1u) ? sv : nv;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------ quantizer
+// Stages rows [t0, t0 + rows) of group g (decoded from SRC), then quantizes them to MODE.
+template <int MODE, int SRC>
 __global__ void __launch_bounds__(kQuantThreads)
-quant_kernel(const __half* __restrict__ x, int64_t n_rows, int D, int tile_rows, float sigma,
-             uint8_t* __restrict__ payload, __half* __restrict__ s_out, __half* __restrict__ mn_out,
+quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int tile_rows, float sigma,
              __half* __restrict__ outv, uint8_t* __restrict__ mask) {
-    constexpr int per = ModeTraits<MODE>::per;
+    constexpr int per = mode_per(MODE);
+    constexpr int sper = mode_per(SRC);
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int stride = D + 8;  // halfs; +16 B keeps 16 B alignment and staggers banks by row
     __half* tile = reinterpret_cast<__half*>(smem_raw);
     float* st_a = reinterpret_cast<float*>(smem_raw + (size_t)tile_rows * stride * sizeof(__half));
     float* st_b = st_a + tile_rows;
 
-    const int vec_per_row = D / 8;
-    const int64_t n_tiles = (n_rows + tile_rows - 1) / tile_rows;
+    const int tiles_per_group = (group_rows + tile_rows - 1) / tile_rows;
+    const int64_t n_tiles = n_groups * tiles_per_group;
+    const int c8n = D / 8;
     for (int64_t tix = blockIdx.x; tix < n_tiles; tix += gridDim.x) {
-        const int64_t r0 = tix * tile_rows;
-        const int rows = (int)((n_rows - r0) < tile_rows ? (n_rows - r0) : tile_rows);
-        // 1. stage the tile (16-byte loads, coalesced: the tile is one contiguous block)
-        const uint4* src = reinterpret_cast<const uint4*>(x + r0 * D);
-        for (int v = threadIdx.x; v < rows * vec_per_row; v += kQuantThreads) {
-            int r = v / vec_per_row, c = v - r * vec_per_row;
-            uint4 val = __ldg(src + v);
-            if (MODE == Q_OUTLIER) {
-                __half* hv = reinterpret_cast<__half*>(&val);
+        const int64_t g = tix / tiles_per_group;
+        const int t0 = (int)(tix - g * tiles_per_group) * tile_rows;
+        const int rows = min(tile_rows, group_rows - t0);
+        // 1. stage the tile, decoded to fp16
+        const int prows = rows / sper;
+        for (int w = threadIdx.x; w < prows * c8n; w += kQuantThreads) {
+            const int pr = w / c8n, c8 = w - pr * c8n;
+            __half v[8][8];
+            decode8<SRC>(src, g, t0 / sper + pr, c8, D, v);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) hv[e] = clean_nan_inf(hv[e]);
+            for (int i = 0; i < sper; ++i) {
+                if (MODE == Q_OUTLIER) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[i][e] = clean_nan_inf(v[i][e]);
+                }
+                *reinterpret_cast<uint4*>(tile + (pr * sper + i) * stride + c8 * 8) = *reinterpret_cast<uint4*>(v[i]);
             }
-            *reinterpret_cast<uint4*>(tile + r * stride + c * 8) = val;
         }
         __syncthreads();
         // 2. per-row statistics, 8 lanes per row
@@ -166,24 +238,26 @@ quant_kernel(const __half* __restrict__ x, int64_t n_rows, int D, int tile_rows,
                     a = rh(__fdiv_rn(rh(__fsub_rn(hi, lo)), qmax));  // s = fp16(fp16(max-min)/qmax)
                     b = lo;
                 }
-            } else {  // Q_SIGN1, Q_OUTLIER: mean|x| in ATen order (|x| of an fp16 value is exact)
+            } else if (MODE == Q_SIGN1 || MODE == Q_OUTLIER) {  // mean|x| in ATen order
                 const float lane_sum = cascade_lane_sum<true>(row, D / 8, lane8);
                 const float total = cascade_combine(lane_sum);
                 const float mean = rh(__fdiv_rn(total, (float)D));  // fp16(sum / D)
-                if (MODE == Q_SIGN1) {
-                    a = mean;
-                } else {
-                    a = rh(__fmul_rn(mean, sigma));  // threshold fp16(mean * sigma)
-                }
+                a = (MODE == Q_SIGN1) ? mean : rh(__fmul_rn(mean, sigma));  // outliers: fp16(mean * sigma)
             }
             if (live && lane8 == 0) { st_a[rb] = a; st_b[rb] = b; }
         }
         __syncthreads();
-        // 3. codes: 4 consecutive columns x `per` rows per thread -> 4 output bytes
+        // 3. outputs: 4 consecutive columns x `per` rows per thread
         const int quads = D / 4;
-        const int prows = rows / per;
-        for (int w = threadIdx.x; w < prows * quads; w += kQuantThreads) {
+        const int prw = rows / per;
+        for (int w = threadIdx.x; w < prw * quads; w += kQuantThreads) {
             const int pr = w / quads, cq = w - pr * quads;
+            if (MODE == Q_FP16) {
+                // plain fp16 store (a page decoded into an fp16 page)
+                unsigned char* dp = dst.payload + g * dst.group_stride + (int64_t)(dst.row0 + t0 + pr) * D * 2;
+                *reinterpret_cast<uint2*>(dp + cq * 8) = *reinterpret_cast<const uint2*>(tile + pr * stride + cq * 4);
+                continue;
+            }
             uint32_t word = 0;
 #pragma unroll
             for (int i = 0; i < per; ++i) {
@@ -212,9 +286,9 @@ quant_kernel(const __half* __restrict__ x, int64_t n_rows, int D, int tile_rows,
                     }
                 }
             }
-            const int64_t prow = r0 / per + pr;
             if (MODE == Q_OUTLIER) {
-                const int64_t base = (r0 + pr) * (int64_t)D + cq * 4;
+                // flat layout only: normal -> dst.payload (fp16), outliers -> outv, mask -> mask
+                const int64_t base = (g * group_rows + t0 + pr) * (int64_t)D + cq * 4;
                 *reinterpret_cast<uint32_t*>(mask + base) = word;
                 const __half* hp = tile + pr * stride + cq * 4;
                 __half nv[4], ov[4];
@@ -224,17 +298,18 @@ quant_kernel(const __half* __restrict__ x, int64_t n_rows, int D, int tile_rows,
                     nv[e] = m ? __ushort_as_half(0) : hp[e];
                     ov[e] = m ? hp[e] : __ushort_as_half(0);
                 }
-                *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(payload) + base) = *reinterpret_cast<uint2*>(nv);
+                *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(dst.payload) + base) = *reinterpret_cast<uint2*>(nv);
                 *reinterpret_cast<uint2*>(outv + base) = *reinterpret_cast<uint2*>(ov);
             } else {
-                *reinterpret_cast<uint32_t*>(payload + prow * D + cq * 4) = word;
+                unsigned char* dp = dst.payload + g * dst.group_stride + (int64_t)((dst.row0 + t0) / per + pr) * D;
+                *reinterpret_cast<uint32_t*>(dp + cq * 4) = word;
             }
         }
         // 4. per-row scales / mins
-        if (MODE != Q_OUTLIER) {
+        if (MODE != Q_OUTLIER && MODE != Q_FP16) {
             for (int r = threadIdx.x; r < rows; r += kQuantThreads) {
-                if (s_out) s_out[r0 + r] = f2h(st_a[r]);
-                if (MODE == Q_INT4 || MODE == Q_INT2) mn_out[r0 + r] = f2h(st_b[r]);
+                if (dst.scales) dst.scales[g * dst.sgroup_stride + dst.row0 + t0 + r] = f2h(st_a[r]);
+                if (MODE == Q_INT4 || MODE == Q_INT2) dst.mins[g * dst.sgroup_stride + dst.row0 + t0 + r] = f2h(st_b[r]);
             }
         }
         __syncthreads();
@@ -252,74 +327,23 @@ __global__ void cleanse_kernel(const __half* __restrict__ x, int64_t n, __half* 
 }
 
 // ------------------------------------------------------------------------- dequantizers
-// INT8 / FP8-sim: out = fp16(q * s); 8 columns per thread.
-__global__ void dequant_sym8_kernel(const int8_t* __restrict__ q, const __half* __restrict__ s, int64_t n_rows,
-                                    int D, __half* __restrict__ out) {
-    const int cols8 = D / 8;
-    const int64_t items = n_rows * cols8;
+// Register-only decode of SRC rows into fp16 rows: one packed row x 8 columns per thread.
+template <int SRC>
+__global__ void dequant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D) {
+    constexpr int per = mode_per(SRC);
+    const int c8n = D / 8;
+    const int prg = group_rows / per;
+    const int64_t items = n_groups * prg * c8n;
     for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < items; w += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = w / cols8;
-        const int c = (int)(w - r * cols8);
-        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(q + r * D) + c);
-        const __half2 s2 = __half2half2(s[r]);
-        const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
-        __half2 o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            o[e] = __hmul2_rn(__halves2half2(__short2half_rn(b[2 * e]), __short2half_rn(b[2 * e + 1])), s2);
-        *reinterpret_cast<uint4*>(out + r * D + c * 8) = *reinterpret_cast<uint4*>(o);
-    }
-}
-
-// INT4 / INT2: out = fp16(fp16(u * s) + min), `per` rows from each packed byte row.
-template <int BITS>
-__global__ void dequant_asym_kernel(const uint8_t* __restrict__ p, const __half* __restrict__ s,
-                                    const __half* __restrict__ mn, int64_t n_prows, int D, __half* __restrict__ out) {
-    constexpr int per = 8 / BITS;
-    constexpr uint32_t m = (1u << BITS) - 1u;
-    const int cols8 = D / 8;
-    const int64_t items = n_prows * cols8;
-    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < items; w += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t pr = w / cols8;
-        const int c = (int)(w - pr * cols8);
-        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p + pr * D) + c);
-        const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
+        const int64_t g = w / ((int64_t)prg * c8n);
+        const int rem = (int)(w - g * prg * c8n);
+        const int pr = rem / c8n, c8 = rem - pr * c8n;
+        __half v[8][8];
+        decode8<SRC>(src, g, pr, c8, D, v);
 #pragma unroll
         for (int i = 0; i < per; ++i) {
-            const int64_t r = pr * per + i;
-            const __half2 s2 = __half2half2(s[r]);
-            const __half2 m2 = __half2half2(mn[r]);
-            __half2 o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const __half2 u = __halves2half2(__uint2half_rn((b[2 * e] >> (BITS * i)) & m),
-                                                 __uint2half_rn((b[2 * e + 1] >> (BITS * i)) & m));
-                o[e] = __hadd2_rn(__hmul2_rn(u, s2), m2);
-            }
-            *reinterpret_cast<uint4*>(out + r * D + c * 8) = *reinterpret_cast<uint4*>(o);
-        }
-    }
-}
-
-// 1-bit: out = +s or -s (exactly (2b - 1) * s).
-__global__ void dequant_sign1_kernel(const uint8_t* __restrict__ p, const __half* __restrict__ s, int64_t n_prows,
-                                     int D, __half* __restrict__ out) {
-    const int cols8 = D / 8;
-    const int64_t items = n_prows * cols8;
-    for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < items; w += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t pr = w / cols8;
-        const int c = (int)(w - pr * cols8);
-        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p + pr * D) + c);
-        const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int64_t r = pr * 8 + i;
-            const __half sv = s[r];
-            const __half nv = __hneg(sv);
-            __half o[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = ((b[e] >> i) & 1u) ? sv : nv;
-            *reinterpret_cast<uint4*>(out + r * D + c * 8) = *reinterpret_cast<uint4*>(o);
+            unsigned char* dp = dst.payload + g * dst.group_stride + (int64_t)(dst.row0 + pr * per + i) * D * 2;
+            *reinterpret_cast<uint4*>(dp + c8 * 16) = *reinterpret_cast<uint4*>(v[i]);
         }
     }
 }
@@ -333,6 +357,115 @@ __global__ void pack_int4_codes_kernel(const uint8_t* __restrict__ codes, int64_
         const int d = (int)(w - pr * D);
         packed[w] = (uint8_t)(codes[(2 * pr) * D + d] | (codes[(2 * pr + 1) * D + d] << 4));
     }
+}
+
+// ---------------------------------------------------------------------------- launchers
+Rows flat_rows(const void* payload, const uint16_t* scales, const uint16_t* mins) {
+    Rows r;
+    r.payload = const_cast<unsigned char*>(static_cast<const unsigned char*>(payload));
+    r.scales = const_cast<__half*>(reinterpret_cast<const __half*>(scales));
+    r.mins = const_cast<__half*>(reinterpret_cast<const __half*>(mins));
+    r.group_stride = 0;
+    r.sgroup_stride = 0;
+    r.row0 = 0;
+    return r;
+}
+
+int tile_rows_for(int D, int group_rows) {
+    int tr = 8192 / (2 * D);
+    tr = (tr / 8) * 8;
+    if (tr < 8) tr = 8;
+    if (tr > 256) tr = 256;
+    if (group_rows < tr) tr = ((group_rows + 7) / 8) * 8;
+    return tr;
+}
+
+template <int MODE, int SRC>
+int launch_quant(const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, int D, float sigma,
+                 uint16_t* outv, uint8_t* mask, cudaStream_t st) {
+    if (n_groups == 0 || group_rows == 0) return ARGUS_OK;
+    const int tile_rows = tile_rows_for(D, group_rows);
+    const size_t smem = (size_t)tile_rows * (D + 8) * sizeof(__half) + 2 * tile_rows * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(quant_kernel<MODE, SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return argus_set_cuda_error(e);
+    }
+    const int64_t tiles = n_groups * ((group_rows + tile_rows - 1) / tile_rows);
+    quant_kernel<MODE, SRC><<<argus_grid_cap(tiles), kQuantThreads, smem, st>>>(
+        src, dst, n_groups, group_rows, D, tile_rows, sigma, reinterpret_cast<__half*>(outv), mask);
+    ARGUS_CHECK_LAUNCH();
+    return ARGUS_OK;
+}
+
+// Runtime dispatch over (destination mode, source mode).
+int quant_dispatch(int mode, int src_mode, const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, int D,
+                   cudaStream_t st) {
+#define ARGUS_Q(M)                                                                                            \
+    switch (src_mode) {                                                                                       \
+        case Q_FP16: return launch_quant<M, Q_FP16>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
+        case Q_FP8SIM: return launch_quant<M, Q_FP8SIM>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
+        case Q_INT8: return launch_quant<M, Q_INT8>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
+        case Q_INT4: return launch_quant<M, Q_INT4>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
+        case Q_INT2: return launch_quant<M, Q_INT2>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
+        case Q_SIGN1: return launch_quant<M, Q_SIGN1>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
+        default: return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad source tier");                       \
+    }
+    switch (mode) {
+        case Q_INT8: ARGUS_Q(Q_INT8)
+        case Q_FP8SIM: ARGUS_Q(Q_FP8SIM)
+        case Q_INT4: ARGUS_Q(Q_INT4)
+        case Q_INT2: ARGUS_Q(Q_INT2)
+        case Q_SIGN1: ARGUS_Q(Q_SIGN1)
+        case Q_FP16: ARGUS_Q(Q_FP16)
+        default: return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad destination tier");
+    }
+#undef ARGUS_Q
+}
+
+int dq_blocks(int64_t items) { return argus_grid_cap((items + 255) / 256); }
+
+int dequant_dispatch(int src_mode, const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, int D,
+                     cudaStream_t st) {
+    if (n_groups == 0 || group_rows == 0) return ARGUS_OK;
+    const int64_t items = n_groups * (group_rows / mode_per(src_mode)) * (D / 8);
+    switch (src_mode) {
+        case Q_FP16: dequant_kernel<Q_FP16><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
+        case Q_FP8SIM: dequant_kernel<Q_FP8SIM><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
+        case Q_INT8: dequant_kernel<Q_INT8><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
+        case Q_INT4: dequant_kernel<Q_INT4><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
+        case Q_INT2: dequant_kernel<Q_INT2><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
+        case Q_SIGN1: dequant_kernel<Q_SIGN1><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
+        default: return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad source tier");
+    }
+    ARGUS_CHECK_LAUNCH();
+    return ARGUS_OK;
+}
+
+// Rows of the K (which = 0) or V (which = 1) half of page `slot` of a record arena, as B*H groups.
+Rows page_rows(const argus_kv_arena* a, int slot, int which, int D) {
+    const int P = a->page_tokens;
+    const int bits = a->tier == ARGUS_TIER_FP16 ? 16 : a->tier == ARGUS_TIER_INT4 ? 4 : a->tier == ARGUS_TIER_INT2 ? 2 : a->tier == ARGUS_TIER_1BIT ? 1 : 8;
+    const int64_t pb = (int64_t)P * D * bits / 8;
+    unsigned char* rec = const_cast<unsigned char*>(static_cast<const unsigned char*>(a->k)) + (int64_t)slot * a->record_bytes;
+    Rows r;
+    r.payload = rec + (which ? pb : 0);
+    r.scales = reinterpret_cast<__half*>(rec + 2 * pb + (which ? 2 * P : 0));
+    r.mins = reinterpret_cast<__half*>(rec + 2 * pb + 4 * P + (which ? 2 * P : 0));
+    r.group_stride = a->bh_stride;
+    r.sgroup_stride = a->bh_stride / 2;
+    r.row0 = 0;
+    return r;
+}
+
+int check_arena(const argus_kv_arena* a, int D) {
+    if (!a || !a->k) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null arena");
+    if (a->layout != ARGUS_LAYOUT_RECORD) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "page codecs need a record arena");
+    if (a->tier < ARGUS_TIER_FP16 || a->tier > ARGUS_TIER_1BIT) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad tier");
+    if (D % 8 || D <= 0) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "head dim must be a multiple of 8");
+    if (a->page_tokens <= 0 || a->page_tokens % 8) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "page size must be a multiple of 8");
+    if (!argus_aligned(a->k, 16) || a->bh_stride % 16 || a->record_bytes % 16)
+        return argus_set_error(ARGUS_ERR_MISALIGNED, "record arena must be 16-byte aligned");
+    return ARGUS_OK;
 }
 
 }  // namespace argus
@@ -352,33 +485,40 @@ int check_rows(const void* a, const void* b, int64_t n_rows, int D, int per) {
     return ARGUS_OK;
 }
 
-template <int MODE>
-int launch_quant(const uint16_t* x, int64_t n_rows, int D, float sigma, void* payload, uint16_t* s, uint16_t* mn,
-                 uint16_t* outv, uint8_t* mask, cudaStream_t st) {
-    constexpr int per = ModeTraits<MODE>::per;
+// Flat tensors: one group, or groups of 2^24 rows when the row count exceeds the int range.
+constexpr int64_t kFlatGroup = (int64_t)1 << 24;
+
+int flat_quant(int mode, const uint16_t* x, int64_t n_rows, int D, void* payload, uint16_t* s, uint16_t* mn,
+               cudaStream_t st) {
     if (!argus_aligned(x, 16)) return argus_set_error(ARGUS_ERR_MISALIGNED, "input must be 16-byte aligned");
     if (!argus_aligned(payload, 4)) return argus_set_error(ARGUS_ERR_MISALIGNED, "output must be 4-byte aligned");
     if (n_rows == 0) return ARGUS_OK;
-    // ~8 KB of fp16 rows per tile, a multiple of 8 rows (and of `per`)
-    int tile_rows = 8192 / (2 * D);
-    tile_rows = (tile_rows / 8) * 8;
-    if (tile_rows < 8) tile_rows = 8;
-    if (tile_rows > 256) tile_rows = 256;
-    const size_t smem = (size_t)tile_rows * (D + 8) * sizeof(__half) + 2 * tile_rows * sizeof(float);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(quant_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return argus_set_cuda_error(e);
+    if (n_rows > ((int64_t)1 << 30)) {
+        if (n_rows % kFlatGroup) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "above 2^30 rows: use a multiple of 2^24");
+        Rows src = flat_rows(x, nullptr, nullptr), dst = flat_rows(payload, s, mn);
+        src.group_stride = kFlatGroup * D * 2;
+        dst.group_stride = kFlatGroup / mode_per(mode) * D;
+        dst.sgroup_stride = kFlatGroup;
+        return quant_dispatch(mode, Q_FP16, src, dst, n_rows / kFlatGroup, (int)kFlatGroup, D, st);
     }
-    const int64_t tiles = (n_rows + tile_rows - 1) / tile_rows;
-    quant_kernel<MODE><<<argus_grid_cap(tiles), kQuantThreads, smem, st>>>(
-        reinterpret_cast<const __half*>(x), n_rows, D, tile_rows, sigma, reinterpret_cast<uint8_t*>(payload),
-        reinterpret_cast<__half*>(s), reinterpret_cast<__half*>(mn), reinterpret_cast<__half*>(outv), mask);
-    static_assert(per >= 1, "packing factor");
-    ARGUS_CHECK_LAUNCH();
-    return ARGUS_OK;
+    return quant_dispatch(mode, Q_FP16, flat_rows(x, nullptr, nullptr), flat_rows(payload, s, mn), 1, (int)n_rows, D, st);
 }
 
-int dq_blocks(int64_t items) { return argus_grid_cap((items + 255) / 256); }
+int flat_dequant(int mode, const void* payload, const uint16_t* s, const uint16_t* mn, int64_t n_rows, int D,
+                 uint16_t* out, cudaStream_t st) {
+    if (!argus_aligned(payload, 8) || !argus_aligned(out, 16))
+        return argus_set_error(ARGUS_ERR_MISALIGNED, "payload must be 8-byte and output 16-byte aligned");
+    if (n_rows == 0) return ARGUS_OK;
+    if (n_rows > ((int64_t)1 << 30)) {
+        if (n_rows % kFlatGroup) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "above 2^30 rows: use a multiple of 2^24");
+        Rows src = flat_rows(payload, s, mn), dst = flat_rows(out, nullptr, nullptr);
+        src.group_stride = kFlatGroup / mode_per(mode) * D;
+        src.sgroup_stride = kFlatGroup;
+        dst.group_stride = kFlatGroup * D * 2;
+        return dequant_dispatch(mode, src, dst, n_rows / kFlatGroup, (int)kFlatGroup, D, st);
+    }
+    return dequant_dispatch(mode, flat_rows(payload, s, mn), flat_rows(out, nullptr, nullptr), 1, (int)n_rows, D, st);
+}
 
 }  // namespace
 
@@ -387,42 +527,49 @@ extern "C" {
 int argus_quant_int8(const uint16_t* x, int64_t n_rows, int D, int8_t* q, uint16_t* scales, argus_stream_t stream) {
     int rc = check_rows(x, q, n_rows, D, 1);
     if (rc || !scales) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
-    return launch_quant<Q_INT8>(x, n_rows, D, 0.f, q, scales, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+    return flat_quant(Q_INT8, x, n_rows, D, q, scales, nullptr, (cudaStream_t)stream);
 }
 
 int argus_quant_fp8sim(const uint16_t* x, int64_t n_rows, int D, int8_t* q, uint16_t* scales, argus_stream_t stream) {
     int rc = check_rows(x, q, n_rows, D, 1);
     if (rc || !scales) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
-    return launch_quant<Q_FP8SIM>(x, n_rows, D, 0.f, q, scales, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+    return flat_quant(Q_FP8SIM, x, n_rows, D, q, scales, nullptr, (cudaStream_t)stream);
 }
 
 int argus_quant_int4(const uint16_t* x, int64_t n_rows, int D, uint8_t* packed, uint16_t* scales, uint16_t* mins,
                      argus_stream_t stream) {
     int rc = check_rows(x, packed, n_rows, D, 2);
     if (rc || !scales || !mins) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales/mins");
-    return launch_quant<Q_INT4>(x, n_rows, D, 0.f, packed, scales, mins, nullptr, nullptr, (cudaStream_t)stream);
+    return flat_quant(Q_INT4, x, n_rows, D, packed, scales, mins, (cudaStream_t)stream);
 }
 
 int argus_quant_int2(const uint16_t* x, int64_t n_rows, int D, uint8_t* packed, uint16_t* scales, uint16_t* mins,
                      argus_stream_t stream) {
     int rc = check_rows(x, packed, n_rows, D, 4);
     if (rc || !scales || !mins) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales/mins");
-    return launch_quant<Q_INT2>(x, n_rows, D, 0.f, packed, scales, mins, nullptr, nullptr, (cudaStream_t)stream);
+    return flat_quant(Q_INT2, x, n_rows, D, packed, scales, mins, (cudaStream_t)stream);
 }
 
 int argus_quant_1bit(const uint16_t* x, int64_t n_rows, int D, uint8_t* packed, uint16_t* scales,
                      argus_stream_t stream) {
     int rc = check_rows(x, packed, n_rows, D, 8);
     if (rc || !scales) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
-    return launch_quant<Q_SIGN1>(x, n_rows, D, 0.f, packed, scales, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+    return flat_quant(Q_SIGN1, x, n_rows, D, packed, scales, nullptr, (cudaStream_t)stream);
+}
+
+int argus_pack_1bit_signs(const uint16_t* x, int64_t n_rows, int D, uint8_t* packed, argus_stream_t stream) {
+    // the 1-bit quantizer with its scale output switched off (null sink)
+    int rc = check_rows(x, packed, n_rows, D, 8);
+    if (rc) return rc;
+    return flat_quant(Q_SIGN1, x, n_rows, D, packed, nullptr, nullptr, (cudaStream_t)stream);
 }
 
 int argus_isolate_outliers(const uint16_t* x, int64_t n_rows, int D, float sigma, uint16_t* normal, uint16_t* outv,
                            uint8_t* mask, argus_stream_t stream) {
     int rc = check_rows(x, normal, n_rows, D, 1);
     if (rc || !outv || !mask) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null output");
+    if (n_rows == 0) return ARGUS_OK;
     if (!(sigma > 0.0f)) {
-        if (n_rows == 0) return ARGUS_OK;
         const int64_t n = n_rows * D;
         cleanse_kernel<<<dq_blocks(n), 256, 0, (cudaStream_t)stream>>>(
             reinterpret_cast<const __half*>(x), n, reinterpret_cast<__half*>(normal), reinterpret_cast<__half*>(outv),
@@ -430,29 +577,18 @@ int argus_isolate_outliers(const uint16_t* x, int64_t n_rows, int D, float sigma
         ARGUS_CHECK_LAUNCH();
         return ARGUS_OK;
     }
-    if (!argus_aligned(outv, 8) || !argus_aligned(normal, 8) || !argus_aligned(mask, 4))
+    if (!argus_aligned(x, 16) || !argus_aligned(outv, 8) || !argus_aligned(normal, 8) || !argus_aligned(mask, 4))
         return argus_set_error(ARGUS_ERR_MISALIGNED, "outputs must be 8-byte aligned");
-    return launch_quant<Q_OUTLIER>(x, n_rows, D, sigma, normal, nullptr, nullptr, outv, mask, (cudaStream_t)stream);
-}
-
-static int dequant_check(const void* a, const void* s, const void* out, int64_t n_rows, int D, int per) {
-    int rc = check_rows(a, out, n_rows, D, per);
-    if (rc) return rc;
-    if (!s) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
-    if (!argus_aligned(a, 8) || !argus_aligned(out, 16))
-        return argus_set_error(ARGUS_ERR_MISALIGNED, "payload must be 8-byte and output 16-byte aligned");
-    return ARGUS_OK;
+    if (n_rows > ((int64_t)1 << 30)) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "above 2^30 rows");
+    return launch_quant<Q_OUTLIER, Q_FP16>(flat_rows(x, nullptr, nullptr), flat_rows(normal, nullptr, nullptr), 1,
+                                           (int)n_rows, D, sigma, outv, mask, (cudaStream_t)stream);
 }
 
 int argus_dequant_int8(const int8_t* q, const uint16_t* scales, int64_t n_rows, int D, uint16_t* out,
                        argus_stream_t stream) {
-    int rc = dequant_check(q, scales, out, n_rows, D, 1);
-    if (rc) return rc;
-    if (n_rows == 0) return ARGUS_OK;
-    dequant_sym8_kernel<<<dq_blocks(n_rows * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-        q, reinterpret_cast<const __half*>(scales), n_rows, D, reinterpret_cast<__half*>(out));
-    ARGUS_CHECK_LAUNCH();
-    return ARGUS_OK;
+    int rc = check_rows(q, out, n_rows, D, 1);
+    if (rc || !scales) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
+    return flat_dequant(Q_INT8, q, scales, nullptr, n_rows, D, out, (cudaStream_t)stream);
 }
 
 int argus_dequant_fp8sim(const int8_t* q, const uint16_t* scales, int64_t n_rows, int D, uint16_t* out,
@@ -462,40 +598,23 @@ int argus_dequant_fp8sim(const int8_t* q, const uint16_t* scales, int64_t n_rows
 
 int argus_dequant_int4(const uint8_t* packed, const uint16_t* scales, const uint16_t* mins, int64_t n_rows, int D,
                        uint16_t* out, argus_stream_t stream) {
-    int rc = dequant_check(packed, scales, out, n_rows, D, 2);
-    if (rc || !mins) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null mins");
-    if (n_rows == 0) return ARGUS_OK;
-    const int64_t pr = n_rows / 2;
-    dequant_asym_kernel<4><<<dq_blocks(pr * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-        packed, reinterpret_cast<const __half*>(scales), reinterpret_cast<const __half*>(mins), pr, D,
-        reinterpret_cast<__half*>(out));
-    ARGUS_CHECK_LAUNCH();
-    return ARGUS_OK;
+    int rc = check_rows(packed, out, n_rows, D, 2);
+    if (rc || !scales || !mins) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales/mins");
+    return flat_dequant(Q_INT4, packed, scales, mins, n_rows, D, out, (cudaStream_t)stream);
 }
 
 int argus_dequant_int2(const uint8_t* packed, const uint16_t* scales, const uint16_t* mins, int64_t n_rows, int D,
                        uint16_t* out, argus_stream_t stream) {
-    int rc = dequant_check(packed, scales, out, n_rows, D, 4);
-    if (rc || !mins) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null mins");
-    if (n_rows == 0) return ARGUS_OK;
-    const int64_t pr = n_rows / 4;
-    dequant_asym_kernel<2><<<dq_blocks(pr * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-        packed, reinterpret_cast<const __half*>(scales), reinterpret_cast<const __half*>(mins), pr, D,
-        reinterpret_cast<__half*>(out));
-    ARGUS_CHECK_LAUNCH();
-    return ARGUS_OK;
+    int rc = check_rows(packed, out, n_rows, D, 4);
+    if (rc || !scales || !mins) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales/mins");
+    return flat_dequant(Q_INT2, packed, scales, mins, n_rows, D, out, (cudaStream_t)stream);
 }
 
 int argus_dequant_1bit(const uint8_t* packed, const uint16_t* scales, int64_t n_rows, int D, uint16_t* out,
                        argus_stream_t stream) {
-    int rc = dequant_check(packed, scales, out, n_rows, D, 8);
-    if (rc) return rc;
-    if (n_rows == 0) return ARGUS_OK;
-    const int64_t pr = n_rows / 8;
-    dequant_sign1_kernel<<<dq_blocks(pr * (D / 8)), 256, 0, (cudaStream_t)stream>>>(
-        packed, reinterpret_cast<const __half*>(scales), pr, D, reinterpret_cast<__half*>(out));
-    ARGUS_CHECK_LAUNCH();
-    return ARGUS_OK;
+    int rc = check_rows(packed, out, n_rows, D, 8);
+    if (rc || !scales) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
+    return flat_dequant(Q_SIGN1, packed, scales, nullptr, n_rows, D, out, (cudaStream_t)stream);
 }
 
 int argus_pack_int4_codes(const uint8_t* codes, int64_t n_rows, int D, uint8_t* packed, argus_stream_t stream) {
@@ -508,11 +627,56 @@ int argus_pack_int4_codes(const uint8_t* codes, int64_t n_rows, int D, uint8_t* 
     return ARGUS_OK;
 }
 
-int argus_pack_1bit_signs(const uint16_t* x, int64_t n_rows, int D, uint8_t* packed, argus_stream_t stream) {
-    // The sign pack is the 1-bit quantizer with its scale output switched off (null sink).
-    int rc = check_rows(x, packed, n_rows, D, 8);
+// ------------------------------------------------------------------------- page codecs
+int argus_page_quantize(const uint16_t* k, const uint16_t* v, int32_t n_bh, int D, const argus_kv_arena* dst,
+                        int32_t dst_slot, argus_stream_t stream) {
+    int rc = check_arena(dst, D);
     if (rc) return rc;
-    return launch_quant<Q_SIGN1>(x, n_rows, D, 0.f, packed, nullptr, nullptr, nullptr, nullptr, (cudaStream_t)stream);
+    if (!k || !v || n_bh <= 0 || dst_slot < 0) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad page arguments");
+    if (!argus_aligned(k, 16) || !argus_aligned(v, 16)) return argus_set_error(ARGUS_ERR_MISALIGNED, "k/v alignment");
+    const int P = dst->page_tokens;
+    for (int which = 0; which < 2; ++which) {
+        Rows src = flat_rows(which ? v : k, nullptr, nullptr);
+        src.group_stride = (int64_t)P * D * 2;
+        rc = quant_dispatch(tier_mode(dst->tier), Q_FP16, src, page_rows(dst, dst_slot, which, D), n_bh, P, D,
+                            (cudaStream_t)stream);
+        if (rc) return rc;
+    }
+    return ARGUS_OK;
+}
+
+int argus_page_requant(const argus_kv_arena* src, int32_t src_slot, const argus_kv_arena* dst, int32_t dst_slot,
+                       int32_t n_bh, int D, argus_stream_t stream) {
+    int rc = check_arena(src, D);
+    if (!rc) rc = check_arena(dst, D);
+    if (rc) return rc;
+    if (src->page_tokens != dst->page_tokens) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "page sizes differ");
+    if (n_bh <= 0 || src_slot < 0 || dst_slot < 0) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad page arguments");
+    for (int which = 0; which < 2; ++which) {
+        rc = quant_dispatch(tier_mode(dst->tier), tier_mode(src->tier), page_rows(src, src_slot, which, D),
+                            page_rows(dst, dst_slot, which, D), n_bh, src->page_tokens, D, (cudaStream_t)stream);
+        if (rc) return rc;
+    }
+    return ARGUS_OK;
+}
+
+int argus_page_dequantize(const argus_kv_arena* src, int32_t src_slot, int32_t n_bh, int D, uint16_t* k_out,
+                          uint16_t* v_out, int64_t out_bh_stride, int64_t out_tok0, argus_stream_t stream) {
+    int rc = check_arena(src, D);
+    if (rc) return rc;
+    if (!k_out || !v_out || n_bh <= 0 || src_slot < 0 || out_tok0 < 0 || out_tok0 > (1 << 30))
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad page arguments");
+    if (!argus_aligned(k_out, 16) || !argus_aligned(v_out, 16) || (out_bh_stride * 2) % 16)
+        return argus_set_error(ARGUS_ERR_MISALIGNED, "outputs must be 16-byte aligned");
+    for (int which = 0; which < 2; ++which) {
+        Rows dst = flat_rows(which ? v_out : k_out, nullptr, nullptr);
+        dst.group_stride = out_bh_stride * 2;
+        dst.row0 = (int)out_tok0;
+        rc = dequant_dispatch(tier_mode(src->tier), page_rows(src, src_slot, which, D), dst, n_bh, src->page_tokens, D,
+                              (cudaStream_t)stream);
+        if (rc) return rc;
+    }
+    return ARGUS_OK;
 }
 
 }  // extern "C"

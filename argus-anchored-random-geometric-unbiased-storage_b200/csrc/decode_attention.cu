@@ -73,7 +73,8 @@ struct Params {
     float* lse;
     float* part_o;    // [B*Hkv*NQG][S][8][D]
     float* part_lse;  // [B*Hkv*NQG][S][8]
-    int B, Hkv, G, qlen, S, nqg;
+    float* tile_lse;  // optional [B*Hkv*NQG][n_chunks][16][8]: log2-sum-exp of each tile's scores
+    int B, Hkv, G, qlen, S, nqg, n_chunks;
     float scale_log2;
 };
 
@@ -495,10 +496,10 @@ __device__ __forceinline__ void tile_pv(const TilePtr& tp, int g4, int t4, const
 // Online softmax over NT tiles' scores at once: one max reduction and at most one rescale.  The
 // weights go to the PV contraction as two fp16 fragments, p = hi + lo (lo = fp16(p - hi)), so the
 // product keeps ~22 bits of the fp32 weight instead of fp16's 11.
-template <int KC, int NT, bool PRECISE>
+template <int KC, int NT, bool PRECISE, bool MASS>
 __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxState& st, float (&o)[KC][4],
                                                uint32_t (&b01)[NT], uint32_t (&b23)[NT], uint32_t (&c01)[NT],
-                                               uint32_t (&c23)[NT]) {
+                                               uint32_t (&c23)[NT], float* mass_out) {
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int i = 0; i < NT; ++i) { mx0 = fmaxf(mx0, fmaxf(x[i][0], x[i][2])); mx1 = fmaxf(mx1, fmaxf(x[i][1], x[i][3])); }
@@ -523,6 +524,20 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
         const float p2 = exp2f(x[i][2] - m0), p3 = exp2f(x[i][3] - m1);
         st.l[0] += p0 + p2;
         st.l[1] += p1 + p3;
+        if constexpr (MASS) {
+            // this tile's log2-sum-exp per query: sum over the 16 tokens, relative to the reference max
+            float s0 = p0 + p2, s1 = p1 + p3;
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+            }
+            if ((threadIdx.x & 31) < 4) {
+                const int t = threadIdx.x & 3;
+                mass_out[i * kQ + 2 * t] = (s0 > 0.f) ? __log2f(s0) + m0 : -INFINITY;
+                mass_out[i * kQ + 2 * t + 1] = (s1 > 0.f) ? __log2f(s1) + m1 : -INFINITY;
+            }
+        }
         const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
         const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
         b01[i] = movmatrix_t(h2u(h01));  // mma rows 0..7 (tokens 2g)
@@ -535,10 +550,10 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
 }
 
 // Processes tiles i0 and (if pair) i0+1 of a staged chunk with interleaved independent work.
-template <int D, int TIER, bool PAIR, bool PRECISE>
+template <int D, int TIER, bool PAIR, bool PRECISE, bool MASS>
 __device__ __forceinline__ void process_tiles(const TilePtr& ta, const TilePtr& tb, int g4, int t4,
                                               const uint32_t (&qf)[D / 16][2], float scale_log2, SoftmaxState& st,
-                                              float (&o)[D / 16][4]) {
+                                              float (&o)[D / 16][4], float* mass_out) {
     constexpr int NT = PAIR ? 2 : 1;
     TokScale tk[NT], tv[NT];
     float x[NT][4];
@@ -547,13 +562,13 @@ __device__ __forceinline__ void process_tiles(const TilePtr& ta, const TilePtr& 
     tile_scores<D, TIER>(ta, g4, t4, tk[0], qf, scale_log2, x[0]);
     if constexpr (PAIR) tile_scores<D, TIER>(tb, g4, t4, tk[NT - 1], qf, scale_log2, x[NT - 1]);
     uint32_t b01[NT], b23[NT], c01[NT], c23[NT];
-    softmax_update<D / 16, NT, PRECISE>(x, st, o, b01, b23, c01, c23);
+    softmax_update<D / 16, NT, PRECISE, MASS>(x, st, o, b01, b23, c01, c23, mass_out);
     tile_pv<D, TIER, PRECISE>(ta, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
     if constexpr (PAIR)
         tile_pv<D, TIER, PRECISE>(tb, g4, t4, tv[NT - 1], b01[NT - 1], b23[NT - 1], c01[NT - 1], c23[NT - 1], o);
 }
 
-template <int D, bool PRECISE>
+template <int D, bool PRECISE, bool MASS>
 __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_constant__ Params p) {
     constexpr int KC = D / 16;
     constexpr int STAGE = stage_bytes(D);
@@ -668,6 +683,9 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
         const int n = ch.ntiles;
         const ChunkView cv = chunk_view<D>(ar, n);
         const unsigned char* sb = wbuf + stage * STAGE;
+        float* mass_base = nullptr;
+        if constexpr (MASS)
+            mass_base = p.tile_lse + (((int64_t)bh * p.nqg + qg) * p.n_chunks + (first + j * kWarps)) * 16 * kQ;
         switch (ar.tier) {
 #define ARGUS_TILE_CASE(T)                                                                                        \
     case T: {                                                                                                     \
@@ -687,11 +705,13 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
         /* tile pairs (ARGUS_DA_PAIR=1) measured slower on B200: register pressure; D = 256 never pairs */      \
         for (; ARGUS_DA_PAIR && D <= 128 && i + 1 < n; i += 2) {                                                                   \
             const TilePtr ta = tile(i), tb = tile(i + 1);                                                         \
-            process_tiles<D, T, true, PRECISE>(ta, tb, g4, t4, qf, p.scale_log2, st, o);                          \
+            process_tiles<D, T, true, PRECISE, MASS>(ta, tb, g4, t4, qf, p.scale_log2, st, o,                     \
+                                                     mass_base ? mass_base + i * kQ : nullptr);                   \
         }                                                                                                         \
         for (; i < n; ++i) {                                                                                      \
             const TilePtr ta = tile(i);                                                                           \
-            process_tiles<D, T, false, PRECISE>(ta, ta, g4, t4, qf, p.scale_log2, st, o);                         \
+            process_tiles<D, T, false, PRECISE, MASS>(ta, ta, g4, t4, qf, p.scale_log2, st, o,                    \
+                                                      mass_base ? mass_base + i * kQ : nullptr);                  \
         }                                                                                                         \
         break;                                                                                                    \
     }
@@ -812,7 +832,9 @@ int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
     const size_t smem = (size_t)kWarps * kStages * stage_bytes(D) + stage_slack(D);
     static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kWarps * kStages * stage_bytes(D),
                   "merge buffer must fit in the stage memory");
-    auto kern = precise ? decode_attn_kernel<D, true> : decode_attn_kernel<D, false>;
+    const bool mass = prm.tile_lse != nullptr;
+    auto kern = precise ? (mass ? decode_attn_kernel<D, true, true> : decode_attn_kernel<D, true, false>)
+                        : (mass ? decode_attn_kernel<D, false, true> : decode_attn_kernel<D, false, false>);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
     dim3 grid(n_splits, prm.B * prm.Hkv, prm.nqg);
@@ -855,8 +877,8 @@ int64_t argus_decode_attention_workspace_size(const argus_attn_shape* s) {
 }
 
 int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
-                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, void* workspace,
-                           argus_stream_t stream) {
+                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, float* tile_lse,
+                           void* workspace, argus_stream_t stream) {
     if (!s || !arenas || !split_chunk0 || !q || !out)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
     if (s->batch <= 0 || s->heads_kv <= 0 || s->group <= 0 || s->q_len <= 0 || s->n_splits <= 0)
@@ -902,6 +924,8 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
     prm.G = s->group;
     prm.qlen = s->q_len;
     prm.S = s->n_splits;
+    prm.n_chunks = s->n_chunks;
+    prm.tile_lse = tile_lse;
     prm.nqg = (s->group * s->q_len + da::kQ - 1) / da::kQ;
     if (prm.nqg > 65535) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "too many query groups");
     prm.scale_log2 = s->scale * 1.4426950408889634f;

@@ -25,6 +25,8 @@ extern "C" {
 
 typedef void* argus_stream_t; /* a cudaStream_t */
 
+struct argus_kv_arena;
+
 enum argus_status {
     ARGUS_OK = 0,
     ARGUS_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, divisibility */
@@ -41,6 +43,11 @@ const char* argus_status_string(int status);
 const char* argus_last_error(void);
 /* Library version as 10000*major + 100*minor + patch. */
 int argus_version(void);
+
+/* Asynchronous copy of `bytes` between any two of device memory and pinned host memory on `stream`
+ * (one cudaMemcpyAsync).  The host-spill transport: replaces the synchronous pageable .to("cpu") /
+ * .to(device) moves of swap_out_to_host / swap_in_to_device (core/memory_manager.py:1658-1713). */
+int argus_memcpy_async(void* dst, const void* src, int64_t bytes, argus_stream_t stream);
 
 /* ------------------------------------------------------------------------------- codecs */
 
@@ -98,6 +105,39 @@ int argus_pack_1bit_signs(const uint16_t* x, int64_t n_rows, int D, uint8_t* pac
  * Replaces isolate_outliers, core/memory_manager.py:89-113.  mask is one byte per element. */
 int argus_isolate_outliers(const uint16_t* x, int64_t n_rows, int D, float sigma, uint16_t* normal,
                            uint16_t* outv, uint8_t* mask, argus_stream_t stream);
+
+/* ----------------------------------------------------------------------- page codecs (cascade) */
+/* These address pages of record arenas (see argus_kv_arena below): page `slot` holds B*H_kv
+ * (batch, kv_head) blocks `bh_stride` bytes apart, each [K payload][V payload][K scales][V scales]
+ * [K mins][V mins].  n_bh = B*H_kv. */
+
+/* Quantizes an fp16 page, k and v contiguous [n_bh][page_tokens][D], into slot dst_slot of a record
+ * arena of any tier.  The K/V halves of _demote_active_to_fp8's quantize step
+ * (core/memory_manager.py:944-949) and of building any tier directly from fp16. */
+int argus_page_quantize(const uint16_t* k, const uint16_t* v, int32_t n_bh, int D, const struct argus_kv_arena* dst,
+                        int32_t dst_slot, argus_stream_t stream);
+/* Fused demotion of one page: dequantize slot src_slot of `src` exactly as the reference does and
+ * re-quantize it into slot dst_slot of `dst` (any tier pair with equal page size), without leaving
+ * the chip.  Replaces the dequantize + quantize pairs of _demote_fp8_to_int8, _demote_int8_to_int4,
+ * _demote_int4_to_int2 and _demote_int2_to_one_bit (core/memory_manager.py:989-1123). */
+int argus_page_requant(const struct argus_kv_arena* src, int32_t src_slot, const struct argus_kv_arena* dst,
+                       int32_t dst_slot, int32_t n_bh, int D, argus_stream_t stream);
+/* Dequantizes page src_slot of `src` to fp16 rows: K into k_out + bh*out_bh_stride + (out_tok0 + t)*D
+ * (elements), V likewise into v_out.  The per-page dequantization of get_all_keys_values,
+ * _resurrect_page and speculate_and_prefetch (core/memory_manager.py:832-866, 1157-1290, 1578-1621). */
+int argus_page_dequantize(const struct argus_kv_arena* src, int32_t src_slot, int32_t n_bh, int D, uint16_t* k_out,
+                          uint16_t* v_out, int64_t out_bh_stride, int64_t out_tok0, argus_stream_t stream);
+
+/* Overwrites out[(b*H + h)*out_bh_stride + (out_tok0 + t)*D + d] with vals[i] for each COO entry
+ * idx[i] = (b, h, t, d) (int16); entries outside [B, H, P, D] are skipped.  The sidecar scatter of
+ * core/memory_manager.py:1190-1199 (and every other reader of key/value_out_indices). */
+int argus_scatter_coo(uint16_t* out, int64_t out_bh_stride, int64_t out_tok0, int B, int H, int P, int D,
+                      const int16_t* idx, const uint16_t* vals, int64_t n, argus_stream_t stream);
+/* Compacts a [B,H,P,D] outlier mask (one byte per element) and its values into COO entries in
+ * row-major order, as torch.nonzero(mask).to(int16) and outv[mask] (core/memory_manager.py:951-955).
+ * Writes at most `capacity` entries; *count_out (device int64) receives the total count. */
+int argus_outliers_to_coo(const uint8_t* mask, const uint16_t* outv, int B, int H, int P, int D, int16_t* idx_out,
+                          uint16_t* vals_out, int64_t capacity, int64_t* count_out, argus_stream_t stream);
 
 /* --------------------------------------------------------------------------- JL archive */
 
@@ -193,6 +233,10 @@ int argus_record_bytes(int tier, int page_tokens, int head_dim);
  * [B][H_q][q_len] fp32 natural-log sum-exp.  The chunk list covers the cached tokens in any order;
  * split_chunk0[s] .. split_chunk0[s+1] are the chunks of split s (n_splits + 1 entries, device).
  * chunks and split_chunk0 are device arrays; arenas is a host array copied into the launch.
+ * tile_lse: optional [B*H_kv*ceil(group*q_len/8)][n_chunks][16][8] fp32 receiving, per tile of
+ * each chunk and per query of each 8-query group, log2 of the tile's sum of exp2-scaled scores
+ * (natural scores times log2 e); with lse it gives each page's share of the attention mass, the
+ * signal of the reference's importance and resurrection policy (core/memory_manager.py:1453-1522).
  * workspace: device scratch of argus_decode_attention_workspace_size bytes (may be null when
  * n_splits == 1).
  * Replaces PagedDynamicKVCache.inplace_paged_attention, core/memory_manager.py:1317-1447 (its
@@ -200,8 +244,8 @@ int argus_record_bytes(int tier, int page_tokens, int head_dim);
  * get_all_keys_values + transformers' attention (core/memory_manager.py:1157-1315,
  * models/attention_wrapper.py:87-88), which it matches within fp32-accumulation tolerance. */
 int argus_decode_attention(const argus_attn_shape* shape, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
-                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, void* workspace,
-                           argus_stream_t stream);
+                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, float* tile_lse,
+                           void* workspace, argus_stream_t stream);
 
 /* Reads (and clears) the device-side status word that bounded waits in the kernels set on a
  * timeout; writes ARGUS_OK or ARGUS_ERR_TIMEOUT to *status after synchronising `stream`. */
