@@ -31,7 +31,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def _np(t):
-    return t.detach().cpu().contiguous().numpy()
+    # a copy: numpy views of CPU tensors would alias pool memory that later calls overwrite
+    return t.detach().cpu().contiguous().numpy().copy()
 
 
 def load_reference(path):
