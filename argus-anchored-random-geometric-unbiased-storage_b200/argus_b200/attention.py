@@ -34,7 +34,8 @@ NUM_SMS = 148
 CTAS_PER_SM = 3
 # C-ABI entry points bound in this module (with structure-typed arguments)
 BOUND_SYMBOLS = ("argus_decode_attention", "argus_decode_attention_workspace_size",
-                 "argus_decode_attention_chunk_tiles", "argus_record_bytes", "argus_device_status")
+                 "argus_decode_attention_chunk_tiles", "argus_record_bytes", "argus_device_status",
+                 "argus_decode_attention_noalloc", "argus_decode_attention_noalloc_capacity")
 
 
 class ArenaC(ctypes.Structure):
@@ -67,6 +68,13 @@ def _bind():
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.argus_decode_attention.restype = ctypes.c_int
+        L.argus_decode_attention_noalloc.argtypes = [ctypes.POINTER(ShapeC), ctypes.POINTER(ArenaC),
+                                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                     ctypes.c_void_p]
+        L.argus_decode_attention_noalloc.restype = ctypes.c_int
+        L.argus_decode_attention_noalloc_capacity.argtypes = []
+        L.argus_decode_attention_noalloc_capacity.restype = ctypes.c_int64
         L.argus_decode_attention_workspace_size.argtypes = [ctypes.POINTER(ShapeC)]
         L.argus_decode_attention_workspace_size.restype = ctypes.c_int64
         L.argus_decode_attention_chunk_tiles.argtypes = [ctypes.c_int] * 4

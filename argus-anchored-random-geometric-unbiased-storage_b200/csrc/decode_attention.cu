@@ -18,6 +18,8 @@
 // The score tile is moved into the PV operand layout with movmatrix (8x8 transpose).  Online
 // softmax runs in the log2 domain; warps merge in shared memory; splits merge in a second kernel
 // (log-sum-exp combine).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace argus {
@@ -959,3 +961,56 @@ int argus_device_status(int* status, argus_stream_t stream) {
 }
 
 }  // extern "C"
+
+// --------------------------------------------------------------------------- allocation-free entry
+// Split-K scratch for argus_decode_attention_noalloc: a fixed array in the module's own device
+// memory, so callers that cannot allocate device memory (see the header) still get split-K.
+#define ARGUS_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ARGUS_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.  Host code
+// must not pass the symbol itself to a kernel: in host code it names a host-side stand-in.
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    if (dev < 0 || dev >= kMaxDevices) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return argus_set_cuda_error(e);
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return ARGUS_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t argus_decode_attention_noalloc_capacity(void) { return ARGUS_NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int argus_decode_attention_noalloc(const argus_attn_shape* s, const argus_kv_arena* arenas,
+                                              const argus_kv_chunk* chunks, const int32_t* split_chunk0,
+                                              const uint16_t* q, uint16_t* out, float* lse, float* tile_lse,
+                                              argus_stream_t stream) {
+    if (!s) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null shape");
+    const int64_t need = argus_decode_attention_workspace_size(s);
+    if (need > (int64_t)ARGUS_NOALLOC_SCRATCH_BYTES)
+        return argus_set_error(ARGUS_ERR_CAPACITY,
+                               "split-K partials exceed the 8 MiB built-in scratch: use fewer splits or "
+                               "argus_decode_attention with a caller workspace");
+    void* scratch = nullptr;
+    if (need > 0) {
+        const int rc = noalloc_scratch(&scratch);
+        if (rc) return rc;
+    }
+    return argus_decode_attention(s, arenas, chunks, split_chunk0, q, out, lse, tile_lse, scratch, stream);
+}

@@ -247,6 +247,24 @@ int argus_decode_attention(const argus_attn_shape* shape, const argus_kv_arena* 
                            const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, float* tile_lse,
                            void* workspace, argus_stream_t stream);
 
+/* Allocation-free variant of argus_decode_attention, for callers that cannot allocate device memory
+ * (a host that must not call cudaMalloc during decode, such as an embedding runtime holding a fixed
+ * memory budget or code running inside a region where allocation is forbidden): the split-K
+ * partials go to a fixed scratch array that the library holds in its own device memory (8 MiB,
+ * argus_decode_attention_noalloc_capacity(); every GPU that loads the library keeps it until the
+ * process exits), so nothing is allocated.  Arguments as argus_decode_attention without workspace;
+ * shapes whose partials need more than the capacity fail with ARGUS_ERR_CAPACITY.  The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress) once, with that device current,
+ * so make that first call before any stream capture.  All calls on a device share the one array and
+ * each launch writes every partial it reads, so nothing has to start at zero; calls that overlap on
+ * the GPU (concurrent streams) race on it and must be serialised by the caller.
+ * This entry point has no counterpart in the reference. */
+int argus_decode_attention_noalloc(const argus_attn_shape* shape, const argus_kv_arena* arenas,
+                                   const argus_kv_chunk* chunks, const int32_t* split_chunk0, const uint16_t* q,
+                                   uint16_t* out, float* lse, float* tile_lse, argus_stream_t stream);
+/* Bytes of the built-in scratch of argus_decode_attention_noalloc. */
+int64_t argus_decode_attention_noalloc_capacity(void);
+
 /* Reads (and clears) the device-side status word that bounded waits in the kernels set on a
  * timeout; writes ARGUS_OK or ARGUS_ERR_TIMEOUT to *status after synchronising `stream`. */
 int argus_device_status(int* status, argus_stream_t stream);
