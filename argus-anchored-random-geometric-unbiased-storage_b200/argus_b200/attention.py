@@ -31,7 +31,12 @@ TIER_PAYLOAD_DTYPE = {TIER_FP16: torch.float16, TIER_FP8SIM: torch.int8, TIER_IN
                       TIER_INT4: torch.uint8, TIER_INT2: torch.uint8, TIER_1BIT: torch.uint8}
 MAX_ARENAS = 8
 NUM_SMS = 148
-CTAS_PER_SM = 3
+
+
+def ctas_per_sm(head_dim):
+    """Decode-attention CTAs resident per SM (the kernel's launch bounds and shared memory)."""
+    return 2 if head_dim >= 256 else 4
+
 # C-ABI entry points bound in this module (with structure-typed arguments)
 BOUND_SYMBOLS = ("argus_decode_attention", "argus_decode_attention_workspace_size",
                  "argus_decode_attention_chunk_tiles", "argus_record_bytes", "argus_device_status",
@@ -183,6 +188,39 @@ def _tile_cost(tier, head_dim, ntok):
     return float(ntok) * head_dim / 128
 
 
+def _deal_chunks(chunk_arena, cost, n_splits):
+    """Orders the chunks for n_splits split-K slices and returns (order, bounds): slice s runs
+    chunks order[bounds[s]:bounds[s+1]].
+
+    Every slice takes a contiguous share of EVERY arena's chunks, and lists its shares in the
+    same arena order, so all CTAs move through the tiers together and the SMs' instruction caches
+    hold one tier's code at a time.  Shares are cut by cost, and the rounding error of each cut is
+    carried into the next arena's cut so the slices' total costs stay within about one chunk."""
+    n = len(cost)
+    if n == 0:
+        return [], np.zeros(n_splits + 1, np.int32)
+    groups = {}
+    for i, ai in enumerate(chunk_arena):
+        groups.setdefault(ai, []).append(i)
+    cuts = []
+    carry = np.zeros(n_splits + 1)  # cost placed before each boundary minus its ideal share, so far
+    for ai, idx in groups.items():
+        cum = np.concatenate([[0.0], np.cumsum([cost[i] for i in idx])])
+        ideal = cum[-1] * np.arange(n_splits + 1) / n_splits
+        b = np.searchsorted(cum, ideal - carry, side="left")
+        b = np.clip(b, 0, len(idx))
+        b[0], b[-1] = 0, len(idx)
+        b = np.maximum.accumulate(b)
+        carry += cum[b] - ideal
+        cuts.append((idx, b))
+    order, bounds = [], [0]
+    for s in range(n_splits):
+        for idx, b in cuts:
+            order += idx[b[s]:b[s + 1]]
+        bounds.append(len(order))
+    return order, np.asarray(bounds, np.int32)
+
+
 class AttentionPlan:
     """Device tables for one page list.
 
@@ -199,17 +237,19 @@ class AttentionPlan:
         caps = [chunk_capacity(a, self.D) for a in self.arenas]
         if min(caps) <= 0:
             raise ValueError(f"head_dim {self.D} is not supported")
-        chunks, ccost = [], []
+        chunks, ccost, srcs = [], [], []  # srcs: per chunk, the index in `pages` of each tile
         cur = None  # open chunk: [slot0, tok0, arena, ntiles, ntok_last, next_slot]
+        cur_src = []
         total_tokens = 0
 
         def close():
-            nonlocal cur
+            nonlocal cur, cur_src
             if cur is not None:
                 chunks.append(tuple(cur[:5]))
-                cur = None
+                srcs.append(cur_src)
+                cur, cur_src = None, []
 
-        for ai, slot, ntok in pages:
+        for pi, (ai, slot, ntok) in enumerate(pages):
             ntok = int(ntok)
             if ntok <= 0:
                 continue
@@ -224,6 +264,7 @@ class AttentionPlan:
                 else:
                     close()
                     cur = [slot, 0, ai, 1, ntok, slot + 1]
+                cur_src.append(pi)
             elif a.layout == LAYOUT_RECORD:
                 close()
                 if a.tier != TIER_FP16 and ntok % 8:
@@ -233,6 +274,7 @@ class AttentionPlan:
                     nt = min(caps[ai], ntiles_page - t0)
                     last = ntok - 16 * (t0 + nt - 1)
                     chunks.append((slot, 16 * t0, ai, nt, min(16, last)))
+                    srcs.append([pi] * nt)
             else:  # split fp16: slot = 16-token block
                 if ntok > 16:
                     raise ValueError("split fp16 slots hold at most 16 tokens")
@@ -243,6 +285,7 @@ class AttentionPlan:
                 else:
                     close()
                     cur = [slot, 0, ai, 1, ntok, slot + 1]
+                cur_src.append(pi)
         close()
         self.n_tokens = total_tokens
         for slot, tok0, ai, nt, last in chunks:
@@ -254,17 +297,12 @@ class AttentionPlan:
         groups = self.B * self.Hkv * nqg
         if n_splits is None:
             # as many splits as fill one wave of CTAs, with at least ~2 chunks per warp
-            n_splits = max(1, min(NUM_SMS * CTAS_PER_SM // groups, max(1, self.n_chunks // 8)))
+            n_splits = max(1, min(NUM_SMS * ctas_per_sm(self.D) // groups, max(1, self.n_chunks // 8)))
         n_splits = max(1, min(int(n_splits), max(1, self.n_chunks)))
         self.n_splits = n_splits
-        if self.n_chunks:
-            cum = np.concatenate([[0.0], np.cumsum(ccost)])
-            targets = cum[-1] * np.arange(n_splits + 1) / n_splits
-            bounds = np.searchsorted(cum, targets, side="left").astype(np.int32)
-            bounds[0], bounds[-1] = 0, self.n_chunks
-            bounds = np.maximum.accumulate(bounds)
-        else:
-            bounds = np.zeros(n_splits + 1, np.int32)
+        order, bounds = _deal_chunks([c[2] for c in chunks], ccost, n_splits)
+        chunks = [chunks[i] for i in order]
+        srcs = [srcs[i] for i in order]
         arr = (ChunkC * max(1, len(chunks)))()
         for i, (slot, tok0, ai, nt, last) in enumerate(chunks):
             arr[i] = ChunkC(slot, tok0, ai, nt, last)
@@ -277,6 +315,7 @@ class AttentionPlan:
         ws = _bind().argus_decode_attention_workspace_size(ctypes.byref(self._shape))
         self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=self.device) if ws > 0 else None
         self.chunks = chunks
+        self.chunk_pages = srcs  # per chunk (in launch order), the index in `pages` of each of its tiles
         self.compressed_bytes = self._algorithmic_bytes(pages)
 
     def _algorithmic_bytes(self, pages):

@@ -641,7 +641,7 @@ class PagedDynamicKVCache:
             index["scratch"] = len(arenas)
             arenas.append(A.KVArena.from_fp16(sk, sv))
         pos = 0
-        page_seg, page_tiles = [], []  # per entry of `pages`: its segment and its number of 16-token tiles
+        page_seg = []  # per entry of `pages`: its segment
         for seg, (kind, page, n) in enumerate(order):
             if kind in ("sinks", "anchors", "buffer") or kind.startswith("scratch:"):
                 sk, sv = scratch
@@ -669,7 +669,6 @@ class PagedDynamicKVCache:
                 for t0 in range(0, n, 16):
                     pages.append((index["scratch"], (pos + t0) // 16, min(16, n - t0)))
                     page_seg.append(seg)
-                    page_tiles.append(1)
                 pos += -(-n // 16) * 16
             else:
                 if kind not in index:
@@ -677,20 +676,15 @@ class PagedDynamicKVCache:
                     arenas.append(self.arenas[kind])
                 pages.append((index[kind], page["pool_idx"], n))
                 page_seg.append(seg)
-                page_tiles.append(1 if P <= 16 else -(-n // 16))
         # attention is order-free: give each record arena's pages in slot order so runs merge into chunks
         perm = sorted(range(len(pages)), key=lambda i: (pages[i][0], pages[i][1]))
         plan = A.AttentionPlan(arenas, [pages[i] for i in perm], batch=B, heads_kv=Hkv, group=Hq // Hkv,
                                head_dim=D, q_len=qlen)
-        # the plan's tiles follow the page order it was given: map (chunk, tile) -> segment
-        tile_seg = [page_seg[i] for i in perm for _ in range(page_tiles[i])]
+        # map (chunk, tile) of the launch -> segment of the reference's attention order
         cmap = torch.full((max(1, plan.n_chunks), 16), -1, dtype=torch.long)
-        t = 0
-        for c, (slot, tok0, ai, nt, last) in enumerate(plan.chunks):
-            for i in range(nt):
-                cmap[c, i] = tile_seg[t]
-                t += 1
-        assert t == len(tile_seg)
+        for c, src in enumerate(plan.chunk_pages):
+            for i, pi in enumerate(src):
+                cmap[c, i] = page_seg[perm[pi]]
         plan.tile_segment = cmap.to(dev)
         plan.segments = order
         self._plan, self._plan_key = plan, key

@@ -27,16 +27,20 @@ namespace da {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 2;
+constexpr int kPairWarps = 2;                 // warps sharing one staging ring
+constexpr int kPairs = kWarps / kPairWarps;
+constexpr int kStages = 3;                    // ring slots per warp pair
 constexpr int kMaxTiles = 16;
 constexpr int kQ = 8;                       // queries per CTA (mma N)
 constexpr long long kSpinLimit = 1ll << 26; // bounded mbarrier waits
 
 __device__ int g_status = 0;
 
-__host__ __device__ constexpr int stage_bytes(int D) {
-    return (64 * D + 128) > 9216 ? ((64 * D + 128 + 127) / 128) * 128 : 9216;
-}
+// One ring slot: a whole fp16 tile (16 tokens of K and V, 64 D bytes) plus 4 D, at least 8.5 KB
+// (so 4 CTAs of two 3-slot rings fit in an SM's shared memory up to D = 128).
+__host__ __device__ constexpr int stage_bytes(int D) { return 68 * D > 8704 ? 68 * D : 8704; }
+// CTAs per SM the launch bounds and shared memory are sized for
+__host__ __device__ constexpr int ctas_per_sm(int D) { return D >= 256 ? 2 : 4; }
 // Shared memory past the last stage that fragment loads of short (8-token) pages may touch.
 __host__ __device__ constexpr int stage_slack(int D) { return 16 * D; }
 __host__ __device__ constexpr int tier_bits(int tier) {
@@ -571,18 +575,19 @@ __device__ __forceinline__ void process_tiles(const TilePtr& ta, const TilePtr& 
 }
 
 template <int D, bool PRECISE, bool MASS>
-__global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(const __grid_constant__ Params p) {
     constexpr int KC = D / 16;
     constexpr int STAGE = stage_bytes(D);
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t mbar[kWarps][kStages];
+    __shared__ __align__(8) uint64_t mbar[kPairs][kStages];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g4 = lane >> 2, t4 = lane & 3;
     const int split = blockIdx.x, bh = blockIdx.y, qg = blockIdx.z;
     const int b = bh / p.Hkv, h = bh - b * p.Hkv;
     const int NQ = p.G * p.qlen;
-    unsigned char* wbuf = smem + (size_t)warp * kStages * STAGE;
+    const int pair = warp / kPairWarps, wip = warp - pair * kPairWarps;
+    unsigned char* wbuf = smem + (size_t)pair * kStages * STAGE;
 
     // ---- Q^T fragments (query qg*8 + g4, dims t4*D/4 ..) and per-query sums
     uint32_t qf[KC][2];
@@ -609,24 +614,27 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
 #pragma unroll
     for (int t = 0; t < KC; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
 
+    // The split's chunks are dealt to the warp pairs round-robin; pair chunk j sits in ring slot
+    // j % kStages and is processed by warp j % kPairWarps of the pair.  The warp that finishes a
+    // slot refills it with pair chunk j + kStages (which its partner will process).
     const int c_begin = p.split_chunk0[split], c_end = p.split_chunk0[split + 1];
-    const int first = c_begin + warp;
-    const int n_my = first < c_end ? (c_end - first + kWarps - 1) / kWarps : 0;
+    const int first = c_begin + pair;
+    const int n_pair = first < c_end ? (c_end - first + kPairs - 1) / kPairs : 0;
 
-    if (lane == 0) {
+    if (wip == 0 && lane == 0) {
 #pragma unroll
-        for (int s = 0; s < kStages; ++s) mbar_init(&mbar[warp][s], 1);
+        for (int s = 0; s < kStages; ++s) mbar_init(&mbar[pair][s], 1);
         fence_mbar_init();
     }
-    __syncwarp();
+    __syncthreads();
 
-    // Issue the bulk copies of chunk j of this warp into stage j % kStages (lane 0 only).
+    // Issue the bulk copies of pair chunk j into slot j % kStages (one lane).
     auto issue = [&](int j) {
-        const argus_kv_chunk ch = p.chunks[first + j * kWarps];
+        const argus_kv_chunk ch = p.chunks[first + j * kPairs];
         const argus_kv_arena& ar = p.arenas[ch.arena];
         const int tier = ar.tier, n = ch.ntiles, P = ar.page_tokens;
         unsigned char* dst = wbuf + (j % kStages) * STAGE;
-        uint64_t* bar = &mbar[warp][j % kStages];
+        uint64_t* bar = &mbar[pair][j % kStages];
         const unsigned char* blk = static_cast<const unsigned char*>(ar.k) + (int64_t)bh * ar.bh_stride;
         fence_proxy_async();
         if (whole_records(ar.layout, P)) {
@@ -668,26 +676,26 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
         }
     };
 
-    if (lane == 0) {
-        for (int j = 0; j < kStages && j < n_my; ++j) issue(j);
+    if (wip == 0 && lane == 0) {
+        for (int j = 0; j < kStages && j < n_pair; ++j) issue(j);
     }
     __syncwarp();
 
     bool failed = false;
-    for (int j = 0; j < n_my; ++j) {
+    for (int j = wip; j < n_pair; j += kPairWarps) {
         const int stage = j % kStages;
-        if (!mbar_wait(&mbar[warp][stage], (uint32_t)((j / kStages) & 1))) {
+        if (!mbar_wait(&mbar[pair][stage], (uint32_t)((j / kStages) & 1))) {
             failed = true;
             break;
         }
-        const argus_kv_chunk ch = p.chunks[first + j * kWarps];
+        const argus_kv_chunk ch = p.chunks[first + j * kPairs];
         const argus_kv_arena& ar = p.arenas[ch.arena];
         const int n = ch.ntiles;
         const ChunkView cv = chunk_view<D>(ar, n);
         const unsigned char* sb = wbuf + stage * STAGE;
         float* mass_base = nullptr;
         if constexpr (MASS)
-            mass_base = p.tile_lse + (((int64_t)bh * p.nqg + qg) * p.n_chunks + (first + j * kWarps)) * 16 * kQ;
+            mass_base = p.tile_lse + (((int64_t)bh * p.nqg + qg) * p.n_chunks + (first + j * kPairs)) * 16 * kQ;
         switch (ar.tier) {
 #define ARGUS_TILE_CASE(T)                                                                                        \
     case T: {                                                                                                     \
@@ -727,13 +735,13 @@ __global__ void __launch_bounds__(kThreads, 3) decode_attn_kernel(const __grid_c
             default: break;
         }
         __syncwarp();
-        if (lane == 0 && j + kStages < n_my) issue(j + kStages);
+        if (lane == 0 && j + kStages < n_pair) issue(j + kStages);
         __syncwarp();
     }
     if (failed) {
         if (lane == 0) atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
         // let copies still in flight land before the shared memory is released (bounded again)
-        for (int s = 0; s < kStages; ++s) (void)mbar_wait(&mbar[warp][s], 0u);
+        for (int s = 0; s < kStages; ++s) (void)mbar_wait(&mbar[pair][s], 0u);
     }
 
     // ---- finish this warp: reduce l over the 8 token lanes
@@ -831,13 +839,16 @@ __global__ void combine_kernel(const __grid_constant__ Params p) {
 
 template <int D>
 int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
-    const size_t smem = (size_t)kWarps * kStages * stage_bytes(D) + stage_slack(D);
-    static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kWarps * kStages * stage_bytes(D),
+    const size_t smem = (size_t)kPairs * kStages * stage_bytes(D) + stage_slack(D);
+    static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kPairs * kStages * stage_bytes(D),
                   "merge buffer must fit in the stage memory");
     const bool mass = prm.tile_lse != nullptr;
     auto kern = precise ? (mass ? decode_attn_kernel<D, true, true> : decode_attn_kernel<D, true, false>)
                         : (mass ? decode_attn_kernel<D, false, true> : decode_attn_kernel<D, false, false>);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    // all of the unified L1/shared array as shared memory, so ctas_per_sm(D) CTAs fit
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
     dim3 grid(n_splits, prm.B * prm.Hkv, prm.nqg);
     kern<<<grid, kThreads, smem, st>>>(prm);

@@ -21,7 +21,7 @@ def test_record_sizes_and_capacity():
     D, P = 128, 16
     assert [A.record_bytes(t, P, D) for t in range(6)] == [8192, 4160, 4160, 2176, 1152, 576]
     caps = [A.chunk_capacity(arena(t, 4), D) for t in range(6)]
-    assert caps == [1, 2, 2, 4, 8, 16]
+    assert caps == [1, 2, 2, 4, 7, 15]
 
 
 def test_consecutive_slots_merge_up_to_capacity():
@@ -63,6 +63,24 @@ def test_splits_cover_chunks_in_order():
     # algorithmic bytes: per token K+V payload + scales/mins, over B*H
     per_tok = {A.TIER_1BIT: 2 * 16 + 4, A.TIER_INT2: 2 * 32 + 8, A.TIER_INT4: 2 * 64 + 8, A.TIER_FP16: 2 * 256}
     assert plan.compressed_bytes == sum(per_tok.values()) * 64 * 16 * 4
+
+
+def test_splits_take_a_share_of_every_arena_in_the_same_order():
+    arenas = [arena(t, 96) for t in (A.TIER_1BIT, A.TIER_INT2, A.TIER_INT4, A.TIER_INT8)]
+    pages = [(i, s, 16) for i in range(4) for s in range(96)]
+    plan = A.AttentionPlan(arenas, pages, batch=2, heads_kv=2, group=4, head_dim=128, n_splits=7)
+    b = plan.splits_dev.numpy()
+    costs = []
+    for s in range(7):
+        part = plan.chunks[b[s]:b[s + 1]]
+        seq = [c[2] for c in part]
+        assert seq == sorted(seq)  # arenas in the same order in every split
+        assert set(seq) == {0, 1, 2, 3}  # a share of every arena
+        costs.append(sum(A._tile_cost(arenas[c[2]].tier, 128, 16 * c[3]) for c in part))
+    assert max(costs) - min(costs) <= max(A._tile_cost(t, 128, 16 * 16) for t in range(6))
+    # every page's tiles are covered once, in page order within a chunk
+    seen = sorted(pi for src in plan.chunk_pages for pi in src)
+    assert seen == list(range(len(pages)))
 
 
 def test_record_views_share_storage():
