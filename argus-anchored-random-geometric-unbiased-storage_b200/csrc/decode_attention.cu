@@ -222,6 +222,19 @@ __device__ __forceinline__ void lds_small(const unsigned char* p, uint32_t* r) {
 constexpr uint32_t kMagic1024 = 0x64006400u;  // fp16 1024.0 in both halves: 1024 + u for u in 0..1023
 constexpr uint32_t kMagic1152 = 0x64806480u;  // 1024 + 128 (bias of sign-flipped int8 codes)
 
+// A code u masked in place at mantissa bit p of an fp16 half whose exponent field is 25 - p reads
+// as 2^(10-p) + u exactly (u < 2^(10-p)), so packed codes need no shift before the dequantization.
+__host__ __device__ constexpr uint32_t magic_at(int p) { return (uint32_t)(25 - p) << 10; }
+__host__ __device__ constexpr uint32_t magic2(int p_lo, int p_hi) { return magic_at(p_lo) | (magic_at(p_hi) << 16); }
+
+// x * y (mod 2^32) kept as an integer multiply, so left shifts by a per-thread amount run on the
+// FMA pipe instead of the busier ALU pipe.
+__device__ __forceinline__ uint32_t imul(uint32_t x, uint32_t y) {
+    uint32_t r;
+    asm("mul.lo.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
+    return r;
+}
+
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 // (~a & m) ^ c: the sign bit of c flipped where the bit of a is clear (1-bit tier: b ? s : -s)
@@ -231,10 +244,11 @@ __device__ __forceinline__ uint32_t lop_sign(uint32_t a, uint32_t m, uint32_t c)
     return r;
 }
 
-// Exact dequantization of unsigned codes held as (1024 + u) in fp16 halves: fp16(fp16(u*s) + mn).
-// r = fma(1024 + u, s*2^-k, -s*2^(10-k)) is fp16(u*s)*2^-k with a single rounding (the addend is
-// exact, and for k = 10 the scaled product stays a normal number), then fma(r, 2^k, mn) =
-// fp16(fp16(u*s) + mn).  k = 0 for s < 64, k = 10 above, so every finite scale is exact.
+// Exact dequantization of unsigned codes held as (2^(10-p) + u) in fp16 halves (magic_at(p)):
+// fp16(fp16(u*s) + mn).  r = fma(2^(10-p) + u, s*2^-k, -2^(10-p)*s*2^-k) is fp16(u*s)*2^-k with a
+// single rounding (both operands are exact: s*2^-k is s or a normal number, the addend is s scaled
+// up by 2^(10-p) >= 16 or, for k = 10, a normal number), then fma(r, 2^k, mn) = fp16(fp16(u*s) + mn).
+// k = 0 for s < 64, k = 10 above, so every finite scale, subnormal ones included, is exact.
 __device__ __forceinline__ uint32_t deq_u(uint32_t biased, __half2 b, __half2 c, __half2 f, __half2 mn) {
     return h2u(__hfma2(__hfma2(u2h(biased), b, c), f, mn));
 }
@@ -243,25 +257,28 @@ __device__ __forceinline__ uint32_t deq_u(uint32_t biased, __half2 b, __half2 c,
 struct TokScale {
     __half2 s[2];   // scale
     __half2 b[2];   // s * 2^-k
-    __half2 c[2];   // -s * 2^(10-k)
+    __half2 c[2];   // -2^(10-p) * s * 2^-k   (p: mantissa bit the token's codes sit at)
     __half2 f[2];   // 2^k
     __half2 mn[2];  // min
 };
 
-// Fills b, c, f from s: k = 10 where s >= 64 (so -1024*s would overflow fp16), else 0.
-__device__ __forceinline__ void scale_terms(TokScale& t, int i) {
+// Fills b, c, f from s and the codes' base 2^(10-p) per half: k = 10 where s >= 64 (so the addend
+// cannot overflow fp16), else 0.
+__device__ __forceinline__ void scale_terms(TokScale& t, int i, __half2 base) {
     const __half2 big = __hge2(t.s[i], __float2half2_rn(64.0f));  // 1.0 where s >= 64
     const __half2 kf = __hfma2(big, __float2half2_rn(1023.0f), __float2half2_rn(1.0f));  // 2^k: 1 or 1024
     const __half2 ik = __hfma2(big, __float2half2_rn(-0.9990234375f), __float2half2_rn(1.0f));  // 2^-k
     t.f[i] = kf;
     t.b[i] = __hmul2(t.s[i], ik);
-    t.c[i] = __hmul2(__hneg2(t.s[i]), __hmul2(__float2half2_rn(1024.0f), ik));
+    t.c[i] = __hmul2(__hneg2(t.s[i]), __hmul2(base, ik));
 }
 
 // ------------------------------------------------------------------------ K fragments (QK^T)
-// a[c][0..3] for k-chunk c: (token 2g, dims 4c..4c+1), (token 2g+1, same), (token 2g, 4c+2..3),
-// (token 2g+1, 4c+2..3), dims relative to this thread's span t*D/4.  Values are the reference's
-// fp16 dequantization, bit for bit.  ts.s[0] is token 2g broadcast, ts.s[1] token 2g+1.
+// a[c][0..3] for k-chunk c: (token 2g, dims 4c and 4c+2), (token 2g+1, same), (token 2g, dims 4c+1
+// and 4c+3), (token 2g+1, same), dims relative to this thread's span t*D/4 (the query fragments use
+// the same pairing).  Pairing dims two bytes apart lets a 32-bit word of packed codes feed two
+// fragments with a mask each.  Values are the reference's fp16 dequantization, bit for bit.
+// ts.s[0] is token 2g broadcast, ts.s[1] token 2g+1.
 template <int D, int TIER>
 __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4, const TokScale& ts,
                                         uint32_t (&a)[D / 16][4]) {
@@ -271,7 +288,12 @@ __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4,
         lds<D / 2>(kp + (2 * g4) * D * 2 + t4 * (D / 2), ra);
         lds<D / 2>(kp + (2 * g4 + 1) * D * 2 + t4 * (D / 2), rb);
 #pragma unroll
-        for (int c = 0; c < KC; ++c) { a[c][0] = ra[2 * c]; a[c][1] = rb[2 * c]; a[c][2] = ra[2 * c + 1]; a[c][3] = rb[2 * c + 1]; }
+        for (int c = 0; c < KC; ++c) {
+            a[c][0] = prmt(ra[2 * c], ra[2 * c + 1], 0x5410);
+            a[c][2] = prmt(ra[2 * c], ra[2 * c + 1], 0x7632);
+            a[c][1] = prmt(rb[2 * c], rb[2 * c + 1], 0x5410);
+            a[c][3] = prmt(rb[2 * c], rb[2 * c + 1], 0x7632);
+        }
     } else if constexpr (TIER == ARGUS_TIER_INT8 || TIER == ARGUS_TIER_FP8SIM) {
         uint32_t ra[KC], rb[KC];
         lds<D / 4>(kp + (2 * g4) * D + t4 * (D / 4), ra);
@@ -280,42 +302,44 @@ __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4,
         for (int c = 0; c < KC; ++c) {
             const uint32_t wa = ra[c] ^ 0x80808080u, wb = rb[c] ^ 0x80808080u;
             // fp16(q * s): exact code (bias removed) times the token's scale
-            a[c][0] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7170), kMagic1152)), ts.s[0]));
-            a[c][2] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7372), kMagic1152)), ts.s[0]));
-            a[c][1] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7170), kMagic1152)), ts.s[1]));
-            a[c][3] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7372), kMagic1152)), ts.s[1]));
+            a[c][0] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7270), kMagic1152)), ts.s[0]));
+            a[c][2] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7371), kMagic1152)), ts.s[0]));
+            a[c][1] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7270), kMagic1152)), ts.s[1]));
+            a[c][3] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7371), kMagic1152)), ts.s[1]));
         }
     } else if constexpr (TIER == ARGUS_TIER_INT4 || TIER == ARGUS_TIER_INT2) {
-        constexpr uint32_t M = TIER == ARGUS_TIER_INT4 ? 0x000F000Fu : 0x00030003u;
-        uint32_t r[KC];
-        int shA, shB;
+        // codes of token 2g at mantissa bit pA of each byte, of token 2g+1 at pB
+        uint32_t r[KC], mA, mB, gA, gB;
         if constexpr (TIER == ARGUS_TIER_INT4) {
             lds<D / 4>(kp + g4 * D + t4 * (D / 4), r);
-            shA = 0; shB = 4;
+            mA = 0x000F000Fu; mB = 0x00F000F0u; gA = magic2(0, 0); gB = magic2(4, 4);
         } else {
             lds<D / 4>(kp + (g4 >> 1) * D + t4 * (D / 4), r);
-            shA = 4 * (g4 & 1); shB = shA + 2;
+            const int pA = 4 * (g4 & 1);
+            mA = 0x00030003u << pA; mB = mA << 2;
+            gA = (g4 & 1) ? magic2(4, 4) : magic2(0, 0);
+            gB = (g4 & 1) ? magic2(6, 6) : magic2(2, 2);
         }
 #pragma unroll
         for (int c = 0; c < KC; ++c) {
-            const uint32_t x01 = prmt(r[c], 0u, 0x4140), x23 = prmt(r[c], 0u, 0x4342);
-            a[c][0] = deq_u(lop_and_or(x01 >> shA, M, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[c][1] = deq_u(lop_and_or(x01 >> shB, M, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
-            a[c][2] = deq_u(lop_and_or(x23 >> shA, M, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[c][3] = deq_u(lop_and_or(x23 >> shB, M, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            const uint32_t r8 = r[c] >> 8;  // bytes 1 and 3 moved to 0 and 2
+            a[c][0] = deq_u(lop_and_or(r[c], mA, gA), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[c][1] = deq_u(lop_and_or(r[c], mB, gB), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            a[c][2] = deq_u(lop_and_or(r8, mA, gA), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[c][3] = deq_u(lop_and_or(r8, mB, gB), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
         }
     } else {  // 1-bit: b ? +s : -s, the sign bit taken from the packed bit moved to bit 15 / 31
         uint32_t r[KC];
         lds<D / 4>(kp + (g4 >> 2) * D + t4 * (D / 4), r);
-        const int k = 2 * (g4 & 3);
+        const int k = 2 * (g4 & 3);  // bit of token 2g; token 2g+1 at k + 1
+        const uint32_t pA = 1u << (15 - k), pB = 1u << (14 - k), pC = 1u << (7 - k), pD = 1u << (6 - k);
         const uint32_t sA = h2u(ts.s[0]), sB = h2u(ts.s[1]);
 #pragma unroll
         for (int c = 0; c < KC; ++c) {
-            const uint32_t x01 = prmt(r[c], 0u, 0x4140), x23 = prmt(r[c], 0u, 0x4342);
-            a[c][0] = lop_sign(x01 << (15 - k), 0x80008000u, sA);
-            a[c][1] = lop_sign(x01 << (14 - k), 0x80008000u, sB);
-            a[c][2] = lop_sign(x23 << (15 - k), 0x80008000u, sA);
-            a[c][3] = lop_sign(x23 << (14 - k), 0x80008000u, sB);
+            a[c][0] = lop_sign(imul(r[c], pA), 0x80008000u, sA);  // bytes 0, 2
+            a[c][1] = lop_sign(imul(r[c], pB), 0x80008000u, sB);
+            a[c][2] = lop_sign(imul(r[c], pC), 0x80008000u, sA);  // bytes 1, 3
+            a[c][3] = lop_sign(imul(r[c], pD), 0x80008000u, sB);
         }
     }
 }
@@ -371,10 +395,11 @@ __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4,
             const int w = t >> 1, e0 = 2 * (t & 1);
             const uint32_t y0 = prmt(ra[w], rb[w], e0 | ((4 + e0) << 8));              // (A.d0, -, B.d0, -)
             const uint32_t y1 = prmt(ra[w], rb[w], (e0 + 1) | ((5 + e0) << 8));        // (A.d1, -, B.d1, -)
-            a[t][0] = deq_u(lop_and_or(y0, 0x000F000Fu, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[t][2] = deq_u(lop_and_or(y0 >> 4, 0x000F000Fu, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
-            a[t][1] = deq_u(lop_and_or(y1, 0x000F000Fu, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[t][3] = deq_u(lop_and_or(y1 >> 4, 0x000F000Fu, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            // low nibbles: tokens 4u, 4u+2; high nibbles (read in place): tokens 4u+1, 4u+3
+            a[t][0] = deq_u(lop_and_or(y0, 0x000F000Fu, magic2(0, 0)), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][2] = deq_u(lop_and_or(y0, 0x00F000F0u, magic2(4, 4)), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            a[t][1] = deq_u(lop_and_or(y1, 0x000F000Fu, magic2(0, 0)), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][3] = deq_u(lop_and_or(y1, 0x00F000F0u, magic2(4, 4)), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
         }
     } else if constexpr (TIER == ARGUS_TIER_INT2) {
         uint32_t r[W];
@@ -382,18 +407,19 @@ __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4,
 #pragma unroll
         for (int t = 0; t < KC; ++t) {
             const int w = t >> 1, e0 = 2 * (t & 1);
-            const uint32_t rs = r[w] >> 4;  // bits 4..7 of each byte moved down
-            const uint32_t y0 = prmt(r[w], rs, e0 | ((4 + e0) << 8));             // (d0 bits0-3, -, d0 bits4-7, -)
-            const uint32_t y1 = prmt(r[w], rs, (e0 + 1) | ((5 + e0) << 8));
-            a[t][0] = deq_u(lop_and_or(y0, 0x00030003u, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[t][2] = deq_u(lop_and_or(y0 >> 2, 0x00030003u, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
-            a[t][1] = deq_u(lop_and_or(y1, 0x00030003u, kMagic1024), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[t][3] = deq_u(lop_and_or(y1 >> 2, 0x00030003u, kMagic1024), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            const uint32_t y0 = prmt(r[w], 0u, e0 | (e0 << 8));              // the byte of dim d0 in both halves
+            const uint32_t y1 = prmt(r[w], 0u, (e0 + 1) | ((e0 + 1) << 8));  // dim d1
+            // codes read in place: token 4u (bits 0-1) | 4u+2 (bits 4-5); 4u+1 (2-3) | 4u+3 (6-7)
+            a[t][0] = deq_u(lop_and_or(y0, 0x00300003u, magic2(0, 4)), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][2] = deq_u(lop_and_or(y0, 0x00C0000Cu, magic2(2, 6)), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            a[t][1] = deq_u(lop_and_or(y1, 0x00300003u, magic2(0, 4)), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
+            a[t][3] = deq_u(lop_and_or(y1, 0x00C0000Cu, magic2(2, 6)), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
         }
     } else {  // 1-bit: tokens 4u+i sit in bit k0+i of row u/2, k0 = 4(u&1)
         uint32_t r[W];
         lds_small<D / 8>(vp + (t4 >> 1) * D + g4 * (D / 8), r);
         const int k0 = 4 * (t4 & 1);
+        const uint32_t pA = 1u << (15 - k0), pB = 1u << (14 - k0);
         const uint32_t s02 = h2u(ts.s[0]), s13 = h2u(ts.s[1]);
 #pragma unroll
         for (int t = 0; t < KC; ++t) {
@@ -401,10 +427,10 @@ __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4,
             const uint32_t rs = r[w] >> 2;  // bit k0+2 moved to k0
             const uint32_t y0 = prmt(r[w], rs, e0 | ((4 + e0) << 8));
             const uint32_t y1 = prmt(r[w], rs, (e0 + 1) | ((5 + e0) << 8));
-            a[t][0] = lop_sign(y0 << (15 - k0), 0x80008000u, s02);  // tokens 4u, 4u+2
-            a[t][2] = lop_sign(y0 << (14 - k0), 0x80008000u, s13);  // tokens 4u+1, 4u+3
-            a[t][1] = lop_sign(y1 << (15 - k0), 0x80008000u, s02);
-            a[t][3] = lop_sign(y1 << (14 - k0), 0x80008000u, s13);
+            a[t][0] = lop_sign(imul(y0, pA), 0x80008000u, s02);  // tokens 4u, 4u+2
+            a[t][2] = lop_sign(imul(y0, pB), 0x80008000u, s13);  // tokens 4u+1, 4u+3
+            a[t][1] = lop_sign(imul(y1, pA), 0x80008000u, s02);
+            a[t][3] = lop_sign(imul(y1, pB), 0x80008000u, s13);
         }
     }
 }
@@ -450,8 +476,18 @@ __device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t
             const uint2 w4 = *reinterpret_cast<const uint2*>(tp.vm + 4 * t4);
             tv.mn[0] = u2h(prmt(w4.x, w4.y, 0x5410));
             tv.mn[1] = u2h(prmt(w4.x, w4.y, 0x7632));
-#pragma unroll
-            for (int i = 0; i < 2; ++i) { scale_terms(tk, i); scale_terms(tv, i); }
+            // code bases 2^(10-p) of each token's in-place codes (see k_frags / v_frags)
+            const __half2 b1024 = __float2half2_rn(1024.0f), b256 = __float2half2_rn(256.0f);
+            const __half2 b64 = __float2half2_rn(64.0f), b16 = __float2half2_rn(16.0f);
+            if constexpr (TIER == ARGUS_TIER_INT4) {
+                scale_terms(tk, 0, b1024); scale_terms(tk, 1, b64);
+                scale_terms(tv, 0, b1024); scale_terms(tv, 1, b64);
+            } else {
+                const bool odd = (g4 & 1) != 0;
+                scale_terms(tk, 0, odd ? b64 : b1024); scale_terms(tk, 1, odd ? b16 : b256);
+                scale_terms(tv, 0, __halves2half2(__float2half_rn(1024.0f), __float2half_rn(64.0f)));
+                scale_terms(tv, 1, __halves2half2(__float2half_rn(256.0f), __float2half_rn(16.0f)));
+            }
         }
     }
 }
@@ -598,8 +634,10 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
             const __half* qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
 #pragma unroll
             for (int c = 0; c < KC; ++c) {
-                qf[c][0] = *reinterpret_cast<const uint32_t*>(qrow + 4 * c);
-                qf[c][1] = *reinterpret_cast<const uint32_t*>(qrow + 4 * c + 2);
+                const uint32_t q01 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c);
+                const uint32_t q23 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c + 2);
+                qf[c][0] = prmt(q01, q23, 0x5410);  // dims 4c, 4c+2
+                qf[c][1] = prmt(q01, q23, 0x7632);  // dims 4c+1, 4c+3
             }
         } else {
 #pragma unroll
@@ -726,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
         break;                                                                                                    \
     }
             ARGUS_TILE_CASE(ARGUS_TIER_FP16)
-            ARGUS_TILE_CASE(ARGUS_TIER_FP8SIM)
+            case ARGUS_TIER_FP8SIM:  // same dequantization as INT8: fp16(q * s)
             ARGUS_TILE_CASE(ARGUS_TIER_INT8)
             ARGUS_TILE_CASE(ARGUS_TIER_INT4)
             ARGUS_TILE_CASE(ARGUS_TIER_INT2)
