@@ -439,6 +439,9 @@ struct SoftmaxState {
     float m[2];  // reference max (log2 domain) for queries 2t, 2t+1; weights are 2^(x - m)
     float l[2];  // this thread's partial sum of weights
 };
+// Reference max before any score: finite, so that 2^(x - m) of masked (-inf) scores is 0, far below
+// any score fp16 inputs can produce, and 2^(kNoMax - score) underflows to 0 at the first rescale.
+constexpr float kNoMax = -1.0e30f;
 
 // Lazy rescaling: the reference max only moves when a score exceeds it by more than this (log2
 // units), so weights stay <= 2^8 (exact range for fp16 P) and rescales of O are rare.
@@ -492,14 +495,38 @@ __device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t
     }
 }
 
+// Query fragments live in shared memory (read again for every tile, which keeps 2*D/16 registers
+// free): lane l's words j are at word ((j / V) * 32 + l) * V + j % V with V = 4 (2 for D = 16), so
+// each vector load of a warp is conflict-free.
+template <int D>
+__device__ __forceinline__ void load_qfrags(uint32_t qs, int lane, uint32_t (&qf)[D / 16][2]) {
+    constexpr int W = 2 * (D / 16);
+    if constexpr (W % 4 == 0) {
+#pragma unroll
+        for (int v = 0; v < W / 4; ++v) {
+            uint32_t r0, r1, r2, r3;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                         : "r"(qs + (uint32_t)((v * 32 + lane) * 16)));
+            qf[2 * v][0] = r0; qf[2 * v][1] = r1; qf[2 * v + 1][0] = r2; qf[2 * v + 1][1] = r3;
+        }
+    } else {
+        uint32_t r0, r1;
+        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(qs + (uint32_t)(lane * 8)));
+        qf[0][0] = r0; qf[0][1] = r1;
+    }
+}
+
 // Scores of one tile in the log2 domain: x[0..3] = (token 2g, query 2t), (2g, 2t+1), (2g+1, 2t),
 // (2g+1, 2t+1); tokens past the tile's end are -inf.
 template <int D, int TIER>
 __device__ __forceinline__ void tile_scores(const TilePtr& tp, int g4, int t4, const TokScale& tk,
-                                            const uint32_t (&qf)[D / 16][2], float scale_log2, float (&x)[4]) {
+                                            uint32_t qs, float scale_log2, float (&x)[4]) {
     constexpr int KC = D / 16;
     uint32_t a[KC][4];
     k_frags<D, TIER>(tp.k, g4, t4, tk, a);
+    uint32_t qf[KC][2];
+    load_qfrags<D>(qs, threadIdx.x & 31, qf);
     float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < KC; c += 2) {
@@ -542,24 +569,29 @@ template <int KC, int NT, bool PRECISE, bool MASS>
 __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxState& st, float (&o)[KC][4],
                                                uint32_t (&b01)[NT], uint32_t (&b23)[NT], uint32_t (&c01)[NT],
                                                uint32_t (&c23)[NT], float* mass_out) {
-    float mx0 = -INFINITY, mx1 = -INFINITY;
+    // The tile's maxima are reduced across the 8 token lanes only when some lane holds a score above
+    // the reference max plus the slack; otherwise the reference max stands and no O rescale is due.
+    const float t0 = st.m[0] + kRescaleSlack, t1 = st.m[1] + kRescaleSlack;
+    bool over = false;
 #pragma unroll
-    for (int i = 0; i < NT; ++i) { mx0 = fmaxf(mx0, fmaxf(x[i][0], x[i][2])); mx1 = fmaxf(mx1, fmaxf(x[i][1], x[i][3])); }
+    for (int i = 0; i < NT; ++i) over |= (fmaxf(x[i][0], x[i][2]) > t0) | (fmaxf(x[i][1], x[i][3]) > t1);
+    if (__any_sync(0xffffffffu, over)) {
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-    }
-    if (mx0 > st.m[0] + kRescaleSlack || mx1 > st.m[1] + kRescaleSlack) {
+        for (int i = 0; i < NT; ++i) { mx0 = fmaxf(mx0, fmaxf(x[i][0], x[i][2])); mx1 = fmaxf(mx1, fmaxf(x[i][1], x[i][3])); }
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
         const float n0 = fmaxf(st.m[0], mx0), n1 = fmaxf(st.m[1], mx1);
-        const float f0 = exp2f(st.m[0] - n0), f1 = exp2f(st.m[1] - n1);  // -inf - finite -> 0
+        const float f0 = exp2f(st.m[0] - n0), f1 = exp2f(st.m[1] - n1);  // kNoMax - finite -> 0
 #pragma unroll
         for (int t = 0; t < KC; ++t) { o[t][0] *= f0; o[t][2] *= f0; o[t][1] *= f1; o[t][3] *= f1; }
         st.l[0] *= f0; st.l[1] *= f1;
         st.m[0] = n0; st.m[1] = n1;
     }
-    const float m0 = (st.m[0] == -INFINITY) ? 0.f : st.m[0];
-    const float m1 = (st.m[1] == -INFINITY) ? 0.f : st.m[1];
+    const float m0 = st.m[0], m1 = st.m[1];
 #pragma unroll
     for (int i = 0; i < NT; ++i) {
         const float p0 = exp2f(x[i][0] - m0), p1 = exp2f(x[i][1] - m1);
@@ -594,15 +626,15 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
 // Processes tiles i0 and (if pair) i0+1 of a staged chunk with interleaved independent work.
 template <int D, int TIER, bool PAIR, bool PRECISE, bool MASS>
 __device__ __forceinline__ void process_tiles(const TilePtr& ta, const TilePtr& tb, int g4, int t4,
-                                              const uint32_t (&qf)[D / 16][2], float scale_log2, SoftmaxState& st,
+                                              uint32_t qs, float scale_log2, SoftmaxState& st,
                                               float (&o)[D / 16][4], float* mass_out) {
     constexpr int NT = PAIR ? 2 : 1;
     TokScale tk[NT], tv[NT];
     float x[NT][4];
     load_tok_scales<TIER>(ta, g4, t4, tk[0], tv[0]);
     if constexpr (PAIR) load_tok_scales<TIER>(tb, g4, t4, tk[NT - 1], tv[NT - 1]);
-    tile_scores<D, TIER>(ta, g4, t4, tk[0], qf, scale_log2, x[0]);
-    if constexpr (PAIR) tile_scores<D, TIER>(tb, g4, t4, tk[NT - 1], qf, scale_log2, x[NT - 1]);
+    tile_scores<D, TIER>(ta, g4, t4, tk[0], qs, scale_log2, x[0]);
+    if constexpr (PAIR) tile_scores<D, TIER>(tb, g4, t4, tk[NT - 1], qs, scale_log2, x[NT - 1]);
     uint32_t b01[NT], b23[NT], c01[NT], c23[NT];
     softmax_update<D / 16, NT, PRECISE, MASS>(x, st, o, b01, b23, c01, c23, mass_out);
     tile_pv<D, TIER, PRECISE>(ta, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
@@ -625,28 +657,36 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
     const int pair = warp / kPairWarps, wip = warp - pair * kPairWarps;
     unsigned char* wbuf = smem + (size_t)pair * kStages * STAGE;
 
-    // ---- Q^T fragments (query qg*8 + g4, dims t4*D/4 ..) and per-query sums
-    uint32_t qf[KC][2];
-    {
+    // ---- Q^T fragments (query qg*8 + g4, dims t4*D/4 ..), written once by warp 0 into the shared
+    // memory past the last ring slot (load_qfrags layout), read back for every tile
+    uint32_t* qsw = reinterpret_cast<uint32_t*>(smem + (size_t)kPairs * kStages * STAGE);
+    const uint32_t qs = smem_u32(qsw);
+    if (warp == 0) {
+        constexpr int V = (2 * KC) % 4 == 0 ? 4 : 2;
         const int n = qg * kQ + g4;
-        if (n < NQ) {
+        const bool live = n < NQ;
+        const __half* qrow = p.q;
+        if (live) {
             const int gi = n / p.qlen, qi = n - gi * p.qlen;
-            const __half* qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
+            qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
+        }
 #pragma unroll
-            for (int c = 0; c < KC; ++c) {
+        for (int c = 0; c < KC; ++c) {
+            uint32_t f0 = 0u, f1 = 0u;
+            if (live) {
                 const uint32_t q01 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c);
                 const uint32_t q23 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c + 2);
-                qf[c][0] = prmt(q01, q23, 0x5410);  // dims 4c, 4c+2
-                qf[c][1] = prmt(q01, q23, 0x7632);  // dims 4c+1, 4c+3
+                f0 = prmt(q01, q23, 0x5410);  // dims 4c, 4c+2
+                f1 = prmt(q01, q23, 0x7632);  // dims 4c+1, 4c+3
             }
-        } else {
-#pragma unroll
-            for (int c = 0; c < KC; ++c) { qf[c][0] = 0u; qf[c][1] = 0u; }
+            const int j0 = 2 * c, j1 = 2 * c + 1;
+            qsw[((j0 / V) * 32 + lane) * V + j0 % V] = f0;
+            qsw[((j1 / V) * 32 + lane) * V + j1 % V] = f1;
         }
     }
 
     SoftmaxState st;
-    st.m[0] = st.m[1] = -INFINITY;
+    st.m[0] = st.m[1] = kNoMax;
     st.l[0] = st.l[1] = 0.f;
     float o[KC][4];
 #pragma unroll
@@ -720,13 +760,16 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
     __syncwarp();
 
     bool failed = false;
+    argus_kv_chunk nch;  // descriptor of this warp's next chunk, loaded one chunk ahead
+    if (wip < n_pair) nch = p.chunks[first + wip * kPairs];
     for (int j = wip; j < n_pair; j += kPairWarps) {
+        const argus_kv_chunk ch = nch;
+        if (j + kPairWarps < n_pair) nch = p.chunks[first + (j + kPairWarps) * kPairs];
         const int stage = j % kStages;
         if (!mbar_wait(&mbar[pair][stage], (uint32_t)((j / kStages) & 1))) {
             failed = true;
             break;
         }
-        const argus_kv_chunk ch = p.chunks[first + j * kPairs];
         const argus_kv_arena& ar = p.arenas[ch.arena];
         const int n = ch.ntiles;
         const ChunkView cv = chunk_view<D>(ar, n);
@@ -753,12 +796,12 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
         /* tile pairs (ARGUS_DA_PAIR=1) measured slower on B200: register pressure; D = 256 never pairs */      \
         for (; ARGUS_DA_PAIR && D <= 128 && i + 1 < n; i += 2) {                                                                   \
             const TilePtr ta = tile(i), tb = tile(i + 1);                                                         \
-            process_tiles<D, T, true, PRECISE, MASS>(ta, tb, g4, t4, qf, p.scale_log2, st, o,                     \
+            process_tiles<D, T, true, PRECISE, MASS>(ta, tb, g4, t4, qs, p.scale_log2, st, o,                     \
                                                      mass_base ? mass_base + i * kQ : nullptr);                   \
         }                                                                                                         \
         for (; i < n; ++i) {                                                                                      \
             const TilePtr ta = tile(i);                                                                           \
-            process_tiles<D, T, false, PRECISE, MASS>(ta, ta, g4, t4, qf, p.scale_log2, st, o,                    \
+            process_tiles<D, T, false, PRECISE, MASS>(ta, ta, g4, t4, qs, p.scale_log2, st, o,                    \
                                                       mass_base ? mass_base + i * kQ : nullptr);                  \
         }                                                                                                         \
         break;                                                                                                    \
