@@ -449,9 +449,6 @@ constexpr float kNoMax = -1.0e30f;
 #define ARGUS_DA_RESCALE_SLACK 8.0f
 #endif
 constexpr float kRescaleSlack = ARGUS_DA_RESCALE_SLACK;
-#ifndef ARGUS_DA_PAIR
-#define ARGUS_DA_PAIR 0
-#endif
 
 __device__ __forceinline__ __half2 load_h2(const __half* p) { return *reinterpret_cast<const __half2*>(p); }
 
@@ -482,14 +479,26 @@ __device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t
             // code bases 2^(10-p) of each token's in-place codes (see k_frags / v_frags)
             const __half2 b1024 = __float2half2_rn(1024.0f), b256 = __float2half2_rn(256.0f);
             const __half2 b64 = __float2half2_rn(64.0f), b16 = __float2half2_rn(16.0f);
+            __half2 bk0, bk1, bv0, bv1;
             if constexpr (TIER == ARGUS_TIER_INT4) {
-                scale_terms(tk, 0, b1024); scale_terms(tk, 1, b64);
-                scale_terms(tv, 0, b1024); scale_terms(tv, 1, b64);
+                bk0 = b1024; bk1 = b64; bv0 = b1024; bv1 = b64;
             } else {
                 const bool odd = (g4 & 1) != 0;
-                scale_terms(tk, 0, odd ? b64 : b1024); scale_terms(tk, 1, odd ? b16 : b256);
-                scale_terms(tv, 0, __halves2half2(__float2half_rn(1024.0f), __float2half_rn(64.0f)));
-                scale_terms(tv, 1, __halves2half2(__float2half_rn(256.0f), __float2half_rn(16.0f)));
+                bk0 = odd ? b64 : b1024; bk1 = odd ? b16 : b256;
+                bv0 = __halves2half2(__float2half_rn(1024.0f), __float2half_rn(64.0f));
+                bv1 = __halves2half2(__float2half_rn(256.0f), __float2half_rn(16.0f));
+            }
+            const __half2 smax = __hmax2(__hmax2(tk.s[0], tk.s[1]), __hmax2(tv.s[0], tv.s[1]));
+            if (__all_sync(0xffffffffu, __hblt2(smax, __float2half2_rn(64.0f)))) {
+                // every scale of the tile is below 64: k = 0 (b = s, f = 1)
+                const __half2 one = __float2half2_rn(1.0f);
+                tk.b[0] = tk.s[0]; tk.c[0] = __hmul2(tk.s[0], __hneg2(bk0)); tk.f[0] = one;
+                tk.b[1] = tk.s[1]; tk.c[1] = __hmul2(tk.s[1], __hneg2(bk1)); tk.f[1] = one;
+                tv.b[0] = tv.s[0]; tv.c[0] = __hmul2(tv.s[0], __hneg2(bv0)); tv.f[0] = one;
+                tv.b[1] = tv.s[1]; tv.c[1] = __hmul2(tv.s[1], __hneg2(bv1)); tv.f[1] = one;
+            } else {
+                scale_terms(tk, 0, bk0); scale_terms(tk, 1, bk1);
+                scale_terms(tv, 0, bv0); scale_terms(tv, 1, bv1);
             }
         }
     }
@@ -623,23 +632,17 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
     }
 }
 
-// Processes tiles i0 and (if pair) i0+1 of a staged chunk with interleaved independent work.
-template <int D, int TIER, bool PAIR, bool PRECISE, bool MASS>
-__device__ __forceinline__ void process_tiles(const TilePtr& ta, const TilePtr& tb, int g4, int t4,
-                                              uint32_t qs, float scale_log2, SoftmaxState& st,
-                                              float (&o)[D / 16][4], float* mass_out) {
-    constexpr int NT = PAIR ? 2 : 1;
-    TokScale tk[NT], tv[NT];
-    float x[NT][4];
-    load_tok_scales<TIER>(ta, g4, t4, tk[0], tv[0]);
-    if constexpr (PAIR) load_tok_scales<TIER>(tb, g4, t4, tk[NT - 1], tv[NT - 1]);
-    tile_scores<D, TIER>(ta, g4, t4, tk[0], qs, scale_log2, x[0]);
-    if constexpr (PAIR) tile_scores<D, TIER>(tb, g4, t4, tk[NT - 1], qs, scale_log2, x[NT - 1]);
-    uint32_t b01[NT], b23[NT], c01[NT], c23[NT];
-    softmax_update<D / 16, NT, PRECISE, MASS>(x, st, o, b01, b23, c01, c23, mass_out);
-    tile_pv<D, TIER, PRECISE>(ta, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
-    if constexpr (PAIR)
-        tile_pv<D, TIER, PRECISE>(tb, g4, t4, tv[NT - 1], b01[NT - 1], b23[NT - 1], c01[NT - 1], c23[NT - 1], o);
+// Processes one staged tile: scores, online softmax, PV.
+template <int D, int TIER, bool PRECISE, bool MASS>
+__device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, uint32_t qs, float scale_log2,
+                                             SoftmaxState& st, float (&o)[D / 16][4], float* mass_out) {
+    TokScale tk[1], tv[1];
+    float x[1][4];
+    load_tok_scales<TIER>(tp, g4, t4, tk[0], tv[0]);
+    tile_scores<D, TIER>(tp, g4, t4, tk[0], qs, scale_log2, x[0]);
+    uint32_t b01[1], b23[1], c01[1], c23[1];
+    softmax_update<D / 16, 1, PRECISE, MASS>(x, st, o, b01, b23, c01, c23, mass_out);
+    tile_pv<D, TIER, PRECISE>(tp, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
 }
 
 template <int D, bool PRECISE, bool MASS>
@@ -648,6 +651,11 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
     constexpr int STAGE = stage_bytes(D);
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t mbar[kPairs][kStages];
+    // pair chunk most recently issued into each slot.  A slot's consumers alternate between the
+    // two warps, so a warp may reach chunk j + kStages before its partner's chunk j (same slot) has
+    // even landed; an mbarrier parity test would then match the previous, completed phase.  Waiters
+    // first see their chunk issued here, then test the parity.
+    __shared__ int issued[kPairs][kStages];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g4 = lane >> 2, t4 = lane & 3;
@@ -701,7 +709,10 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
 
     if (wip == 0 && lane == 0) {
 #pragma unroll
-        for (int s = 0; s < kStages; ++s) mbar_init(&mbar[pair][s], 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&mbar[pair][s], 1);
+            issued[pair][s] = -1;
+        }
         fence_mbar_init();
     }
     __syncthreads();
@@ -752,6 +763,8 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
                 }
             }
         }
+        __threadfence_block();  // the arrive above is visible before the slot's issued mark
+        *reinterpret_cast<volatile int*>(&issued[pair][j % kStages]) = j;
     };
 
     if (wip == 0 && lane == 0) {
@@ -766,43 +779,61 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
         const argus_kv_chunk ch = nch;
         if (j + kPairWarps < n_pair) nch = p.chunks[first + (j + kPairWarps) * kPairs];
         const int stage = j % kStages;
+        {
+            // bounded: chunk j is issued by whichever warp finishes chunk j - kStages
+            long long spin = 0;
+            while (*reinterpret_cast<volatile int*>(&issued[pair][stage]) != j && spin < kSpinLimit) ++spin;
+            if (spin >= kSpinLimit) {
+                failed = true;
+                break;
+            }
+            __threadfence_block();
+        }
         if (!mbar_wait(&mbar[pair][stage], (uint32_t)((j / kStages) & 1))) {
             failed = true;
             break;
         }
         const argus_kv_arena& ar = p.arenas[ch.arena];
         const int n = ch.ntiles;
-        const ChunkView cv = chunk_view<D>(ar, n);
         const unsigned char* sb = wbuf + stage * STAGE;
         float* mass_base = nullptr;
         if constexpr (MASS)
             mass_base = p.tile_lse + (((int64_t)bh * p.nqg + qg) * p.n_chunks + (first + j * kPairs)) * 16 * kQ;
+        const bool rec16 = ar.layout == ARGUS_LAYOUT_RECORD && ar.page_tokens == 16;
         switch (ar.tier) {
 #define ARGUS_TILE_CASE(T)                                                                                        \
     case T: {                                                                                                     \
-        auto tile = [&](int i) {                                                                                  \
-            TilePtr tp;                                                                                           \
-            const int po = i * cv.pstride, so = i * cv.sstride;                                                   \
-            tp.k = sb + cv.k_off + po;                                                                            \
-            tp.v = sb + cv.v_off + po;                                                                            \
-            tp.ks = reinterpret_cast<const __half*>(sb + cv.ks_off + so);                                         \
-            tp.vs = reinterpret_cast<const __half*>(sb + cv.vs_off + so);                                         \
-            tp.km = reinterpret_cast<const __half*>(sb + cv.km_off + so);                                         \
-            tp.vm = reinterpret_cast<const __half*>(sb + cv.vm_off + so);                                         \
-            tp.ntok = (i == n - 1) ? ch.ntok_last : cv.ntok_full;                                                 \
-            return tp;                                                                                            \
-        };                                                                                                        \
-        int i = 0;                                                                                                \
-        /* tile pairs (ARGUS_DA_PAIR=1) measured slower on B200: register pressure; D = 256 never pairs */      \
-        for (; ARGUS_DA_PAIR && D <= 128 && i + 1 < n; i += 2) {                                                                   \
-            const TilePtr ta = tile(i), tb = tile(i + 1);                                                         \
-            process_tiles<D, T, true, PRECISE, MASS>(ta, tb, g4, t4, qs, p.scale_log2, st, o,                     \
-                                                     mass_base ? mass_base + i * kQ : nullptr);                   \
-        }                                                                                                         \
-        for (; i < n; ++i) {                                                                                      \
-            const TilePtr ta = tile(i);                                                                           \
-            process_tiles<D, T, false, PRECISE, MASS>(ta, ta, g4, t4, qs, p.scale_log2, st, o,                    \
-                                                      mass_base ? mass_base + i * kQ : nullptr);                  \
+        if (rec16) {                                                                                              \
+            /* one full 16-token page per record: compile-time offsets */                                        \
+            constexpr int RB = record_bytes(T, 16, D), PB = payload_bytes(T, 16, D);                              \
+            for (int i = 0; i < n; ++i) {                                                                         \
+                const unsigned char* r = sb + i * RB;                                                             \
+                TilePtr tp;                                                                                       \
+                tp.k = r;                                                                                         \
+                tp.v = r + PB;                                                                                    \
+                tp.ks = reinterpret_cast<const __half*>(r + 2 * PB);                                              \
+                tp.vs = reinterpret_cast<const __half*>(r + 2 * PB + 32);                                         \
+                tp.km = reinterpret_cast<const __half*>(r + 2 * PB + 64);                                         \
+                tp.vm = reinterpret_cast<const __half*>(r + 2 * PB + 96);                                         \
+                tp.ntok = 16;                                                                                     \
+                process_tile<D, T, PRECISE, MASS>(tp, g4, t4, qs, p.scale_log2, st, o,                            \
+                                                  mass_base ? mass_base + i * kQ : nullptr);                      \
+            }                                                                                                     \
+        } else {                                                                                                  \
+            const ChunkView cv = chunk_view<D>(ar, n);                                                            \
+            for (int i = 0; i < n; ++i) {                                                                         \
+                TilePtr tp;                                                                                       \
+                const int po = i * cv.pstride, so = i * cv.sstride;                                               \
+                tp.k = sb + cv.k_off + po;                                                                        \
+                tp.v = sb + cv.v_off + po;                                                                        \
+                tp.ks = reinterpret_cast<const __half*>(sb + cv.ks_off + so);                                     \
+                tp.vs = reinterpret_cast<const __half*>(sb + cv.vs_off + so);                                     \
+                tp.km = reinterpret_cast<const __half*>(sb + cv.km_off + so);                                     \
+                tp.vm = reinterpret_cast<const __half*>(sb + cv.vm_off + so);                                     \
+                tp.ntok = (i == n - 1) ? ch.ntok_last : cv.ntok_full;                                             \
+                process_tile<D, T, PRECISE, MASS>(tp, g4, t4, qs, p.scale_log2, st, o,                            \
+                                                  mass_base ? mass_base + i * kQ : nullptr);                      \
+            }                                                                                                     \
         }                                                                                                         \
         break;                                                                                                    \
     }
