@@ -313,7 +313,8 @@ class AttentionPlan:
         self._shape = ShapeC(self.B, self.Hkv, self.G, self.qlen, self.D, n_splits, len(self.arenas), self.n_chunks,
                              1.0 / math.sqrt(self.D), ATTN_PRECISE_PV if precise_pv else 0)
         ws = _bind().argus_decode_attention_workspace_size(ctypes.byref(self._shape))
-        self.workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=self.device) if ws > 0 else None
+        # zero-filled: the split-arrival counters at its front start at zero (launches leave them so)
+        self.workspace = torch.zeros(max(ws, 16), dtype=torch.uint8, device=self.device) if ws > 0 else None
         self.chunks = chunks
         self.chunk_pages = srcs  # per chunk (in launch order), the index in `pages` of each of its tiles
         self.compressed_bytes = self._algorithmic_bytes(pages)

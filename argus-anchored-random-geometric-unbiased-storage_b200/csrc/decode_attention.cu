@@ -79,6 +79,7 @@ struct Params {
     float* lse;
     float* part_o;    // [B*Hkv*NQG][S][8][D]
     float* part_lse;  // [B*Hkv*NQG][S][8]
+    int* counters;    // [B*Hkv*NQG] split arrivals; zero between launches
     float* tile_lse;  // optional [B*Hkv*NQG][n_chunks][16][8]: log2-sum-exp of each tile's scores
     int B, Hkv, G, qlen, S, nqg, n_chunks;
     float scale_log2;
@@ -645,6 +646,34 @@ __device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, 
     tile_pv<D, TIER, PRECISE>(tp, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
 }
 
+// Merges the split partials of one (batch, kv_head, query group): out = sum_s 2^(lse_s - LSE) O_s,
+// LSE = log2 sum_s 2^lse_s.  Run by the group's last CTA to finish; the other CTAs' partials are
+// read through L2.
+template <int D>
+__device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int b, int h, int qg) {
+    const int NQ = p.G * p.qlen;
+    for (int e = threadIdx.x; e < kQ * D; e += kThreads) {
+        const int n = e / D, d = e - n * D;
+        const int ng = qg * kQ + n;
+        if (ng >= NQ) continue;
+        const float* pl = p.part_lse + grp * p.S * kQ + n;
+        float M = -INFINITY;
+        for (int s = 0; s < p.S; ++s) M = fmaxf(M, __ldcg(pl + s * kQ));
+        float W = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+            for (int s = 0; s < p.S; ++s) {
+                const float w = exp2f(__ldcg(pl + s * kQ) - M);
+                W += w;
+                acc += w * __ldcg(p.part_o + ((grp * p.S + s) * kQ + n) * D + d);
+            }
+        }
+        const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
+        const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
+        p.out[row * D + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
+        if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
+    }
+}
+
 template <int D, bool PRECISE, bool MASS>
 __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(const __grid_constant__ Params p) {
     constexpr int KC = D / 16;
@@ -917,35 +946,21 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
             if (d == 0) p.part_lse[(grp * p.S + split) * kQ + n] = (L > 0.f) ? M + log2f(L) : -INFINITY;
         }
     }
-}
-
-// Merges the split partials: out = sum_s 2^(lse_s - LSE) O_s, LSE = log2 sum_s 2^lse_s.
-template <int D>
-__global__ void combine_kernel(const __grid_constant__ Params p) {
-    const int64_t grp = blockIdx.x;  // (b*Hkv + h) * nqg + qg
-    const int qg = (int)(grp % p.nqg);
-    const int64_t bh = grp / p.nqg;
-    const int b = (int)(bh / p.Hkv), h = (int)(bh - (int64_t)b * p.Hkv);
-    const int NQ = p.G * p.qlen;
-    for (int e = threadIdx.x; e < kQ * D; e += blockDim.x) {
-        const int n = e / D, d = e - n * D;
-        const int ng = qg * kQ + n;
-        if (ng >= NQ) continue;
-        const float* pl = p.part_lse + grp * p.S * kQ + n;
-        float M = -INFINITY;
-        for (int s = 0; s < p.S; ++s) M = fmaxf(M, pl[s * kQ]);
-        float W = 0.f, acc = 0.f;
-        if (M != -INFINITY) {
-            for (int s = 0; s < p.S; ++s) {
-                const float w = exp2f(pl[s * kQ] - M);
-                W += w;
-                acc += w * p.part_o[((grp * p.S + s) * kQ + n) * D + d];
-            }
+    if (p.S > 1) {
+        // the group's last CTA to arrive merges the splits (and resets the counter for the next launch)
+        __shared__ int last;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int prev = atomicAdd(&p.counters[grp], 1);
+            last = (prev == p.S - 1);
+            if (last) p.counters[grp] = 0;
         }
-        const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
-        const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
-        p.out[row * D + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
-        if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            combine_group<D>(p, grp, b, h, qg);
+        }
     }
 }
 
@@ -965,10 +980,6 @@ int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
     dim3 grid(n_splits, prm.B * prm.Hkv, prm.nqg);
     kern<<<grid, kThreads, smem, st>>>(prm);
     ARGUS_CHECK_LAUNCH();
-    if (n_splits > 1) {
-        combine_kernel<D><<<(unsigned)((int64_t)prm.B * prm.Hkv * prm.nqg), 256, 0, st>>>(prm);
-        ARGUS_CHECK_LAUNCH();
-    }
     return ARGUS_OK;
 }
 
@@ -998,7 +1009,8 @@ int64_t argus_decode_attention_workspace_size(const argus_attn_shape* s) {
     if (!s || s->n_splits <= 1) return 0;
     const int64_t nqg = (s->group * (int64_t)s->q_len + da::kQ - 1) / da::kQ;
     const int64_t groups = (int64_t)s->batch * s->heads_kv * nqg;
-    return groups * s->n_splits * da::kQ * ((int64_t)s->head_dim + 1) * (int64_t)sizeof(float) + 256;
+    // [counters: groups ints, padded to 256 B][part_lse][part_o], plus alignment slack
+    return ((groups * 4 + 255) & ~255LL) + groups * s->n_splits * da::kQ * ((int64_t)s->head_dim + 1) * (int64_t)sizeof(float) + 256;
 }
 
 int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
@@ -1058,8 +1070,9 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
         if (!workspace || !argus_aligned(workspace, 16))
             return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "split-K needs a 16-byte aligned workspace");
         const int64_t groups = (int64_t)prm.B * prm.Hkv * prm.nqg;
-        prm.part_o = reinterpret_cast<float*>(workspace);
-        prm.part_lse = prm.part_o + groups * s->n_splits * da::kQ * D;
+        prm.counters = reinterpret_cast<int*>(workspace);
+        prm.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + ((groups * 4 + 255) & ~255LL));
+        prm.part_o = prm.part_lse + groups * s->n_splits * da::kQ;
     }
     cudaStream_t st = (cudaStream_t)stream;
     const bool precise = (s->flags & ARGUS_ATTN_PRECISE_PV) != 0;
@@ -1137,6 +1150,11 @@ extern "C" int argus_decode_attention_noalloc(const argus_attn_shape* s, const a
     if (need > 0) {
         const int rc = noalloc_scratch(&scratch);
         if (rc) return rc;
+        // the split-arrival counters at the front of the scratch start at zero (a previous call may
+        // have used the array with another layout)
+        const int64_t groups = (int64_t)s->batch * s->heads_kv * ((s->group * (int64_t)s->q_len + da::kQ - 1) / da::kQ);
+        const cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)((groups * 4 + 255) & ~255LL), (cudaStream_t)stream);
+        if (e != cudaSuccess) return argus_set_cuda_error(e);
     }
     return argus_decode_attention(s, arenas, chunks, split_chunk0, q, out, lse, tile_lse, scratch, stream);
 }

@@ -216,7 +216,10 @@ typedef struct argus_attn_shape {
  * (two MMAs), keeping ~22 bits of each weight instead of fp16's 11; costs ~12% at head_dim 128. */
 #define ARGUS_ATTN_PRECISE_PV 1
 
-/* Bytes of scratch argus_decode_attention needs for split-K partials (0 when n_splits == 1). */
+/* Bytes of scratch argus_decode_attention needs for split-K partials (0 when n_splits == 1).  The
+ * workspace begins with one arrival counter per (batch, kv_head, query group): it must be
+ * zero-filled before its first use with a given shape (or after a call that reported an error);
+ * every completed launch leaves the counters at zero again. */
 int64_t argus_decode_attention_workspace_size(const argus_attn_shape* shape);
 
 /* Chunk capacity: the largest number of tiles of an arena that one staged chunk may hold for
@@ -255,9 +258,10 @@ int argus_decode_attention(const argus_attn_shape* shape, const argus_kv_arena* 
  * process exits), so nothing is allocated.  Arguments as argus_decode_attention without workspace;
  * shapes whose partials need more than the capacity fail with ARGUS_ERR_CAPACITY.  The first call on
  * a device looks up the array's device address (cudaGetSymbolAddress) once, with that device current,
- * so make that first call before any stream capture.  All calls on a device share the one array and
- * each launch writes every partial it reads, so nothing has to start at zero; calls that overlap on
- * the GPU (concurrent streams) race on it and must be serialised by the caller.
+ * so make that first call before any stream capture.  All calls on a device share the one array; each
+ * call clears its split-arrival counters (an asynchronous memset on `stream`) and writes every
+ * partial it reads, so nothing else has to start at zero.  Calls that overlap on the GPU (concurrent
+ * streams) race on the array and must be serialised by the caller.
  * This entry point has no counterpart in the reference. */
 int argus_decode_attention_noalloc(const argus_attn_shape* shape, const argus_kv_arena* arenas,
                                    const argus_kv_chunk* chunks, const int32_t* split_chunk0, const uint16_t* q,
