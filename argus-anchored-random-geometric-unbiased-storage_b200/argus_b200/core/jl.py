@@ -4,6 +4,9 @@ batched contraction C[b] = A @ X[b] on the GPU (libargus_b200 argus_jl_apply).
 Reference lines: core/memory_manager.py:227-282 (W and R of the manager, ratio 4, seed 42),
 core/quantization.py:224-290 (per-call W and the solve-form R).
 """
+import ctypes
+import math
+
 import torch
 
 from .. import _lib
@@ -66,4 +69,114 @@ def apply_left(A, X):
     out = torch.empty(X.shape[:-2] + (M, N), dtype=torch.float16, device=X.device)
     _lib.call("argus_jl_apply", _lib.ptr(Ac), _lib.ptr(Xc), batch, M, K, N, _lib.ptr(out),
               _lib.stream_handle(X.device))
+    return out
+
+
+# ------------------------------------------------------------------ attention over archived blocks
+BOUND_SYMBOLS = ("argus_jl_operator_fragments", "argus_jl_attention_workspace_size", "argus_jl_attention",
+                 "argus_attention_merge")
+
+
+class JLShapeC(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("heads_kv", ctypes.c_int32), ("group", ctypes.c_int32),
+                ("q_len", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("block_rows", ctypes.c_int32),
+                ("block_tokens", ctypes.c_int32), ("n_blocks", ctypes.c_int32), ("n_splits", ctypes.c_int32),
+                ("scale", ctypes.c_float), ("bh_stride", ctypes.c_int64), ("block_stride", ctypes.c_int64)]
+
+
+_jl_bound = None
+
+
+def _jl_bind():
+    global _jl_bound
+    if _jl_bound is None:
+        L = _lib.lib()
+        p = ctypes.c_void_p
+        L.argus_jl_operator_fragments.argtypes = [p, ctypes.c_int, ctypes.c_int, p, p, p]
+        L.argus_jl_operator_fragments.restype = ctypes.c_int
+        L.argus_jl_attention_workspace_size.argtypes = [ctypes.POINTER(JLShapeC)]
+        L.argus_jl_attention_workspace_size.restype = ctypes.c_int64
+        L.argus_jl_attention.argtypes = [ctypes.POINTER(JLShapeC), p, p, p, p, p, p, p, p, p]
+        L.argus_jl_attention.restype = ctypes.c_int
+        L.argus_attention_merge.argtypes = [p, p, p, p, ctypes.c_int64, ctypes.c_int, p, p, p]
+        L.argus_attention_merge.restype = ctypes.c_int
+        _jl_bound = L
+    return _jl_bound
+
+
+def _check(name, rc):
+    if rc != 0:
+        raise _lib.ArgusError(name, rc, _lib.lib().argus_last_error().decode())
+
+
+class JLAttention:
+    """Decode attention over JL-archived blocks for one reconstruction operator R [N, MJ] (fp16):
+    the same result as softmax attention over K = R @ Yk, V = R @ Yv of every block, computed
+    without rebuilding them (libargus_b200 argus_jl_attention).  Blocks are
+    yk, yv [B, H_kv, n_blocks, MJ, D] fp16."""
+
+    def __init__(self, recon_operator):
+        _lib.require_cuda(recon_operator, "reconstruction operator")
+        R = recon_operator.to(torch.float16).contiguous()
+        self.N, self.MJ = R.shape
+        n = self.N * self.MJ * 2
+        self.r_frag = torch.empty(n, dtype=torch.uint8, device=R.device)
+        self.rt_frag = torch.empty(n, dtype=torch.uint8, device=R.device)
+        _check("argus_jl_operator_fragments", _jl_bind().argus_jl_operator_fragments(
+            R.data_ptr(), self.N, self.MJ, self.r_frag.data_ptr(), self.rt_frag.data_ptr(),
+            _lib.stream_handle(R.device)))
+        self._ws = {}
+
+    def shape(self, q, yk, n_splits=None, scale=None):
+        B, Hq, qlen, D = q.shape
+        _, Hkv, nb, MJ, D2 = yk.shape
+        if MJ != self.MJ or D2 != D:
+            raise ValueError(f"blocks {tuple(yk.shape)} do not match operator rows {self.MJ} / head_dim {D}")
+        if n_splits is None:
+            # about one CTA per SM (each holds two 64 KB block pairs), at least a block pair per split
+            n_splits = max(1, min(148 // max(1, B * Hkv), nb // 2))
+        n_splits = max(1, min(int(n_splits), max(1, nb)))
+        return JLShapeC(B, Hkv, Hq // Hkv, qlen, D, MJ, self.N, nb, n_splits,
+                        1.0 / math.sqrt(D) if scale is None else float(scale), nb * MJ * D, MJ * D)
+
+    def run(self, q, yk, yv, n_splits=None, scale=None, out=None, lse=None):
+        """q [B, H_q, q_len, D] fp16 -> out (fp16, same shape) and lse (natural log, fp32 [B, H_q, q_len])
+        over the archived tokens only."""
+        for t, name in ((q, "q"), (yk, "yk"), (yv, "yv")):
+            _lib.require_cuda(t, name)
+            if t.dtype != torch.float16:
+                raise TypeError(f"{name} must be float16")
+        if yk.shape != yv.shape:
+            raise ValueError("yk and yv shapes differ")
+        q, yk, yv = q.contiguous(), yk.contiguous(), yv.contiguous()
+        s = self.shape(q, yk, n_splits, scale)
+        if out is None:
+            out = torch.empty_like(q)
+        if lse is None:
+            lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
+        L = _jl_bind()
+        ws_bytes = L.argus_jl_attention_workspace_size(ctypes.byref(s))
+        key = (s.batch, s.heads_kv, s.n_splits, q.device)
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < ws_bytes:
+            ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)  # counters start at zero
+            self._ws[key] = ws
+        _check("argus_jl_attention", L.argus_jl_attention(
+            ctypes.byref(s), yk.data_ptr(), yv.data_ptr(), self.r_frag.data_ptr(), self.rt_frag.data_ptr(),
+            q.data_ptr(), out.data_ptr(), lse.data_ptr(), ws.data_ptr(), _lib.stream_handle(q.device)))
+        return out, lse
+
+
+def merge_attention(out_a, lse_a, out_b, lse_b, out=None, lse=None):
+    """Joins two attention results over disjoint token sets (fp16 rows, natural-log LSE)."""
+    for t in (out_a, lse_a, out_b, lse_b):
+        _lib.require_cuda(t)
+    D = out_a.shape[-1]
+    rows = out_a.numel() // D
+    if out is None:
+        out = torch.empty_like(out_a)
+    _check("argus_attention_merge", _jl_bind().argus_attention_merge(
+        out_a.contiguous().data_ptr(), lse_a.contiguous().data_ptr(), out_b.contiguous().data_ptr(),
+        lse_b.contiguous().data_ptr(), rows, D, out.data_ptr(), lse.data_ptr() if lse is not None else None,
+        _lib.stream_handle(out_a.device)))
     return out

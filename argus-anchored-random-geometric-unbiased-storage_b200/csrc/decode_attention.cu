@@ -1092,10 +1092,11 @@ int argus_device_status(int* status, argus_stream_t stream) {
     if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(da::g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
-    int jl = 0;
-    const int rc = argus_jl_take_status(&jl, (cudaStream_t)stream);
+    int jl = 0, jla = 0;
+    int rc = argus_jl_take_status(&jl, (cudaStream_t)stream);
+    if (rc == ARGUS_OK) rc = argus_jla_take_status(&jla, (cudaStream_t)stream);
     if (rc != ARGUS_OK) return rc;
-    *status = v != 0 ? v : jl;
+    *status = v != 0 ? v : (jl != 0 ? jl : jla);
     return ARGUS_OK;
 }
 

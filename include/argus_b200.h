@@ -148,6 +148,49 @@ int argus_outliers_to_coo(const uint8_t* mask, const uint16_t* outv, int B, int 
 int argus_jl_apply(const uint16_t* A, const uint16_t* X, int64_t batch, int M, int K, int N, uint16_t* C,
                    argus_stream_t stream);
 
+/* ---------------------------------------------------------------- JL archive decode attention */
+
+/* One decode step of attention over JL-archived blocks: each block of `block_tokens` tokens is
+ * stored as Yk = W . K, Yv = W . V ([block_rows][head_dim] fp16), and the reference rebuilds it as
+ * R . Yk, R . Yv before softmax attention (core/memory_manager.py:1176-1178, 1317-1447).  The kernel
+ * computes the same attention without rebuilding K and V: s = R (Yk q^T), w = R^T p, o = Yv^T w.
+ * Block j of (b, h) is at yk + (b*heads_kv + h)*bh_stride + j*block_stride (elements); supported:
+ * head_dim 128, block_rows 128, block_tokens a multiple of 128, group*q_len <= 8. */
+typedef struct argus_jl_attn_shape {
+    int32_t batch;
+    int32_t heads_kv;
+    int32_t group;
+    int32_t q_len;
+    int32_t head_dim;
+    int32_t block_rows;    /* rows of a projected block (N / ratio) */
+    int32_t block_tokens;  /* tokens a block stands for (N) */
+    int32_t n_blocks;
+    int32_t n_splits;      /* split-K partitions of the blocks (<= n_blocks) */
+    float scale;
+    int64_t bh_stride;     /* elements */
+    int64_t block_stride;  /* elements */
+} argus_jl_attn_shape;
+
+/* Writes R [n_tokens][n_rows] (fp16, the reconstruction operator of core/memory_manager.py:241-282)
+ * into the MMA fragment orders the JL attention reads: r_frag and rt_frag, n_tokens*n_rows*2 bytes
+ * each, 16-byte aligned.  Done once per operator. */
+int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, void* r_frag, void* rt_frag,
+                                argus_stream_t stream);
+/* Workspace bytes of argus_jl_attention: one arrival counter per (batch, kv_head) at the front
+ * (zero before the first use with a shape; every completed launch leaves them zero) and the split
+ * partials. */
+int64_t argus_jl_attention_workspace_size(const argus_jl_attn_shape* shape);
+/* q [B, heads_kv*group, q_len, 128] fp16 -> out (same shape, fp16) and optional lse (natural log,
+ * [B, heads_kv*group, q_len] fp32) over the archived tokens only. */
+int argus_jl_attention(const argus_jl_attn_shape* shape, const uint16_t* yk, const uint16_t* yv, const void* r_frag,
+                       const void* rt_frag, const uint16_t* q, uint16_t* out, float* lse, void* workspace,
+                       argus_stream_t stream);
+/* Merges two attention results over disjoint token sets: rows of head_dim fp16 values with their
+ * natural-log LSE -> out (and lse, if given).  Used to join the JL archive with the other tiers
+ * (the concatenation of core/memory_manager.py:1373-1430). */
+int argus_attention_merge(const uint16_t* out_a, const float* lse_a, const uint16_t* out_b, const float* lse_b,
+                          int64_t rows, int head_dim, uint16_t* out, float* lse, argus_stream_t stream);
+
 /* ------------------------------------------------------------------- mixed-tier decode attention */
 
 /* Storage tiers of a KV arena. */
