@@ -15,7 +15,15 @@
 // blocks share the 8 query columns of every MMA.  Per block pair: warp w forms u rows 16w..16w+15,
 // then streams token tiles w, w+8, ... through scores, online softmax (per column, log2 domain)
 // and w accumulation; the warps' partial w merge in shared memory; warp w then adds Yv^T . w for
-// dims 16w..16w+15.  Yk / Yv blocks arrive by bulk copy, each refilled as soon as it is consumed.
+// dims 16w..16w+15.  Yk / Yv blocks arrive by TMA tensor copies in 128-byte swizzle (two 64-column
+// halves of 128 rows x 128 bytes, 16-byte chunk c of row r stored at chunk c ^ (r % 8)) so the
+// ldmatrix reads of both contractions are free of bank conflicts; each buffer is refilled as soon as
+// it is consumed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 
 namespace argus {
@@ -33,6 +41,8 @@ constexpr float kSlack = 8.0f;
 __device__ int g_status = 0;
 
 struct Params {
+    CUtensorMap tmk;    // Yk as [B*Hkv][n_blocks][MJ][D], box 64 x MJ, 128-byte swizzle
+    CUtensorMap tmv;    // Yv, same
     const __half* yk;   // block j of (b, h) at yk + bh * bh_stride + j * block_stride
     const __half* yv;
     const uint4* rf;    // R [N x MJ] in A-fragment order: [N/16][MJ/16][32 lanes]
@@ -48,9 +58,12 @@ struct Params {
     float scale_log2;
 };
 
+constexpr int kRowPad = kMJ + 8;  // u^T / w^T row stride in halves (272 bytes: conflict-free reads)
+
 __host__ __device__ constexpr size_t smem_bytes(int pack) {
-    return (size_t)2 * pack * kMJ * kD * 2      // Yk, Yv blocks
-           + (size_t)2 * 2 * kCols * kMJ * 2    // u^T and w^T, fp16 hi / lo
+    return 1024                                 // alignment of the swizzled tiles
+           + (size_t)2 * pack * kMJ * kD * 2    // Yk, Yv blocks
+           + (size_t)2 * 2 * kCols * kRowPad * 2  // u^T and w^T, fp16 hi / lo
            + (size_t)kWarps * 32 * 33 * 4       // per-warp partial w (lane stride 33)
            + (size_t)(2 * kWarps * kCols + kWarps * kCols + 4 * kCols) * 4 + 64;
 }
@@ -115,25 +128,42 @@ __device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
     return r;
 }
 
-// Copies blocks j .. j+nb-1 of (b, h) into `dst` ([nb][MJ][D]) and arms `bar` for the bytes.
-__device__ __forceinline__ void issue_blocks(const Params& p, const __half* base, int64_t bh, int j, int nb, __half* dst,
-                                             uint32_t bar) {
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+
+// Copies blocks j .. j+nb-1 of (b, h) into `dst` (per block two swizzled 64-column halves) and arms
+// `bar` for the bytes.
+__device__ __forceinline__ void issue_blocks(const CUtensorMap* map, int64_t bh, int j, int nb, __half* dst, uint32_t bar) {
     constexpr uint32_t bytes = kMJ * kD * 2;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_expect_tx(bar, bytes * nb);
-    for (int i = 0; i < nb; ++i)
-        bulk_g2s(su32(dst + (size_t)i * kMJ * kD), base + bh * p.bh_stride + (int64_t)(j + i) * p.block_stride, bytes, bar);
+    for (int i = 0; i < nb; ++i) {
+        const uint32_t d = su32(dst + (size_t)i * kMJ * kD);
+        tma_load_4d(d, map, 0, 0, j + i, (int)bh, bar);
+        tma_load_4d(d + kMJ * 128, map, 64, 0, j + i, (int)bh, bar);
+    }
+}
+
+// Shared-memory address of element (row r, column c) of a swizzled [MJ][D] block.
+__device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) {
+    return base + (uint32_t)((c >> 6) * (kMJ * 128) + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
 }
 
 template <int PACK>
 __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_constant__ Params p) {
     constexpr int KD = kD / 16, KM = kMJ / 16;
-    extern __shared__ __align__(128) unsigned char smem[];
-    __half* ykbuf = reinterpret_cast<__half*>(smem);               // [PACK][MJ][D]
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __half* ykbuf = reinterpret_cast<__half*>(smem);               // [PACK][MJ][D] swizzled
     __half* yvbuf = ykbuf + PACK * kMJ * kD;                        // [PACK][MJ][D]
-    __half* uT = yvbuf + PACK * kMJ * kD;                           // [2][8][MJ]
-    __half* wt = uT + 2 * kCols * kMJ;                              // [2][8][MJ]
-    float* wpart = reinterpret_cast<float*>(wt + 2 * kCols * kMJ);  // [warps][32 lanes][33]
+    __half* uT = yvbuf + PACK * kMJ * kD;                           // [2][8][MJ + pad]
+    __half* wt = uT + 2 * kCols * kRowPad;                          // [2][8][MJ + pad]
+    float* wpart = reinterpret_cast<float*>(wt + 2 * kCols * kRowPad);  // [warps][32 lanes][33]
     float* mw = wpart + kWarps * 32 * 33;                           // [warps][8]
     float* lw = mw + kWarps * kCols;                                // [warps][8]
     float* fw = lw + kWarps * kCols;                                // [warps][8] merge factors
@@ -179,8 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
     __syncthreads();
     if (tid == 0 && j0 < j1) {
         const int nb = (j1 - j0) < PACK ? (j1 - j0) : PACK;
-        issue_blocks(p, p.yk, bh, j0, nb, ykbuf, ykbar);
-        issue_blocks(p, p.yv, bh, j0, nb, yvbuf, yvbar);
+        issue_blocks(&p.tmk, bh, j0, nb, ykbuf, ykbar);
+        issue_blocks(&p.tmv, bh, j0, nb, yvbuf, yvbar);
     }
 
     float oacc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 16*warp + g (+8), columns 2t, 2t+1
@@ -195,13 +225,14 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             float u[4] = {0.f, 0.f, 0.f, 0.f};
             const int row = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
             const int colo = 8 * (lane >> 4);
+            const uint32_t ka = su32(ykbuf), kb = su32(ykbuf + (size_t)kMJ * kD);
 #pragma unroll
             for (int kk = 0; kk < KD; ++kk) {
                 uint32_t a[4];
-                ldsm_x4(su32(ykbuf + (size_t)row * kD + 16 * kk + colo), a);
+                ldsm_x4(swz(ka, row, 16 * kk + colo), a);
                 mma16816(u, a, qa[kk][0], qa[kk][1]);
                 if (hasB) {
-                    ldsm_x4(su32(ykbuf + (size_t)kMJ * kD + (size_t)row * kD + 16 * kk + colo), a);
+                    ldsm_x4(swz(kb, row, 16 * kk + colo), a);
                     mma16816(u, a, qb[kk][0], qb[kk][1]);
                 }
             }
@@ -211,14 +242,14 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
                 const int m = m0 + 8 * (c >> 1), n = 2 * t + (c & 1);
                 __half hi, lo;
                 split_hl(u[c], hi, lo);
-                uT[n * kMJ + m] = hi;
-                uT[kCols * kMJ + n * kMJ + m] = lo;
+                uT[n * kRowPad + m] = hi;
+                uT[kCols * kRowPad + n * kRowPad + m] = lo;
             }
         }
         __syncthreads();
         if (tid == 0 && j + PACK < j1) {  // Yk buffer consumed: bring the next pair
             const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
-            issue_blocks(p, p.yk, bh, j + PACK, nb, ykbuf, ykbar);
+            issue_blocks(&p.tmk, bh, j + PACK, nb, ykbuf, ykbar);
         }
         // ---- scores, softmax and w over this warp's token tiles
         uint32_t ub[KM][2][2];
@@ -226,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         for (int kk = 0; kk < KM; ++kk)
 #pragma unroll
             for (int hl = 0; hl < 2; ++hl) {
-                const __half* r = uT + hl * kCols * kMJ + g * kMJ + 16 * kk + 2 * t;
+                const __half* r = uT + hl * kCols * kRowPad + g * kRowPad + 16 * kk + 2 * t;
                 ub[kk][hl][0] = *reinterpret_cast<const uint32_t*>(r);
                 ub[kk][hl][1] = *reinterpret_cast<const uint32_t*>(r + 8);
             }
@@ -339,8 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             for (int w = 0; w < kWarps; ++w) wv += fw[w * kCols + n] * wpart[((size_t)w * 32 + ln) * 33 + idx];
             __half hi, lo;
             split_hl(wv, hi, lo);
-            wt[n * kMJ + m] = hi;
-            wt[kCols * kMJ + n * kMJ + m] = lo;
+            wt[n * kRowPad + m] = hi;
+            wt[kCols * kRowPad + n * kRowPad + m] = lo;
         }
         __syncthreads();
         ok = __syncthreads_and(mbar_wait(yvbar, (uint32_t)(it & 1)));
@@ -353,16 +384,16 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             const bool inA = PACK == 1 || g < 4;
 #pragma unroll
             for (int kk = 0; kk < KM; ++kk) {
-                const __half* wr = wt + g * kMJ + 16 * kk + 2 * t;
+                const __half* wr = wt + g * kRowPad + 16 * kk + 2 * t;
                 const uint32_t wh0 = *reinterpret_cast<const uint32_t*>(wr), wh1 = *reinterpret_cast<const uint32_t*>(wr + 8);
-                const uint32_t wl0 = *reinterpret_cast<const uint32_t*>(wr + kCols * kMJ);
-                const uint32_t wl1 = *reinterpret_cast<const uint32_t*>(wr + kCols * kMJ + 8);
+                const uint32_t wl0 = *reinterpret_cast<const uint32_t*>(wr + kCols * kRowPad);
+                const uint32_t wl1 = *reinterpret_cast<const uint32_t*>(wr + kCols * kRowPad + 8);
                 uint32_t a[4];
-                ldsm_x4_t(su32(yvbuf + (size_t)(16 * kk + mrow) * kD + dcol), a);
+                ldsm_x4_t(swz(su32(yvbuf), 16 * kk + mrow, dcol), a);
                 mma16816(oacc, a, inA ? wh0 : 0u, inA ? wh1 : 0u);
                 mma16816(oacc, a, inA ? wl0 : 0u, inA ? wl1 : 0u);
                 if (hasB) {
-                    ldsm_x4_t(su32(yvbuf + (size_t)kMJ * kD + (size_t)(16 * kk + mrow) * kD + dcol), a);
+                    ldsm_x4_t(swz(su32(yvbuf + (size_t)kMJ * kD), 16 * kk + mrow, dcol), a);
                     mma16816(oacc, a, inA ? 0u : wh0, inA ? 0u : wh1);
                     mma16816(oacc, a, inA ? 0u : wl0, inA ? 0u : wl1);
                 }
@@ -371,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         __syncthreads();
         if (tid == 0 && j + PACK < j1) {  // Yv buffer consumed
             const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
-            issue_blocks(p, p.yv, bh, j + PACK, nb, yvbuf, yvbar);
+            issue_blocks(&p.tmv, bh, j + PACK, nb, yvbuf, yvbar);
         }
     }
     if (!ok) {
@@ -517,6 +548,36 @@ int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, voi
     return ARGUS_OK;
 }
 
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+// Yk / Yv as a 4-D tensor [B*Hkv][n_blocks][MJ][D] of fp16, box 64 x MJ x 1 x 1, 128-byte swizzle.
+int make_block_map(CUtensorMap* map, const void* base, const argus_jl_attn_shape* s) {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[4] = {(cuuint64_t)s->head_dim, (cuuint64_t)s->block_rows, (cuuint64_t)s->n_blocks,
+                                (cuuint64_t)s->batch * (cuuint64_t)s->heads_kv};
+    const cuuint64_t strides[3] = {(cuuint64_t)s->head_dim * 2, (cuuint64_t)s->block_stride * 2,
+                                   (cuuint64_t)s->bh_stride * 2};
+    const cuuint32_t box[4] = {64, (cuuint32_t)s->block_rows, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "tensor map for the JL blocks was refused");
+    return ARGUS_OK;
+}
+
+}  // namespace
+
 int64_t argus_jl_attention_workspace_size(const argus_jl_attn_shape* s) {
     if (!s || s->batch <= 0 || s->heads_kv <= 0 || s->n_splits <= 0) return 0;
     const int64_t groups = (int64_t)s->batch * s->heads_kv;
@@ -541,7 +602,11 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     if (!argus_aligned(yk, 16) || !argus_aligned(yv, 16) || !argus_aligned(workspace, 16) ||
         (s->bh_stride * 2) % 16 || (s->block_stride * 2) % 16)
         return argus_set_error(ARGUS_ERR_MISALIGNED, "blocks must start on 16-byte boundaries");
+    if (s->n_blocks == 0) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "no archived blocks");
     jla::Params p;
+    int rc = make_block_map(&p.tmk, yk, s);
+    if (rc == ARGUS_OK) rc = make_block_map(&p.tmv, yv, s);
+    if (rc != ARGUS_OK) return rc;
     p.yk = reinterpret_cast<const __half*>(yk);
     p.yv = reinterpret_cast<const __half*>(yv);
     p.rf = static_cast<const uint4*>(r_frag);
