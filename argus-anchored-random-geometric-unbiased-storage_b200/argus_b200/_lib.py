@@ -41,6 +41,8 @@ SIGNATURES = {
     "argus_isolate_outliers": [_p, _i64, _i32, _f32, _p, _p, _p, _p],
     "argus_jl_apply": [_p, _p, _i64, _i32, _i32, _i32, _p, _p],
     "argus_memcpy_async": [_p, _p, _i64, _p],
+    "argus_memcpy2d_async": [_p, _i64, _p, _i64, _i64, _i64, _p],
+    "argus_attention_accumulate": [_p, _p, _p, _p, _i64, _i32, _p],
     "argus_scatter_coo": [_p, _i64, _i64, _i32, _i32, _i32, _i32, _p, _p, _i64, _p],
     "argus_outliers_to_coo": [_p, _p, _i32, _i32, _i32, _i32, _p, _p, _i64, _p, _p],
 }

@@ -5,6 +5,8 @@ stream, ordered against the compute stream with CUDA events.
 Replaces the synchronous, pageable per-tensor .to("cpu") / .to(device) moves of
 swap_out_to_host / swap_in_to_device (core/memory_manager.py:1658-1713).
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -65,3 +67,78 @@ def arenas_to_device(host_arenas, device, event_out=None):
     if event_out is not None:
         event_out.append(ev)
     return out
+
+
+class StreamedArenaAttention:
+    """Attention over a record arena that stays in pinned host memory (a spilled tier), without
+    bringing it all back first: runs of `chunk_slots` slots of every (batch, kv_head) are copied
+    (one 2-D asynchronous copy per run) into two device staging arenas on a side stream while the
+    previous run is attended on the compute stream; the runs' results are joined by their LSE in
+    fp32.  The reference instead moves every spilled tensor back synchronously before attending
+    (core/memory_manager.py:1163, 1686-1713)."""
+
+    def __init__(self, host_arena: KVArena, *, group, chunk_slots=256, n_slots=None, device="cuda"):
+        if host_arena.k.is_cuda or not host_arena.k.is_pinned():
+            raise ValueError("the arena must live in pinned host memory")
+        from .attention import LAYOUT_RECORD
+        if host_arena.layout != LAYOUT_RECORD:
+            raise ValueError("only record arenas stream")
+        self.h, self.G = host_arena, int(group)
+        self.n = int(n_slots if n_slots is not None else host_arena.slots)
+        self.chunk = max(1, min(int(chunk_slots), self.n))
+        self.device = torch.device(device)
+        a = host_arena
+        self.bufs = [torch.empty(a.B * a.H, self.chunk, a.record_bytes, dtype=torch.uint8, device=self.device)
+                     for _ in range(2)]
+        self.arenas = [KVArena(a.tier, a.layout, b, None, bh_stride=self.chunk * a.record_bytes,
+                               record_bytes=a.record_bytes, page_tokens=a.page_tokens, head_dim=a.D, batch=a.B,
+                               heads=a.H, slots=self.chunk) for b in self.bufs]
+        self._plans = {}
+        self.copied = [torch.cuda.Event() for _ in range(2)]
+        self.released = [torch.cuda.Event() for _ in range(2)]
+
+    def _plan(self, buf, ns, q_len):
+        from .attention import AttentionPlan
+        key = (buf, ns, q_len)
+        if key not in self._plans:
+            a = self.h
+            self._plans[key] = AttentionPlan([self.arenas[buf]], [(0, j, a.page_tokens) for j in range(ns)], batch=a.B,
+                                             heads_kv=a.H, group=self.G, head_dim=a.D, q_len=q_len)
+        return self._plans[key]
+
+    def _copy(self, run, s0, ns, stream):
+        a = self.h
+        rec = a.record_bytes
+        _lib.call("argus_memcpy2d_async", _lib.ptr(self.bufs[run % 2]), self.chunk * rec,
+                  ctypes.c_void_p(a.k.data_ptr() + s0 * rec), a.bh_stride, ns * rec, a.B * a.H, _lib.ptr_stream(stream))
+
+    def run(self, q, scale=None):
+        """q [B, H_q, q_len, D] fp16 (on the device) -> (out fp16, lse natural log fp32) over the spilled tier."""
+        _lib.require_cuda(q, "q")
+        q = q.contiguous()
+        compute = torch.cuda.current_stream(q.device)
+        copy = side_stream(q.device)
+        runs = [(s0, min(self.chunk, self.n - s0)) for s0 in range(0, self.n, self.chunk)]
+        rows = q.numel() // q.shape[-1]
+        acc_o = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+        acc_lse = torch.full(q.shape[:3], float("-inf"), dtype=torch.float32, device=q.device)
+        out_i = torch.empty_like(q)
+        lse_i = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
+        # the staging buffers are free once the previous call's attention has read them; work issued
+        # on the compute stream before this call (the resident tiers) overlaps the first copies
+        for ev in self.released:
+            copy.wait_event(ev)
+        for i, (s0, ns) in enumerate(runs[:2]):
+            self._copy(i, s0, ns, copy)
+            self.copied[i % 2].record(copy)
+        for i, (s0, ns) in enumerate(runs):
+            compute.wait_event(self.copied[i % 2])
+            self._plan(i % 2, ns, q.shape[2]).run(q, scale=scale, out=out_i, lse=lse_i)
+            _lib.call("argus_attention_accumulate", _lib.ptr(acc_o), _lib.ptr(acc_lse), _lib.ptr(out_i),
+                      _lib.ptr(lse_i), rows, q.shape[-1], _lib.ptr_stream(compute))
+            self.released[i % 2].record(compute)
+            if i + 2 < len(runs):  # the buffer is free once this run's attention has read it
+                copy.wait_event(self.released[i % 2])
+                self._copy(i + 2, *runs[i + 2], copy)
+                self.copied[i % 2].record(copy)
+        return acc_o.to(torch.float16), acc_lse

@@ -39,6 +39,17 @@ int argus_version(void) { return 100; /* 0.1.0 */ }
 
 }  // extern "C"
 
+extern "C" int argus_memcpy2d_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
+                                    int64_t height, argus_stream_t stream) {
+    if (width < 0 || height < 0 || dst_pitch < width || src_pitch < width)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad 2-D copy");
+    if (width == 0 || height == 0) return ARGUS_OK;
+    if (!dst || !src) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dst_pitch, src, (size_t)src_pitch, (size_t)width, (size_t)height,
+                                      cudaMemcpyDefault, (cudaStream_t)stream);
+    return e == cudaSuccess ? ARGUS_OK : argus_set_cuda_error(e);
+}
+
 extern "C" int argus_memcpy_async(void* dst, const void* src, int64_t bytes, argus_stream_t stream) {
     if (bytes < 0 || (bytes > 0 && (!dst || !src))) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad copy");
     if (bytes == 0) return ARGUS_OK;

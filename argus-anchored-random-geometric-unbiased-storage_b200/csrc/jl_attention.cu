@@ -517,6 +517,23 @@ __global__ void merge_kernel(const __half* __restrict__ oa, const float* __restr
     }
 }
 
+// acc <- join(acc, b) in fp32, in place: acc_o [rows][D] fp32, acc_lse natural log (-inf: empty).
+__global__ void accumulate_kernel(float* __restrict__ acc_o, float* __restrict__ acc_lse, const __half* __restrict__ ob,
+                                  const float* __restrict__ lb, int64_t rows, int D) {
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float A = acc_lse[r], Bv = lb[r], M = fmaxf(A, Bv);
+        float wa = 0.f, wb = 0.f;
+        if (M != -INFINITY) { wa = __expf(A - M); wb = __expf(Bv - M); }
+        const float W = wa + wb;
+        for (int d = threadIdx.x; d < D; d += blockDim.x) {
+            const float v = W > 0.f ? (wa * acc_o[r * D + d] + wb * __half2float(ob[r * D + d])) / W : 0.f;
+            acc_o[r * D + d] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) acc_lse[r] = W > 0.f ? M + __logf(W) : -INFINITY;
+    }
+}
+
 }  // namespace jla
 }  // namespace argus
 
@@ -630,6 +647,17 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
     kern<<<dim3(s->n_splits, (unsigned)groups), jla::kThreads, smem, st>>>(p);
+    ARGUS_CHECK_LAUNCH();
+    return ARGUS_OK;
+}
+
+int argus_attention_accumulate(float* acc_o, float* acc_lse, const uint16_t* out_b, const float* lse_b, int64_t rows,
+                               int head_dim, argus_stream_t stream) {
+    if (!acc_o || !acc_lse || !out_b || !lse_b) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    if (rows < 0 || head_dim <= 0) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad size");
+    if (rows == 0) return ARGUS_OK;
+    jla::accumulate_kernel<<<argus_grid_cap(rows), 128, 0, (cudaStream_t)stream>>>(
+        acc_o, acc_lse, reinterpret_cast<const __half*>(out_b), lse_b, rows, head_dim);
     ARGUS_CHECK_LAUNCH();
     return ARGUS_OK;
 }

@@ -48,6 +48,13 @@ int argus_version(void);
  * (one cudaMemcpyAsync).  The host-spill transport: replaces the synchronous pageable .to("cpu") /
  * .to(device) moves of swap_out_to_host / swap_in_to_device (core/memory_manager.py:1658-1713). */
 int argus_memcpy_async(void* dst, const void* src, int64_t bytes, argus_stream_t stream);
+/* Asynchronous 2-D copy (one cudaMemcpy2DAsync): `height` rows of `width` bytes, row starts
+ * `src_pitch` / `dst_pitch` bytes apart, between pinned host and device memory on `stream`.  Moves a
+ * run of slots of every (batch, kv_head) of a spilled record arena in one call, for streaming a
+ * host-resident tier into a device staging arena (the swap_in_to_device of
+ * core/memory_manager.py:1686-1713, in pieces that overlap the attention of the resident tiers). */
+int argus_memcpy2d_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
+                         int64_t height, argus_stream_t stream);
 
 /* ------------------------------------------------------------------------------- codecs */
 
@@ -190,6 +197,11 @@ int argus_jl_attention(const argus_jl_attn_shape* shape, const uint16_t* yk, con
  * (the concatenation of core/memory_manager.py:1373-1430). */
 int argus_attention_merge(const uint16_t* out_a, const float* lse_a, const uint16_t* out_b, const float* lse_b,
                           int64_t rows, int head_dim, uint16_t* out, float* lse, argus_stream_t stream);
+/* In-place fp32 form of argus_attention_merge for joining many partial results (runs of a streamed
+ * host-resident tier): acc_o [rows][head_dim] fp32 and acc_lse (natural log; -inf and zeros before
+ * the first join) <- join(acc, (out_b, lse_b)). */
+int argus_attention_accumulate(float* acc_o, float* acc_lse, const uint16_t* out_b, const float* lse_b, int64_t rows,
+                               int head_dim, argus_stream_t stream);
 
 /* ------------------------------------------------------------------- mixed-tier decode attention */
 
