@@ -13,6 +13,14 @@ is the whole-job KV tokens/s (ranks x 8 x 32768 / max-over-ranks step time).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
+Two further single-GPU workloads (not the headline line) are measured by the same script:
+
+    python bench.py --workload jl-archive          # attention over the JL archive: B 4, H_q 32,
+                                                   # H_kv 8, D 128, 64 blocks of 1024 tokens -> 128 rows
+    python bench.py --workload llama3-70b-spill    # Llama-3-70B layer on one GPU: B 64, H_q 64, H_kv 8,
+                                                   # context 131072 (the 8B tier ratios x4); the 1-bit
+                                                   # tier (oldest 25%) in pinned host memory, streamed
+
 --impl reference times the CPU restatement of the reference's path (dequantize every page, then
 softmax attention over the reconstructed K/V; argus_cache core/memory_manager.py:1157-1315 +
 1424-1430) on the host cores, on a bounded sample (one sequence, all KV heads, full context).
@@ -319,6 +327,97 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def _timed(fn, steps, warmup):
+    """Device time per call (ms) of `steps` back-to-back calls; a device-side sleep queued first keeps
+    host launch overhead out of the measured span."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(5_000_000)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_jl_archive(args):
+    import torch
+
+    from argus_b200.core import jl
+
+    dev = torch.device("cuda", 0)
+    Bj, HQj, HKVj, Dj, N, ratio, NB = 4, 32, 8, 128, 1024, 8, 64
+    MJ = N // ratio
+    g = torch.Generator(device=dev).manual_seed(4321)
+    W = jl.projection_matrix(N, dtype=torch.float16, device="cpu", ratio=ratio)
+    R = jl.reconstruction_operator_solve(W).half().to(dev)
+    att = jl.JLAttention(R)
+    yk = torch.randn(Bj, HKVj, NB, MJ, Dj, device=dev, generator=g).half()
+    yv = torch.randn(Bj, HKVj, NB, MJ, Dj, device=dev, generator=g).half()
+    q = (torch.randn(Bj, HQj, 1, Dj, device=dev, generator=g) / math.sqrt(Dj)).half()
+    out = torch.empty_like(q)
+    lse = torch.empty(Bj, HQj, 1, device=dev)
+    ms = _timed(lambda: att.run(q, yk, yv, out=out, lse=lse), args.steps, args.warmup)
+    hbm, peak_kind = peaks()
+    ybytes = 2 * yk.numel() * 2
+    tokens = Bj * NB * N
+    print(json.dumps({"metric": "JL-archive decode attention, archived KV tokens/s", "value": tokens / (ms * 1e-3),
+                      "unit": "KV tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": ms, "higher_is_better": True, "dtype": "fp16", "data": "synthetic",
+                      "config": {"workload": "jl-archive", "batch": Bj, "q_heads": HQj, "kv_heads": HKVj,
+                                 "head_dim": Dj, "blocks": NB, "block_tokens": N, "block_rows": MJ},
+                      "roofline": {"bound": "hbm", "achieved": ybytes / (ms * 1e-3) / 1e9, "peak": hbm,
+                                   "unit": "GB/s", "frac": ybytes / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
+                                   "algorithmic_bytes_per_launch": ybytes}}), flush=True)
+
+
+def run_70b_spill(args):
+    import torch
+
+    from argus_b200 import attention as A
+    from argus_b200 import spill
+    from argus_b200.core import jl
+
+    global B, HQ, L, SPLIT
+    B, HQ, L = 64, 64, 131072
+    SPLIT = [(t, 4 * n) for t, n in SPLIT]
+    dev = torch.device("cuda", 0)
+    plan_all, q = build_cache(dev, seed=77)
+    res = plan_all.arenas[1:]  # SPLIT starts with the 1-bit tier: it is the spilled one
+    plan_res = A.AttentionPlan(res, [(ai, j, P) for ai, a in enumerate(res) for j in range(a.slots)], batch=B,
+                               heads_kv=HKV, group=HQ // HKV, head_dim=D)
+    host = spill.arenas_to_host([plan_all.arenas[0]])[0]
+    st = spill.StreamedArenaAttention(host, group=HQ // HKV, chunk_slots=512)
+    lse_r = torch.empty(B, HQ, 1, device=dev)
+    ms_resident_all = _timed(lambda: plan_all.run(q), args.steps, args.warmup)
+    ms_res = _timed(lambda: plan_res.run(q, lse=lse_r), args.steps, args.warmup)
+
+    def layer():
+        o_r = plan_res.run(q, lse=lse_r)
+        o_s, l_s = st.run(q)
+        return jl.merge_attention(o_r, lse_r, o_s, l_s)
+
+    ms = _timed(layer, max(3, args.steps // 10), 2)
+    hbm, peak_kind = peaks()
+    spilled = host.k.numel()
+    print(json.dumps({"metric": "Llama-3-70B layer decode with the 1-bit tier spilled to host, KV tokens/s",
+                      "value": B * L / (ms * 1e-3), "unit": "KV tokens/s", "n_gpus": 1, "ms_per_step": ms,
+                      "higher_is_better": True, "dtype": "fp16", "data": "synthetic",
+                      "config": {"workload": "llama3-70b-spill", "batch": B, "q_heads": HQ, "kv_heads": HKV,
+                                 "head_dim": D, "context": L, "tiers_oldest_first": dict(SPLIT),
+                                 "spilled": "one_bit (pinned host, streamed in runs of 512 slots)"},
+                      "all_resident": {"ms": ms_resident_all, "GB/s": plan_all.compressed_bytes / ms_resident_all / 1e6,
+                                       "frac_of_hbm": plan_all.compressed_bytes / ms_resident_all / 1e6 / hbm,
+                                       "peak_kind": peak_kind},
+                      "resident_tiers_ms": ms_res,
+                      "host_link": {"spilled_bytes": spilled, "GB/s": spilled / ms / 1e6}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -326,8 +425,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b-spill"),
+                    default="llama3-8b-layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "jl-archive":
+        run_jl_archive(args)
+        return
+    if args.workload == "llama3-70b-spill":
+        run_70b_spill(args)
+        return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
