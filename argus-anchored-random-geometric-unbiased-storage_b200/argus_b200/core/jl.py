@@ -96,7 +96,7 @@ def _jl_bind():
         L.argus_jl_operator_fragments.restype = ctypes.c_int
         L.argus_jl_attention_workspace_size.argtypes = [ctypes.POINTER(JLShapeC)]
         L.argus_jl_attention_workspace_size.restype = ctypes.c_int64
-        L.argus_jl_attention.argtypes = [ctypes.POINTER(JLShapeC), p, p, p, p, p, p, p, p, p]
+        L.argus_jl_attention.argtypes = [ctypes.POINTER(JLShapeC), p, p, p, p, p, p, p, p, p, p]
         L.argus_jl_attention.restype = ctypes.c_int
         L.argus_attention_merge.argtypes = [p, p, p, p, ctypes.c_int64, ctypes.c_int, p, p, p]
         L.argus_attention_merge.restype = ctypes.c_int
@@ -139,9 +139,10 @@ class JLAttention:
         return JLShapeC(B, Hkv, Hq // Hkv, qlen, D, MJ, self.N, nb, n_splits,
                         1.0 / math.sqrt(D) if scale is None else float(scale), nb * MJ * D, MJ * D)
 
-    def run(self, q, yk, yv, n_splits=None, scale=None, out=None, lse=None):
+    def run(self, q, yk, yv, n_splits=None, scale=None, out=None, lse=None, block_lse=None):
         """q [B, H_q, q_len, D] fp16 -> out (fp16, same shape) and lse (natural log, fp32 [B, H_q, q_len])
-        over the archived tokens only."""
+        over the archived tokens only; block_lse ([B*H_kv, n_blocks, 8] fp32), if given, receives each
+        block's natural-log LSE per query."""
         for t, name in ((q, "q"), (yk, "yk"), (yv, "yv")):
             _lib.require_cuda(t, name)
             if t.dtype != torch.float16:
@@ -163,7 +164,8 @@ class JLAttention:
             self._ws[key] = ws
         _check("argus_jl_attention", L.argus_jl_attention(
             ctypes.byref(s), yk.data_ptr(), yv.data_ptr(), self.r_frag.data_ptr(), self.rt_frag.data_ptr(),
-            q.data_ptr(), out.data_ptr(), lse.data_ptr(), ws.data_ptr(), _lib.stream_handle(q.device)))
+            q.data_ptr(), out.data_ptr(), lse.data_ptr(), block_lse.data_ptr() if block_lse is not None else None,
+            ws.data_ptr(), _lib.stream_handle(q.device)))
         return out, lse
 
 

@@ -171,6 +171,10 @@ class PagedDynamicKVCache:
         self._host_arenas = {}
         self._plan = None
         self._plan_key = None
+        # attend JL pages without rebuilding them (argus_b200.core.jl.JLAttention) when their shape
+        # allows it (128-row blocks, i.e. 512-token pages, head_dim 128, <= 8 queries per kv head)
+        self.fused_jl_attention = True
+        self._jl_attention = None
 
     # ------------------------------------------------------------------- JL matrices
     def get_jl_projection_matrix(self, device, dtype):
@@ -622,8 +626,16 @@ class PagedDynamicKVCache:
             order.append(("fp16", page, P))
         if self.k_buffer is not None and self.k_buffer.shape[-2] > 0:
             order.append(("buffer", None, self.buffer_length))
+        others = (self.sink_k is not None or self.anchor_k is not None or bool(self.active_pages)
+                  or (self.k_buffer is not None and self.k_buffer.shape[-2] > 0)
+                  or any(lst for name, lst in self._compressed_order() if name != "jl"))
+        fused_jl = (self.fused_jl_attention and len(self.jl_pages) > 0 and others and P // 4 == 128 and D == 128
+                    and (Hq // (self.H if self._pools_allocated else self.sink_k.shape[1])) * qlen <= 8)
         for name, lst in self._compressed_order():
             for page in lst:
+                if name == "jl" and fused_jl:
+                    order.append(("jl_fused", page, P))
+                    continue
                 side = name == "jl" or (page.get("key_out_indices") is not None and page["key_out_indices"].numel() > 0) \
                     or (page.get("value_out_indices") is not None and page["value_out_indices"].numel() > 0)
                 order.append((("scratch:" + name) if side else name, page, P))
@@ -642,7 +654,11 @@ class PagedDynamicKVCache:
             arenas.append(A.KVArena.from_fp16(sk, sv))
         pos = 0
         page_seg = []  # per entry of `pages`: its segment
+        jl_segs = []
         for seg, (kind, page, n) in enumerate(order):
+            if kind == "jl_fused":
+                jl_segs.append(seg)
+                continue
             if kind in ("sinks", "anchors", "buffer") or kind.startswith("scratch:"):
                 sk, sv = scratch
                 if kind == "sinks":
@@ -687,6 +703,15 @@ class PagedDynamicKVCache:
                 cmap[c, i] = page_seg[perm[pi]]
         plan.tile_segment = cmap.to(dev)
         plan.segments = order
+        plan.jl = None
+        if jl_segs:
+            R = self.get_jl_reconstruction_operator(dev, torch.float16)
+            if self._jl_attention is None or self._jl_attention[0] is not R:
+                self._jl_attention = (R, _jl.JLAttention(R))
+            pages_jl = [order[i][1] for i in jl_segs]
+            plan.jl = {"att": self._jl_attention[1], "segs": jl_segs,
+                       "yk": torch.stack([pg["key_proj"] for pg in pages_jl], dim=2).contiguous(),
+                       "yv": torch.stack([pg["value_proj"] for pg in pages_jl], dim=2).contiguous()}
         self._plan, self._plan_key = plan, key
         return plan
 
@@ -721,6 +746,15 @@ class PagedDynamicKVCache:
         lse = torch.empty(B, Hq, qlen, dtype=torch.float32, device=q.device)
         tile_lse = torch.empty(plan.tile_lse_shape(), dtype=torch.float32, device=q.device)
         out = plan.run(q, scale=scale, lse=lse, tile_lse=tile_lse)
+        block_lse = None
+        if plan.jl is not None:
+            # JL pages attended without rebuilding them, then joined with the other tiers by LSE
+            jl_blocks = plan.jl["yk"].shape[2]
+            block_lse = torch.empty(B * plan.Hkv, jl_blocks, 8, dtype=torch.float32, device=q.device)
+            out_j, lse_j = plan.jl["att"].run(q, plan.jl["yk"], plan.jl["yv"], scale=scale, block_lse=block_lse)
+            lse_tot = torch.empty_like(lse)
+            out = _jl.merge_attention(out, lse, out_j, lse_j, lse=lse_tot)
+            lse = lse_tot
         self.generation_step += 1
         # per-segment attention mass: mean over (b, h_q, q) of the segment's token probabilities
         nqg = tile_lse.shape[0] // (B * plan.Hkv)
@@ -736,6 +770,11 @@ class PagedDynamicKVCache:
         tile_mass = w.sum(dim=(0, 1, 2, 5)) / float(B * Hq * qlen)
         seg_mass = torch.zeros(len(plan.segments), device=q.device, dtype=torch.float32)
         seg_mass.index_add_(0, plan.tile_segment[valid], tile_mass[valid])
+        if block_lse is not None:
+            nq = G * qlen
+            wj = torch.exp(block_lse[:, :, :nq] - lse.view(B * plan.Hkv, 1, nq))
+            jl_mass = wj.sum(dim=(0, 2)) / float(B * Hq * qlen)
+            seg_mass.index_add_(0, torch.tensor(plan.jl["segs"], device=q.device), jl_mass)
         masses = seg_mass.tolist()
         resurrect = []
         compressed = {id(p): name for name, lst in self._compressed_order() for p in lst}

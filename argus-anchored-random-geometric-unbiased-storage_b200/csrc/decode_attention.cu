@@ -694,34 +694,6 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
     const int pair = warp / kPairWarps, wip = warp - pair * kPairWarps;
     unsigned char* wbuf = smem + (size_t)pair * kStages * STAGE;
 
-    // ---- Q^T fragments (query qg*8 + g4, dims t4*D/4 ..), written once by warp 0 into the shared
-    // memory past the last ring slot (load_qfrags layout), read back for every tile
-    uint32_t* qsw = reinterpret_cast<uint32_t*>(smem + (size_t)kPairs * kStages * STAGE);
-    const uint32_t qs = smem_u32(qsw);
-    if (warp == 0) {
-        constexpr int V = (2 * KC) % 4 == 0 ? 4 : 2;
-        const int n = qg * kQ + g4;
-        const bool live = n < NQ;
-        const __half* qrow = p.q;
-        if (live) {
-            const int gi = n / p.qlen, qi = n - gi * p.qlen;
-            qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
-        }
-#pragma unroll
-        for (int c = 0; c < KC; ++c) {
-            uint32_t f0 = 0u, f1 = 0u;
-            if (live) {
-                const uint32_t q01 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c);
-                const uint32_t q23 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c + 2);
-                f0 = prmt(q01, q23, 0x5410);  // dims 4c, 4c+2
-                f1 = prmt(q01, q23, 0x7632);  // dims 4c+1, 4c+3
-            }
-            const int j0 = 2 * c, j1 = 2 * c + 1;
-            qsw[((j0 / V) * 32 + lane) * V + j0 % V] = f0;
-            qsw[((j1 / V) * 32 + lane) * V + j1 % V] = f1;
-        }
-    }
-
     SoftmaxState st;
     st.m[0] = st.m[1] = kNoMax;
     st.l[0] = st.l[1] = 0.f;
@@ -735,16 +707,6 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
     const int c_begin = p.split_chunk0[split], c_end = p.split_chunk0[split + 1];
     const int first = c_begin + pair;
     const int n_pair = first < c_end ? (c_end - first + kPairs - 1) / kPairs : 0;
-
-    if (wip == 0 && lane == 0) {
-#pragma unroll
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&mbar[pair][s], 1);
-            issued[pair][s] = -1;
-        }
-        fence_mbar_init();
-    }
-    __syncthreads();
 
     // Issue the bulk copies of pair chunk j into slot j % kStages (one lane).
     auto issue = [&](int j) {
@@ -796,10 +758,47 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
         *reinterpret_cast<volatile int*>(&issued[pair][j % kStages]) = j;
     };
 
+    // The pair's leading lane sets up its ring and starts the first copies before anything else, so
+    // their DRAM latency overlaps the query setup.
     if (wip == 0 && lane == 0) {
+#pragma unroll
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&mbar[pair][s], 1);
+            issued[pair][s] = -1;
+        }
+        fence_mbar_init();
         for (int j = 0; j < kStages && j < n_pair; ++j) issue(j);
     }
-    __syncwarp();
+
+    // ---- Q^T fragments (query qg*8 + g4, dims t4*D/4 ..), written once by warp 0 into the shared
+    // memory past the last ring slot (load_qfrags layout), read back for every tile
+    uint32_t* qsw = reinterpret_cast<uint32_t*>(smem + (size_t)kPairs * kStages * STAGE);
+    const uint32_t qs = smem_u32(qsw);
+    if (warp == 0) {
+        constexpr int V = (2 * KC) % 4 == 0 ? 4 : 2;
+        const int n = qg * kQ + g4;
+        const bool live = n < NQ;
+        const __half* qrow = p.q;
+        if (live) {
+            const int gi = n / p.qlen, qi = n - gi * p.qlen;
+            qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
+        }
+#pragma unroll
+        for (int c = 0; c < KC; ++c) {
+            uint32_t f0 = 0u, f1 = 0u;
+            if (live) {
+                const uint32_t q01 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c);
+                const uint32_t q23 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c + 2);
+                f0 = prmt(q01, q23, 0x5410);  // dims 4c, 4c+2
+                f1 = prmt(q01, q23, 0x7632);  // dims 4c+1, 4c+3
+            }
+            const int j0 = 2 * c, j1 = 2 * c + 1;
+            qsw[((j0 / V) * 32 + lane) * V + j0 % V] = f0;
+            qsw[((j1 / V) * 32 + lane) * V + j1 % V] = f1;
+        }
+    }
+
+    __syncthreads();  // rings initialised, first copies issued, query fragments in place
 
     bool failed = false;
     argus_kv_chunk nch;  // descriptor of this warp's next chunk, loaded one chunk ahead

@@ -50,6 +50,7 @@ struct Params {
     const __half* q;    // [B, Hkv*G, qlen, D]
     __half* out;
     float* lse;
+    float* block_lse;   // optional [B*Hkv][n_blocks][8]: natural-log LSE of each block's scores
     float* part_o;      // [B*Hkv][S][8][D]
     float* part_lse;    // [B*Hkv][S][8]
     int* counters;      // [B*Hkv]
@@ -353,6 +354,12 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             for (int w = 0; w < kWarps; ++w) mb = fmaxf(mb, mw[w * kCols + n]);
             float lb = 0.f;
             for (int w = 0; w < kWarps; ++w) lb += exp2f(mw[w * kCols + n] - mb) * lw[w * kCols + n];
+            if (p.block_lse) {  // column n belongs to block j (+1 for the upper columns when packed)
+                const int blk = j + ((PACK == 2 && n >= 4) ? 1 : 0), qn = n % qpb;
+                if (qn < NQ && blk < j1)
+                    p.block_lse[(bh * p.n_blocks + blk) * kCols + qn] =
+                        lb > 0.f ? (mb + log2f(lb)) * 0.69314718055994530942f : -INFINITY;
+            }
             const float mo = mrun[n], mn = fmaxf(mo, mb);
             const float a = exp2f(mo - mn), be = exp2f(mb - mn);
             lrun[n] = a * lrun[n] + be * lb;
@@ -602,8 +609,8 @@ int64_t argus_jl_attention_workspace_size(const argus_jl_attn_shape* s) {
 }
 
 int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const uint16_t* yv, const void* r_frag,
-                       const void* rt_frag, const uint16_t* q, uint16_t* out, float* lse, void* workspace,
-                       argus_stream_t stream) {
+                       const void* rt_frag, const uint16_t* q, uint16_t* out, float* lse, float* block_lse,
+                       void* workspace, argus_stream_t stream) {
     if (!s || !yk || !yv || !r_frag || !rt_frag || !q || !out || !workspace)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
     if (s->batch <= 0 || s->heads_kv <= 0 || s->group <= 0 || s->q_len <= 0 || s->n_blocks < 0 || s->n_splits <= 0)
@@ -631,6 +638,7 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     p.q = reinterpret_cast<const __half*>(q);
     p.out = reinterpret_cast<__half*>(out);
     p.lse = lse;
+    p.block_lse = block_lse;
     const int64_t groups = (int64_t)s->batch * s->heads_kv;
     p.counters = static_cast<int*>(workspace);
     p.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + ((groups * 4 + 255) & ~255LL));

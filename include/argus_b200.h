@@ -188,10 +188,13 @@ int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, voi
  * partials. */
 int64_t argus_jl_attention_workspace_size(const argus_jl_attn_shape* shape);
 /* q [B, heads_kv*group, q_len, 128] fp16 -> out (same shape, fp16) and optional lse (natural log,
- * [B, heads_kv*group, q_len] fp32) over the archived tokens only. */
+ * [B, heads_kv*group, q_len] fp32) over the archived tokens only.  Optional block_lse
+ * [B*heads_kv][n_blocks][8] fp32 receives each block's natural-log LSE per query (group*q_len
+ * queries used): the per-page attention mass of the importance policy
+ * (core/memory_manager.py:1453-1522) is exp(block_lse - lse). */
 int argus_jl_attention(const argus_jl_attn_shape* shape, const uint16_t* yk, const uint16_t* yv, const void* r_frag,
-                       const void* rt_frag, const uint16_t* q, uint16_t* out, float* lse, void* workspace,
-                       argus_stream_t stream);
+                       const void* rt_frag, const uint16_t* q, uint16_t* out, float* lse, float* block_lse,
+                       void* workspace, argus_stream_t stream);
 /* Merges two attention results over disjoint token sets: rows of head_dim fp16 values with their
  * natural-log LSE -> out (and lse, if given).  Used to join the JL archive with the other tiers
  * (the concatenation of core/memory_manager.py:1373-1430). */

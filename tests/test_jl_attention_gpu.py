@@ -70,7 +70,8 @@ def test_jl_attention_matches_rebuilt_attention(B, Hkv, G, ql, N, ratio, nb, spl
     yv = torch.randn(B, Hkv, nb, MJ, D, generator=g).half()
     q = (torch.randn(B, Hkv * G, ql, D, generator=g) / math.sqrt(D) * 2.0).half()
     att = jl.JLAttention(R.cuda())
-    out, lse = att.run(q.cuda(), yk.cuda(), yv.cuda(), n_splits=splits)
+    block_lse = torch.empty(B * Hkv, nb, 8, dtype=torch.float32, device="cuda")
+    out, lse = att.run(q.cuda(), yk.cuda(), yv.cuda(), n_splits=splits, block_lse=block_lse)
     torch.cuda.synchronize()
     assert A.device_status() == 0
     K, V = rebuild(R, yk), rebuild(R, yv)
@@ -83,6 +84,13 @@ def test_jl_attention_matches_rebuilt_attention(B, Hkv, G, ql, N, ratio, nb, spl
     mx = s.max(-1)
     ref_lse = mx + np.log(np.exp(s - mx[..., None]).sum(-1))
     assert np.allclose(lse.cpu().numpy(), ref_lse, rtol=0, atol=2e-3)
+    # per-block LSE (the per-page attention mass of the importance policy is exp(block - total))
+    sb = s.reshape(B, Hkv, G, ql, nb, N)
+    mb = sb.max(-1)
+    ref_blk = mb + np.log(np.exp(sb - mb[..., None]).sum(-1))          # [B, Hkv, G, ql, nb]
+    ref_blk = ref_blk.reshape(B * Hkv, G * ql, nb).transpose(0, 2, 1)  # [B*Hkv, nb, G*ql]
+    got_blk = block_lse.cpu().numpy()[:, :, :G * ql]
+    assert np.allclose(got_blk, ref_blk, rtol=0, atol=2e-3), np.abs(got_blk - ref_blk).max()
     # the materializing path: tensor-core rebuild, then the fused mixed-tier kernel
     Kg = jl.apply_left(R.cuda(), yk.cuda().reshape(B * Hkv * nb, MJ, D)).reshape(B, Hkv, nb * N, D)
     Vg = jl.apply_left(R.cuda(), yv.cuda().reshape(B * Hkv * nb, MJ, D)).reshape(B, Hkv, nb * N, D)
