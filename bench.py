@@ -217,7 +217,9 @@ def cpu_sample(seed=0):
     return pages, q
 
 
-def time_cpu(steps, warmup, threads):
+def time_cpu(steps, warmup, threads, min_seconds=0.0):
+    """Seconds per step of the CPU path; runs at least `steps` steps and at least `min_seconds`.
+    Returns (KV tokens/s, seconds per step, steps run)."""
     import torch
 
     torch.set_num_threads(threads)
@@ -225,17 +227,19 @@ def time_cpu(steps, warmup, threads):
     for _ in range(warmup):
         cpu_reference_step(pages, q, threads)
     t0 = time.perf_counter()
-    for _ in range(steps):
+    n = 0
+    while n < steps or time.perf_counter() - t0 < min_seconds:
         cpu_reference_step(pages, q, threads)
-    dt = (time.perf_counter() - t0) / steps
-    return L / dt, dt
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return L / dt, dt, n
 
 
 def run_reference(args, rank):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    value, dt = time_cpu(args.steps, args.warmup, threads)
+    value, dt, _ = time_cpu(args.steps, args.warmup, threads)
     sample = f"1 sequence x {HKV} KV heads x {L} tokens per step (one of the {B} sequences of the workload)"
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
@@ -320,10 +324,10 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "splits": plan.n_splits}
     if not args.no_cpu_baseline:
-        cpu_steps = 2
-        value, dt = time_cpu(cpu_steps, 1, os.cpu_count() or 1)
+        value, dt, cpu_steps = time_cpu(3, 1, os.cpu_count() or 1, min_seconds=10.0)
         line["cpu_baseline"] = {"value": value, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
-                                "sample": f"1 sequence x {HKV} KV heads x {L} tokens, {cpu_steps} timed steps"}
+                                "sample": f"1 sequence x {HKV} KV heads x {L} tokens per step, {cpu_steps} timed steps "
+                                          f"({cpu_steps * dt:.1f} s of CPU work)"}
     print(json.dumps(line), flush=True)
 
 
