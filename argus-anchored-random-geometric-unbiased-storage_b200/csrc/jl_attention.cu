@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         if (!ok) break;
         // ---- u = Yk . q^T: rows 16*warp .. +15, block A in columns 0..3 (or 0..7), block B in 4..7
         {
-            float u[4] = {0.f, 0.f, 0.f, 0.f};
+            float u[4] = {0.f, 0.f, 0.f, 0.f}, u2[4] = {0.f, 0.f, 0.f, 0.f};  // two independent chains
             const int row = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
             const int colo = 8 * (lane >> 4);
             const uint32_t ka = su32(ykbuf), kb = su32(ykbuf + (size_t)kMJ * kD);
@@ -231,12 +231,14 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             for (int kk = 0; kk < KD; ++kk) {
                 uint32_t a[4];
                 ldsm_x4(swz(ka, row, 16 * kk + colo), a);
-                mma16816(u, a, qa[kk][0], qa[kk][1]);
+                mma16816((kk & 1) ? u2 : u, a, qa[kk][0], qa[kk][1]);
                 if (hasB) {
                     ldsm_x4(swz(kb, row, 16 * kk + colo), a);
-                    mma16816(u, a, qb[kk][0], qb[kk][1]);
+                    mma16816((kk & 1) ? u : u2, a, qb[kk][0], qb[kk][1]);
                 }
             }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) u[c] += u2[c];
             const int m0 = 16 * warp + g;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -280,12 +282,15 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
 #pragma unroll
             for (int mt = 0; mt < KM; ++mt) rt[mt] = ldg_nc(rtf + (size_t)mt * ntiles * 32);
             float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+            float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
 #pragma unroll
             for (int kk = 0; kk < KM; ++kk) {
                 const uint32_t a[4] = {rcur[kk].x, rcur[kk].y, rcur[kk].z, rcur[kk].w};
-                mma16816(sa, a, ub[kk][0][0], ub[kk][0][1]);
-                mma16816(sb, a, ub[kk][1][0], ub[kk][1][1]);
+                mma16816((kk & 1) ? sc : sa, a, ub[kk][0][0], ub[kk][0][1]);
+                mma16816((kk & 1) ? sd : sb, a, ub[kk][1][0], ub[kk][1][1]);
             }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) { sa[c] += sc[c]; sb[c] += sd[c]; }
             if (tt + kWarps < ntiles) {
 #pragma unroll
                 for (int kk = 0; kk < KM; ++kk) rcur[kk] = ldg_nc(p.rf + ((size_t)(tt + kWarps) * KM + kk) * 32 + lane);
@@ -325,6 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             for (int mt = 0; mt < KM; ++mt) {
                 const uint32_t a[4] = {rt[mt].x, rt[mt].y, rt[mt].z, rt[mt].w};
                 mma16816(wacc[mt], a, b01, b23);
+            }
+#pragma unroll
+            for (int mt = 0; mt < KM; ++mt) {
+                const uint32_t a[4] = {rt[mt].x, rt[mt].y, rt[mt].z, rt[mt].w};
                 mma16816(wacc[mt], a, c01, c23);
             }
         }
@@ -387,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         {
             const float a0 = alpha[2 * t], a1 = alpha[2 * t + 1];
             oacc[0] *= a0; oacc[2] *= a0; oacc[1] *= a1; oacc[3] *= a1;
+            float olo[4] = {0.f, 0.f, 0.f, 0.f};  // the lo parts of w: an independent chain
             const int mrow = (lane & 7) + 8 * (lane >> 4), dcol = 16 * warp + 8 * ((lane >> 3) & 1);
             const bool inA = PACK == 1 || g < 4;
 #pragma unroll
@@ -398,13 +408,15 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
                 uint32_t a[4];
                 ldsm_x4_t(swz(su32(yvbuf), 16 * kk + mrow, dcol), a);
                 mma16816(oacc, a, inA ? wh0 : 0u, inA ? wh1 : 0u);
-                mma16816(oacc, a, inA ? wl0 : 0u, inA ? wl1 : 0u);
+                mma16816(olo, a, inA ? wl0 : 0u, inA ? wl1 : 0u);
                 if (hasB) {
                     ldsm_x4_t(swz(su32(yvbuf + (size_t)kMJ * kD), 16 * kk + mrow, dcol), a);
                     mma16816(oacc, a, inA ? 0u : wh0, inA ? 0u : wh1);
-                    mma16816(oacc, a, inA ? 0u : wl0, inA ? 0u : wl1);
+                    mma16816(olo, a, inA ? 0u : wl0, inA ? 0u : wl1);
                 }
             }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) oacc[c] += olo[c];
         }
         __syncthreads();
         if (tid == 0 && j + PACK < j1) {  // Yv buffer consumed
