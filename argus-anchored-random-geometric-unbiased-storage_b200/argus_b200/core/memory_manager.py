@@ -720,6 +720,31 @@ class PagedDynamicKVCache:
                 self.anchor_k.shape[-2] if self.anchor_k is not None else 0, self._page_counter, self.num_resurrections,
                 self.total_demotions)
 
+    def attend(self, q, scale=None):
+        """softmax(q K^T * scale) V over every tier straight from the compressed pages, without the
+        importance / resurrection side effects of inplace_paged_attention: what the HuggingFace path
+        computes from get_all_keys_values + SDPA (models/attention_wrapper.py:87-88), without
+        rebuilding the full K/V.  q: [B, H_q, q_len, D] fp16 (every query attends to every cached
+        token)."""
+        B, Hq, qlen, D = q.shape
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        if self.is_swapped_out:
+            self.swap_in_to_device()
+        if self.sink_k is None and self.anchor_k is None and not self.active_pages and self.k_buffer is None and \
+                not any(lst for _, lst in self._compressed_order()):
+            return torch.zeros_like(q)
+        _lib.require_cuda(q, "q")
+        if q.dtype != torch.float16:
+            raise TypeError("q must be float16")
+        plan = self._attention_plan(q)
+        if plan.jl is None:
+            return plan.run(q, scale=scale)
+        lse = torch.empty(B, Hq, qlen, dtype=torch.float32, device=q.device)
+        out = plan.run(q, scale=scale, lse=lse)
+        out_j, lse_j = plan.jl["att"].run(q, plan.jl["yk"], plan.jl["yv"], scale=scale)
+        return _jl.merge_attention(out, lse, out_j, lse_j)
+
     def inplace_paged_attention(self, q, scale=None):
         """softmax(q K^T * scale) V over every tier, straight from the compressed pages, plus the
         per-page attention mass, importance update and resurrection (memory_manager.py:1317-1524).

@@ -5,6 +5,14 @@ auto-adaptive tier budgets (low-precision key dtypes get shorter FP16/FP8 stages
 heavily-compressed ones, attention_wrapper.py:49-79).  update() pushes the new tokens (page
 formation and the fused demotion cascade run on the GPU) and returns the full K/V rebuilt by the
 page kernels, which is what transformers' attention consumes (attention_wrapper.py:87-88).
+
+With fused_decode=True, update() returns placeholders instead and the "argus" attention
+implementation (registered with transformers' AttentionInterface; load the model with
+attn_implementation="argus") sends each single-token decode step straight to the fused
+mixed-tier kernel over the compressed pages, so the full K/V is never rebuilt (only pages with
+outlier sidecars, and JL pages the fused JL kernel does not take, pass through the manager's fp16
+scratch arena); prefill (several query tokens) and padded batches still rebuild K/V and run
+transformers' SDPA.
 """
 import torch
 
@@ -20,7 +28,7 @@ except ImportError:  # transformers absent: a bare base class keeps the adapter 
 
 class PagedDynamicQuantizedCache(Cache):
     def __init__(self, page_size=4096, max_active_pages=2, max_fp8_pages=2, max_int8_pages=2, max_int4_pages=2,
-                 max_int2_pages=2, max_one_bit_pages=2, sink_tokens=4, threshold_sigma=3.0):
+                 max_int2_pages=2, max_one_bit_pages=2, sink_tokens=4, threshold_sigma=3.0, fused_decode=False):
         try:
             super().__init__(layers=[])
         except TypeError:
@@ -34,6 +42,7 @@ class PagedDynamicQuantizedCache(Cache):
         self.max_one_bit_pages = max_one_bit_pages
         self.sink_tokens = sink_tokens
         self.threshold_sigma = threshold_sigma
+        self.fused_decode = fused_decode
         self.layer_caches = {}
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, layer_idx: int, cache_kwargs=None):
@@ -52,6 +61,13 @@ class PagedDynamicQuantizedCache(Cache):
         cache = self.layer_caches[layer_idx]
         is_anchor = cache_kwargs.get("is_anchor") if cache_kwargs is not None else None
         cache.push_new_tokens(key_states, value_states, is_anchor=is_anchor)
+        if self.fused_decode:
+            # placeholders that carry the layer's cache to argus_attention_forward
+            k = torch.empty(0, dtype=key_states.dtype, device=key_states.device)
+            v = torch.empty(0, dtype=value_states.dtype, device=value_states.device)
+            k._argus_layer_cache = cache
+            v._argus_layer_cache = cache
+            return k, v
         return cache.get_all_keys_values()
 
     def get_seq_length(self, layer_idx: int = 0) -> int:
@@ -69,6 +85,13 @@ class PagedDynamicQuantizedCache(Cache):
         if c.k_buffer is not None:
             n += c.k_buffer.shape[-2]
         return n
+
+    def get_mask_sizes(self, query_length, layer_idx: int = 0):
+        """(kv_length, kv_offset) for transformers' mask builders: every cached token plus the new
+        ones (older transformers pass cache_position instead of the query length)."""
+        if torch.is_tensor(query_length):
+            query_length = query_length.shape[0]
+        return self.get_seq_length(layer_idx) + query_length, 0
 
     def get_usable_length(self, seq_len: int, layer_idx: int = 0) -> int:
         return self.get_seq_length(layer_idx)
@@ -94,3 +117,36 @@ class PagedDynamicQuantizedCache(Cache):
 
     def reset(self):
         self.layer_caches.clear()
+
+
+def argus_attention_forward(module, query, key, value, attention_mask, dropout=0.0, scaling=None, is_causal=None,
+                            **kwargs):
+    """transformers attention function ("argus"): a decode step (one query token, no padding mask)
+    over a PagedDynamicQuantizedCache(fused_decode=True) layer runs the fused mixed-tier kernel on
+    the compressed pages; anything else rebuilds K/V and runs transformers' SDPA.  Returns
+    ([B, q_len, H_q, D], None) as transformers' attention functions do."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    cache = getattr(key, "_argus_layer_cache", None)
+    if cache is None:
+        return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
+                                      is_causal=is_causal, **kwargs)
+    if query.shape[2] == 1 and attention_mask is None and dropout == 0.0 and query.dtype == torch.float16:
+        out = cache.attend(query.contiguous(), scale=scaling)
+        return out.transpose(1, 2).contiguous(), None
+    K, V = cache.get_all_keys_values()
+    return sdpa_attention_forward(module, query, K.to(query.dtype), V.to(query.dtype), attention_mask,
+                                  dropout=dropout, scaling=scaling, is_causal=is_causal, **kwargs)
+
+
+def _register():
+    try:
+        from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+        from transformers.modeling_utils import AttentionInterface
+    except ImportError:
+        return
+    AttentionInterface.register("argus", argus_attention_forward)
+    AttentionMaskInterface.register("argus", sdpa_mask)
+
+
+_register()

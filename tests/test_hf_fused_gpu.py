@@ -1,0 +1,97 @@
+"""Decode attention for transformers without rebuilding K/V: PagedDynamicKVCache.attend() over the
+reference's cascade runs (tests/golden/cascade.npz), and the "argus" attention implementation
+with PagedDynamicQuantizedCache(fused_decode=True) against the materializing adapter.
+
+Reference: the HuggingFace adapter returns get_all_keys_values() to transformers' attention
+(argus_cache/models/attention_wrapper.py:87-88); attend() must give that attention (2e-3 max-abs
+plus the fp16 output's half-ulp, as the other attention tests) and leave the cache as it was."""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from test_manager_gpu import RUNS, counts, host, replay
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", list(RUNS))
+def test_attend_matches_reference_attention_without_side_effects(golden, name, tmp_path):
+    import oracle
+    z = golden("cascade")
+    cache = replay(z, name, tmp_path)
+    q = z[f"{name}/q"]
+    before = (counts(cache), cache.generation_step, cache.total_attention_calls)
+    out = host(cache.attend(torch.from_numpy(q).cuda())).astype(np.float64)
+    ref = oracle.sdpa_f64(q, z[f"{name}/K"], z[f"{name}/V"], 1.0 / math.sqrt(q.shape[-1]))
+    bar = 2e-3 + np.abs(ref) * 2.0 ** -11 + 4e-3 * (len(cache.jl_pages) > 0)
+    assert (np.abs(out - ref) <= bar).all(), np.abs(out - ref).max()
+    assert (counts(cache), cache.generation_step, cache.total_attention_calls) == before
+
+
+def _models(num_layers, hidden, heads, kv_heads, head_dim):
+    transformers = pytest.importorskip("transformers")
+    from argus_b200.models import attention_wrapper  # noqa: F401  registers "argus"
+    cfg = transformers.LlamaConfig(vocab_size=256, hidden_size=hidden, intermediate_size=2 * hidden,
+                                   num_hidden_layers=num_layers, num_attention_heads=heads,
+                                   num_key_value_heads=kv_heads, head_dim=head_dim, max_position_embeddings=1024)
+    torch.manual_seed(0)
+    ref = transformers.LlamaForCausalLM(cfg).cuda().half().eval()
+    cfg2 = transformers.LlamaConfig(**cfg.to_dict())
+    cfg2._attn_implementation = "argus"
+    fused = transformers.LlamaForCausalLM(cfg2).cuda().half().eval()
+    fused.load_state_dict(ref.state_dict())
+    assert fused.config._attn_implementation == "argus"
+    return ref, fused
+
+
+def _cache(fused):
+    from argus_b200.models.attention_wrapper import PagedDynamicQuantizedCache
+    return PagedDynamicQuantizedCache(page_size=16, max_active_pages=1, max_fp8_pages=1, max_int8_pages=1,
+                                      max_int4_pages=1, max_int2_pages=1, max_one_bit_pages=1, sink_tokens=4,
+                                      fused_decode=fused)
+
+
+@pytest.mark.parametrize("num_layers,hidden,heads,kv_heads,head_dim,atol", [
+    (1, 256, 8, 2, 32, 1e-2),    # one layer: both caches receive identical K/V
+    (1, 512, 4, 1, 128, 1e-2),
+    (2, 256, 4, 2, 64, 5e-2),    # two layers: layer 1's K/V differ by the rounding of layer 0's attention
+])
+def test_fused_decode_matches_materializing_adapter(num_layers, hidden, heads, kv_heads, head_dim, atol, tmp_path,
+                                                    monkeypatch):
+    from argus_b200.core.memory_manager import PagedDynamicKVCache
+    monkeypatch.setenv("ARGUS_LOG_LEVEL", "quiet")
+    monkeypatch.chdir(tmp_path)
+    ref_model, fused_model = _models(num_layers, hidden, heads, kv_heads, head_dim)
+    ref_cache, fused_cache = _cache(False), _cache(True)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    ids = torch.randint(0, 256, (1, 130), device="cuda", generator=g)
+    steps = torch.randint(0, 256, (1, 24), device="cuda", generator=g)
+    rebuilt = []
+    real = PagedDynamicKVCache.get_all_keys_values
+
+    def counting(self):
+        rebuilt.append(1)
+        return real(self)
+
+    with torch.no_grad():
+        a = ref_model(ids, past_key_values=ref_cache, use_cache=True).logits
+        b = fused_model(ids, past_key_values=fused_cache, use_cache=True).logits
+        assert (a.float() - b.float()).abs().max() <= 1e-3
+        monkeypatch.setattr(PagedDynamicKVCache, "get_all_keys_values", counting)
+        worst = 0.0
+        for t in range(steps.shape[1]):
+            tok = steps[:, t:t + 1]
+            n_before = len(rebuilt)
+            a = ref_model(tok, past_key_values=ref_cache, use_cache=True).logits
+            assert len(rebuilt) > n_before
+            n_before = len(rebuilt)
+            b = fused_model(tok, past_key_values=fused_cache, use_cache=True).logits
+            assert len(rebuilt) == n_before, "fused decode rebuilt K/V"
+            worst = max(worst, float((a.float() - b.float()).abs().max()))
+    c0 = fused_cache.layer_caches[0]
+    assert len(c0.jl_pages) >= 1 and len(c0.one_bit_pages) == 1
+    assert fused_cache.get_seq_length(0) == ref_cache.get_seq_length(0) == 154
+    assert worst <= atol, worst
