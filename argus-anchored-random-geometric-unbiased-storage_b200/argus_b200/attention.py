@@ -46,7 +46,8 @@ BOUND_SYMBOLS = ("argus_decode_attention", "argus_decode_attention_workspace_siz
 class ArenaC(ctypes.Structure):
     _fields_ = [("tier", ctypes.c_int32), ("layout", ctypes.c_int32), ("k", ctypes.c_void_p),
                 ("v", ctypes.c_void_p), ("bh_stride", ctypes.c_int64), ("record_bytes", ctypes.c_int32),
-                ("page_tokens", ctypes.c_int32)]
+                ("page_tokens", ctypes.c_int32), ("outlier_dir", ctypes.c_void_p), ("dir_slots", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 class ChunkC(ctypes.Structure):
@@ -106,6 +107,10 @@ class KVArena:
         self.k, self.v = k, v
         self.bh_stride, self.record_bytes, self.page_tokens = int(bh_stride), int(record_bytes), int(page_tokens)
         self.D, self.B, self.H, self.slots = int(head_dim), int(batch), int(heads), int(slots)
+        # outlier sidecars: directory [B*H, slots] of correction-block addresses (0 = none), and
+        # the blocks of each slot kept referenced while the directory points at them
+        self.outlier_dir = None
+        self._outlier_blocks = {}
 
     # ---------------------------------------------------------------- record arenas
     @classmethod
@@ -172,9 +177,34 @@ class KVArena:
         return cls(TIER_FP16, LAYOUT_SPLIT_FP16, k, v, bh_stride=k.stride(1) * 2, page_tokens=16, head_dim=D,
                    batch=B, heads=H, slots=(L + 15) // 16)
 
+    # ---------------------------------------------------------------- outlier sidecars
+    def set_outliers(self, slot, blocks, block_addr):
+        """Points the directory of page `slot` at its correction blocks (paged.outlier_corrections:
+        a uint8 buffer and the [B*H] int64 block addresses), so the fused attention applies the
+        page's sidecars while reading it compressed."""
+        if self.layout != LAYOUT_RECORD or self.tier == TIER_FP16:
+            raise ValueError("outlier sidecars belong to quantized record arenas")
+        if self.outlier_dir is None:
+            self.outlier_dir = torch.zeros(self.B * self.H, self.slots, dtype=torch.int64, device=self.k.device)
+        self.outlier_dir[:, slot].copy_(block_addr)
+        self._outlier_blocks[slot] = blocks
+
+    def clear_outliers(self, slot=None):
+        """Drops the sidecar corrections of page `slot` (of every page when slot is None)."""
+        if self.outlier_dir is None:
+            return
+        if slot is None:
+            self.outlier_dir = None
+            self._outlier_blocks.clear()
+        else:
+            self.outlier_dir[:, slot].zero_()
+            self._outlier_blocks.pop(slot, None)
+
     def c_struct(self):
+        d = self.outlier_dir
         return ArenaC(self.tier, self.layout, self.k.data_ptr(), self.v.data_ptr() if self.v is not None else None,
-                      self.bh_stride, self.record_bytes, self.page_tokens)
+                      self.bh_stride, self.record_bytes, self.page_tokens, d.data_ptr() if d is not None else None,
+                      self.slots if d is not None else 0, 0)
 
 
 def chunk_capacity(arena, head_dim):
@@ -310,6 +340,9 @@ class AttentionPlan:
         self.chunks_dev = torch.from_numpy(raw).to(self.device)
         self.splits_dev = torch.from_numpy(bounds.astype(np.int32)).to(self.device)
         self._arena_c = (ArenaC * MAX_ARENAS)(*[a.c_struct() for a in self.arenas])
+        # the outlier directories the launch reads stay alive with the plan
+        self._outlier_dirs = [a.outlier_dir for a in self.arenas]
+        self.pages = list(pages)
         self._shape = ShapeC(self.B, self.Hkv, self.G, self.qlen, self.D, n_splits, len(self.arenas), self.n_chunks,
                              1.0 / math.sqrt(self.D), ATTN_PRECISE_PV if precise_pv else 0)
         ws = _bind().argus_decode_attention_workspace_size(ctypes.byref(self._shape))

@@ -12,7 +12,8 @@ import torch
 from . import _lib
 from .attention import ArenaC, KVArena
 
-BOUND_SYMBOLS = ("argus_page_quantize", "argus_page_requant", "argus_page_dequantize")
+BOUND_SYMBOLS = ("argus_page_quantize", "argus_page_requant", "argus_page_dequantize", "argus_outlier_blocks_bytes",
+                 "argus_outlier_corrections")
 
 
 def _bind():
@@ -25,8 +26,14 @@ def _bind():
                                          ctypes.c_void_p]
         L.argus_page_dequantize.argtypes = [P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int, ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
+        L.argus_outlier_blocks_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64]
+        L.argus_outlier_corrections.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                                ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         for f in BOUND_SYMBOLS:
             getattr(L, f).restype = ctypes.c_int
+        L.argus_outlier_blocks_bytes.restype = ctypes.c_int64
         L._argus_pages_bound = True
     return L
 
@@ -105,3 +112,38 @@ def outliers_to_coo(mask, outv):
         _lib.call("argus_outliers_to_coo", _lib.ptr(m), _lib.ptr(o), B, H, P, D, _lib.ptr(idx), _lib.ptr(vals), n,
                   _lib.ptr(count), st)
     return idx[:n], vals[:n]
+
+
+def outlier_corrections(arena: KVArena, slot, k_idx, k_val, v_idx, v_val, k_deq=None, v_deq=None):
+    """Correction blocks of page `slot` of a quantized record arena from its COO sidecars
+    (row-major (b, h, t, d) int16 indices and fp16 values, as outliers_to_coo returns them): returns
+    (blocks, block_addr) for KVArena.set_outliers.  k_deq / v_deq: the page dequantized without its
+    sidecars ([B, H, P, D] fp16); computed here when not given."""
+    if k_deq is None:
+        k_deq, v_deq = dequantize_page(arena, slot)
+    dev = arena.k.device
+    empty_i = torch.zeros(0, 4, dtype=torch.int16, device=dev)
+    empty_v = torch.zeros(0, dtype=torch.float16, device=dev)
+    k_idx = (k_idx if k_idx is not None else empty_i).contiguous()
+    v_idx = (v_idx if v_idx is not None else empty_i).contiguous()
+    k_val = (k_val if k_val is not None else empty_v).contiguous().view(torch.float16).reshape(-1)
+    v_val = (v_val if v_val is not None else empty_v).contiguous().view(torch.float16).reshape(-1)
+    nk, nv = k_idx.shape[0], v_idx.shape[0]
+    L = _bind()
+    BH = arena.B * arena.H
+    nbytes = L.argus_outlier_blocks_bytes(BH, arena.page_tokens, nk, nv)
+    blocks = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    addr = torch.empty(BH, dtype=torch.int64, device=dev)
+    k_deq, v_deq = k_deq.contiguous(), v_deq.contiguous()
+    _check("argus_outlier_corrections", L.argus_outlier_corrections(
+        k_idx.data_ptr() if nk else None, k_val.data_ptr() if nk else None, nk,
+        v_idx.data_ptr() if nv else None, v_val.data_ptr() if nv else None, nv,
+        k_deq.data_ptr(), v_deq.data_ptr(), arena.B, arena.H, arena.page_tokens, arena.D, blocks.data_ptr(),
+        addr.data_ptr(), _lib.stream_handle(dev)))
+    return blocks, addr
+
+
+def attach_outliers(arena: KVArena, slot, k_idx, k_val, v_idx, v_val):
+    """Builds page `slot`'s correction blocks and points the arena's directory at them."""
+    blocks, addr = outlier_corrections(arena, slot, k_idx, k_val, v_idx, v_val)
+    arena.set_outliers(slot, blocks, addr)

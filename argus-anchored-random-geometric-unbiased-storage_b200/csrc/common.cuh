@@ -17,10 +17,11 @@
 int argus_set_cuda_error(cudaError_t e);
 // Records a message for argus_last_error() and returns `status`.
 int argus_set_error(int status, const char* msg);
-// Read and clear the device status words of the JL contraction (jl.cu) and the JL attention
-// (jl_attention.cu) kernels after synchronising `st`.
+// Read and clear the device status words of the JL contraction (jl.cu), the JL attention
+// (jl_attention.cu) and the outlier-correction builder (sidecar.cu) after synchronising `st`.
 int argus_jl_take_status(int* status, cudaStream_t st);
 int argus_jla_take_status(int* status, cudaStream_t st);
+int argus_side_take_status(int* status, cudaStream_t st);
 
 static inline bool argus_aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

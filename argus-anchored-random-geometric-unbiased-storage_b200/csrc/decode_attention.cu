@@ -633,16 +633,107 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
     }
 }
 
-// Processes one staged tile: scores, online softmax, PV.
-template <int D, int TIER, bool PRECISE, bool MASS>
+// ------------------------------------------------------------------------------ outlier sidecars
+// The reference overwrites each sidecar position of a dequantized page with the sidecar's fp16 value
+// before attending.  Here the page stays compressed: the tile's scores get delta * q for every key
+// outlier, and its output gets p * delta for every value outlier, delta = sidecar value minus the
+// dequantized value (argus_outlier_corrections builds the per-page blocks).
+
+// Where the correction block of a tile's page is: the directory entry of its (b, h, slot), the
+// tile's index within the page and the page's tile count.
+struct OutlierRef {
+    const unsigned long long* entry;
+    int ti, nt;
+};
+
+// q[n][d] of the CTA's query group from the Q^T fragments in shared memory (load_qfrags layout:
+// lane 4n + d/(D/4) holds dims 4c, 4c+2 in word 2c and 4c+1, 4c+3 in word 2c+1 of its block).
+template <int D>
+__device__ __forceinline__ float q_at(uint32_t qs, int n, int d) {
+    constexpr int KC = D / 16;
+    constexpr int V = (2 * KC) % 4 == 0 ? 4 : 2;
+    const int src = 4 * n + d / (D / 4), dd = d % (D / 4);
+    const int j = 2 * (dd >> 2) + (dd & 1), half = (dd >> 1) & 1;
+    const uint32_t addr = qs + (uint32_t)((((j / V) * 32 + src) * V + (j % V)) * 4 + 2 * half);
+    unsigned short h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(addr));
+    return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ const uint32_t* outlier_block(const OutlierRef& r) {
+    return reinterpret_cast<const uint32_t*>(__ldg(r.entry));
+}
+
+// x[.] (log2-domain scores of tokens 2g4, 2g4+1 for queries 2t4, 2t4+1) += scale_log2 * delta * q.
+template <int D>
+__device__ __forceinline__ void apply_k_outliers(const OutlierRef& r, int g4, int t4, uint32_t qs, float scale_log2,
+                                                 int ntok, float (&x)[4]) {
+    const uint32_t* hdr = outlier_block(r);
+    if (!hdr) return;
+    const int e0 = (int)__ldg(hdr + r.ti), e1 = (int)__ldg(hdr + r.ti + 1);
+    const uint2* ent = reinterpret_cast<const uint2*>(hdr + 2 * (r.nt + 1));
+    for (int i = e0; i < e1; ++i) {
+        const uint2 raw = __ldg(ent + i);
+        const int tok = (int)(raw.x & 0xffffu) - 16 * r.ti, d = (int)(raw.x >> 16);
+        if (tok < 0 || tok >= ntok || d >= D) continue;
+        if ((tok >> 1) == g4) {
+            const float c = __uint_as_float(raw.y) * scale_log2;
+            const float q0 = q_at<D>(qs, 2 * t4, d), q1 = q_at<D>(qs, 2 * t4 + 1, d);
+            if (tok & 1) { x[2] += c * q0; x[3] += c * q1; }
+            else         { x[0] += c * q0; x[1] += c * q1; }
+        }
+    }
+}
+
+// O^T[d][n] += p[n][tok] * delta for every value outlier (tok, d); p = 2^(x - m) as the tile's
+// weights (the owner of O^T[d][.] is lane 4 (d / (D/8)) + t4, the scores of token tok sit in lane
+// 4 (tok / 2) + t4).
+template <int D>
+__device__ __forceinline__ void apply_v_outliers(const OutlierRef& r, int g4, int t4, int ntok, const SoftmaxState& st,
+                                                 const float (&x)[4], float (&o)[D / 16][4]) {
+    const uint32_t* hdr = outlier_block(r);
+    if (!hdr) return;
+    const int e0 = (int)__ldg(hdr + r.nt + 1 + r.ti), e1 = (int)__ldg(hdr + r.nt + 2 + r.ti);
+    const uint2* ent = reinterpret_cast<const uint2*>(hdr + 2 * (r.nt + 1));
+    for (int i = e0; i < e1; ++i) {
+        const uint2 raw = __ldg(ent + i);
+        const int tok = (int)(raw.x & 0xffffu) - 16 * r.ti, d = (int)(raw.x >> 16);
+        if (tok < 0 || tok >= ntok || d >= D) continue;
+        const int src = 4 * (tok >> 1) + t4;
+        const float xa = __shfl_sync(0xffffffffu, (tok & 1) ? x[2] : x[0], src);
+        const float xb = __shfl_sync(0xffffffffu, (tok & 1) ? x[3] : x[1], src);
+        if (g4 == d / (D / 8)) {
+            const float delta = __uint_as_float(raw.y);
+            const float pa = exp2f(xa - st.m[0]) * delta, pb = exp2f(xb - st.m[1]) * delta;
+            const int dd = d % (D / 8);
+            // register-resident update: every o[t][.] takes a 0/1-weighted FMA (no dynamic index)
+            const float ea = (dd & 1) ? 0.f : pa, eb = (dd & 1) ? 0.f : pb;
+            const float fa = (dd & 1) ? pa : 0.f, fb = (dd & 1) ? pb : 0.f;
+#pragma unroll
+            for (int t = 0; t < D / 16; ++t) {
+                const float w = (t == (dd >> 1)) ? 1.f : 0.f;
+                o[t][0] = fmaf(w, ea, o[t][0]);
+                o[t][1] = fmaf(w, eb, o[t][1]);
+                o[t][2] = fmaf(w, fa, o[t][2]);
+                o[t][3] = fmaf(w, fb, o[t][3]);
+            }
+        }
+    }
+}
+
+// Processes one staged tile: scores, online softmax, PV (OUT: with the page's outlier corrections).
+template <int D, int TIER, bool PRECISE, bool MASS, bool OUT>
 __device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, uint32_t qs, float scale_log2,
-                                             SoftmaxState& st, float (&o)[D / 16][4], float* mass_out) {
+                                             SoftmaxState& st, float (&o)[D / 16][4], float* mass_out,
+                                             const OutlierRef& orf) {
     TokScale tk[1], tv[1];
     float x[1][4];
     load_tok_scales<TIER>(tp, g4, t4, tk[0], tv[0]);
     tile_scores<D, TIER>(tp, g4, t4, tk[0], qs, scale_log2, x[0]);
+    if constexpr (OUT) apply_k_outliers<D>(orf, g4, t4, qs, scale_log2, tp.ntok, x[0]);
     uint32_t b01[1], b23[1], c01[1], c23[1];
     softmax_update<D / 16, 1, PRECISE, MASS>(x, st, o, b01, b23, c01, c23, mass_out);
+    if constexpr (OUT) apply_v_outliers<D>(orf, g4, t4, tp.ntok, st, x[0], o);
     tile_pv<D, TIER, PRECISE>(tp, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
 }
 
@@ -674,7 +765,9 @@ __device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int 
     }
 }
 
-template <int D, bool PRECISE, bool MASS>
+// SIDE: some arena carries outlier sidecars (a separate instantiation, so launches without them run
+// the plain kernel's register allocation).
+template <int D, bool PRECISE, bool MASS, bool SIDE>
 __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(const __grid_constant__ Params p) {
     constexpr int KC = D / 16;
     constexpr int STAGE = stage_bytes(D);
@@ -828,9 +921,13 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
         if constexpr (MASS)
             mass_base = p.tile_lse + (((int64_t)bh * p.nqg + qg) * p.n_chunks + (first + j * kPairs)) * 16 * kQ;
         const bool rec16 = ar.layout == ARGUS_LAYOUT_RECORD && ar.page_tokens == 16;
+        // outlier corrections: directory row of this (b, h), or null
+        const unsigned long long* odir =
+            (SIDE && ar.outlier_dir)
+                ? reinterpret_cast<const unsigned long long*>(ar.outlier_dir) + (int64_t)bh * ar.dir_slots
+                : nullptr;
         switch (ar.tier) {
-#define ARGUS_TILE_CASE(T)                                                                                        \
-    case T: {                                                                                                     \
+#define ARGUS_TILE_LOOPS(T, OUT)                                                                                  \
         if (rec16) {                                                                                              \
             /* one full 16-token page per record: compile-time offsets */                                        \
             constexpr int RB = record_bytes(T, 16, D), PB = payload_bytes(T, 16, D);                              \
@@ -844,8 +941,10 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
                 tp.km = reinterpret_cast<const __half*>(r + 2 * PB + 64);                                         \
                 tp.vm = reinterpret_cast<const __half*>(r + 2 * PB + 96);                                         \
                 tp.ntok = 16;                                                                                     \
-                process_tile<D, T, PRECISE, MASS>(tp, g4, t4, qs, p.scale_log2, st, o,                            \
-                                                  mass_base ? mass_base + i * kQ : nullptr);                      \
+                OutlierRef orf;                                                                                   \
+                if constexpr (OUT) { orf.entry = odir + ch.slot0 + i; orf.ti = 0; orf.nt = 1; }                  \
+                process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, st, o,                       \
+                                                       mass_base ? mass_base + i * kQ : nullptr, orf);            \
             }                                                                                                     \
         } else {                                                                                                  \
             const ChunkView cv = chunk_view<D>(ar, n);                                                            \
@@ -859,19 +958,42 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
                 tp.km = reinterpret_cast<const __half*>(sb + cv.km_off + so);                                     \
                 tp.vm = reinterpret_cast<const __half*>(sb + cv.vm_off + so);                                     \
                 tp.ntok = (i == n - 1) ? ch.ntok_last : cv.ntok_full;                                             \
-                process_tile<D, T, PRECISE, MASS>(tp, g4, t4, qs, p.scale_log2, st, o,                            \
-                                                  mass_base ? mass_base + i * kQ : nullptr);                      \
+                OutlierRef orf;                                                                                   \
+                if constexpr (OUT) {                                                                              \
+                    if (whole_records(ar.layout, ar.page_tokens)) { /* tile i is page slot0 + i */               \
+                        orf.entry = odir + ch.slot0 + i;                                                          \
+                        orf.ti = 0;                                                                               \
+                        orf.nt = 1;                                                                               \
+                    } else { /* tile i is tokens tok0 + 16 i .. of page slot0 */                                 \
+                        orf.entry = odir + ch.slot0;                                                              \
+                        orf.ti = (ch.tok0 >> 4) + i;                                                              \
+                        orf.nt = (ar.page_tokens + 15) >> 4;                                                      \
+                    }                                                                                             \
+                }                                                                                                 \
+                process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, st, o,                       \
+                                                       mass_base ? mass_base + i * kQ : nullptr, orf);            \
             }                                                                                                     \
+        }
+#define ARGUS_TILE_CASE(T)                                                                                        \
+    case T: {                                                                                                     \
+        if (SIDE && odir) {                                                                                       \
+            ARGUS_TILE_LOOPS(T, SIDE)                                                                             \
+        } else {                                                                                                  \
+            ARGUS_TILE_LOOPS(T, false)                                                                            \
         }                                                                                                         \
         break;                                                                                                    \
     }
-            ARGUS_TILE_CASE(ARGUS_TIER_FP16)
+            case ARGUS_TIER_FP16: {  // fp16 arenas carry no sidecars
+                ARGUS_TILE_LOOPS(ARGUS_TIER_FP16, false)
+                break;
+            }
             case ARGUS_TIER_FP8SIM:  // same dequantization as INT8: fp16(q * s)
             ARGUS_TILE_CASE(ARGUS_TIER_INT8)
             ARGUS_TILE_CASE(ARGUS_TIER_INT4)
             ARGUS_TILE_CASE(ARGUS_TIER_INT2)
             ARGUS_TILE_CASE(ARGUS_TIER_1BIT)
 #undef ARGUS_TILE_CASE
+#undef ARGUS_TILE_LOOPS
             default: break;
         }
         __syncwarp();
@@ -969,8 +1091,12 @@ int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
     static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kPairs * kStages * stage_bytes(D),
                   "merge buffer must fit in the stage memory");
     const bool mass = prm.tile_lse != nullptr;
-    auto kern = precise ? (mass ? decode_attn_kernel<D, true, true> : decode_attn_kernel<D, true, false>)
-                        : (mass ? decode_attn_kernel<D, false, true> : decode_attn_kernel<D, false, false>);
+    bool side = false;
+    for (int i = 0; i < ARGUS_MAX_ARENAS; ++i) side |= prm.arenas[i].outlier_dir != nullptr;
+    auto kern = side ? (precise ? (mass ? decode_attn_kernel<D, true, true, true> : decode_attn_kernel<D, true, false, true>)
+                                : (mass ? decode_attn_kernel<D, false, true, true> : decode_attn_kernel<D, false, false, true>))
+                     : (precise ? (mass ? decode_attn_kernel<D, true, true, false> : decode_attn_kernel<D, true, false, false>)
+                                : (mass ? decode_attn_kernel<D, false, true, false> : decode_attn_kernel<D, false, false, false>));
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
     // all of the unified L1/shared array as shared memory, so ctas_per_sm(D) CTAs fit
@@ -1048,6 +1174,12 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
         } else {
             return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad arena layout");
         }
+        if (a.outlier_dir) {
+            if (a.layout != ARGUS_LAYOUT_RECORD || a.tier == ARGUS_TIER_FP16)
+                return argus_set_error(ARGUS_ERR_UNSUPPORTED, "outlier sidecars belong to quantized record arenas");
+            if (a.dir_slots <= 0 || !argus_aligned(a.outlier_dir, 8))
+                return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "outlier directory needs dir_slots > 0, 8-byte alignment");
+        }
         prm.arenas[i] = a;
     }
     prm.chunks = chunks;
@@ -1091,11 +1223,12 @@ int argus_device_status(int* status, argus_stream_t stream) {
     if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(da::g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
-    int jl = 0, jla = 0;
+    int jl = 0, jla = 0, side = 0;
     int rc = argus_jl_take_status(&jl, (cudaStream_t)stream);
     if (rc == ARGUS_OK) rc = argus_jla_take_status(&jla, (cudaStream_t)stream);
+    if (rc == ARGUS_OK) rc = argus_side_take_status(&side, (cudaStream_t)stream);
     if (rc != ARGUS_OK) return rc;
-    *status = v != 0 ? v : (jl != 0 ? jl : jla);
+    *status = v != 0 ? v : (jl != 0 ? jl : (jla != 0 ? jla : side));
     return ARGUS_OK;
 }
 

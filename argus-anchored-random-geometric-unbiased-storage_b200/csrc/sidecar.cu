@@ -66,9 +66,138 @@ outliers_to_coo_kernel(const uint8_t* __restrict__ mask, const __half* __restric
     }
 }
 
+// ------------------------------------------------------- correction blocks for the fused attention
+// Layout of one (b, h) block: uint32 k_off[NT + 1], uint32 v_off[NT + 1], argus_outlier entries[]
+// (key entries, then value entries), at byte offset
+//     bh * 8 (NT + 1) + 8 (key entries of earlier (b, h) + value entries of earlier (b, h))
+// of the page's buffer.  Entries of a row-major sidecar are already grouped by (b, h) and sorted by
+// token, so every offset is a binary search over the sidecar.
+
+__device__ int g_side_status = 0;
+
+__device__ __forceinline__ int64_t coo_row(const int16_t* idx, int64_t i, int H, int P) {
+    return ((int64_t)idx[4 * i] * H + idx[4 * i + 1]) * P + idx[4 * i + 2];
+}
+
+// flag |= 1 when an entry lies outside [B,H,P,D] or precedes its predecessor in row-major order.
+__global__ void outlier_validate_kernel(const int16_t* __restrict__ idx, int64_t n, int B, int H, int P, int D,
+                                        int* flag) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int b = idx[4 * i], h = idx[4 * i + 1], t = idx[4 * i + 2], d = idx[4 * i + 3];
+        bool bad = b < 0 || b >= B || h < 0 || h >= H || t < 0 || t >= P || d < 0 || d >= D;
+        if (!bad && i > 0) {
+            const int64_t prev = coo_row(idx, i - 1, H, P) * D + idx[4 * (i - 1) + 3];
+            bad = prev >= coo_row(idx, i, H, P) * D + d;
+        }
+        if (bad) atomicOr(flag, 1);
+    }
+}
+
+// first i in [lo, hi) with row(i) >= key (row = (b*H + h)*P + t)
+__device__ __forceinline__ int64_t lower_row(const int16_t* idx, int64_t lo, int64_t hi, int64_t key, int H, int P) {
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (coo_row(idx, mid, H, P) < key) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+// One CTA per (b, h).
+__global__ void outlier_blocks_kernel(const int16_t* __restrict__ k_idx, const __half* __restrict__ k_val, int64_t nk,
+                                      const int16_t* __restrict__ v_idx, const __half* __restrict__ v_val, int64_t nv,
+                                      const __half* __restrict__ k_deq, const __half* __restrict__ v_deq, int H,
+                                      int P, int D, unsigned char* __restrict__ blocks,
+                                      unsigned long long* __restrict__ block_addr, const int* __restrict__ flag) {
+    const int bh = blockIdx.x;
+    if (*flag) {
+        if (threadIdx.x == 0) {
+            block_addr[bh] = 0ull;
+            if (bh == 0) atomicExch(&g_side_status, (int)ARGUS_ERR_INVALID_ARGUMENT);
+        }
+        return;
+    }
+    const int NT = (P + 15) >> 4;
+    const int64_t r0 = (int64_t)bh * P, r1 = r0 + P;
+    const int64_t kb = lower_row(k_idx, 0, nk, r0, H, P), ke = lower_row(k_idx, kb, nk, r1, H, P);
+    const int64_t vb = lower_row(v_idx, 0, nv, r0, H, P), ve = lower_row(v_idx, vb, nv, r1, H, P);
+    const int64_t nkb = ke - kb, nvb = ve - vb;
+    unsigned char* blk = blocks + (int64_t)bh * 8 * (NT + 1) + 8 * (kb + vb);
+    if (threadIdx.x == 0) block_addr[bh] = (nkb + nvb) > 0 ? (unsigned long long)(uintptr_t)blk : 0ull;
+    if (nkb + nvb == 0) return;
+    uint32_t* hdr = reinterpret_cast<uint32_t*>(blk);
+    for (int i = threadIdx.x; i <= NT; i += blockDim.x) {
+        const int64_t tk = min((int64_t)P, (int64_t)16 * i);
+        hdr[i] = (uint32_t)(lower_row(k_idx, kb, ke, r0 + tk, H, P) - kb);
+        hdr[NT + 1 + i] = (uint32_t)(nkb + lower_row(v_idx, vb, ve, r0 + tk, H, P) - vb);
+    }
+    argus_outlier* ent = reinterpret_cast<argus_outlier*>(hdr + 2 * (NT + 1));
+    const int64_t deq_bh = (int64_t)bh * P * D;
+    for (int64_t e = threadIdx.x; e < nkb + nvb; e += blockDim.x) {
+        const bool isv = e >= nkb;
+        const int16_t* idx = isv ? v_idx : k_idx;
+        const int64_t i = isv ? vb + (e - nkb) : kb + e;
+        const int t = idx[4 * i + 2], d = idx[4 * i + 3];
+        const float ov = __half2float(isv ? v_val[i] : k_val[i]);
+        const float dq = __half2float((isv ? v_deq : k_deq)[deq_bh + (int64_t)t * D + d]);
+        argus_outlier o;
+        o.tok = (uint16_t)t;
+        o.dim = (uint16_t)d;
+        o.delta = ov - dq;
+        ent[e] = o;
+    }
+}
+
 }  // namespace argus
 
+int argus_side_take_status(int* status, cudaStream_t st) {
+    int v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, argus::g_side_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(argus::g_side_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    *status = v;
+    return ARGUS_OK;
+}
+
 extern "C" {
+
+int64_t argus_outlier_blocks_bytes(int32_t bh, int32_t page_tokens, int64_t nk, int64_t nv) {
+    if (bh <= 0 || page_tokens <= 0 || nk < 0 || nv < 0) return 0;
+    return (int64_t)bh * 8 * ((page_tokens + 15) / 16 + 1) + 8 * (nk + nv) + 16;
+}
+
+int argus_outlier_corrections(const int16_t* k_idx, const uint16_t* k_val, int64_t nk, const int16_t* v_idx,
+                              const uint16_t* v_val, int64_t nv, const uint16_t* k_deq, const uint16_t* v_deq,
+                              int32_t batch, int32_t heads, int32_t page_tokens, int32_t head_dim, void* blocks,
+                              uint64_t* block_addr, argus_stream_t stream) {
+    if (batch <= 0 || heads <= 0 || page_tokens <= 0 || head_dim <= 0 || nk < 0 || nv < 0 || page_tokens > 32767 ||
+        head_dim > 32767 || (int64_t)batch * heads > 65535)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad sizes");
+    if (!block_addr || !k_deq || !v_deq || !blocks || (nk > 0 && (!k_idx || !k_val)) || (nv > 0 && (!v_idx || !v_val)))
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    if (!argus_aligned(blocks, 16) || !argus_aligned(block_addr, 8) || (nk > 0 && !argus_aligned(k_idx, 8)) ||
+        (nv > 0 && !argus_aligned(v_idx, 8)) || !argus_aligned(k_val ? (const void*)k_val : blocks, 2) ||
+        !argus_aligned(v_val ? (const void*)v_val : blocks, 2))
+        return argus_set_error(ARGUS_ERR_MISALIGNED, "blocks must be 16-byte aligned, indices 8-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    // the validation flag: the 16 bytes past the last entry (counted by argus_outlier_blocks_bytes)
+    int* flag = reinterpret_cast<int*>(static_cast<unsigned char*>(blocks) +
+                                       argus_outlier_blocks_bytes(batch * heads, page_tokens, nk, nv) - 16);
+    cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), st);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    if (nk > 0)
+        argus::outlier_validate_kernel<<<argus_grid_cap((nk + 255) / 256), 256, 0, st>>>(k_idx, nk, batch, heads,
+                                                                                         page_tokens, head_dim, flag);
+    if (nv > 0)
+        argus::outlier_validate_kernel<<<argus_grid_cap((nv + 255) / 256), 256, 0, st>>>(v_idx, nv, batch, heads,
+                                                                                         page_tokens, head_dim, flag);
+    argus::outlier_blocks_kernel<<<batch * heads, 256, 0, st>>>(
+        k_idx, reinterpret_cast<const __half*>(k_val), nk, v_idx, reinterpret_cast<const __half*>(v_val), nv,
+        reinterpret_cast<const __half*>(k_deq), reinterpret_cast<const __half*>(v_deq), heads, page_tokens, head_dim,
+        static_cast<unsigned char*>(blocks), reinterpret_cast<unsigned long long*>(block_addr), flag);
+    ARGUS_CHECK_LAUNCH();
+    return ARGUS_OK;
+}
 
 int argus_scatter_coo(uint16_t* out, int64_t out_bh_stride, int64_t out_tok0, int B, int H, int P, int D,
                       const int16_t* idx, const uint16_t* vals, int64_t n, argus_stream_t stream) {

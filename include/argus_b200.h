@@ -146,6 +146,36 @@ int argus_scatter_coo(uint16_t* out, int64_t out_bh_stride, int64_t out_tok0, in
 int argus_outliers_to_coo(const uint8_t* mask, const uint16_t* outv, int B, int H, int P, int D, int16_t* idx_out,
                           uint16_t* vals_out, int64_t capacity, int64_t* count_out, argus_stream_t stream);
 
+/* One outlier of a page as the fused attention applies it: the page's rebuilt value at (tok, dim)
+ * (the sidecar's fp16 value, scattered over the dequantized page by core/memory_manager.py:1190-1199,
+ * 1402-1409) minus the dequantized value there, in fp32. */
+typedef struct argus_outlier {
+    uint16_t tok;  /* token within the page */
+    uint16_t dim;
+    float delta;
+} argus_outlier;
+
+/* Bytes of the correction blocks of one page (argus_outlier_corrections) for bh = B*H (b, h)
+ * pairs, nk key and nv value sidecar entries (the last 16 bytes are the builder's own scratch). */
+int64_t argus_outlier_blocks_bytes(int32_t bh, int32_t page_tokens, int64_t nk, int64_t nv);
+/* Correction blocks of one quantized page for the fused decode attention, so that the attention
+ * reads the page compressed and still sees its sidecars (the reference scatters them over the
+ * dequantized page before attending, core/memory_manager.py:1402-1409).  Inputs: the page's key and
+ * value sidecars as COO (b, h, t, d) int16 indices in row-major order (torch.nonzero order, as
+ * argus_outliers_to_coo writes them) with fp16 values; k_deq / v_deq: the page dequantized without
+ * its sidecars, [B][H][P][D] fp16 (argus_page_dequantize).  Writes into `blocks` (16-byte aligned,
+ * argus_outlier_blocks_bytes) one block per (b, h) with entries,
+ *     uint32 k_off[NT + 1], uint32 v_off[NT + 1], argus_outlier entries[]   (NT = ceil(P / 16)),
+ * k_off[i] / v_off[i] being the first key / value entry of 16-token tile i (k_off[NT] = key count,
+ * value entries follow the key entries and v_off counts from the block's first entry), and
+ * block_addr[b*H + h] = the block's device address, or 0 for a (b, h) without entries.  A sidecar
+ * with an index outside [B, H, P, D] or out of row-major order makes every address 0 and sets the
+ * status word argus_device_status reports (ARGUS_ERR_INVALID_ARGUMENT). */
+int argus_outlier_corrections(const int16_t* k_idx, const uint16_t* k_val, int64_t nk, const int16_t* v_idx,
+                              const uint16_t* v_val, int64_t nv, const uint16_t* k_deq, const uint16_t* v_deq,
+                              int32_t batch, int32_t heads, int32_t page_tokens, int32_t head_dim, void* blocks,
+                              uint64_t* block_addr, argus_stream_t stream);
+
 /* --------------------------------------------------------------------------- JL archive */
 
 /* C[b] = A . X[b] for a shared fp16 operator A [M][K] and fp16 pages X[b] [K][N], fp32
@@ -238,6 +268,12 @@ typedef struct argus_kv_arena {
     int64_t bh_stride;    /* bytes between consecutive (b, h) blocks */
     int32_t record_bytes; /* bytes per record (record layout) */
     int32_t page_tokens;  /* tokens per slot: page size for records, 16 for the split layout */
+    /* Outlier sidecars of the arena's pages (quantized record arenas only; null = none):
+     * outlier_dir[(b*H_kv + h)*dir_slots + slot] is the device address of that page's
+     * correction block for (b, h), as argus_outlier_corrections writes it, or 0. */
+    const uint64_t* outlier_dir;
+    int32_t dir_slots;
+    int32_t reserved;
 } argus_kv_arena;
 
 /* A run of up to 16 consecutive 16-token tiles of one arena, staged as one unit:
@@ -327,8 +363,9 @@ int argus_decode_attention_noalloc(const argus_attn_shape* shape, const argus_kv
 /* Bytes of the built-in scratch of argus_decode_attention_noalloc. */
 int64_t argus_decode_attention_noalloc_capacity(void);
 
-/* Reads (and clears) the device-side status word that bounded waits in the kernels set on a
- * timeout; writes ARGUS_OK or ARGUS_ERR_TIMEOUT to *status after synchronising `stream`. */
+/* Reads (and clears) the device-side status words that bounded waits in the kernels set on a
+ * timeout, and argus_outlier_corrections on a bad sidecar; writes ARGUS_OK, ARGUS_ERR_TIMEOUT or
+ * ARGUS_ERR_INVALID_ARGUMENT to *status after synchronising `stream`. */
 int argus_device_status(int* status, argus_stream_t stream);
 
 #ifdef __cplusplus

@@ -26,8 +26,9 @@ def golden_pages(z, case):
     return pages
 
 
-def arenas_from_pages(pages, device="cuda"):
-    """Writes each tier's pages into a record arena and returns (arenas, page list)."""
+def arenas_from_pages(pages, device="cuda", sidecars=True):
+    """Writes each tier's pages into a record arena and returns (arenas, page list); pages with COO
+    sidecars get their outlier corrections attached (sidecars=True)."""
     from argus_b200 import attention as A
 
     tier_id = {"fp16": A.TIER_FP16, "fp8": A.TIER_FP8SIM, "int8": A.TIER_INT8, "int4": A.TIER_INT4,
@@ -51,14 +52,27 @@ def arenas_from_pages(pages, device="cuda"):
                           stack("key_min"), stack("value_min"))
         else:
             a.write_pages(0, stack("key_packed"), stack("value_packed"), stack("key_scales"), stack("value_scales"))
+        if sidecars and tier != "fp16":
+            from argus_b200 import paged
+            for j, pg in enumerate(lst):
+                ki, vi = pg.get("key_out_indices"), pg.get("value_out_indices")
+                if (ki is None or not len(ki)) and (vi is None or not len(vi)):
+                    continue
+                t = lambda key: torch.from_numpy(np.ascontiguousarray(pg[key])).to(device) \
+                    if pg.get(key) is not None and len(pg[key]) else None  # noqa: E731
+                paged.attach_outliers(a, j, t("key_out_indices"), t("key_out_values"), t("value_out_indices"),
+                                      t("value_out_values"))
         ai = len(arenas)
         arenas.append(a)
         plist += [(ai, j, P) for j in range(len(lst))]
     return arenas, plist
 
 
-def random_pages(rng, tiers_tokens, B, Hkv, D, P, outlier_frac=0.01):
-    """Seeded fp16 pages quantized by the CPU oracle: {tier: [page dicts]}, tokens per tier."""
+def random_pages(rng, tiers_tokens, B, Hkv, D, P, outlier_frac=0.01, sigma=None, shared_sidecar=False):
+    """Seeded fp16 pages quantized by the CPU oracle: {tier: [page dicts]}, tokens per tier.  With
+    sigma, quantized pages first have their outliers isolated into COO sidecars, as the reference's
+    first demotion does (shared_sidecar: the V sidecar is the K sidecar, as the reference's INT8 and
+    lower tiers store it)."""
     pages = {}
     for tier, ntok in tiers_tokens:
         lst = []
@@ -70,6 +84,15 @@ def random_pages(rng, tiers_tokens, B, Hkv, D, P, outlier_frac=0.01):
                 t[m] = rng.laplace(0, 4, m.sum())
             k, v = k.astype(np.float16), v.astype(np.float16)
             pg = {}
+            if sigma is not None and tier != "fp16":
+                kn, ko, km = oracle.isolate_outliers(k, sigma)
+                vn, vo, vm = oracle.isolate_outliers(v, sigma)
+                pg["key_out_indices"], pg["key_out_values"] = oracle.sidecar(km, ko)
+                if shared_sidecar:
+                    pg["value_out_indices"], pg["value_out_values"] = pg["key_out_indices"], pg["key_out_values"]
+                else:
+                    pg["value_out_indices"], pg["value_out_values"] = oracle.sidecar(vm, vo)
+                k, v = kn, vn
             if tier == "fp16":
                 pg = {"key": k, "value": v}
             elif tier in ("fp8", "int8"):
