@@ -23,6 +23,7 @@ Reference lines: ArgusConfig :17-48, argus_log :50-72, calculate_tensor_entropy 
 isolate_outliers :89-113, PagedDynamicKVCache :115-1824 (methods cited below).
 Only float16 K/V are supported (the tier codecs are fp16-exact).
 """
+import ctypes
 import math
 import os
 import time
@@ -171,6 +172,7 @@ class PagedDynamicKVCache:
         self._host_arenas = {}
         self._plan = None
         self._plan_key = None
+        self._plan_base_cache = None
         # attend JL pages without rebuilding them (argus_b200.core.jl.JLAttention) when their shape
         # allows it (128-row blocks, i.e. 512-token pages, head_dim 128, <= 8 queries per kv head)
         self.fused_jl_attention = True
@@ -252,6 +254,7 @@ class PagedDynamicKVCache:
     def _invalidate(self):
         self._plan = None
         self._plan_key = None
+        self._plan_base_cache = None
 
     def _page_views(self, name, idx):
         """The reference-schema tensors of slot idx of tier `name` (views into the record arena)."""
@@ -314,9 +317,10 @@ class PagedDynamicKVCache:
         self.static_k_buffer[..., self.buffer_length:self.buffer_length + num_new, :].copy_(keys)
         self.static_v_buffer[..., self.buffer_length:self.buffer_length + num_new, :].copy_(values)
         self.buffer_length += num_new
-        self._invalidate()
+        # the attention plan reads the static buffer in place and tracks buffer_length itself
         P = self.page_size
         while self.buffer_length >= P:
+            self._invalidate()
             if len(self.active_pages) >= self.max_active_pages:
                 self.manage_memory_lifecycle()
             idx = self._get_free_pool_idx(self.active_pages, self.max_active_pages)
@@ -608,14 +612,74 @@ class PagedDynamicKVCache:
         return K, V
 
     def _attention_plan(self, q):
-        """Fused-kernel tables for the current pages, rebuilt only when the cache changed.  Pages with
-        outlier sidecars and JL pages are first rebuilt to fp16 (exactly) into a scratch arena shared
-        with the sinks, anchors and staging buffer; everything else is read compressed."""
+        """Fused-kernel tables for the current cache.  What depends on the pages (a scratch fp16
+        arena for the sinks, anchors and JL pages the fused JL kernel does not take; the pages'
+        outlier corrections; the JL operands) is rebuilt only when pages change.  The staging
+        buffer is an fp16 arena of its own over the static buffer, so a decode step that only
+        appends a token patches the token count of the buffer's last tile in place; the tables are
+        rebuilt when the buffer starts a new 16-token tile."""
         B, Hq, qlen, D = q.shape
-        key = (B, Hq, qlen, D, self.buffer_length, len(self.active_pages),
-               tuple(len(lst) for _, lst in self._compressed_order()), self._scratch_version())
-        if self._plan is not None and self._plan_key == key:
-            return self._plan
+        nbuf = self.buffer_length if self.k_buffer is not None else 0
+        base_key = (B, Hq, qlen, D, len(self.active_pages), tuple(len(lst) for _, lst in self._compressed_order()),
+                    self._scratch_version())
+        key = (base_key, self.static_k_buffer.data_ptr() if nbuf else 0, (nbuf + 15) // 16)
+        plan = self._plan
+        if plan is not None and self._plan_key == key:
+            if plan.buffer_tokens != nbuf:
+                self._patch_buffer_tokens(plan, nbuf)
+            return plan
+        base = self._plan_base(q, base_key)
+        arenas, pages, page_seg = list(base["arenas"]), list(base["pages"]), list(base["page_seg"])
+        segments = list(base["order"])
+        buf_ai = -1
+        if nbuf:
+            buf_ai = len(arenas)
+            arenas.append(A.KVArena.from_fp16(self.static_k_buffer, self.static_v_buffer))
+            seg = len(segments)
+            segments.append(("buffer", None, nbuf))
+            for t0 in range(0, nbuf, 16):
+                pages.append((buf_ai, t0 // 16, min(16, nbuf - t0)))
+                page_seg.append(seg)
+        Hkv = base["Hkv"]
+        # attention is order-free: give each arena's pages in slot order so runs merge into chunks
+        perm = sorted(range(len(pages)), key=lambda i: (pages[i][0], pages[i][1]))
+        plan = A.AttentionPlan(arenas, [pages[i] for i in perm], batch=B, heads_kv=Hkv, group=Hq // Hkv,
+                               head_dim=D, q_len=qlen)
+        # map (chunk, tile) of the launch -> segment
+        cmap = torch.full((max(1, plan.n_chunks), 16), -1, dtype=torch.long)
+        for c, src in enumerate(plan.chunk_pages):
+            for i, pi in enumerate(src):
+                cmap[c, i] = page_seg[perm[pi]]
+        plan.tile_segment = cmap.to(q.device)
+        plan.segments = segments
+        plan.jl = base["jl"]
+        plan.buffer_tokens = nbuf
+        plan.buffer_chunk = -1
+        if nbuf:
+            last = (nbuf - 1) // 16
+            plan.buffer_chunk = next(c for c, (slot, _, ai, nt, _) in enumerate(plan.chunks)
+                                     if ai == buf_ai and slot <= last < slot + nt)
+        self._plan, self._plan_key = plan, key
+        return plan
+
+    def _patch_buffer_tokens(self, plan, nbuf):
+        """The staging buffer grew within its last 16-token tile: update that tile's token count in
+        the plan's device chunk table (one byte) and the buffer segment's length."""
+        c = plan.buffer_chunk
+        slot, tok0, ai, nt, _ = plan.chunks[c]
+        last = nbuf - 16 * ((nbuf - 1) // 16)
+        plan.chunks[c] = (slot, tok0, ai, nt, last)
+        # ntok_last is byte 8 of the 12-byte argus_kv_chunk
+        plan.chunks_dev[c * ctypes.sizeof(A.ChunkC) + 8] = last
+        plan.n_tokens += nbuf - plan.buffer_tokens
+        plan.segments[-1] = ("buffer", None, nbuf)
+        plan.buffer_tokens = nbuf
+
+    def _plan_base(self, q, base_key):
+        """The page-dependent part of the attention tables (see _attention_plan), cached by key."""
+        if self._plan_base_cache is not None and self._plan_base_cache[0] == base_key:
+            return self._plan_base_cache[1]
+        B, Hq, qlen, D = q.shape
         P = self.page_size
         order = []  # (segment kind, page or None, tokens) in the reference's attention order
         if self.sink_k is not None:
@@ -624,27 +688,24 @@ class PagedDynamicKVCache:
             order.append(("anchors", None, self.anchor_k.shape[-2]))
         for page in self.active_pages:
             order.append(("fp16", page, P))
-        if self.k_buffer is not None and self.k_buffer.shape[-2] > 0:
-            order.append(("buffer", None, self.buffer_length))
         others = (self.sink_k is not None or self.anchor_k is not None or bool(self.active_pages)
                   or (self.k_buffer is not None and self.k_buffer.shape[-2] > 0)
                   or any(lst for name, lst in self._compressed_order() if name != "jl"))
+        Hkv = self.H if self._pools_allocated else (self.sink_k.shape[1])
         fused_jl = (self.fused_jl_attention and len(self.jl_pages) > 0 and others and P // 4 == 128 and D == 128
-                    and (Hq // (self.H if self._pools_allocated else self.sink_k.shape[1])) * qlen <= 8)
+                    and (Hq // Hkv) * qlen <= 8)
         for name, lst in self._compressed_order():
             for page in lst:
                 if name == "jl" and fused_jl:
                     order.append(("jl_fused", page, P))
                     continue
-                side = name == "jl" or (page.get("key_out_indices") is not None and page["key_out_indices"].numel() > 0) \
-                    or (page.get("value_out_indices") is not None and page["value_out_indices"].numel() > 0)
-                order.append((("scratch:" + name) if side else name, page, P))
-        # scratch fp16 tensor: sinks, anchors, buffer and rebuilt pages, each padded to 16 tokens
-        scratch_len = sum(-(-n // 16) * 16 for kind, _, n in order
-                          if kind in ("sinks", "anchors", "buffer") or kind.startswith("scratch:"))
+                # JL pages not taken by the fused JL kernel are rebuilt into the scratch arena; pages
+                # with outlier sidecars are read compressed, their sidecars applied by the kernel
+                order.append(("scratch:jl" if name == "jl" else name, page, P))
+        # scratch fp16 tensor: sinks, anchors and rebuilt JL pages, each padded to 16 tokens
+        scratch_len = sum(-(-n // 16) * 16 for kind, _, n in order if kind in ("sinks", "anchors", "scratch:jl"))
         dev = q.device
         arenas, index, pages = [], {}, []
-        Hkv = self.H if self._pools_allocated else (self.sink_k.shape[1])
         scratch = None
         if scratch_len:
             sk = torch.empty(B, Hkv, scratch_len, D, dtype=torch.float16, device=dev)
@@ -659,7 +720,7 @@ class PagedDynamicKVCache:
             if kind == "jl_fused":
                 jl_segs.append(seg)
                 continue
-            if kind in ("sinks", "anchors", "buffer") or kind.startswith("scratch:"):
+            if kind in ("sinks", "anchors", "scratch:jl"):
                 sk, sv = scratch
                 if kind == "sinks":
                     sk[:, :, pos:pos + n].copy_(self.sink_k)
@@ -667,21 +728,10 @@ class PagedDynamicKVCache:
                 elif kind == "anchors":
                     sk[:, :, pos:pos + n].copy_(self.anchor_k)
                     sv[:, :, pos:pos + n].copy_(self.anchor_v)
-                elif kind == "buffer":
-                    sk[:, :, pos:pos + n].copy_(self.k_buffer)
-                    sv[:, :, pos:pos + n].copy_(self.v_buffer)
                 else:
-                    name = kind.split(":", 1)[1]
-                    if name == "jl":
-                        k, v = self._dequant_with_sidecars("jl", page)
-                        sk[:, :, pos:pos + n].copy_(k)
-                        sv[:, :, pos:pos + n].copy_(v)
-                    else:
-                        paged.dequantize_page(self.arenas[name], page["pool_idx"], sk, sv, tok0=pos)
-                        paged.scatter_coo(sk, page.get("key_out_indices"), page.get("key_out_values"), tok0=pos,
-                                          page_tokens=P)
-                        paged.scatter_coo(sv, page.get("value_out_indices"), page.get("value_out_values"), tok0=pos,
-                                          page_tokens=P)
+                    k, v = self._dequant_with_sidecars("jl", page)
+                    sk[:, :, pos:pos + n].copy_(k)
+                    sv[:, :, pos:pos + n].copy_(v)
                 for t0 in range(0, n, 16):
                     pages.append((index["scratch"], (pos + t0) // 16, min(16, n - t0)))
                     page_seg.append(seg)
@@ -692,28 +742,41 @@ class PagedDynamicKVCache:
                     arenas.append(self.arenas[kind])
                 pages.append((index[kind], page["pool_idx"], n))
                 page_seg.append(seg)
-        # attention is order-free: give each record arena's pages in slot order so runs merge into chunks
-        perm = sorted(range(len(pages)), key=lambda i: (pages[i][0], pages[i][1]))
-        plan = A.AttentionPlan(arenas, [pages[i] for i in perm], batch=B, heads_kv=Hkv, group=Hq // Hkv,
-                               head_dim=D, q_len=qlen)
-        # map (chunk, tile) of the launch -> segment of the reference's attention order
-        cmap = torch.full((max(1, plan.n_chunks), 16), -1, dtype=torch.long)
-        for c, src in enumerate(plan.chunk_pages):
-            for i, pi in enumerate(src):
-                cmap[c, i] = page_seg[perm[pi]]
-        plan.tile_segment = cmap.to(dev)
-        plan.segments = order
-        plan.jl = None
+        for name in _TIERS:
+            if name in index:
+                self._attach_outliers(name)
+        jl = None
         if jl_segs:
             R = self.get_jl_reconstruction_operator(dev, torch.float16)
             if self._jl_attention is None or self._jl_attention[0] is not R:
                 self._jl_attention = (R, _jl.JLAttention(R))
             pages_jl = [order[i][1] for i in jl_segs]
-            plan.jl = {"att": self._jl_attention[1], "segs": jl_segs,
-                       "yk": torch.stack([pg["key_proj"] for pg in pages_jl], dim=2).contiguous(),
-                       "yv": torch.stack([pg["value_proj"] for pg in pages_jl], dim=2).contiguous()}
-        self._plan, self._plan_key = plan, key
-        return plan
+            jl = {"att": self._jl_attention[1], "segs": jl_segs,
+                  "yk": torch.stack([pg["key_proj"] for pg in pages_jl], dim=2).contiguous(),
+                  "yv": torch.stack([pg["value_proj"] for pg in pages_jl], dim=2).contiguous()}
+        base = {"order": order, "arenas": arenas, "pages": pages, "page_seg": page_seg, "jl": jl, "Hkv": Hkv,
+                "scratch": scratch}
+        self._plan_base_cache = (base_key, base)
+        return base
+
+    def _attach_outliers(self, name):
+        """Points tier `name`'s arena directory at the correction blocks of its pages' outlier
+        sidecars, so the fused kernel applies them while reading the pages compressed.  A page's
+        blocks are built once per (arena, slot) it occupies and kept in the page dict."""
+        arena = self.arenas[name]
+        arena.clear_outliers()
+        for page in getattr(self, _TIERS[name][0]):
+            ki, vi = page.get("key_out_indices"), page.get("value_out_indices")
+            if (ki is None or ki.numel() == 0) and (vi is None or vi.numel() == 0):
+                continue
+            key = (arena.k.data_ptr(), page["pool_idx"])
+            cached = page.get("_outlier_blocks")
+            if cached is None or cached[0] != key:
+                blocks, addr = paged.outlier_corrections(arena, page["pool_idx"], ki, page.get("key_out_values"), vi,
+                                                         page.get("value_out_values"))
+                cached = (key, blocks, addr)
+                page["_outlier_blocks"] = cached
+            arena.set_outliers(page["pool_idx"], cached[1], cached[2])
 
     def _scratch_version(self):
         return (self.sink_k.data_ptr() if self.sink_k is not None else 0,
@@ -880,6 +943,7 @@ class PagedDynamicKVCache:
                     page.update(self._page_views(name, page["pool_idx"]))
         for _, lst in self._compressed_order():
             for page in lst:
+                page.pop("_outlier_blocks", None)  # derived device data, rebuilt after swap-in
                 for k in self._SWAP_KEYS + ("key_proj", "value_proj"):
                     if isinstance(page.get(k), torch.Tensor) and page[k].is_cuda:
                         page[k] = page[k].to("cpu")

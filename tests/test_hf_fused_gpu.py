@@ -95,3 +95,36 @@ def test_fused_decode_matches_materializing_adapter(num_layers, hidden, heads, k
     assert len(c0.jl_pages) >= 1 and len(c0.one_bit_pages) == 1
     assert fused_cache.get_seq_length(0) == ref_cache.get_seq_length(0) == 154
     assert worst <= atol, worst
+
+
+def test_attend_follows_single_token_appends(tmp_path, monkeypatch):
+    """Decode-style pushes of one token: attend() stays on float64 attention over the rebuilt K/V
+    (get_all_keys_values) through tile and page boundaries, and within a 16-token tile of the
+    staging buffer it reuses its launch tables (the buffer tile's token count is patched)."""
+    import oracle
+    from argus_b200.core.memory_manager import PagedDynamicKVCache
+    monkeypatch.setenv("ARGUS_LOG_LEVEL", "quiet")
+    monkeypatch.chdir(tmp_path)
+    B, H, G, D = 1, 2, 4, 64
+    cache = PagedDynamicKVCache(page_size=32, max_active_pages=1, max_fp8_pages=1, max_int8_pages=1,
+                                max_int4_pages=1, max_int2_pages=1, max_one_bit_pages=1, sink_tokens=4)
+    g = torch.Generator().manual_seed(9)
+    kv = lambda n: (torch.randn(B, H, n, D, generator=g) * 1.5).half().cuda()  # noqa: E731
+    cache.push_new_tokens(kv(200), kv(200))
+    plans = []
+    for step in range(40):
+        cache.push_new_tokens(kv(1), kv(1))
+        q = (torch.randn(B, H * G, 1, D, generator=g) / 8).half()
+        out = host(cache.attend(q.cuda())).astype(np.float64)
+        K, V = cache.get_all_keys_values()
+        ref = oracle.sdpa_f64(q.numpy(), host(K), host(V), 1.0 / math.sqrt(D))
+        bar = 2e-3 + np.abs(ref) * 2.0 ** -11
+        assert (np.abs(out - ref) <= bar).all(), (step, np.abs(out - ref).max())
+        plans.append((id(cache._plan), cache.buffer_length))
+    # consecutive steps inside one buffer tile share the launch tables
+    same = sum(1 for (a, na), (b, nb) in zip(plans, plans[1:]) if (na - 1) // 16 == (nb - 1) // 16 and nb > na)
+    reused = sum(1 for (a, na), (b, nb) in zip(plans, plans[1:])
+                 if (na - 1) // 16 == (nb - 1) // 16 and nb > na and a == b)
+    assert same > 20 and reused == same
+    assert any(pg.get("key_out_indices") is not None and pg["key_out_indices"].numel()
+               for _, lst in cache._compressed_order() for pg in lst)
