@@ -33,9 +33,12 @@ MAX_ARENAS = 8
 NUM_SMS = 148
 
 
-def ctas_per_sm(head_dim):
-    """Decode-attention CTAs resident per SM (the kernel's launch bounds and shared memory)."""
-    return 2 if head_dim >= 256 else 4
+def ctas_per_sm(head_dim, sidecars=False):
+    """Decode-attention CTAs resident per SM (the kernel's launch bounds and shared memory); launches
+    over arenas with outlier sidecars run 3 per SM up to head_dim 128."""
+    if head_dim >= 256:
+        return 2
+    return 3 if sidecars else 4
 
 # C-ABI entry points bound in this module (with structure-typed arguments)
 BOUND_SYMBOLS = ("argus_decode_attention", "argus_decode_attention_workspace_size",
@@ -327,7 +330,8 @@ class AttentionPlan:
         groups = self.B * self.Hkv * nqg
         if n_splits is None:
             # as many splits as fill one wave of CTAs, with at least ~2 chunks per warp
-            n_splits = max(1, min(NUM_SMS * ctas_per_sm(self.D) // groups, max(1, self.n_chunks // 8)))
+            side = any(a.outlier_dir is not None for a in self.arenas)
+            n_splits = max(1, min(NUM_SMS * ctas_per_sm(self.D, side) // groups, max(1, self.n_chunks // 8)))
         n_splits = max(1, min(int(n_splits), max(1, self.n_chunks)))
         self.n_splits = n_splits
         order, bounds = _deal_chunks([c[2] for c in chunks], ccost, n_splits)

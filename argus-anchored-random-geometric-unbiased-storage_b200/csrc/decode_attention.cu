@@ -635,16 +635,177 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
 
 // ------------------------------------------------------------------------------ outlier sidecars
 // The reference overwrites each sidecar position of a dequantized page with the sidecar's fp16 value
-// before attending.  Here the page stays compressed: the tile's scores get delta * q for every key
-// outlier, and its output gets p * delta for every value outlier, delta = sidecar value minus the
-// dequantized value (argus_outlier_corrections builds the per-page blocks).
+// before attending.  Here the page stays compressed and the kernel adds the difference: the tile's
+// scores get delta . q over its key outliers and its output gets delta^T . p over its value
+// outliers, delta = sidecar value minus dequantized value (argus_outlier_corrections).
+//
+// Head dims up to 128 scatter the tile's deltas into a dense fp16 16 x D tile in the warp's shared
+// memory (zero between uses, stored in MMA fragment order) and run it through the same tensor-core
+// MMAs as the tile itself, so the cost hardly depends on how many outliers a tile has; deltas that
+// fp16 does not hold exactly take a second pass with the remainder.  These kernels run 3 CTAs per SM to make room
+// for the tiles.  Head dim 256 walks each lane's own entries (keys by the token pair whose scores
+// the lane holds, values by the dims of the outputs it holds), using a 512-byte buffer per warp.
+__host__ __device__ constexpr bool side_dense(int D) { return D <= 128; }
+__host__ __device__ constexpr int side_ctas_per_sm(int D) { return side_dense(D) ? 3 : ctas_per_sm(D); }
+__host__ __device__ constexpr int side_warp_bytes(int D) { return side_dense(D) ? 32 * D : 16 * kQ * 4; }
 
-// Where the correction block of a tile's page is: the directory entry of its (b, h, slot), the
-// tile's index within the page and the page's tile count.
-struct OutlierRef {
-    const unsigned long long* entry;
+// The corrections of one tile: the page's block (header and entries; null when it has none), the
+// tile's key and value entry ranges, its index within the page and the page's tile count, this
+// lane's first two key and value entries (entries k0 + lane, k0 + 32 + lane, and likewise for the
+// values; loaded as the tile starts); buf: the warp's shared-memory buffer.
+struct OutlierTile {
+    const uint32_t* hdr;
+    const uint2* ent;
+    int k0, k1, v0, v1;
     int ti, nt;
+    uint2 ke[2], ve[2];
+    unsigned char* buf;
 };
+
+// The dense delta tile is stored in MMA fragment order: lane l's 4 KC words are the A fragments
+// a[c][0..3] (c = 0 .. KC-1) that k_frags / v_frags of an fp16 tile would give lane l, its 16-byte
+// groups rotated by (l mod KC) so that the fragment loads are free of bank conflicts.
+template <int D>
+__device__ __forceinline__ int frag_half(int lane, int c, int r, int half) {
+    constexpr int KC = D / 16;
+    return ((lane * KC + (c ^ (lane & (KC - 1)))) * 4 + r) * 2 + half;
+}
+// (token, dim) of a K tile -> its half in the fragment-ordered tile (k_frags: lane 4 (tok/2) +
+// d/(D/4) holds dims 4c + {0,2} in a[c][0 (even tok) / 1 (odd)], dims 4c + {1,3} in a[c][2 / 3])
+template <int D>
+__device__ __forceinline__ int k_half(int tok, int d) {
+    const int dd = d % (D / 4), w = dd & 3;
+    return frag_half<D>(4 * (tok >> 1) + d / (D / 4), dd >> 2, ((w & 1) << 1) | (tok & 1), w >> 1);
+}
+// (token, dim) of a V tile -> its half (v_frags: lane 4 (d/(D/8)) + tok/4 holds, for t = (d mod D/8)/2,
+// tokens 4u+{0,2} in a[t][0 (even d) / 1 (odd d)], tokens 4u+{1,3} in a[t][2 / 3])
+template <int D>
+__device__ __forceinline__ int v_half(int tok, int d) {
+    const int dd = d % (D / 8), w = tok & 3;
+    return frag_half<D>(4 * (d / (D / 8)) + (tok >> 2), dd >> 1, ((w & 1) << 1) | (dd & 1), w >> 1);
+}
+template <int D>
+__device__ __forceinline__ void load_delta_frags(const unsigned char* buf, uint32_t (&a)[D / 16][4]) {
+    constexpr int KC = D / 16;
+    const int lane = threadIdx.x & 31;
+    const uint4* b4 = reinterpret_cast<const uint4*>(buf);
+#pragma unroll
+    for (int c = 0; c < KC; ++c) {
+        const uint4 v = b4[lane * KC + (c ^ (lane & (KC - 1)))];
+        a[c][0] = v.x; a[c][1] = v.y; a[c][2] = v.z; a[c][3] = v.w;
+    }
+}
+
+// This lane's share of a tile's key or value entries, ready to store: positions (halves of the
+// fragment-ordered tile, -1 = none) and fp16 hi | lo << 16 of each delta.
+struct DeltaSlots {
+    int pos[2];
+    uint32_t hl[2];
+};
+
+template <int D>
+__device__ __forceinline__ void delta_slot(uint2 raw, bool key, int tb, int ntok, int& pos, uint32_t& hl) {
+    const int tok = (int)(raw.x & 0xffffu) - tb, d = (int)(raw.x >> 16);
+    pos = -1;
+    hl = 0u;
+    if (tok < 0 || tok >= ntok || d >= D) return;
+    const float delta = __uint_as_float(raw.y);
+    const __half hi = __float2half_rn(delta);
+    const __half lo = __float2half_rn(delta - __half2float(hi));
+    pos = key ? k_half<D>(tok, d) : v_half<D>(tok, d);
+    hl = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
+}
+
+// Prepares this lane's slots; returns (warp-uniform) whether any delta has a nonzero fp16 remainder.
+template <int D>
+__device__ __forceinline__ bool delta_slots(const OutlierTile& ot, bool key, int ntok, DeltaSlots& ds) {
+    const int lane = threadIdx.x & 31;
+    const int e0 = key ? ot.k0 : ot.v0, e1 = key ? ot.k1 : ot.v1;
+    bool rem = false;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        ds.pos[u] = -1;
+        ds.hl[u] = 0u;
+        if (e0 + 32 * u + lane < e1) {
+            delta_slot<D>(key ? ot.ke[u] : ot.ve[u], key, 16 * ot.ti, ntok, ds.pos[u], ds.hl[u]);
+            rem |= (ds.hl[u] >> 16) != 0u;
+        }
+    }
+    for (int e = e0 + 64 + lane; e < e1; e += 32) {  // tiles with more than 64 entries
+        int pos;
+        uint32_t hl;
+        delta_slot<D>(__ldg(ot.ent + e), key, 16 * ot.ti, ntok, pos, hl);
+        rem |= (hl >> 16) != 0u;
+    }
+    return __any_sync(0xffffffffu, rem);
+}
+
+// Stores pass 0: hi, 1: lo, 2: zero of the slots (and of any entries past the first 64).
+template <int D>
+__device__ __forceinline__ void store_deltas(const OutlierTile& ot, bool key, int ntok, const DeltaSlots& ds, int pass) {
+    unsigned short* buf = reinterpret_cast<unsigned short*>(ot.buf);
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+        if (ds.pos[u] >= 0) buf[ds.pos[u]] = pass == 2 ? (unsigned short)0 : (unsigned short)(ds.hl[u] >> (16 * pass));
+    const int e0 = key ? ot.k0 : ot.v0, e1 = key ? ot.k1 : ot.v1;
+    for (int e = e0 + 64 + (threadIdx.x & 31); e < e1; e += 32) {
+        int pos;
+        uint32_t hl;
+        delta_slot<D>(__ldg(ot.ent + e), key, 16 * ot.ti, ntok, pos, hl);
+        if (pos >= 0) buf[pos] = pass == 2 ? (unsigned short)0 : (unsigned short)(hl >> (16 * pass));
+    }
+    __syncwarp();
+}
+
+// x[.] += scale_log2 * (delta tile) . Q^T for the key outliers of the tile.
+template <int D>
+__device__ __forceinline__ void dense_k_outliers(const OutlierTile& ot, uint32_t qs, float scale_log2, int ntok,
+                                                 float (&x)[4]) {
+    if (ot.k0 >= ot.k1) return;
+    constexpr int KC = D / 16;
+    DeltaSlots ds;
+    const bool rem = delta_slots<D>(ot, true, ntok, ds);
+    uint32_t qf[KC][2];
+    load_qfrags<D>(qs, threadIdx.x & 31, qf);
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int pass = 0; pass < 2; ++pass) {
+        store_deltas<D>(ot, true, ntok, ds, pass);
+        uint32_t a[KC][4];
+        load_delta_frags<D>(ot.buf, a);
+#pragma unroll
+        for (int c = 0; c < KC; ++c) mma16816(s, a[c], qf[c][0], qf[c][1]);
+        __syncwarp();  // every lane has its fragments before the tile is rewritten
+        if (!rem) break;
+    }
+    store_deltas<D>(ot, true, ntok, ds, 2);
+    x[0] += s[0] * scale_log2;
+    x[1] += s[1] * scale_log2;
+    x[2] += s[2] * scale_log2;
+    x[3] += s[3] * scale_log2;
+}
+
+// O^T += (delta tile)^T . P^T for the value outliers of the tile, P the tile's fp16 weights.
+template <int D, bool PRECISE>
+__device__ __forceinline__ void dense_v_outliers(const OutlierTile& ot, int ntok, uint32_t b01, uint32_t b23,
+                                                 uint32_t c01, uint32_t c23, float (&o)[D / 16][4]) {
+    if (ot.v0 >= ot.v1) return;
+    constexpr int KC = D / 16;
+    DeltaSlots ds;
+    const bool rem = delta_slots<D>(ot, false, ntok, ds);
+    for (int pass = 0; pass < 2; ++pass) {
+        store_deltas<D>(ot, false, ntok, ds, pass);
+        uint32_t av[KC][4];
+        load_delta_frags<D>(ot.buf, av);
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            mma16816(o[t], av[t], b01, b23);
+            if constexpr (PRECISE) mma16816(o[t], av[t], c01, c23);
+        }
+        __syncwarp();
+        if (!rem) break;
+    }
+    store_deltas<D>(ot, false, ntok, ds, 2);
+}
 
 // q[n][d] of the CTA's query group from the Q^T fragments in shared memory (load_qfrags layout:
 // lane 4n + d/(D/4) holds dims 4c, 4c+2 in word 2c and 4c+1, 4c+3 in word 2c+1 of its block).
@@ -660,80 +821,117 @@ __device__ __forceinline__ float q_at(uint32_t qs, int n, int d) {
     return __half2float(__ushort_as_half(h));
 }
 
-__device__ __forceinline__ const uint32_t* outlier_block(const OutlierRef& r) {
-    return reinterpret_cast<const uint32_t*>(__ldg(r.entry));
+template <int D>
+__device__ __forceinline__ void k_entry(uint2 raw, int tok0, int g4, int t4, uint32_t qs, float scale_log2, int ntok,
+                                        float (&x)[4]) {
+    const int odd = (int)(raw.x & 0xffffu) - tok0, d = (int)(raw.x >> 16);
+    if (odd < 0 || odd > 1 || 2 * g4 + odd >= ntok || d >= D) return;
+    const float c = __uint_as_float(raw.y) * scale_log2;
+    const float q0 = q_at<D>(qs, 2 * t4, d), q1 = q_at<D>(qs, 2 * t4 + 1, d);
+    if (odd) { x[2] = fmaf(c, q0, x[2]); x[3] = fmaf(c, q1, x[3]); }
+    else     { x[0] = fmaf(c, q0, x[0]); x[1] = fmaf(c, q1, x[1]); }
 }
 
-// x[.] (log2-domain scores of tokens 2g4, 2g4+1 for queries 2t4, 2t4+1) += scale_log2 * delta * q.
+// Walk form of the key corrections: x[.] (scores of tokens 2g4, 2g4+1 for queries 2t4, 2t4+1) +=
+// scale_log2 * delta * q[n][d] over the entries of this lane's token pair, four loads in flight.
 template <int D>
-__device__ __forceinline__ void apply_k_outliers(const OutlierRef& r, int g4, int t4, uint32_t qs, float scale_log2,
-                                                 int ntok, float (&x)[4]) {
-    const uint32_t* hdr = outlier_block(r);
-    if (!hdr) return;
-    const int e0 = (int)__ldg(hdr + r.ti), e1 = (int)__ldg(hdr + r.ti + 1);
-    const uint2* ent = reinterpret_cast<const uint2*>(hdr + 2 * (r.nt + 1));
-    for (int i = e0; i < e1; ++i) {
-        const uint2 raw = __ldg(ent + i);
-        const int tok = (int)(raw.x & 0xffffu) - 16 * r.ti, d = (int)(raw.x >> 16);
-        if (tok < 0 || tok >= ntok || d >= D) continue;
-        if ((tok >> 1) == g4) {
-            const float c = __uint_as_float(raw.y) * scale_log2;
-            const float q0 = q_at<D>(qs, 2 * t4, d), q1 = q_at<D>(qs, 2 * t4 + 1, d);
-            if (tok & 1) { x[2] += c * q0; x[3] += c * q1; }
-            else         { x[0] += c * q0; x[1] += c * q1; }
-        }
-    }
-}
-
-// O^T[d][n] += p[n][tok] * delta for every value outlier (tok, d); p = 2^(x - m) as the tile's
-// weights (the owner of O^T[d][.] is lane 4 (d / (D/8)) + t4, the scores of token tok sit in lane
-// 4 (tok / 2) + t4).
-template <int D>
-__device__ __forceinline__ void apply_v_outliers(const OutlierRef& r, int g4, int t4, int ntok, const SoftmaxState& st,
-                                                 const float (&x)[4], float (&o)[D / 16][4]) {
-    const uint32_t* hdr = outlier_block(r);
-    if (!hdr) return;
-    const int e0 = (int)__ldg(hdr + r.nt + 1 + r.ti), e1 = (int)__ldg(hdr + r.nt + 2 + r.ti);
-    const uint2* ent = reinterpret_cast<const uint2*>(hdr + 2 * (r.nt + 1));
-    for (int i = e0; i < e1; ++i) {
-        const uint2 raw = __ldg(ent + i);
-        const int tok = (int)(raw.x & 0xffffu) - 16 * r.ti, d = (int)(raw.x >> 16);
-        if (tok < 0 || tok >= ntok || d >= D) continue;
-        const int src = 4 * (tok >> 1) + t4;
-        const float xa = __shfl_sync(0xffffffffu, (tok & 1) ? x[2] : x[0], src);
-        const float xb = __shfl_sync(0xffffffffu, (tok & 1) ? x[3] : x[1], src);
-        if (g4 == d / (D / 8)) {
-            const float delta = __uint_as_float(raw.y);
-            const float pa = exp2f(xa - st.m[0]) * delta, pb = exp2f(xb - st.m[1]) * delta;
-            const int dd = d % (D / 8);
-            // register-resident update: every o[t][.] takes a 0/1-weighted FMA (no dynamic index)
-            const float ea = (dd & 1) ? 0.f : pa, eb = (dd & 1) ? 0.f : pb;
-            const float fa = (dd & 1) ? pa : 0.f, fb = (dd & 1) ? pb : 0.f;
+__device__ __forceinline__ void walk_k_outliers(const OutlierTile& ot, int g4, int t4, uint32_t qs, float scale_log2,
+                                                int ntok, float (&x)[4]) {
+    if (ot.k0 >= ot.k1) return;
+    const int j = 8 * ot.ti + g4;
+    int e = (int)__ldg(ot.hdr + j);
+    const int e1 = (int)__ldg(ot.hdr + j + 1);
+    const int tok0 = 16 * ot.ti + 2 * g4;
+    for (; e < e1; e += 4) {
+        uint2 rr[4];
 #pragma unroll
-            for (int t = 0; t < D / 16; ++t) {
-                const float w = (t == (dd >> 1)) ? 1.f : 0.f;
-                o[t][0] = fmaf(w, ea, o[t][0]);
-                o[t][1] = fmaf(w, eb, o[t][1]);
-                o[t][2] = fmaf(w, fa, o[t][2]);
-                o[t][3] = fmaf(w, fb, o[t][3]);
+        for (int u = 0; u < 4; ++u) rr[u] = (e + u < e1) ? __ldg(ot.ent + e + u) : make_uint2(0xffffu, 0u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) k_entry<D>(rr[u], tok0, g4, t4, qs, scale_log2, ntok, x);
+    }
+}
+
+// Walk form of the value corrections: O^T[d][2t4 .. 2t4+1] += p[.][tok] * delta over the entries of
+// this lane's dim group (dims g4 D/8 ..), p = 2^(x - m) staged as fp16 in the warp's buffer.  A
+// lane's entries are sorted by dim, so a static walk over its output registers picks them up.
+template <int D>
+__device__ __forceinline__ void walk_v_outliers(const OutlierTile& ot, int g4, int t4, int ntok, const SoftmaxState& st,
+                                                const float (&x)[4], float (&o)[D / 16][4]) {
+    if (ot.v0 >= ot.v1) return;
+    const uint32_t* voff = ot.hdr + 8 * ot.nt + 1;
+    int e = (int)__ldg(voff + 8 * ot.ti + g4);
+    const int e1 = (int)__ldg(voff + 8 * ot.ti + g4 + 1);
+    __half* ph = reinterpret_cast<__half*>(ot.buf);  // [16 tokens][8 queries] fp16 weights (<= 2^8)
+    *reinterpret_cast<__half2*>(ph + (2 * g4) * kQ + 2 * t4) =
+        __floats2half2_rn(exp2f(x[0] - st.m[0]), exp2f(x[1] - st.m[1]));
+    *reinterpret_cast<__half2*>(ph + (2 * g4 + 1) * kQ + 2 * t4) =
+        __floats2half2_rn(exp2f(x[2] - st.m[0]), exp2f(x[3] - st.m[1]));
+    __syncwarp();
+    const int dlo = g4 * (D / 8), tb = 16 * ot.ti;
+    uint2 n0 = make_uint2(0u, 0xffffffffu), n1 = n0;
+    if (e < e1) n0 = __ldg(ot.ent + e);
+    if (e + 1 < e1) n1 = __ldg(ot.ent + e + 1);
+#pragma unroll
+    for (int t = 0; t < D / 16; ++t) {
+        while (e < e1 && (int)(n0.x >> 16) < dlo + 2 * (t + 1)) {
+            const int tok = (int)(n0.x & 0xffffu) - tb, d = (int)(n0.x >> 16);
+            if (tok >= 0 && tok < ntok && d >= dlo + 2 * t) {
+                const float delta = __uint_as_float(n0.y);
+                const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(ph + tok * kQ + 2 * t4));
+                if (d & 1) { o[t][2] = fmaf(pf.x, delta, o[t][2]); o[t][3] = fmaf(pf.y, delta, o[t][3]); }
+                else       { o[t][0] = fmaf(pf.x, delta, o[t][0]); o[t][1] = fmaf(pf.y, delta, o[t][1]); }
             }
+            ++e;
+            n0 = n1;
+            if (e + 1 < e1) n1 = __ldg(ot.ent + e + 1);
         }
     }
+    __syncwarp();  // the buffer is rewritten by the next tile
+}
+
+// The corrections of tile i of a chunk from the chunk's per-lane prefetch (lane i holds tile i's block
+// address and entry ranges); also starts the loads of this lane's first two key and value entries.
+__device__ __forceinline__ OutlierTile outlier_tile(unsigned long long blk, int k0, int k1, int v0, int v1, int i,
+                                                    int ti, int nt, unsigned char* buf) {
+    OutlierTile ot;
+    const unsigned long long b = __shfl_sync(0xffffffffu, blk, i);
+    ot.hdr = reinterpret_cast<const uint32_t*>(b);
+    ot.ent = b ? reinterpret_cast<const uint2*>(ot.hdr + 2 * (8 * nt + 1)) : nullptr;
+    ot.k0 = __shfl_sync(0xffffffffu, k0, i);
+    ot.k1 = __shfl_sync(0xffffffffu, k1, i);
+    ot.v0 = __shfl_sync(0xffffffffu, v0, i);
+    ot.v1 = __shfl_sync(0xffffffffu, v1, i);
+    ot.ti = ti;
+    ot.nt = nt;
+    ot.buf = buf;
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        ot.ke[u] = (ot.k0 + 32 * u + lane < ot.k1) ? __ldg(ot.ent + ot.k0 + 32 * u + lane) : make_uint2(0u, 0u);
+        ot.ve[u] = (ot.v0 + 32 * u + lane < ot.v1) ? __ldg(ot.ent + ot.v0 + 32 * u + lane) : make_uint2(0u, 0u);
+    }
+    return ot;
 }
 
 // Processes one staged tile: scores, online softmax, PV (OUT: with the page's outlier corrections).
 template <int D, int TIER, bool PRECISE, bool MASS, bool OUT>
 __device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, uint32_t qs, float scale_log2,
                                              SoftmaxState& st, float (&o)[D / 16][4], float* mass_out,
-                                             const OutlierRef& orf) {
+                                             const OutlierTile& ot) {
     TokScale tk[1], tv[1];
     float x[1][4];
     load_tok_scales<TIER>(tp, g4, t4, tk[0], tv[0]);
     tile_scores<D, TIER>(tp, g4, t4, tk[0], qs, scale_log2, x[0]);
-    if constexpr (OUT) apply_k_outliers<D>(orf, g4, t4, qs, scale_log2, tp.ntok, x[0]);
+    if constexpr (OUT) {
+        if constexpr (side_dense(D)) dense_k_outliers<D>(ot, qs, scale_log2, tp.ntok, x[0]);
+        else walk_k_outliers<D>(ot, g4, t4, qs, scale_log2, tp.ntok, x[0]);
+    }
     uint32_t b01[1], b23[1], c01[1], c23[1];
     softmax_update<D / 16, 1, PRECISE, MASS>(x, st, o, b01, b23, c01, c23, mass_out);
-    if constexpr (OUT) apply_v_outliers<D>(orf, g4, t4, tp.ntok, st, x[0], o);
+    if constexpr (OUT) {
+        if constexpr (side_dense(D)) dense_v_outliers<D, PRECISE>(ot, tp.ntok, b01[0], b23[0], c01[0], c23[0], o);
+        else walk_v_outliers<D>(ot, g4, t4, tp.ntok, st, x[0], o);
+    }
     tile_pv<D, TIER, PRECISE>(tp, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
 }
 
@@ -768,7 +966,8 @@ __device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int 
 // SIDE: some arena carries outlier sidecars (a separate instantiation, so launches without them run
 // the plain kernel's register allocation).
 template <int D, bool PRECISE, bool MASS, bool SIDE>
-__global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_per_sm(D))
+    decode_attn_kernel(const __grid_constant__ Params p) {
     constexpr int KC = D / 16;
     constexpr int STAGE = stage_bytes(D);
     extern __shared__ __align__(128) unsigned char smem[];
@@ -867,6 +1066,15 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
     // memory past the last ring slot (load_qfrags layout), read back for every tile
     uint32_t* qsw = reinterpret_cast<uint32_t*>(smem + (size_t)kPairs * kStages * STAGE);
     const uint32_t qs = smem_u32(qsw);
+    // SIDE: each warp's outlier-correction buffer, past the query fragments
+    unsigned char* sbuf = SIDE ? smem + (size_t)kPairs * kStages * STAGE + stage_slack(D) + warp * side_warp_bytes(D)
+                               : nullptr;
+    if constexpr (SIDE && side_dense(D)) {
+        // dense delta tiles start (and are left after every use) all zero
+        for (int i = lane; i < side_warp_bytes(D) / 16; i += 32)
+            reinterpret_cast<uint4*>(sbuf)[i] = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+    }
     if (warp == 0) {
         constexpr int V = (2 * KC) % 4 == 0 ? 4 : 2;
         const int n = qg * kQ + g4;
@@ -900,6 +1108,31 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
         const argus_kv_chunk ch = nch;
         if (j + kPairWarps < n_pair) nch = p.chunks[first + (j + kPairWarps) * kPairs];
         const int stage = j % kStages;
+        // outlier corrections of the chunk's tiles, fetched before the wait: lane i < ntiles holds tile
+        // i's block address and key / value entry ranges (odir: the directory row of this (b, h))
+        const unsigned long long* odir = nullptr;
+        unsigned long long cblk = 0ull;
+        int ck0 = 0, ck1 = 0, cv0 = 0, cv1 = 0, cnt = 1;
+        bool cwhole = true;
+        if constexpr (SIDE) {
+            const argus_kv_arena& oa = p.arenas[ch.arena];
+            if (oa.outlier_dir) {
+                odir = reinterpret_cast<const unsigned long long*>(oa.outlier_dir) + (int64_t)bh * oa.dir_slots;
+                cwhole = whole_records(oa.layout, oa.page_tokens);
+                cnt = cwhole ? 1 : (oa.page_tokens + 15) >> 4;
+                if (lane < ch.ntiles) {
+                    const int ti = cwhole ? 0 : (ch.tok0 >> 4) + lane;
+                    cblk = __ldg(odir + (cwhole ? ch.slot0 + lane : ch.slot0));
+                    if (cblk) {
+                        const uint32_t* h = reinterpret_cast<const uint32_t*>(cblk);
+                        ck0 = (int)__ldg(h + 8 * ti);
+                        ck1 = (int)__ldg(h + 8 * ti + 8);
+                        cv0 = (int)__ldg(h + 8 * cnt + 1 + 8 * ti);
+                        cv1 = (int)__ldg(h + 8 * cnt + 1 + 8 * ti + 8);
+                    }
+                }
+            }
+        }
         {
             // bounded: chunk j is issued by whichever warp finishes chunk j - kStages
             long long spin = 0;
@@ -921,11 +1154,6 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
         if constexpr (MASS)
             mass_base = p.tile_lse + (((int64_t)bh * p.nqg + qg) * p.n_chunks + (first + j * kPairs)) * 16 * kQ;
         const bool rec16 = ar.layout == ARGUS_LAYOUT_RECORD && ar.page_tokens == 16;
-        // outlier corrections: directory row of this (b, h), or null
-        const unsigned long long* odir =
-            (SIDE && ar.outlier_dir)
-                ? reinterpret_cast<const unsigned long long*>(ar.outlier_dir) + (int64_t)bh * ar.dir_slots
-                : nullptr;
         switch (ar.tier) {
 #define ARGUS_TILE_LOOPS(T, OUT)                                                                                  \
         if (rec16) {                                                                                              \
@@ -941,10 +1169,10 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
                 tp.km = reinterpret_cast<const __half*>(r + 2 * PB + 64);                                         \
                 tp.vm = reinterpret_cast<const __half*>(r + 2 * PB + 96);                                         \
                 tp.ntok = 16;                                                                                     \
-                OutlierRef orf;                                                                                   \
-                if constexpr (OUT) { orf.entry = odir + ch.slot0 + i; orf.ti = 0; orf.nt = 1; }                  \
+                OutlierTile ot;                                                                                   \
+                if constexpr (OUT) ot = outlier_tile(cblk, ck0, ck1, cv0, cv1, i, 0, 1, sbuf);                  \
                 process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, st, o,                       \
-                                                       mass_base ? mass_base + i * kQ : nullptr, orf);            \
+                                                       mass_base ? mass_base + i * kQ : nullptr, ot);             \
             }                                                                                                     \
         } else {                                                                                                  \
             const ChunkView cv = chunk_view<D>(ar, n);                                                            \
@@ -958,20 +1186,11 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
                 tp.km = reinterpret_cast<const __half*>(sb + cv.km_off + so);                                     \
                 tp.vm = reinterpret_cast<const __half*>(sb + cv.vm_off + so);                                     \
                 tp.ntok = (i == n - 1) ? ch.ntok_last : cv.ntok_full;                                             \
-                OutlierRef orf;                                                                                   \
-                if constexpr (OUT) {                                                                              \
-                    if (whole_records(ar.layout, ar.page_tokens)) { /* tile i is page slot0 + i */               \
-                        orf.entry = odir + ch.slot0 + i;                                                          \
-                        orf.ti = 0;                                                                               \
-                        orf.nt = 1;                                                                               \
-                    } else { /* tile i is tokens tok0 + 16 i .. of page slot0 */                                 \
-                        orf.entry = odir + ch.slot0;                                                              \
-                        orf.ti = (ch.tok0 >> 4) + i;                                                              \
-                        orf.nt = (ar.page_tokens + 15) >> 4;                                                      \
-                    }                                                                                             \
-                }                                                                                                 \
+                OutlierTile ot;                                                                                   \
+                if constexpr (OUT) /* whole records: tile i is page slot0 + i; else tokens tok0 + 16 i .. */    \
+                    ot = outlier_tile(cblk, ck0, ck1, cv0, cv1, i, cwhole ? 0 : (ch.tok0 >> 4) + i, cnt, sbuf);   \
                 process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, st, o,                       \
-                                                       mass_base ? mass_base + i * kQ : nullptr, orf);            \
+                                                       mass_base ? mass_base + i * kQ : nullptr, ot);             \
             }                                                                                                     \
         }
 #define ARGUS_TILE_CASE(T)                                                                                        \
@@ -1087,12 +1306,13 @@ __global__ void __launch_bounds__(kThreads, ctas_per_sm(D)) decode_attn_kernel(c
 
 template <int D>
 int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
-    const size_t smem = (size_t)kPairs * kStages * stage_bytes(D) + stage_slack(D);
+    bool side = false;
+    for (int i = 0; i < ARGUS_MAX_ARENAS; ++i) side |= prm.arenas[i].outlier_dir != nullptr;
+    // kernels with outlier sidecars also hold one correction buffer per warp
+    const size_t smem = (size_t)kPairs * kStages * stage_bytes(D) + stage_slack(D) + (side ? kWarps * side_warp_bytes(D) : 0);
     static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kPairs * kStages * stage_bytes(D),
                   "merge buffer must fit in the stage memory");
     const bool mass = prm.tile_lse != nullptr;
-    bool side = false;
-    for (int i = 0; i < ARGUS_MAX_ARENAS; ++i) side |= prm.arenas[i].outlier_dir != nullptr;
     auto kern = side ? (precise ? (mass ? decode_attn_kernel<D, true, true, true> : decode_attn_kernel<D, true, false, true>)
                                 : (mass ? decode_attn_kernel<D, false, true, true> : decode_attn_kernel<D, false, false, true>))
                      : (precise ? (mass ? decode_attn_kernel<D, true, true, false> : decode_attn_kernel<D, true, false, false>)

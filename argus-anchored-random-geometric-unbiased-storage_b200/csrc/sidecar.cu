@@ -67,11 +67,17 @@ outliers_to_coo_kernel(const uint8_t* __restrict__ mask, const __half* __restric
 }
 
 // ------------------------------------------------------- correction blocks for the fused attention
-// Layout of one (b, h) block: uint32 k_off[NT + 1], uint32 v_off[NT + 1], argus_outlier entries[]
-// (key entries, then value entries), at byte offset
-//     bh * 8 (NT + 1) + 8 (key entries of earlier (b, h) + value entries of earlier (b, h))
-// of the page's buffer.  Entries of a row-major sidecar are already grouped by (b, h) and sorted by
-// token, so every offset is a binary search over the sidecar.
+// Layout of one (b, h) block (NT = ceil(P / 16) tiles, NH = 8 NT + 1):
+//     uint32 k_off[NH]    first key entry of token pair j (tokens 2j, 2j+1); k_off[8 NT] = key count
+//     uint32 v_off[NH]    first value entry of (tile i, dim group g) at 8i + g, dim group g being
+//                         dims [g D/8, (g+1) D/8); v_off[8 NT] = key count + value count
+//     argus_outlier entries[]   key entries in (token, dim) order, then value entries ordered by tile,
+//                               then dim, then token
+// at byte offset  bh * 8 NH + 8 (key entries of earlier (b, h) + value entries of earlier (b, h))  of
+// the page's buffer.  The offsets give each lane of the attention kernel its own run: key entries by
+// the token pair whose scores a lane holds, value entries by the dims of the output it holds.  A
+// row-major sidecar is already grouped by (b, h) and sorted by (token, dim), so every offset is a
+// binary search or a count over one tile.
 
 __device__ int g_side_status = 0;
 
@@ -116,34 +122,57 @@ __global__ void outlier_blocks_kernel(const int16_t* __restrict__ k_idx, const _
         }
         return;
     }
-    const int NT = (P + 15) >> 4;
+    const int NT = (P + 15) >> 4, NH = 8 * NT + 1, DG = D / 8;
     const int64_t r0 = (int64_t)bh * P, r1 = r0 + P;
     const int64_t kb = lower_row(k_idx, 0, nk, r0, H, P), ke = lower_row(k_idx, kb, nk, r1, H, P);
     const int64_t vb = lower_row(v_idx, 0, nv, r0, H, P), ve = lower_row(v_idx, vb, nv, r1, H, P);
     const int64_t nkb = ke - kb, nvb = ve - vb;
-    unsigned char* blk = blocks + (int64_t)bh * 8 * (NT + 1) + 8 * (kb + vb);
+    unsigned char* blk = blocks + (int64_t)bh * 8 * NH + 8 * (kb + vb);
     if (threadIdx.x == 0) block_addr[bh] = (nkb + nvb) > 0 ? (unsigned long long)(uintptr_t)blk : 0ull;
     if (nkb + nvb == 0) return;
-    uint32_t* hdr = reinterpret_cast<uint32_t*>(blk);
-    for (int i = threadIdx.x; i <= NT; i += blockDim.x) {
-        const int64_t tk = min((int64_t)P, (int64_t)16 * i);
-        hdr[i] = (uint32_t)(lower_row(k_idx, kb, ke, r0 + tk, H, P) - kb);
-        hdr[NT + 1 + i] = (uint32_t)(nkb + lower_row(v_idx, vb, ve, r0 + tk, H, P) - vb);
+    uint32_t* koff = reinterpret_cast<uint32_t*>(blk);
+    uint32_t* voff = koff + NH;
+    argus_outlier* ent = reinterpret_cast<argus_outlier*>(voff + NH);
+    for (int j = threadIdx.x; j < NH; j += blockDim.x) {
+        koff[j] = (uint32_t)(lower_row(k_idx, kb, ke, r0 + min((int64_t)P, 2 * (int64_t)j), H, P) - kb);
+        if (j == 8 * NT) {
+            voff[j] = (uint32_t)(nkb + nvb);
+        } else {
+            const int tile = j >> 3, g = j & 7;
+            const int64_t t0 = lower_row(v_idx, vb, ve, r0 + 16 * (int64_t)tile, H, P);
+            const int64_t t1 = lower_row(v_idx, t0, ve, r0 + min((int64_t)P, 16 * (int64_t)(tile + 1)), H, P);
+            int64_t below = 0;
+            for (int64_t i = t0; i < t1; ++i) below += v_idx[4 * i + 3] < g * DG;
+            voff[j] = (uint32_t)(nkb + (t0 - vb) + below);
+        }
     }
-    argus_outlier* ent = reinterpret_cast<argus_outlier*>(hdr + 2 * (NT + 1));
     const int64_t deq_bh = (int64_t)bh * P * D;
-    for (int64_t e = threadIdx.x; e < nkb + nvb; e += blockDim.x) {
-        const bool isv = e >= nkb;
-        const int16_t* idx = isv ? v_idx : k_idx;
-        const int64_t i = isv ? vb + (e - nkb) : kb + e;
-        const int t = idx[4 * i + 2], d = idx[4 * i + 3];
-        const float ov = __half2float(isv ? v_val[i] : k_val[i]);
-        const float dq = __half2float((isv ? v_deq : k_deq)[deq_bh + (int64_t)t * D + d]);
+    for (int64_t e = threadIdx.x; e < nkb; e += blockDim.x) {
+        const int64_t i = kb + e;
+        const int t = k_idx[4 * i + 2], d = k_idx[4 * i + 3];
         argus_outlier o;
         o.tok = (uint16_t)t;
         o.dim = (uint16_t)d;
-        o.delta = ov - dq;
+        o.delta = __half2float(k_val[i]) - __half2float(k_deq[deq_bh + (int64_t)t * D + d]);
         ent[e] = o;
+    }
+    for (int64_t e = threadIdx.x; e < nvb; e += blockDim.x) {
+        const int64_t i = vb + e;
+        const int t = v_idx[4 * i + 2], d = v_idx[4 * i + 3];
+        // position within the tile: entries of smaller dim, or of the same dim and an earlier token
+        const int tile = t >> 4;
+        const int64_t t0 = lower_row(v_idx, vb, ve, r0 + 16 * (int64_t)tile, H, P);
+        const int64_t t1 = lower_row(v_idx, t0, ve, r0 + min((int64_t)P, 16 * (int64_t)(tile + 1)), H, P);
+        int64_t rank = 0;
+        for (int64_t j = t0; j < t1; ++j) {
+            const int dj = v_idx[4 * j + 3];
+            rank += (dj < d) || (dj == d && j < i);
+        }
+        argus_outlier o;
+        o.tok = (uint16_t)t;
+        o.dim = (uint16_t)d;
+        o.delta = __half2float(v_val[i]) - __half2float(v_deq[deq_bh + (int64_t)t * D + d]);
+        ent[nkb + (t0 - vb) + rank] = o;
     }
 }
 
@@ -163,7 +192,7 @@ extern "C" {
 
 int64_t argus_outlier_blocks_bytes(int32_t bh, int32_t page_tokens, int64_t nk, int64_t nv) {
     if (bh <= 0 || page_tokens <= 0 || nk < 0 || nv < 0) return 0;
-    return (int64_t)bh * 8 * ((page_tokens + 15) / 16 + 1) + 8 * (nk + nv) + 16;
+    return (int64_t)bh * 8 * (8 * ((page_tokens + 15) / 16) + 1) + 8 * (nk + nv) + 16;
 }
 
 int argus_outlier_corrections(const int16_t* k_idx, const uint16_t* k_val, int64_t nk, const int16_t* v_idx,

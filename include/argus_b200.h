@@ -164,13 +164,16 @@ int64_t argus_outlier_blocks_bytes(int32_t bh, int32_t page_tokens, int64_t nk, 
  * value sidecars as COO (b, h, t, d) int16 indices in row-major order (torch.nonzero order, as
  * argus_outliers_to_coo writes them) with fp16 values; k_deq / v_deq: the page dequantized without
  * its sidecars, [B][H][P][D] fp16 (argus_page_dequantize).  Writes into `blocks` (16-byte aligned,
- * argus_outlier_blocks_bytes) one block per (b, h) with entries,
- *     uint32 k_off[NT + 1], uint32 v_off[NT + 1], argus_outlier entries[]   (NT = ceil(P / 16)),
- * k_off[i] / v_off[i] being the first key / value entry of 16-token tile i (k_off[NT] = key count,
- * value entries follow the key entries and v_off counts from the block's first entry), and
- * block_addr[b*H + h] = the block's device address, or 0 for a (b, h) without entries.  A sidecar
- * with an index outside [B, H, P, D] or out of row-major order makes every address 0 and sets the
- * status word argus_device_status reports (ARGUS_ERR_INVALID_ARGUMENT). */
+ * argus_outlier_blocks_bytes) one block per (b, h) with entries (NT = ceil(P / 16), NH = 8 NT + 1):
+ *     uint32 k_off[NH]   first key entry of token pair j (tokens 2j, 2j+1); k_off[8 NT] = key count
+ *     uint32 v_off[NH]   first value entry of tile i (tokens 16i ..) and dim group g (dims g D/8 ..
+ *                        (g+1) D/8 - 1) at 8i + g; v_off[8 NT] = key count + value count
+ *     argus_outlier entries[]   key entries in (token, dim) order, then value entries ordered by
+ *                               tile, dim, token
+ * (offsets index entries[]), and block_addr[b*H + h] = the block's device address, or 0 for a
+ * (b, h) without entries.  A sidecar with an index outside [B, H, P, D] or out of row-major order
+ * makes every address 0 and sets the status word argus_device_status reports
+ * (ARGUS_ERR_INVALID_ARGUMENT). */
 int argus_outlier_corrections(const int16_t* k_idx, const uint16_t* k_val, int64_t nk, const int16_t* v_idx,
                               const uint16_t* v_val, int64_t nv, const uint16_t* k_deq, const uint16_t* v_deq,
                               int32_t batch, int32_t heads, int32_t page_tokens, int32_t head_dim, void* blocks,

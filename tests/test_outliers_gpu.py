@@ -119,12 +119,14 @@ def _one_int8_page(sigma=1.0, seed=0):
 
 
 def test_correction_block_layout():
-    """The block written for each (b, h): tile offsets of key and value entries, then the entries
-    (token, dim, sidecar value minus dequantized value), as the header describes."""
+    """The block written for each (b, h), as the header describes: key offsets per token pair, value
+    offsets per (tile, dim group), key entries in (token, dim) order, value entries by tile, dim,
+    token; each entry carries sidecar value minus dequantized value."""
     from argus_b200 import paged
     import oracle
     pages = _one_int8_page()
     pg = pages["int8"][0]
+    D, P = 64, 16
     arenas, _ = U.arenas_from_pages(pages, sidecars=False)
     a = arenas[0]
     t = lambda key: torch.from_numpy(np.ascontiguousarray(pg[key])).cuda()  # noqa: E731
@@ -135,18 +137,22 @@ def test_correction_block_layout():
     base = blocks.data_ptr()
     kd = oracle.dequantize_from_int8(pg["key_q"], pg["key_scales"]).astype(np.float32)
     vd = oracle.dequantize_from_int8(pg["value_q"], pg["value_scales"]).astype(np.float32)
-    NT = 1
+    NH = 8 * 1 + 1
     for bh, ad in enumerate(addr.cpu().numpy().tolist()):
         h = bh % 2
-        ki = pg["key_out_indices"][pg["key_out_indices"][:, 1] == h]
-        kv = pg["key_out_values"][pg["key_out_indices"][:, 1] == h].astype(np.float32)
-        vi = pg["value_out_indices"][pg["value_out_indices"][:, 1] == h]
-        vv = pg["value_out_values"][pg["value_out_indices"][:, 1] == h].astype(np.float32)
+        sel_k = pg["key_out_indices"][:, 1] == h
+        sel_v = pg["value_out_indices"][:, 1] == h
+        ki, kv = pg["key_out_indices"][sel_k], pg["key_out_values"][sel_k].astype(np.float32)
+        vi, vv = pg["value_out_indices"][sel_v], pg["value_out_values"][sel_v].astype(np.float32)
+        order = np.lexsort((vi[:, 2], vi[:, 3], vi[:, 2] // 16))  # tile, then dim, then token
+        vi, vv = vi[order], vv[order]
         assert ad != 0
         off = ad - base
-        hdr = raw[off:off + 8 * (NT + 1)].view(np.uint32)
-        assert hdr.tolist() == [0, len(ki), len(ki), len(ki) + len(vi)]
-        ent = raw[off + 8 * (NT + 1):off + 8 * (NT + 1) + 8 * (len(ki) + len(vi))].view(np.uint16).reshape(-1, 4)
+        hdr = raw[off:off + 8 * NH].view(np.uint32)
+        koff, voff = hdr[:NH], hdr[NH:]
+        assert koff.tolist() == [int(np.sum(ki[:, 2] < 2 * j)) for j in range(NH)]
+        assert voff.tolist() == [len(ki) + int(np.sum(vi[:, 3] < g * (D // 8))) for g in range(8)] + [len(ki) + len(vi)]
+        ent = raw[off + 8 * NH:off + 8 * NH + 8 * (len(ki) + len(vi))].view(np.uint16).reshape(-1, 4)
         delta = ent[:, 2:].copy().view(np.float32).reshape(-1)
         assert (ent[:len(ki), 0] == ki[:, 2]).all() and (ent[:len(ki), 1] == ki[:, 3]).all()
         assert (ent[len(ki):, 0] == vi[:, 2]).all() and (ent[len(ki):, 1] == vi[:, 3]).all()
