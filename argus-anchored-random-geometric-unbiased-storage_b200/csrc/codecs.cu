@@ -102,6 +102,23 @@ __device__ __forceinline__ float cascade_combine(float mine) {
     return total;
 }
 
+// fl32(x / s) for fp16 values x and s, s finite and > 0: the quotient from the correctly rounded
+// reciprocal r = RN(1/s) and one FMA correction (Markstein's final division step, P. Markstein,
+// IBM J. Res. Dev. 34(1), 1990).  For fp16 operands no intermediate overflows or underflows fp32,
+// and argus_selftest_fp16_quotients checks it against the IEEE-rounded divide for every such pair.
+__device__ __forceinline__ float quot_rn(float x, float s, float r) {
+    const float q0 = __fmul_rn(x, r);
+    const float e = __fmaf_rn(-s, q0, x);
+    return __fmaf_rn(e, r, q0);
+}
+// The per-row divisor of a quantizer: the reciprocal when the fast quotient applies (0 otherwise).
+__device__ __forceinline__ float quot_recip(float s) {
+    return (s > 0.0f && s <= 65504.0f) ? __frcp_rn(s) : 0.0f;
+}
+__device__ __forceinline__ float quot(float x, float s, float r) {
+    return r != 0.0f ? quot_rn(x, s, r) : __fdiv_rn(x, s);
+}
+
 // NaN/Inf cleaned to +0 (isolate_outliers' cleanse step).
 __device__ __forceinline__ __half clean_nan_inf(__half h) {
     unsigned short b = __half_as_ushort(h);
@@ -171,6 +188,7 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
     __half* tile = reinterpret_cast<__half*>(smem_raw);
     float* st_a = reinterpret_cast<float*>(smem_raw + (size_t)tile_rows * stride * sizeof(__half));
     float* st_b = st_a + tile_rows;
+    float* st_r = st_b + tile_rows;  // reciprocal of the scale for the fast quotient (0: IEEE divide)
 
     const int tiles_per_group = (group_rows + tile_rows - 1) / tile_rows;
     const int64_t n_tiles = n_groups * tiles_per_group;
@@ -244,7 +262,11 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
                 const float mean = rh(__fdiv_rn(total, (float)D));  // fp16(sum / D)
                 a = (MODE == Q_SIGN1) ? mean : rh(__fmul_rn(mean, sigma));  // outliers: fp16(mean * sigma)
             }
-            if (live && lane8 == 0) { st_a[rb] = a; st_b[rb] = b; }
+            if (live && lane8 == 0) {
+                st_a[rb] = a;
+                st_b[rb] = b;
+                st_r[rb] = quot_recip(a);
+            }
         }
         __syncthreads();
         // 3. outputs: 4 consecutive columns x `per` rows per thread
@@ -263,7 +285,7 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
             for (int i = 0; i < per; ++i) {
                 const int r = pr * per + i;
                 const __half* hp = tile + r * stride + cq * 4;
-                const float a = st_a[r], b = st_b[r];
+                const float a = st_a[r], b = st_b[r], ra = st_r[r];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const float v = h2f(hp[e]);
@@ -271,11 +293,11 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
                     if (MODE == Q_INT8 || MODE == Q_FP8SIM) {
                         const float lo = (MODE == Q_INT8) ? -128.0f : -240.0f;
                         const float hi = (MODE == Q_INT8) ? 127.0f : 240.0f;
-                        code = w8(clamp_nan(round_even(rh(__fdiv_rn(v, a))), lo, hi));
+                        code = w8(clamp_nan(round_even(rh(quot(v, a, ra))), lo, hi));
                         word |= code << (8 * e);
                     } else if (MODE == Q_INT4 || MODE == Q_INT2) {
                         const float qmax = (MODE == Q_INT4) ? 15.0f : 3.0f;
-                        code = w8(clamp_nan(round_even(rh(__fdiv_rn(rh(__fsub_rn(v, b)), a))), 0.0f, qmax));
+                        code = w8(clamp_nan(round_even(rh(quot(rh(__fsub_rn(v, b)), a, ra))), 0.0f, qmax));
                         word |= code << (8 * e + (MODE == Q_INT4 ? 4 : 2) * i);
                     } else if (MODE == Q_SIGN1) {
                         code = (v >= 0.0f) ? 1u : 0u;  // false for NaN, true for -0
@@ -313,6 +335,174 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
             }
         }
         __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------ register-only packing from fp16
+// The order-free tiers (INT8, FP8-sim: amax; INT4, INT2: min/max) packed straight from fp16 rows
+// without a shared-memory tile: 8 lanes take one packed row (the `per` token rows that share an
+// output byte row), each lane D/8 consecutive columns of every row; the row statistics are reduced
+// across the 8 lanes with shuffles and each lane writes its D/8 output bytes.  Per-element
+// arithmetic is the same as quant_kernel's.
+template <int BYTES>
+__device__ __forceinline__ void ld_bytes(const unsigned char* p, uint32_t (&r)[BYTES / 4]) {
+    if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+        for (int i = 0; i < BYTES / 16; ++i) {
+            const uint4 v = __ldcs(reinterpret_cast<const uint4*>(p) + i);
+            r[4 * i] = v.x; r[4 * i + 1] = v.y; r[4 * i + 2] = v.z; r[4 * i + 3] = v.w;
+        }
+    } else if constexpr (BYTES == 8) {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+        r[0] = v.x; r[1] = v.y;
+    } else {
+        r[0] = __ldcs(reinterpret_cast<const unsigned int*>(p));
+    }
+}
+template <int BYTES>
+__device__ __forceinline__ void st_bytes(unsigned char* p, const uint32_t* r) {
+    if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+        for (int i = 0; i < BYTES / 16; ++i)
+            reinterpret_cast<uint4*>(p)[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+    } else if constexpr (BYTES == 8) {
+        *reinterpret_cast<uint2*>(p) = make_uint2(r[0], r[1]);
+    } else if constexpr (BYTES == 4) {
+        *reinterpret_cast<uint32_t*>(p) = r[0];
+    } else {
+        *reinterpret_cast<uint16_t*>(p) = (uint16_t)r[0];
+    }
+}
+
+template <int MODE, int D>
+__global__ void __launch_bounds__(256) pack_rows_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows) {
+    constexpr int per = mode_per(MODE);
+    constexpr int C = D / 8;                     // columns per lane
+    constexpr int LW = (C * 2 + 3) / 4;          // u32 words of one row's columns
+    constexpr int OW = (C + 3) / 4;              // u32 words of the lane's output bytes
+    const int lane8 = threadIdx.x & 7;
+    const int64_t prg = group_rows / per;        // packed rows per group
+    const int64_t total = n_groups * prg;
+    for (int64_t pr = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3; pr < total;
+         pr += ((int64_t)gridDim.x * blockDim.x) >> 3) {
+        const int64_t g = pr / prg;
+        const int prl = (int)(pr - g * prg);
+        uint32_t raw[per][LW];
+#pragma unroll
+        for (int i = 0; i < per; ++i)
+            ld_bytes<C * 2>(src.payload + g * src.group_stride + (int64_t)(src.row0 + prl * per + i) * D * 2 + lane8 * C * 2,
+                            raw[i]);
+        float sa[per], sb[per], sr[per];
+#pragma unroll
+        for (int i = 0; i < per; ++i) {
+            const __half* hv = reinterpret_cast<const __half*>(raw[i]);
+            bool nan = false;
+            float m = 0.0f, lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const float v = h2f(hv[c]);
+                nan |= (v != v);
+                if (MODE == Q_INT8 || MODE == Q_FP8SIM) m = fmaxf(m, fabsf(v));
+                else { lo = fminf(lo, v); hi = fmaxf(hi, v); }
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                if (MODE == Q_INT8 || MODE == Q_FP8SIM) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                else {
+                    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+                    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+                }
+                nan |= __shfl_xor_sync(0xffffffffu, (int)nan, o) != 0;
+            }
+            if (MODE == Q_INT8 || MODE == Q_FP8SIM) {
+                const float div = (MODE == Q_INT8) ? 127.0f : 240.0f;
+                sa[i] = nan ? __int_as_float(0x7fc00000) : rh(__fdiv_rn(m, div));
+                sb[i] = 0.0f;
+            } else {
+                const float qmax = (MODE == Q_INT4) ? 15.0f : 3.0f;
+                sa[i] = nan ? __int_as_float(0x7fc00000) : rh(__fdiv_rn(rh(__fsub_rn(hi, lo)), qmax));
+                sb[i] = nan ? __int_as_float(0x7fc00000) : lo;
+            }
+            sr[i] = quot_recip(sa[i]);
+        }
+        uint32_t out[OW];
+#pragma unroll
+        for (int w = 0; w < OW; ++w) out[w] = 0u;
+        bool fast = true;
+#pragma unroll
+        for (int i = 0; i < per; ++i) fast &= sr[i] != 0.0f;  // finite positive scales (no NaN row)
+        if (fast) {
+            // Column pairs in half2 lanes.  q = fl32(x / s) by the reciprocal and one FMA correction;
+            // fp16(q) + 1536 rounds q to an integer (RNE at spacing 1) and puts its two's-complement
+            // low byte in the half's low byte (|q| < 512 here), clamped in that offset domain.
+            constexpr float kLo = (MODE == Q_INT8) ? -128.0f : (MODE == Q_FP8SIM ? -240.0f : 0.0f);
+            constexpr float kHi = (MODE == Q_INT8) ? 127.0f : (MODE == Q_FP8SIM ? 240.0f : (MODE == Q_INT4 ? 15.0f : 3.0f));
+            const __half2 off = __float2half2_rn(1536.0f);
+            const __half2 clo = __float2half2_rn(1536.0f + kLo), chi = __float2half2_rn(1536.0f + kHi);
+            uint32_t cw[per][(C + 1) / 2];  // per row, per column pair: offset codes (half2 bits)
+#pragma unroll
+            for (int i = 0; i < per; ++i) {
+                const float2 s2 = make_float2(sa[i], sa[i]), r2 = make_float2(sr[i], sr[i]);
+                const float2 ns2 = make_float2(-sa[i], -sa[i]);
+                const __half2 mn2 = __float2half2_rn(sb[i]);
+#pragma unroll
+                for (int k = 0; k < C / 2; ++k) {
+                    __half2 h = reinterpret_cast<const __half2*>(raw[i])[k];
+                    if (MODE == Q_INT4 || MODE == Q_INT2) h = __hsub2(h, mn2);  // fp16(x - mn)
+                    const float2 x2 = __half22float2(h);
+                    const float2 q0 = __fmul2_rn(x2, r2);
+                    const float2 e = __ffma2_rn(ns2, q0, x2);
+                    const float2 q = __ffma2_rn(e, r2, q0);
+                    const __half2 m = __hmin2(__hmax2(__hadd2(__float22half2_rn(q), off), clo), chi);
+                    cw[i][k] = *reinterpret_cast<const uint32_t*>(&m);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < C / 2; ++k) {
+                uint32_t pairw;  // bytes 0 and 2: the two columns' output bytes
+                if (MODE == Q_INT8 || MODE == Q_FP8SIM) {
+                    pairw = cw[0][k] & 0x00FF00FFu;
+                } else if (MODE == Q_INT4) {
+                    pairw = (cw[0][k] & 0x000F000Fu) | ((cw[1][k] & 0x000F000Fu) << 4);
+                } else {
+                    pairw = (cw[0][k] & 0x00030003u) | ((cw[1][k] & 0x00030003u) << 2) |
+                            ((cw[2][k] & 0x00030003u) << 4) | ((cw[3][k] & 0x00030003u) << 6);
+                }
+                // columns 2k, 2k+1 -> bytes (2k) & 3, (2k+1) & 3 of out[k / 2]
+                if (k & 1) out[k >> 1] |= __byte_perm(pairw, 0u, 0x2044) & 0xFFFF0000u;
+                else       out[k >> 1] |= __byte_perm(pairw, 0u, 0x4420) & 0x0000FFFFu;
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                uint32_t byte = 0;
+#pragma unroll
+                for (int i = 0; i < per; ++i) {
+                    const float v = h2f(reinterpret_cast<const __half*>(raw[i])[c]);
+                    if (MODE == Q_INT8 || MODE == Q_FP8SIM) {
+                        const float lo = (MODE == Q_INT8) ? -128.0f : -240.0f;
+                        const float hi = (MODE == Q_INT8) ? 127.0f : 240.0f;
+                        byte = w8(clamp_nan(round_even(rh(quot(v, sa[i], sr[i]))), lo, hi));
+                    } else {
+                        const float qmax = (MODE == Q_INT4) ? 15.0f : 3.0f;
+                        byte |= w8(clamp_nan(round_even(rh(quot(rh(__fsub_rn(v, sb[i])), sa[i], sr[i]))), 0.0f, qmax))
+                                << ((MODE == Q_INT4 ? 4 : 2) * i);
+                    }
+                }
+                out[c >> 2] |= (byte & 0xffu) << (8 * (c & 3));
+            }
+        }
+        st_bytes<C>(dst.payload + g * dst.group_stride + (int64_t)((dst.row0 + prl * per) / per) * D + lane8 * C, out);
+        if (lane8 < per) {
+            // lane i writes row i's scale (and min)
+            float a = sa[0], b = sb[0];
+#pragma unroll
+            for (int i = 1; i < per; ++i)
+                if (lane8 == i) { a = sa[i]; b = sb[i]; }
+            const int64_t si = g * dst.sgroup_stride + dst.row0 + prl * per + lane8;
+            if (dst.scales) dst.scales[si] = f2h(a);
+            if (MODE == Q_INT4 || MODE == Q_INT2) dst.mins[si] = f2h(b);
+        }
     }
 }
 
@@ -380,12 +570,50 @@ int tile_rows_for(int D, int group_rows) {
     return tr;
 }
 
+template <int MODE, int D>
+int launch_pack_rows(const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, cudaStream_t st) {
+    const int64_t threads = n_groups * (group_rows / mode_per(MODE)) * 8;
+    pack_rows_kernel<MODE, D><<<argus_grid_cap((threads + 255) / 256), 256, 0, st>>>(src, dst, n_groups, group_rows);
+    ARGUS_CHECK_LAUNCH();
+    return ARGUS_OK;
+}
+
+// Whether pack_rows_kernel takes a launch: an order-free tier from fp16, a head dim it is built for,
+// whole packed rows per group and 16-byte aligned rows (its vector loads and stores).
+bool pack_rows_ok(int mode, int src_mode, const Rows& src, const Rows& dst, int group_rows, int D) {
+    if (src_mode != Q_FP16 || !(mode == Q_INT8 || mode == Q_FP8SIM || mode == Q_INT4 || mode == Q_INT2)) return false;
+    if (D != 16 && D != 32 && D != 64 && D != 128 && D != 256) return false;
+    const int per = mode_per(mode);
+    if (group_rows % per || src.row0 % per || dst.row0 % per) return false;
+    const int lb = (D / 8) * 2;  // bytes one lane loads per row
+    const int la = lb >= 16 ? 16 : lb;
+    const int ob = D / 8;        // bytes one lane stores per packed row
+    const int oa = ob >= 16 ? 16 : ob;
+    return argus_aligned(src.payload, la) && src.group_stride % la == 0 && argus_aligned(dst.payload, oa) &&
+           dst.group_stride % oa == 0;
+}
+
+template <int MODE>
+int pack_rows_dispatch(const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, int D, cudaStream_t st) {
+    switch (D) {
+        case 16: return launch_pack_rows<MODE, 16>(src, dst, n_groups, group_rows, st);
+        case 32: return launch_pack_rows<MODE, 32>(src, dst, n_groups, group_rows, st);
+        case 64: return launch_pack_rows<MODE, 64>(src, dst, n_groups, group_rows, st);
+        case 128: return launch_pack_rows<MODE, 128>(src, dst, n_groups, group_rows, st);
+        default: return launch_pack_rows<MODE, 256>(src, dst, n_groups, group_rows, st);
+    }
+}
+
 template <int MODE, int SRC>
 int launch_quant(const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, int D, float sigma,
                  uint16_t* outv, uint8_t* mask, cudaStream_t st) {
     if (n_groups == 0 || group_rows == 0) return ARGUS_OK;
+    if constexpr (SRC == Q_FP16 && (MODE == Q_INT8 || MODE == Q_FP8SIM || MODE == Q_INT4 || MODE == Q_INT2)) {
+        if (pack_rows_ok(MODE, SRC, src, dst, group_rows, D))
+            return pack_rows_dispatch<MODE>(src, dst, n_groups, group_rows, D, st);
+    }
     const int tile_rows = tile_rows_for(D, group_rows);
-    const size_t smem = (size_t)tile_rows * (D + 8) * sizeof(__half) + 2 * tile_rows * sizeof(float);
+    const size_t smem = (size_t)tile_rows * (D + 8) * sizeof(__half) + 3 * tile_rows * sizeof(float);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(quant_kernel<MODE, SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return argus_set_cuda_error(e);
@@ -468,6 +696,24 @@ int check_arena(const argus_kv_arena* a, int D) {
     return ARGUS_OK;
 }
 
+// Every pair of a finite fp16 value x and a positive finite fp16 value s (the divisors quot_recip
+// admits): counts where quot_rn differs from the IEEE-rounded divide (for x = -0 it returns +0,
+// which rounds, clamps and casts to the same code).  One CTA per divisor.
+__global__ void quotient_selftest_kernel(unsigned long long* mismatches) {
+    const unsigned short sb = (unsigned short)(blockIdx.x + 1);  // 0x0001 .. 0x7BFF
+    const float sv = __half2float(__ushort_as_half(sb));
+    const float r = __frcp_rn(sv);
+    unsigned long long bad = 0;
+    for (int xi = threadIdx.x; xi < 0x10000; xi += blockDim.x) {
+        const __half xh = __ushort_as_half((unsigned short)xi);
+        if ((xi & 0x7c00) == 0x7c00) continue;  // inf / NaN
+        const float xv = __half2float(xh);
+        const float a = quot_rn(xv, sv, r), b = __fdiv_rn(xv, sv);
+        bad += a != b;  // +0 and -0 compare equal: the sign of a zero quotient reaches no code
+    }
+    if (bad) atomicAdd(mismatches, bad);
+}
+
 }  // namespace argus
 
 using namespace argus;
@@ -523,6 +769,22 @@ int flat_dequant(int mode, const void* payload, const uint16_t* s, const uint16_
 }  // namespace
 
 extern "C" {
+
+int argus_selftest_fp16_quotients(unsigned long long* mismatches, argus_stream_t stream) {
+    if (!mismatches) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    unsigned long long* d = nullptr;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&d), sizeof(*d), st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(d, 0, sizeof(*d), st);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    argus::quotient_selftest_kernel<<<0x7BFF, 256, 0, st>>>(d);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(mismatches, d, sizeof(*d), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFreeAsync(d, st);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    return ARGUS_OK;
+}
 
 int argus_quant_int8(const uint16_t* x, int64_t n_rows, int D, int8_t* q, uint16_t* scales, argus_stream_t stream) {
     int rc = check_rows(x, q, n_rows, D, 1);

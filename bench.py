@@ -22,6 +22,7 @@ Two further single-GPU workloads (not the headline line) are measured by the sam
                                                    # tier (oldest 25%) in pinned host memory, streamed
     python bench.py --workload tinyllama-sidecars  # TinyLlama-shaped layer: H_q 32, H_kv 4, D 64, 4096
                                                    # tokens, 3840 in INT8 pages with outlier sidecars
+    python bench.py --workload cascade             # pack/unpack of every tier, 1M tokens x 8 heads x 128
 
 --impl reference times the CPU restatement of the reference's path (dequantize every page, then
 softmax attention over the reconstructed K/V; argus_cache core/memory_manager.py:1157-1315 +
@@ -578,6 +579,88 @@ def _tinyllama_cpu(k, v, q, Pt, HQt, min_seconds=10.0):
                       f"({n * dt:.1f} s of CPU work)"}
 
 
+def run_cascade(args):
+    """Quantize/pack cascade microbench: 1,048,576 tokens x 8 KV heads x 128 fp16 (2 GiB, N(0,1)
+    with 1% of the values from Laplace(0,4)) packed into every tier and unpacked again through the
+    public codec API; bytes = input read + payload and metadata written (unpack: the mirror)."""
+    import torch
+
+    from argus_b200.core import quantization as Q
+
+    dev = torch.device("cuda", 0)
+    Bc, Hc, Tc, Dc = 1, 8, 1048576, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(Bc, Hc, Tc, Dc, device=dev, generator=g, dtype=torch.float16)
+    u = torch.rand(Bc, Hc, Tc, Dc, device=dev, generator=g) - 0.5
+    lap = (-4.0 * torch.sign(u) * torch.log1p(-2.0 * u.abs())).half()
+    x = torch.where(torch.rand(Bc, Hc, Tc, Dc, device=dev, generator=g) < 0.01, lap, x)
+    del u, lap
+    torch.cuda.synchronize()
+    tiers = [("fp8_sim", Q.quantize_to_fp8_simulated, Q.dequantize_from_fp8_simulated),
+             ("int8", Q.quantize_to_int8, Q.dequantize_from_int8),
+             ("int4", Q.quantize_to_int4_packed, Q.dequantize_from_int4_packed),
+             ("int2", Q.quantize_to_int2_packed, Q.dequantize_from_int2_packed),
+             ("1bit", Q.quantize_to_1bit_packed, Q.dequantize_from_1bit_packed)]
+    hbm, peak_kind = peaks()
+    xbytes = x.numel() * 2
+    per_tier, tot_bytes, tot_ms = {}, 0, 0.0
+    for name, qf, df in tiers:
+        coded = qf(x)
+        cbytes = sum(t.numel() * t.element_size() for t in coded)
+        ms_p = _timed(lambda: qf(x), args.steps, args.warmup)
+        ms_u = _timed(lambda: df(*coded), args.steps, args.warmup)
+        nb = xbytes + cbytes
+        per_tier[name] = {"pack_ms": ms_p, "unpack_ms": ms_u, "pack_GBs": nb / ms_p / 1e6, "unpack_GBs": nb / ms_u / 1e6,
+                          "pack_frac": nb / ms_p / 1e6 / hbm, "unpack_frac": nb / ms_u / 1e6 / hbm,
+                          "coded_bytes": cbytes}
+        tot_bytes += 2 * nb
+        tot_ms += ms_p + ms_u
+        del coded
+        torch.cuda.empty_cache()
+    value = tot_bytes / tot_ms / 1e6
+    line = {"metric": "quantize/pack cascade microbench, pack+unpack GB/s over all tiers", "value": value,
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms,
+            "higher_is_better": True, "dtype": "fp16->u8/i8", "data": "synthetic",
+            "config": {"workload": "cascade-microbench", "tokens": Tc, "kv_heads": Hc, "head_dim": Dc,
+                       "outliers": "1% Laplace(0,4)", "l2": "inputs larger than L2 (2 GiB), no flush"},
+            "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s", "frac": value / hbm,
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_step": tot_bytes},
+            "tiers": per_tier}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = _cascade_cpu()
+    print(json.dumps(line), flush=True)
+
+
+def _cascade_cpu(min_seconds=10.0):
+    """The reference's CPU codecs (oracle port, bit-exact) on a bounded sample of the same tensor
+    shape: pack+unpack of every tier over 8 heads x 16384 tokens, GB/s by the same byte count."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((1, 8, 16384, 128), dtype=np.float32)
+    m = rng.random(x.shape) < 0.01
+    x[m] = rng.laplace(0, 4, m.sum())
+    x = x.astype(np.float16)
+    fns = [(oracle.quantize_to_fp8_simulated, oracle.dequantize_from_int8),
+           (oracle.quantize_to_int8, oracle.dequantize_from_int8),
+           (oracle.quantize_to_int4_packed, oracle.dequantize_from_int4_packed),
+           (oracle.quantize_to_int2_packed, oracle.dequantize_from_int2_packed),
+           (oracle.quantize_to_1bit_packed, oracle.dequantize_from_1bit_packed)]
+    t0 = time.perf_counter()
+    nbytes, n = 0, 0
+    while n < 1 or time.perf_counter() - t0 < min_seconds:
+        for qf, df in fns:
+            coded = qf(x)
+            df(*coded)
+            nbytes += 2 * (x.nbytes + sum(c.nbytes for c in coded))
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"1 x 8 heads x 16384 tokens x 128, every tier packed and unpacked, {n} rounds ({dt:.1f} s)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -585,8 +668,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b-spill", "tinyllama-sidecars"),
-                    default="llama3-8b-layer")
+    ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b-spill", "tinyllama-sidecars",
+                                           "cascade"), default="llama3-8b-layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "jl-archive":
@@ -597,6 +680,9 @@ def main():
         return
     if args.workload == "tinyllama-sidecars":
         run_tinyllama_sidecars(args)
+        return
+    if args.workload == "cascade":
+        run_cascade(args)
         return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

@@ -366,6 +366,14 @@ int argus_decode_attention_noalloc(const argus_attn_shape* shape, const argus_kv
 /* Bytes of the built-in scratch of argus_decode_attention_noalloc. */
 int64_t argus_decode_attention_noalloc_capacity(void);
 
+/* Self-test of the quantizers' fast exact quotient: for every finite fp16 x and positive finite
+ * fp16 s, the quotient computed from the correctly rounded reciprocal of s with one FMA correction
+ * is compared with the IEEE-rounded fp32 divide (equal values; a zero quotient may differ in sign,
+ * which reaches no code); *mismatches (host) receives the count (0 when the fast path may stand in
+ * for the divide).  Synchronises `stream`.  No counterpart in the
+ * reference. */
+int argus_selftest_fp16_quotients(unsigned long long* mismatches, argus_stream_t stream);
+
 /* Reads (and clears) the device-side status words that bounded waits in the kernels set on a
  * timeout, and argus_outlier_corrections on a bad sidecar; writes ARGUS_OK, ARGUS_ERR_TIMEOUT or
  * ARGUS_ERR_INVALID_ARGUMENT to *status after synchronising `stream`. */
