@@ -506,6 +506,73 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(Rows src, Rows dst, int6
     }
 }
 
+// 1-bit packing from fp16 without a block-wide tile: 8 lanes take one packed row (8 token rows),
+// each lane D/8 consecutive columns of every row.  A row's mean |x| must follow ATen's cascade
+// order (lane l sums columns 8c + l), so each row passes through a small per-group shared-memory
+// buffer where the 8 lanes read it strided; the sign bits come from the lane's own registers.
+template <int D>
+__global__ void __launch_bounds__(256) pack_sign_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows) {
+    constexpr int C = D / 8;
+    constexpr int LW = (C * 2 + 3) / 4;
+    constexpr int OW = (C + 3) / 4;
+    constexpr int RS = D + 8;  // halves per buffered row: 16-byte pad staggers the groups' banks
+    __shared__ __align__(16) __half rowbuf[256 / 8][RS];
+    const int lane8 = threadIdx.x & 7;
+    __half* buf = rowbuf[threadIdx.x >> 3];
+    const int64_t prg = group_rows / 8;
+    const int64_t total = n_groups * prg;
+    const int64_t stride = ((int64_t)gridDim.x * blockDim.x) >> 3;
+    // every lane runs the same number of iterations (the shuffles and warp barriers need the whole warp)
+    const int64_t first = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >> 3;
+    for (int64_t base = first; base < total; base += stride) {
+        const int64_t pr = base + ((threadIdx.x & 31) >> 3);
+        const bool live = pr < total;
+        const int64_t g = live ? pr / prg : 0;
+        const int prl = live ? (int)(pr - g * prg) : 0;
+        uint32_t raw[8][LW];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (live)
+                ld_bytes<C * 2>(src.payload + g * src.group_stride + (int64_t)(src.row0 + prl * 8 + i) * D * 2 + lane8 * C * 2,
+                                raw[i]);
+            else
+#pragma unroll
+                for (int w = 0; w < LW; ++w) raw[i][w] = 0u;
+        }
+        float sa[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+#pragma unroll
+            for (int w = 0; w < LW; ++w) reinterpret_cast<uint32_t*>(buf + lane8 * C)[w] = raw[i][w];
+            __syncwarp();
+            const float lane_sum = cascade_lane_sum<true>(buf, D / 8, lane8);
+            sa[i] = rh(__fdiv_rn(cascade_combine(lane_sum), (float)D));  // fp16(sum |x| / D)
+            __syncwarp();
+        }
+        uint32_t out[OW];
+#pragma unroll
+        for (int w = 0; w < OW; ++w) out[w] = 0u;
+        const __half2 zero2 = __float2half2_rn(0.0f);
+#pragma unroll
+        for (int k = 0; k < C / 2; ++k) {
+            uint32_t pairw = 0u;  // bit i of bytes 0 / 2: x >= 0 for row i, columns 2k / 2k+1 (NaN: 0, -0: 1)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                pairw |= __hge2_mask(reinterpret_cast<const __half2*>(raw[i])[k], zero2) & (0x00010001u << i);
+            if (k & 1) out[k >> 1] |= __byte_perm(pairw, 0u, 0x2044) & 0xFFFF0000u;
+            else       out[k >> 1] |= __byte_perm(pairw, 0u, 0x4420) & 0x0000FFFFu;
+        }
+        if (live) {
+            st_bytes<C>(dst.payload + g * dst.group_stride + (int64_t)((dst.row0 + prl * 8) / 8) * D + lane8 * C, out);
+            float a = sa[0];
+#pragma unroll
+            for (int i = 1; i < 8; ++i)
+                if (lane8 == i) a = sa[i];
+            if (dst.scales) dst.scales[g * dst.sgroup_stride + dst.row0 + prl * 8 + lane8] = f2h(a);
+        }
+    }
+}
+
 // Outlier isolation with sigma <= 0: cleanse NaN/Inf only, no outliers.
 __global__ void cleanse_kernel(const __half* __restrict__ x, int64_t n, __half* __restrict__ normal,
                                __half* __restrict__ outv, uint8_t* __restrict__ mask) {
@@ -578,10 +645,11 @@ int launch_pack_rows(const Rows& src, const Rows& dst, int64_t n_groups, int gro
     return ARGUS_OK;
 }
 
-// Whether pack_rows_kernel takes a launch: an order-free tier from fp16, a head dim it is built for,
-// whole packed rows per group and 16-byte aligned rows (its vector loads and stores).
+// Whether pack_rows_kernel / pack_sign_kernel take a launch: a tier packed from fp16, a head dim
+// they are built for, whole packed rows per group and aligned rows (their vector loads and stores).
 bool pack_rows_ok(int mode, int src_mode, const Rows& src, const Rows& dst, int group_rows, int D) {
-    if (src_mode != Q_FP16 || !(mode == Q_INT8 || mode == Q_FP8SIM || mode == Q_INT4 || mode == Q_INT2)) return false;
+    if (src_mode != Q_FP16 || !(mode == Q_INT8 || mode == Q_FP8SIM || mode == Q_INT4 || mode == Q_INT2 || mode == Q_SIGN1))
+        return false;
     if (D != 16 && D != 32 && D != 64 && D != 128 && D != 256) return false;
     const int per = mode_per(mode);
     if (group_rows % per || src.row0 % per || dst.row0 % per) return false;
@@ -593,14 +661,32 @@ bool pack_rows_ok(int mode, int src_mode, const Rows& src, const Rows& dst, int 
            dst.group_stride % oa == 0;
 }
 
+template <int D>
+int launch_pack_sign(const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, cudaStream_t st) {
+    const int64_t threads = n_groups * (group_rows / 8) * 8;
+    pack_sign_kernel<D><<<argus_grid_cap((threads + 255) / 256), 256, 0, st>>>(src, dst, n_groups, group_rows);
+    ARGUS_CHECK_LAUNCH();
+    return ARGUS_OK;
+}
+
 template <int MODE>
 int pack_rows_dispatch(const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, int D, cudaStream_t st) {
-    switch (D) {
-        case 16: return launch_pack_rows<MODE, 16>(src, dst, n_groups, group_rows, st);
-        case 32: return launch_pack_rows<MODE, 32>(src, dst, n_groups, group_rows, st);
-        case 64: return launch_pack_rows<MODE, 64>(src, dst, n_groups, group_rows, st);
-        case 128: return launch_pack_rows<MODE, 128>(src, dst, n_groups, group_rows, st);
-        default: return launch_pack_rows<MODE, 256>(src, dst, n_groups, group_rows, st);
+    if constexpr (MODE == Q_SIGN1) {
+        switch (D) {
+            case 16: return launch_pack_sign<16>(src, dst, n_groups, group_rows, st);
+            case 32: return launch_pack_sign<32>(src, dst, n_groups, group_rows, st);
+            case 64: return launch_pack_sign<64>(src, dst, n_groups, group_rows, st);
+            case 128: return launch_pack_sign<128>(src, dst, n_groups, group_rows, st);
+            default: return launch_pack_sign<256>(src, dst, n_groups, group_rows, st);
+        }
+    } else {
+        switch (D) {
+            case 16: return launch_pack_rows<MODE, 16>(src, dst, n_groups, group_rows, st);
+            case 32: return launch_pack_rows<MODE, 32>(src, dst, n_groups, group_rows, st);
+            case 64: return launch_pack_rows<MODE, 64>(src, dst, n_groups, group_rows, st);
+            case 128: return launch_pack_rows<MODE, 128>(src, dst, n_groups, group_rows, st);
+            default: return launch_pack_rows<MODE, 256>(src, dst, n_groups, group_rows, st);
+        }
     }
 }
 
@@ -608,7 +694,7 @@ template <int MODE, int SRC>
 int launch_quant(const Rows& src, const Rows& dst, int64_t n_groups, int group_rows, int D, float sigma,
                  uint16_t* outv, uint8_t* mask, cudaStream_t st) {
     if (n_groups == 0 || group_rows == 0) return ARGUS_OK;
-    if constexpr (SRC == Q_FP16 && (MODE == Q_INT8 || MODE == Q_FP8SIM || MODE == Q_INT4 || MODE == Q_INT2)) {
+    if constexpr (SRC == Q_FP16 && (MODE == Q_INT8 || MODE == Q_FP8SIM || MODE == Q_INT4 || MODE == Q_INT2 || MODE == Q_SIGN1)) {
         if (pack_rows_ok(MODE, SRC, src, dst, group_rows, D))
             return pack_rows_dispatch<MODE>(src, dst, n_groups, group_rows, D, st);
     }
