@@ -23,6 +23,8 @@ Two further single-GPU workloads (not the headline line) are measured by the sam
     python bench.py --workload tinyllama-sidecars  # TinyLlama-shaped layer: H_q 32, H_kv 4, D 64, 4096
                                                    # tokens, 3840 in INT8 pages with outlier sidecars
     python bench.py --workload cascade             # pack/unpack of every tier, 1M tokens x 8 heads x 128
+    torchrun --nproc-per-node N bench.py --workload llama3-70b-heads --gpus N
+                                                   # the 70B layer sharded by KV head over N GPUs
 
 --impl reference times the CPU restatement of the reference's path (dequantize every page, then
 softmax attention over the reconstructed K/V; argus_cache core/memory_manager.py:1157-1315 +
@@ -579,6 +581,71 @@ def _tinyllama_cpu(k, v, q, Pt, HQt, min_seconds=10.0):
                       f"({n * dt:.1f} s of CPU work)"}
 
 
+def run_70b_heads(args, rank, world, local_rank):
+    """Llama-3-70B layer sharded by KV head (strong scaling): B 64, H_q 64, H_kv 8, D 128, context
+    131072 with the 8B tier ratios x4 (8.98 GB compressed per layer), every tier resident; rank r of
+    N holds KV heads [8r/N, 8(r+1)/N) of every page and their query heads, runs the fused kernel on
+    them and all-gathers the per-head outputs over NCCL (sharding.HeadShardedDecode).  Value = the
+    layer's KV tokens (B x L) / the max-over-ranks step time."""
+    import torch
+    import torch.distributed as dist
+
+    from argus_b200 import attention as A
+    from argus_b200 import sharding
+
+    global B, HQ, HKV, L, SPLIT
+    B, HQ, L = 64, 64, 131072
+    n_kv = HKV
+    SPLIT = [(t, 4 * n) for t, n in SPLIT]
+    if n_kv % world:
+        raise SystemExit(f"{n_kv} KV heads do not split over {world} ranks")
+    HKV = n_kv // world  # this rank's heads (the cache is built for them only)
+    HQ = HQ // world
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    plan, q_local = build_cache(device, seed=4242 + rank)
+    HKV, HQ = n_kv, HQ * world
+    q_full = torch.empty(B, HQ, 1, D, dtype=torch.float16, device=device)
+    q_full.view(B, world, HQ // world, 1, D)[:, rank].copy_(q_local)
+    if world > 1:
+        step = sharding.HeadShardedDecode(plan, n_kv)
+        run = lambda: step(q_full)  # noqa: E731
+    else:
+        run = lambda: plan.run(q_local)  # noqa: E731
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank != 0:
+        return
+    hbm, peak_kind = peaks()
+    layer_bytes = plan.compressed_bytes * world
+    print(json.dumps({"metric": "Llama-3-70B layer decode, KV-head sharded, KV tokens/s", "value": B * L / (ms * 1e-3),
+                      "unit": "KV tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "dtype": "fp16",
+                      "data": "synthetic",
+                      "config": {"workload": "llama3-70b-heads", "batch": B, "q_heads": HQ, "kv_heads": n_kv,
+                                 "head_dim": D, "context": L, "tiers_oldest_first": dict(SPLIT),
+                                 "parallelism": f"kv-head sharded x{world}, NCCL all-gather of outputs"},
+                      "roofline": {"bound": "hbm", "achieved_per_gpu": layer_bytes / world / (ms * 1e-3) / 1e9,
+                                   "peak": hbm, "unit": "GB/s",
+                                   "frac": layer_bytes / world / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
+                                   "algorithmic_bytes_per_step": layer_bytes}}), flush=True)
+
+
 def run_cascade(args):
     """Quantize/pack cascade microbench: 1,048,576 tokens x 8 KV heads x 128 fp16 (2 GiB, N(0,1)
     with 1% of the values from Laplace(0,4)) packed into every tier and unpacked again through the
@@ -669,7 +736,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b-spill", "tinyllama-sidecars",
-                                           "cascade"), default="llama3-8b-layer")
+                                           "cascade", "llama3-70b-heads"), default="llama3-8b-layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "jl-archive":
@@ -690,6 +757,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
+    if args.workload == "llama3-70b-heads" and world == 1:
+        run_70b_heads(args, 0, 1, local_rank)
+        return
     if world > 1:
         import datetime
 
@@ -699,7 +769,10 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "llama3-70b-heads":
+            run_70b_heads(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
