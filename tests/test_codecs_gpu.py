@@ -195,10 +195,6 @@ def test_fast_quotient_matches_ieee_divide_for_every_fp16_pair():
     import ctypes
 
     from argus_b200 import _lib
-    L = _lib.lib()
-    L.argus_selftest_fp16_quotients.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
-    L.argus_selftest_fp16_quotients.restype = ctypes.c_int
     n = ctypes.c_ulonglong(12345)
-    rc = L.argus_selftest_fp16_quotients(ctypes.byref(n), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    assert rc == 0
+    _lib.call("argus_selftest_fp16_quotients", ctypes.byref(n), _lib.stream_handle())
     assert n.value == 0
