@@ -439,34 +439,23 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(Rows src, Rows dst, int6
             constexpr float kHi = (MODE == Q_INT8) ? 127.0f : (MODE == Q_FP8SIM ? 240.0f : (MODE == Q_INT4 ? 15.0f : 3.0f));
             const __half2 off = __float2half2_rn(1536.0f);
             const __half2 clo = __float2half2_rn(1536.0f + kLo), chi = __float2half2_rn(1536.0f + kHi);
-            uint32_t cw[per][(C + 1) / 2];  // per row, per column pair: offset codes (half2 bits)
-#pragma unroll
-            for (int i = 0; i < per; ++i) {
-                const float2 s2 = make_float2(sa[i], sa[i]), r2 = make_float2(sr[i], sr[i]);
-                const float2 ns2 = make_float2(-sa[i], -sa[i]);
-                const __half2 mn2 = __float2half2_rn(sb[i]);
-#pragma unroll
-                for (int k = 0; k < C / 2; ++k) {
-                    __half2 h = reinterpret_cast<const __half2*>(raw[i])[k];
-                    if (MODE == Q_INT4 || MODE == Q_INT2) h = __hsub2(h, mn2);  // fp16(x - mn)
-                    const float2 x2 = __half22float2(h);
-                    const float2 q0 = __fmul2_rn(x2, r2);
-                    const float2 e = __ffma2_rn(ns2, q0, x2);
-                    const float2 q = __ffma2_rn(e, r2, q0);
-                    const __half2 m = __hmin2(__hmax2(__hadd2(__float22half2_rn(q), off), clo), chi);
-                    cw[i][k] = *reinterpret_cast<const uint32_t*>(&m);
-                }
-            }
 #pragma unroll
             for (int k = 0; k < C / 2; ++k) {
-                uint32_t pairw;  // bytes 0 and 2: the two columns' output bytes
-                if (MODE == Q_INT8 || MODE == Q_FP8SIM) {
-                    pairw = cw[0][k] & 0x00FF00FFu;
-                } else if (MODE == Q_INT4) {
-                    pairw = (cw[0][k] & 0x000F000Fu) | ((cw[1][k] & 0x000F000Fu) << 4);
-                } else {
-                    pairw = (cw[0][k] & 0x00030003u) | ((cw[1][k] & 0x00030003u) << 2) |
-                            ((cw[2][k] & 0x00030003u) << 4) | ((cw[3][k] & 0x00030003u) << 6);
+                uint32_t pairw = 0u;  // bytes 0 and 2: the two columns' output bytes
+#pragma unroll
+                for (int i = 0; i < per; ++i) {
+                    __half2 h = reinterpret_cast<const __half2*>(raw[i])[k];
+                    if (MODE == Q_INT4 || MODE == Q_INT2) h = __hsub2(h, __float2half2_rn(sb[i]));  // fp16(x - mn)
+                    const float2 x2 = __half22float2(h);
+                    const float2 r2 = make_float2(sr[i], sr[i]);
+                    const float2 q0 = __fmul2_rn(x2, r2);
+                    const float2 e = __ffma2_rn(make_float2(-sa[i], -sa[i]), q0, x2);
+                    const float2 q = __ffma2_rn(e, r2, q0);
+                    const __half2 m = __hmin2(__hmax2(__hadd2(__float22half2_rn(q), off), clo), chi);
+                    const uint32_t cw = *reinterpret_cast<const uint32_t*>(&m);  // offset codes
+                    if (MODE == Q_INT8 || MODE == Q_FP8SIM) pairw = cw & 0x00FF00FFu;
+                    else if (MODE == Q_INT4) pairw |= (cw & 0x000F000Fu) << (4 * i);
+                    else pairw |= (cw & 0x00030003u) << (2 * i);
                 }
                 // columns 2k, 2k+1 -> bytes (2k) & 3, (2k+1) & 3 of out[k / 2]
                 if (k & 1) out[k >> 1] |= __byte_perm(pairw, 0u, 0x2044) & 0xFFFF0000u;
