@@ -351,6 +351,7 @@ class AttentionPlan:
         # the outlier directories the launch reads stay alive with the plan
         self._outlier_dirs = [a.outlier_dir for a in self.arenas]
         self.pages = list(pages)
+        self._graphs = {}
         self._shape = ShapeC(self.B, self.Hkv, self.G, self.qlen, self.D, n_splits, len(self.arenas), self.n_chunks,
                              1.0 / math.sqrt(self.D), ATTN_PRECISE_PV if precise_pv else 0)
         ws = _bind().argus_decode_attention_workspace_size(ctypes.byref(self._shape))
@@ -399,6 +400,41 @@ class AttentionPlan:
         if rc != 0:
             raise _lib.ArgusError("argus_decode_attention", rc, L.argus_last_error().decode())
         return out
+
+
+    def run_host(self, q_host, out_host, scale=None):
+        """One decode step for a host-resident query and output (pinned CPU tensors of q's shape):
+        copy q in, run the fused kernel, copy the output back, replayed as one CUDA graph captured on
+        the first call for this pair of buffers and this scale.  Returns out_host once the copy-back
+        has been queued on the current stream (synchronize before reading it)."""
+        key = (q_host.data_ptr(), out_host.data_ptr(), scale)
+        entry = self._graphs.get(key)
+        if entry is None:
+            exp = (self.B, self.Hkv * self.G, self.qlen, self.D)
+            if tuple(q_host.shape) != exp or tuple(out_host.shape) != exp:
+                raise ValueError(f"host q/out must be {exp}")
+            if q_host.dtype != torch.float16 or out_host.dtype != torch.float16:
+                raise TypeError("host q/out must be float16")
+            if q_host.is_cuda or out_host.is_cuda or not q_host.is_pinned() or not out_host.is_pinned():
+                raise ValueError("host q/out must be pinned CPU tensors")
+            q_dev = torch.empty(exp, dtype=torch.float16, device=self.device)
+            out_dev = torch.empty_like(q_dev)
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                # one launch outside the capture sets the kernel's attributes
+                q_dev.copy_(q_host, non_blocking=True)
+                self.run(q_dev, scale=scale, out=out_dev)
+            side.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side, capture_error_mode="relaxed"):
+                q_dev.copy_(q_host, non_blocking=True)
+                self.run(q_dev, scale=scale, out=out_dev)
+                out_host.copy_(out_dev, non_blocking=True)
+            entry = (graph, q_dev, out_dev, q_host, out_host)
+            self._graphs[key] = entry
+        entry[0].replay()
+        return out_host
 
 
 def device_status(stream=None):

@@ -118,3 +118,25 @@ def test_lse_output():
         w = np.einsum("bhqd,bhkd->bhqk", q.astype(np.float64), Kr) / math.sqrt(D)
         ref = np.log(np.exp(w - w.max(-1, keepdims=True)).sum(-1)) + w.max(-1)
         assert np.abs(lse.cpu().numpy() - ref).max() < 1e-3
+
+
+def test_run_host_graph_matches_run():
+    """AttentionPlan.run_host (copy in, fused kernel, copy out, replayed as one CUDA graph) gives the
+    same bits as run() on device tensors, also after the pinned query buffer is refilled."""
+    from argus_b200 import attention as A
+    B, Hkv, G, D, P = 2, 2, 4, 128, 16
+    rng = np.random.default_rng(21)
+    pages = U.random_pages(rng, [("int4", 64), ("int8", 32), ("fp16", 32)], B, Hkv, D, P)
+    arenas, plist = U.arenas_from_pages(pages)
+    plan = A.AttentionPlan(arenas, plist, batch=B, heads_kv=Hkv, group=G, head_dim=D, n_splits=3)
+    q_host = torch.empty(B, Hkv * G, 1, D, dtype=torch.float16).pin_memory()
+    out_host = torch.empty_like(q_host).pin_memory()
+    for step in range(3):
+        q = torch.from_numpy((rng.standard_normal((B, Hkv * G, 1, D)) / 8).astype(np.float16))
+        q_host.copy_(q)
+        plan.run_host(q_host, out_host)
+        torch.cuda.synchronize()
+        ref = plan.run(q.cuda())
+        torch.cuda.synchronize()
+        assert torch.equal(out_host.view(torch.int16), ref.cpu().view(torch.int16)), step
+    assert A.device_status() == 0

@@ -21,11 +21,11 @@ def within(out, ref, extra=0.0):
     return np.abs(out - ref) <= ATOL + np.abs(ref) * 2.0 ** -11 + extra
 
 
-def run(pages, B, Hkv, G, D, q, n_splits=None, sidecars=True, tile_lse=False):
+def run(pages, B, Hkv, G, D, q, n_splits=None, sidecars=True, tile_lse=False, precise=False):
     from argus_b200 import attention as A
     arenas, plist = U.arenas_from_pages(pages, sidecars=sidecars)
     plan = A.AttentionPlan(arenas, plist, batch=B, heads_kv=Hkv, group=G, head_dim=D, q_len=q.shape[2],
-                           n_splits=n_splits)
+                           n_splits=n_splits, precise_pv=precise)
     tl = torch.full(plan.tile_lse_shape(), float("nan"), device="cuda") if tile_lse else None
     out = plan.run(torch.from_numpy(q).cuda(), tile_lse=tl)
     torch.cuda.synchronize()
@@ -187,3 +187,45 @@ def test_bad_sidecar_is_rejected_without_corrections(defect):
     bare = {"int8": [{k: v for k, v in pg.items() if "out_" not in k}]}
     K, V = U.reference_kv(bare)
     assert within(got, U.f64_attention(q, K, V)).all()
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+def test_sidecars_with_precise_weights(D):
+    """The fp16 hi + lo weight split (ARGUS_ATTN_PRECISE_PV) also feeds the value corrections."""
+    B, Hkv, G, P = 1, 2, 4, 16
+    rng = np.random.default_rng(D)
+    pages = U.random_pages(rng, [("int2", 32), ("int8", 32), ("fp16", 16)], B, Hkv, D, P, sigma=2.0,
+                           shared_sidecar=True)
+    q = (rng.standard_normal((B, Hkv * G, 1, D)) / math.sqrt(D) * 3.0).astype(np.float16)
+    out, _, _ = run(pages, B, Hkv, G, D, q, n_splits=2, precise=True)
+    K, V = U.reference_kv(pages)
+    ref = U.f64_attention(q, K, V)
+    assert within(out, ref).all(), np.abs(out - ref).max()
+
+
+def test_sidecars_through_the_allocation_free_entry():
+    """argus_decode_attention_noalloc applies the same corrections (the arena struct carries them)."""
+    import ctypes
+
+    from argus_b200 import _lib
+    from argus_b200 import attention as A
+    B, Hkv, G, D, P = 1, 2, 4, 64, 16
+    rng = np.random.default_rng(8)
+    pages = U.random_pages(rng, [("int4", 48), ("fp16", 16)], B, Hkv, D, P, sigma=1.5)
+    arenas, plist = U.arenas_from_pages(pages)
+    plan = A.AttentionPlan(arenas, plist, batch=B, heads_kv=Hkv, group=G, head_dim=D, n_splits=2)
+    q = (rng.standard_normal((B, Hkv * G, 1, D)) / 8.0).astype(np.float16)
+    qd = torch.from_numpy(q).cuda()
+    out = torch.empty_like(qd)
+    L = _lib.lib()
+    rc = L.argus_decode_attention_noalloc(ctypes.byref(plan._shape), plan._arena_c, ctypes.c_void_p(plan.chunks_dev.data_ptr()),
+                                          ctypes.c_void_p(plan.splits_dev.data_ptr()), ctypes.c_void_p(qd.data_ptr()),
+                                          ctypes.c_void_p(out.data_ptr()), None, None,
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert A.device_status() == 0
+    K, V = U.reference_kv(pages)
+    ref = U.f64_attention(q, K, V)
+    got = out.cpu().numpy().astype(np.float64)
+    assert within(got, ref).all(), np.abs(got - ref).max()
