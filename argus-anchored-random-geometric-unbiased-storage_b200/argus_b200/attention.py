@@ -334,8 +334,8 @@ class AttentionPlan:
             wave = NUM_SMS * ctas_per_sm(self.D, side)
             n_splits = max(1, min(wave // groups, max(1, self.n_chunks // 8)))
             if groups * n_splits < NUM_SMS:
-                # too little work for one CTA per SM at 8 chunks each: spread it down to 2 chunks a CTA
-                n_splits = max(n_splits, min(wave // groups, max(1, self.n_chunks // 2)))
+                # too little work for one CTA per SM at 8 chunks each: spread it down to 4 chunks a CTA
+                n_splits = max(n_splits, min(wave // groups, max(1, self.n_chunks // 4)))
         n_splits = max(1, min(int(n_splits), max(1, self.n_chunks)))
         self.n_splits = n_splits
         order, bounds = _deal_chunks([c[2] for c in chunks], ccost, n_splits)

@@ -936,29 +936,52 @@ __device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, 
 }
 
 // Merges the split partials of one (batch, kv_head, query group): out = sum_s 2^(lse_s - LSE) O_s,
-// LSE = log2 sum_s 2^lse_s.  Run by the group's last CTA to finish; the other CTAs' partials are
-// read through L2.
+// LSE = log2 sum_s 2^lse_s.  Run by the group's last CTA to finish (all its threads); the other
+// CTAs' partials are read through L2.  The per-(split, query) weights are formed once in shared
+// memory (wbuf: S*8 + 16 floats), then every output element sums its S partials eight at a time.
 template <int D>
-__device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int b, int h, int qg) {
-    const int NQ = p.G * p.qlen;
+__device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int b, int h, int qg, float* wbuf) {
+    const int NQ = p.G * p.qlen, S = p.S;
+    float* Ms = wbuf;           // [kQ] max lse per query
+    float* Ws = wbuf + kQ;      // [kQ] sum of weights per query
+    float* w = wbuf + 2 * kQ;   // [S][kQ] weights 2^(lse_s - M)
+    const float* pl = p.part_lse + grp * S * kQ;
+    for (int i = threadIdx.x; i < S * kQ; i += kThreads) w[i] = __ldcg(pl + i);
+    __syncthreads();
+    if (threadIdx.x < kQ) {
+        float M = -INFINITY;
+        for (int s = 0; s < S; ++s) M = fmaxf(M, w[s * kQ + threadIdx.x]);
+        Ms[threadIdx.x] = M;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < S * kQ; i += kThreads) {
+        const float M = Ms[i % kQ];
+        w[i] = (M == -INFINITY) ? 0.f : exp2f(w[i] - M);  // an empty split (-inf) weighs 0
+    }
+    __syncthreads();
+    if (threadIdx.x < kQ) {
+        float W = 0.f;
+        for (int s = 0; s < S; ++s) W += w[s * kQ + threadIdx.x];
+        Ws[threadIdx.x] = W;
+    }
+    __syncthreads();
     for (int e = threadIdx.x; e < kQ * D; e += kThreads) {
         const int n = e / D, d = e - n * D;
         const int ng = qg * kQ + n;
         if (ng >= NQ) continue;
-        const float* pl = p.part_lse + grp * p.S * kQ + n;
-        float M = -INFINITY;
-        for (int s = 0; s < p.S; ++s) M = fmaxf(M, __ldcg(pl + s * kQ));
-        float W = 0.f, acc = 0.f;
-        if (M != -INFINITY) {
-            for (int s = 0; s < p.S; ++s) {
-                const float w = exp2f(__ldcg(pl + s * kQ) - M);
-                W += w;
-                acc += w * __ldcg(p.part_o + ((grp * p.S + s) * kQ + n) * D + d);
-            }
+        const float* po = p.part_o + (grp * S * kQ + n) * (int64_t)D + d;  // split s at + s * kQ * D
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        int s = 0;
+        for (; s + 8 <= S; s += 8) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc[u] += w[(s + u) * kQ + n] * __ldcg(po + (int64_t)(s + u) * kQ * D);
         }
+        for (; s < S; ++s) acc[0] += w[s * kQ + n] * __ldcg(po + (int64_t)s * kQ * D);
+        const float sum = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+        const float W = Ws[n], M = Ms[n];
         const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
         const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
-        p.out[row * D + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
+        p.out[row * D + d] = __float2half_rn(W > 0.f ? sum / W : 0.f);
         if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
     }
 }
@@ -1299,7 +1322,7 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
         __syncthreads();
         if (last) {
             __threadfence();
-            combine_group<D>(p, grp, b, h, qg);
+            combine_group<D>(p, grp, b, h, qg, reinterpret_cast<float*>(smem));
         }
     }
 }
@@ -1417,6 +1440,8 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
     prm.nqg = (s->group * s->q_len + da::kQ - 1) / da::kQ;
     if (prm.nqg > 65535) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "too many query groups");
     prm.scale_log2 = s->scale * 1.4426950408889634f;
+    if ((int64_t)(s->n_splits + 2) * da::kQ * 4 > (int64_t)da::kPairs * da::kStages * da::stage_bytes(D))
+        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "too many splits for the split merge");
     if (s->n_splits > 1) {
         if (!workspace || !argus_aligned(workspace, 16))
             return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "split-K needs a 16-byte aligned workspace");
