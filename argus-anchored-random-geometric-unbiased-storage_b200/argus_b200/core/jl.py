@@ -81,7 +81,8 @@ class JLShapeC(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("heads_kv", ctypes.c_int32), ("group", ctypes.c_int32),
                 ("q_len", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("block_rows", ctypes.c_int32),
                 ("block_tokens", ctypes.c_int32), ("n_blocks", ctypes.c_int32), ("n_splits", ctypes.c_int32),
-                ("scale", ctypes.c_float), ("bh_stride", ctypes.c_int64), ("block_stride", ctypes.c_int64)]
+                ("n_ctas", ctypes.c_int32), ("scale", ctypes.c_float), ("reserved", ctypes.c_int32),
+                ("bh_stride", ctypes.c_int64), ("block_stride", ctypes.c_int64)]
 
 
 _jl_bound = None
@@ -127,22 +128,28 @@ class JLAttention:
             _lib.stream_handle(R.device)))
         self._ws = {}
 
-    def shape(self, q, yk, n_splits=None, scale=None):
+    def shape(self, q, yk, n_splits=None, scale=None, n_ctas=None):
         B, Hq, qlen, D = q.shape
         _, Hkv, nb, MJ, D2 = yk.shape
         if MJ != self.MJ or D2 != D:
             raise ValueError(f"blocks {tuple(yk.shape)} do not match operator rows {self.MJ} / head_dim {D}")
+        if n_ctas is not None:
+            n_splits = 1
+        n_ctas = int(n_ctas or 0)
         if n_splits is None:
-            # about one CTA per SM (each holds two 64 KB block pairs), at least a block pair per split
-            n_splits = max(1, min(148 // max(1, B * Hkv), nb // 2))
+            # one CTA per SM (each holds two 64 KB block pairs) sharing all heads' block pairs evenly
+            pack = 2 if (Hq // Hkv) * qlen <= 4 else 1
+            n_ctas = min(148, B * Hkv * ((nb + pack - 1) // pack))
+            n_splits = 1
         n_splits = max(1, min(int(n_splits), max(1, nb)))
-        return JLShapeC(B, Hkv, Hq // Hkv, qlen, D, MJ, self.N, nb, n_splits,
-                        1.0 / math.sqrt(D) if scale is None else float(scale), nb * MJ * D, MJ * D)
+        return JLShapeC(B, Hkv, Hq // Hkv, qlen, D, MJ, self.N, nb, n_splits, n_ctas,
+                        1.0 / math.sqrt(D) if scale is None else float(scale), 0, nb * MJ * D, MJ * D)
 
-    def run(self, q, yk, yv, n_splits=None, scale=None, out=None, lse=None, block_lse=None):
+    def run(self, q, yk, yv, n_splits=None, scale=None, out=None, lse=None, block_lse=None, n_ctas=None):
         """q [B, H_q, q_len, D] fp16 -> out (fp16, same shape) and lse (natural log, fp32 [B, H_q, q_len])
         over the archived tokens only; block_lse ([B*H_kv, n_blocks, 8] fp32), if given, receives each
-        block's natural-log LSE per query."""
+        block's natural-log LSE per query.  By default one CTA per SM shares all heads' blocks evenly;
+        n_splits gives each (batch, kv_head) that many CTAs instead, n_ctas an explicit CTA count."""
         for t, name in ((q, "q"), (yk, "yk"), (yv, "yv")):
             _lib.require_cuda(t, name)
             if t.dtype != torch.float16:
@@ -150,14 +157,14 @@ class JLAttention:
         if yk.shape != yv.shape:
             raise ValueError("yk and yv shapes differ")
         q, yk, yv = q.contiguous(), yk.contiguous(), yv.contiguous()
-        s = self.shape(q, yk, n_splits, scale)
+        s = self.shape(q, yk, n_splits, scale, n_ctas)
         if out is None:
             out = torch.empty_like(q)
         if lse is None:
             lse = torch.empty(q.shape[:3], dtype=torch.float32, device=q.device)
         L = _jl_bind()
         ws_bytes = L.argus_jl_attention_workspace_size(ctypes.byref(s))
-        key = (s.batch, s.heads_kv, s.n_splits, q.device)
+        key = (s.batch, s.heads_kv, s.n_splits, s.n_ctas, q.device)
         ws = self._ws.get(key)
         if ws is None or ws.numel() < ws_bytes:
             ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)  # counters start at zero

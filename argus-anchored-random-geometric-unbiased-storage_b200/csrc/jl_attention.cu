@@ -11,8 +11,10 @@
 // accumulation; u, p and w enter as fp16 hi + lo pairs).  R and R^T are stored once in MMA fragment
 // order so every operand load is one coalesced 16-byte read per lane from L2.
 //
-// One CTA (8 warps) per (split, batch*kv_head); with at most 4 queries per kv head two archive
-// blocks share the 8 query columns of every MMA.  Per block pair: warp w forms u rows 16w..16w+15,
+// The CTAs (8 warps each) share the block pairs of all (batch, kv_head) in equal contiguous ranges,
+// so every SM gets the same work whatever the head count; a range that spans two heads yields a
+// partial for each, and the last CTA to finish a head merges its partials.  With at most 4 queries
+// per kv head two archive blocks share the 8 query columns of every MMA.  Per block pair: warp w forms u rows 16w..16w+15,
 // then streams token tiles w, w+8, ... through scores, online softmax (per column, log2 domain)
 // and w accumulation; the warps' partial w merge in shared memory; warp w then adds Yv^T . w for
 // dims 16w..16w+15.  Yk / Yv blocks arrive by TMA tensor copies in 128-byte swizzle (two 64-column
@@ -51,7 +53,7 @@ struct Params {
     __half* out;
     float* lse;
     float* block_lse;   // optional [B*Hkv][n_blocks][8]: natural-log LSE of each block's scores
-    float* part_o;      // [B*Hkv][S][8][D]
+    float* part_o;      // [B*Hkv][S][8][D]  (S: partial slots per (b, h))
     float* part_lse;    // [B*Hkv][S][8]
     int* counters;      // [B*Hkv]
     int64_t bh_stride, block_stride;  // elements
@@ -175,13 +177,34 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
     uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(beta + kCols) + 15) & ~(uintptr_t)15);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-    const int split = blockIdx.x;
-    const int64_t bh = blockIdx.y;
-    const int b = (int)(bh / p.Hkv), h = (int)(bh - (int64_t)b * p.Hkv);
     const int NQ = p.G * p.qlen;
     const int qpb = PACK == 2 ? 4 : 8;  // query columns per block
     const uint32_t ykbar = su32(&bars[0]), yvbar = su32(&bars[1]);
-    const int j0 = (int)((int64_t)p.n_blocks * split / p.S), j1 = (int)((int64_t)p.n_blocks * (split + 1) / p.S);
+    if (tid == 0) {
+        mbar_init(ykbar);
+        mbar_init(yvbar);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __shared__ int last;
+
+    // The block pairs of all (batch, kv_head) groups, group after group, are dealt to the CTAs in
+    // equal contiguous ranges: pair x goes to CTA floor(x C / T).  A CTA whose range crosses groups
+    // finishes one group's segment (a partial) and starts the next.
+    const int64_t groups = (int64_t)p.B * p.Hkv;
+    const int64_t PP = (p.n_blocks + PACK - 1) / PACK, T = groups * PP;
+    const int64_t C = gridDim.x, c = blockIdx.x;
+    const int64_t x_end = ((c + 1) * T + C - 1) / C;
+    bool ok = true;
+    int it = 0;
+    for (int64_t xs = (c * T + C - 1) / C; xs < x_end && ok;) {
+    const int64_t bh = xs / PP;
+    const int64_t xe = (x_end < (bh + 1) * PP) ? x_end : (bh + 1) * PP;
+    const int j0 = (int)((xs - bh * PP) * PACK);
+    const int j1 = (int)(((xe - bh * PP) * PACK < p.n_blocks) ? (xe - bh * PP) * PACK : p.n_blocks);
+    const int64_t first_c = bh * PP * C / T, last_c = ((bh + 1) * PP - 1) * C / T;
+    const int n_seg = (int)(last_c - first_c + 1), split = (int)(c - first_c);  // this group's partials
+    xs = xe;
+    const int b = (int)(bh / p.Hkv), h = (int)(bh - (int64_t)b * p.Hkv);
 
     // query fragments: column n of the U contraction is query n (block A) or n - 4 (block B)
     uint32_t qa[KD][2], qb[KD][2];
@@ -198,11 +221,6 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             qb[kk][1] = lb ? *reinterpret_cast<const uint32_t*>(qbase + (int64_t)nb_ * kD + d + 8) : 0u;
         }
     }
-    if (tid == 0) {
-        mbar_init(ykbar);
-        mbar_init(yvbar);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
     if (tid < kCols) {
         mrun[tid] = kNoMax;
         lrun[tid] = 0.f;
@@ -215,8 +233,6 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
     }
 
     float oacc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 16*warp + g (+8), columns 2t, 2t+1
-    bool ok = true;
-    int it = 0;
     for (int j = j0; j < j1 && ok; j += PACK, ++it) {
         const bool hasB = PACK == 2 && j + 1 < j1;
         ok = __syncthreads_and(mbar_wait(ykbar, (uint32_t)(it & 1)));
@@ -428,6 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         if (tid == 0) atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
         (void)mbar_wait(ykbar, 0u);  // let copies in flight land before the CTA exits (bounded)
         (void)mbar_wait(yvbar, 0u);
+        break;
     }
     __syncthreads();
 
@@ -450,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
     const int d0 = 16 * warp + g;
     if (writer) {
         const int n0 = 2 * t, n1 = 2 * t + 1;  // query index (t < 2 when packed)
-        float* po = p.part_o + ((bh * p.S + split) * kCols) * kD;
+        float* po = p.part_o + ((bh * p.S + split) * kCols) * kD;  // p.S: partial slots per group
         po[n0 * kD + d0] = L0 > 0.f ? o0 / L0 : 0.f;
         po[n0 * kD + d0 + 8] = L0 > 0.f ? o2 / L0 : 0.f;
         po[n1 * kD + d0] = L1 > 0.f ? o1 / L1 : 0.f;
@@ -460,26 +477,25 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             p.part_lse[(bh * p.S + split) * kCols + n1] = L1 > 0.f ? M1 + log2f(L1) : -INFINITY;
         }
     }
-    // ---- the last split CTA of this (b, h) merges the splits
-    __shared__ int last;
+    // ---- the last segment CTA of this (b, h) merges its partials
     __threadfence();
     __syncthreads();
     if (tid == 0) {
         const int prev = atomicAdd(&p.counters[bh], 1);
-        last = prev == p.S - 1;
+        last = prev == n_seg - 1;
         if (last) p.counters[bh] = 0;
     }
     __syncthreads();
-    if (!last) return;
+    if (last) {
     __threadfence();
     for (int e = tid; e < NQ * kD; e += kThreads) {
         const int n = e / kD, d = e - n * kD;
         const float* pl = p.part_lse + bh * p.S * kCols + n;
         float M = -INFINITY;
-        for (int s = 0; s < p.S; ++s) M = fmaxf(M, __ldcg(pl + s * kCols));
+        for (int s = 0; s < n_seg; ++s) M = fmaxf(M, __ldcg(pl + s * kCols));
         float W = 0.f, acc = 0.f;
         if (M != -INFINITY) {
-            for (int s = 0; s < p.S; ++s) {
+            for (int s = 0; s < n_seg; ++s) {
                 const float wgt = exp2f(__ldcg(pl + s * kCols) - M);
                 W += wgt;
                 acc += wgt * __ldcg(p.part_o + ((bh * p.S + s) * kCols + n) * kD + d);
@@ -489,6 +505,9 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
         p.out[row * kD + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
         if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
+    }
+    }
+    __syncthreads();  // shared state is reset for the next segment
     }
 }
 
@@ -614,10 +633,21 @@ int make_block_map(CUtensorMap* map, const void* base, const argus_jl_attn_shape
 
 }  // namespace
 
-int64_t argus_jl_attention_workspace_size(const argus_jl_attn_shape* s) {
-    if (!s || s->batch <= 0 || s->heads_kv <= 0 || s->n_splits <= 0) return 0;
+namespace {
+// CTAs of a launch and the partial slots each (batch, kv_head) needs (see argus_jl_attn_shape.n_ctas).
+int64_t jl_ctas(const argus_jl_attn_shape* s) {
+    return s->n_ctas > 0 ? (int64_t)s->n_ctas : (int64_t)s->batch * s->heads_kv * s->n_splits;
+}
+int64_t jl_slots(const argus_jl_attn_shape* s) {
     const int64_t groups = (int64_t)s->batch * s->heads_kv;
-    return ((groups * 4 + 255) & ~255LL) + groups * s->n_splits * jla::kCols * (int64_t)(jla::kD + 1) * 4 + 256;
+    return (jl_ctas(s) + groups - 1) / groups + 1;
+}
+}  // namespace
+
+int64_t argus_jl_attention_workspace_size(const argus_jl_attn_shape* s) {
+    if (!s || s->batch <= 0 || s->heads_kv <= 0 || s->n_splits <= 0 || s->n_ctas < 0) return 0;
+    const int64_t groups = (int64_t)s->batch * s->heads_kv;
+    return ((groups * 4 + 255) & ~255LL) + groups * jl_slots(s) * jla::kCols * (int64_t)(jla::kD + 1) * 4 + 256;
 }
 
 int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const uint16_t* yv, const void* r_frag,
@@ -635,6 +665,7 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     if (NQ > jla::kCols) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "at most 8 queries per kv head");
     if (s->n_splits > (s->n_blocks > 0 ? s->n_blocks : 1))
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "more splits than blocks");
+    if (s->n_ctas < 0) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "negative CTA count");
     if (!argus_aligned(yk, 16) || !argus_aligned(yv, 16) || !argus_aligned(workspace, 16) ||
         (s->bh_stride * 2) % 16 || (s->block_stride * 2) % 16)
         return argus_set_error(ARGUS_ERR_MISALIGNED, "blocks must start on 16-byte boundaries");
@@ -654,19 +685,23 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     const int64_t groups = (int64_t)s->batch * s->heads_kv;
     p.counters = static_cast<int*>(workspace);
     p.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + ((groups * 4 + 255) & ~255LL));
-    p.part_o = p.part_lse + groups * s->n_splits * jla::kCols;
+    p.part_o = p.part_lse + groups * jl_slots(s) * jla::kCols;
     p.bh_stride = s->bh_stride;
     p.block_stride = s->block_stride;
     p.B = s->batch; p.Hkv = s->heads_kv; p.G = s->group; p.qlen = s->q_len;
-    p.n_blocks = s->n_blocks; p.N = s->block_tokens; p.S = s->n_splits;
+    p.n_blocks = s->n_blocks; p.N = s->block_tokens; p.S = (int)jl_slots(s);
     p.scale_log2 = s->scale * 1.4426950408889634f;
     cudaStream_t st = (cudaStream_t)stream;
     const bool pack = NQ <= 4;
+    const int64_t pairs = groups * ((s->n_blocks + (pack ? 1 : 0)) / (pack ? 2 : 1));
+    const int64_t ctas = jl_ctas(s);
+    if (ctas > pairs || ctas > 0x7fffffff)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "more CTAs than block pairs");
     const size_t smem = jla::smem_bytes(pack ? 2 : 1);
     auto kern = pack ? jla::jl_attn_kernel<2> : jla::jl_attn_kernel<1>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
-    kern<<<dim3(s->n_splits, (unsigned)groups), jla::kThreads, smem, st>>>(p);
+    kern<<<(unsigned)ctas, jla::kThreads, smem, st>>>(p);
     ARGUS_CHECK_LAUNCH();
     return ARGUS_OK;
 }

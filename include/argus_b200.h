@@ -205,8 +205,12 @@ typedef struct argus_jl_attn_shape {
     int32_t block_rows;    /* rows of a projected block (N / ratio) */
     int32_t block_tokens;  /* tokens a block stands for (N) */
     int32_t n_blocks;
-    int32_t n_splits;      /* split-K partitions of the blocks (<= n_blocks) */
+    int32_t n_splits;      /* split-K partitions of each (batch, kv_head)'s blocks (<= n_blocks) */
+    int32_t n_ctas;        /* > 0: this many CTAs share the block pairs of all (batch, kv_head) in equal
+                              contiguous ranges (a range may span two heads), instead of n_splits per
+                              (batch, kv_head); at most the number of block pairs */
     float scale;
+    int32_t reserved;
     int64_t bh_stride;     /* elements */
     int64_t block_stride;  /* elements */
 } argus_jl_attn_shape;

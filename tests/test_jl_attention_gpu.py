@@ -101,6 +101,43 @@ def test_jl_attention_matches_rebuilt_attention(B, Hkv, G, ql, N, ratio, nb, spl
     assert within(got, mat).all(), np.abs(got - mat).max()
 
 
+@pytest.mark.parametrize("B,Hkv,G,nb,n_ctas", [
+    (2, 2, 4, 7, 5),      # CTA ranges of block pairs that span two heads
+    (1, 3, 4, 9, 4),
+    (2, 2, 8, 3, 5),      # 8 queries per head: one block per MMA, ranges of single blocks
+    (1, 2, 4, 6, None),   # the default: one CTA per block pair here
+])
+def test_jl_attention_ctas_span_heads(B, Hkv, G, nb, n_ctas):
+    """CTAs that take a contiguous range of all heads' block pairs (crossing from one head to the
+    next) give the same attention and per-block LSE as the rebuilt K/V, on two launches in a row
+    (the arrival counters are left at zero)."""
+    from argus_b200 import attention as A
+    from argus_b200.core import jl
+    N, ratio, D, ql = 512, 4, 128, 1
+    MJ = N // ratio
+    R = operator(N, ratio)
+    g = torch.Generator().manual_seed(100 + nb + (n_ctas or 0))
+    yk = torch.randn(B, Hkv, nb, MJ, D, generator=g).half()
+    yv = torch.randn(B, Hkv, nb, MJ, D, generator=g).half()
+    q = (torch.randn(B, Hkv * G, ql, D, generator=g) / math.sqrt(D) * 2.0).half()
+    att = jl.JLAttention(R.cuda())
+    K, V = rebuild(R, yk), rebuild(R, yv)
+    ref, _ = f64_attention(q.numpy(), K, V, 1.0 / math.sqrt(D))
+    Kx = np.repeat(K.astype(np.float64), G, axis=1)
+    s = np.einsum("bhqd,bhkd->bhqk", q.numpy().astype(np.float64), Kx) / math.sqrt(D)
+    sb = s.reshape(B, Hkv, G, ql, nb, N)
+    mb = sb.max(-1)
+    ref_blk = (mb + np.log(np.exp(sb - mb[..., None]).sum(-1))).reshape(B * Hkv, G * ql, nb).transpose(0, 2, 1)
+    block_lse = torch.empty(B * Hkv, nb, 8, dtype=torch.float32, device="cuda")
+    for _ in range(2):
+        out, lse = att.run(q.cuda(), yk.cuda(), yv.cuda(), block_lse=block_lse, n_ctas=n_ctas)
+        torch.cuda.synchronize()
+        assert A.device_status() == 0
+        got = out.cpu().numpy().astype(np.float64)
+        assert within(got, ref).all(), np.abs(got - ref).max()
+        assert np.allclose(block_lse.cpu().numpy()[:, :, :G * ql], ref_blk, rtol=0, atol=2e-3)
+
+
 def test_merge_joins_jl_archive_with_other_tiers():
     from argus_b200 import attention as A
     from argus_b200.core import jl
