@@ -103,6 +103,26 @@ def isolate_outliers(tensor, threshold_sigma=3.0):
     return normal, outv, mask
 
 
+def _causal_sdpa(q, k, v, scale, with_lse=False):
+    """Attention of q [B, H_q, q_len, D] over k, v [B, H_kv, L, D] with the bottom-right causal
+    mask (query i sees keys j <= L - q_len + i), in fp32; fp16 output and, with with_lse, the
+    natural-log LSE [B, H_q, q_len] in fp32."""
+    B, Hq, ql, D = q.shape
+    Hkv, L = k.shape[1], k.shape[-2]
+    G = Hq // Hkv
+    qf = q.float().view(B, Hkv, G, ql, D)
+    s = torch.einsum("bhgqd,bhkd->bhgqk", qf, k.float()) * scale
+    j = torch.arange(L, device=q.device)
+    i = torch.arange(ql, device=q.device)
+    s = s.masked_fill(j.view(1, -1) > (L - ql + i).view(-1, 1), float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    out = torch.einsum("bhgqk,bhkd->bhgqd", torch.exp(s - lse.unsqueeze(-1)), v.float())
+    out = out.reshape(B, Hq, ql, D).half()
+    if with_lse:
+        return out, lse.reshape(B, Hq, ql).contiguous()
+    return out
+
+
 def _allocated_bytes(dev):
     """torch.cuda.memory_allocated(dev) without flattening the allocator's whole statistics dict
     (that flattening costs ~0.2 ms, and the check runs on every push)."""
@@ -620,15 +640,16 @@ class PagedDynamicKVCache:
             off += n
         return K, V
 
-    def _attention_plan(self, q):
+    def _attention_plan(self, q, tail=0):
         """Fused-kernel tables for the current cache.  What depends on the pages (a scratch fp16
         arena for the sinks, anchors and JL pages the fused JL kernel does not take; the pages'
         outlier corrections; the JL operands) is rebuilt only when pages change.  The staging
         buffer is an fp16 arena of its own over the static buffer, so a decode step that only
         appends a token patches the token count of the buffer's last tile in place; the tables are
-        rebuilt when the buffer starts a new 16-token tile."""
+        rebuilt when the buffer starts a new 16-token tile.  The newest `tail` tokens of the
+        staging buffer are left out (a causal step attends to them separately)."""
         B, Hq, qlen, D = q.shape
-        nbuf = self.buffer_length if self.k_buffer is not None else 0
+        nbuf = max(0, self.buffer_length - tail) if self.k_buffer is not None else 0
         base_key = (B, Hq, qlen, D, len(self.active_pages), tuple(len(lst) for _, lst in self._compressed_order()),
                     self._scratch_version())
         key = (base_key, self.static_k_buffer.data_ptr() if nbuf else 0, (nbuf + 15) // 16)
@@ -792,17 +813,23 @@ class PagedDynamicKVCache:
                 self.anchor_k.shape[-2] if self.anchor_k is not None else 0, self._page_counter, self.num_resurrections,
                 self.total_demotions)
 
-    def attend(self, q, scale=None):
+    def attend(self, q, scale=None, causal=False):
         """softmax(q K^T * scale) V over every tier straight from the compressed pages, without the
         importance / resurrection side effects of inplace_paged_attention: what the HuggingFace path
         computes from get_all_keys_values + SDPA (models/attention_wrapper.py:87-88), without
-        rebuilding the full K/V.  q: [B, H_q, q_len, D] fp16 (every query attends to every cached
-        token)."""
+        rebuilding the full K/V.  q: [B, H_q, q_len, D] fp16.  causal=False: every query attends
+        to every cached token.  causal=True: the q_len queries are the newest q_len cached tokens
+        and query i sees the tokens up to its own (the bottom-right causal mask)."""
         B, Hq, qlen, D = q.shape
         if scale is None:
             scale = 1.0 / math.sqrt(D)
         if self.is_swapped_out:
             self.swap_in_to_device()
+        if causal and qlen > 1:
+            _lib.require_cuda(q, "q")
+            if q.dtype != torch.float16:
+                raise TypeError("q must be float16")
+            return self._attend_causal(q, scale)
         if self.sink_k is None and self.anchor_k is None and not self.active_pages and self.k_buffer is None and \
                 not any(lst for _, lst in self._compressed_order()):
             return torch.zeros_like(q)
@@ -816,6 +843,39 @@ class PagedDynamicKVCache:
         out = plan.run(q, scale=scale, lse=lse)
         out_j, lse_j = plan.jl["att"].run(q, plan.jl["yk"], plan.jl["yv"], scale=scale)
         return _jl.merge_attention(out, lse, out_j, lse_j)
+
+    def newest_in_buffer(self, n):
+        """True when the newest n cached tokens all sit in the fp16 staging buffer, which is what
+        attend(causal=True) reads them from without rebuilding the compressed pages."""
+        return self.k_buffer is not None and self.buffer_length >= n
+
+    def _attend_causal(self, q, scale):
+        """attend(causal=True): the newest q_len tokens (in the staging buffer) under the causal
+        mask, everything older through the fused kernel, joined by LSE.  When the newest tokens
+        are not all in the buffer (a page was just formed from them), the full K/V is rebuilt."""
+        B, Hq, qlen, D = q.shape
+        nbuf = self.buffer_length if self.k_buffer is not None else 0
+        if nbuf < qlen:
+            K, V = self.get_all_keys_values()
+            return _causal_sdpa(q, K, V, scale)
+        k_new = self.static_k_buffer[..., nbuf - qlen:nbuf, :]
+        v_new = self.static_v_buffer[..., nbuf - qlen:nbuf, :]
+        out_n, lse_n = _causal_sdpa(q, k_new, v_new, scale, with_lse=True)
+        older = nbuf - qlen + self.page_size * (len(self.active_pages) +
+                                                sum(len(lst) for _, lst in self._compressed_order()))
+        older += self.sink_k.shape[-2] if self.sink_k is not None else 0
+        older += self.anchor_k.shape[-2] if self.anchor_k is not None else 0
+        if older == 0:
+            return out_n
+        plan = self._attention_plan(q, tail=qlen)
+        lse = torch.empty(B, Hq, qlen, dtype=torch.float32, device=q.device)
+        out = plan.run(q, scale=scale, lse=lse)
+        if plan.jl is not None:
+            out_j, lse_j = plan.jl["att"].run(q, plan.jl["yk"], plan.jl["yv"], scale=scale)
+            lse_t = torch.empty_like(lse)
+            out = _jl.merge_attention(out, lse, out_j, lse_j, lse=lse_t)
+            lse = lse_t
+        return _jl.merge_attention(out, lse, out_n, lse_n)
 
     def inplace_paged_attention(self, q, scale=None):
         """softmax(q K^T * scale) V over every tier, straight from the compressed pages, plus the

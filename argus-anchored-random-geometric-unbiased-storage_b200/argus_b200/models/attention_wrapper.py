@@ -8,11 +8,13 @@ page kernels, which is what transformers' attention consumes (attention_wrapper.
 
 With fused_decode=True, update() returns placeholders instead and the "argus" attention
 implementation (registered with transformers' AttentionInterface; load the model with
-attn_implementation="argus") sends each single-token decode step straight to the fused
-mixed-tier kernel over the compressed pages, so the full K/V is never rebuilt (only pages with
-outlier sidecars, and JL pages the fused JL kernel does not take, pass through the manager's fp16
-scratch arena); prefill (several query tokens) and padded batches still rebuild K/V and run
-transformers' SDPA.
+attn_implementation="argus") sends each decode step straight to the fused mixed-tier kernel over
+the compressed pages, so the full K/V is never rebuilt (JL pages the fused JL kernel does not
+take pass through the manager's fp16 scratch arena).  A step of several new tokens (speculative
+or chunked decoding) takes the same route when those tokens are still in the staging buffer: the
+kernel attends to everything older and the new tokens attend to one another under the causal
+mask, joined by LSE.  A prefill into an empty cache, a step whose tokens just formed a page, and
+padded batches rebuild K/V and run transformers' SDPA.
 """
 import torch
 
@@ -119,34 +121,68 @@ class PagedDynamicQuantizedCache(Cache):
         self.layer_caches.clear()
 
 
+def _bottom_right_causal(q_len, kv_len, device):
+    """Boolean [q_len, kv_len] mask, True where query i (the (kv_len - q_len + i)-th token) may
+    attend to key j."""
+    j = torch.arange(kv_len, device=device)
+    i = torch.arange(q_len, device=device)
+    return j.view(1, -1) <= (kv_len - q_len + i).view(-1, 1)
+
+
 def argus_attention_forward(module, query, key, value, attention_mask, dropout=0.0, scaling=None, is_causal=None,
                             **kwargs):
-    """transformers attention function ("argus"): a decode step (one query token, no padding mask)
-    over a PagedDynamicQuantizedCache(fused_decode=True) layer runs the fused mixed-tier kernel on
-    the compressed pages; anything else rebuilds K/V and runs transformers' SDPA.  Returns
-    ([B, q_len, H_q, D], None) as transformers' attention functions do."""
+    """transformers attention function ("argus"): a decode step (no padding mask) over a
+    PagedDynamicQuantizedCache(fused_decode=True) layer runs the fused mixed-tier kernel on the
+    compressed pages (several query tokens: causal among themselves, see the module docstring);
+    anything else rebuilds K/V and runs transformers' SDPA.  Returns ([B, q_len, H_q, D], None)
+    as transformers' attention functions do."""
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
 
     cache = getattr(key, "_argus_layer_cache", None)
+    causal = getattr(module, "is_causal", True) if is_causal is None else is_causal
+    ql = query.shape[2]
     if cache is None:
+        if attention_mask is None and causal and 1 < ql < key.shape[-2]:
+            attention_mask = _bottom_right_causal(ql, key.shape[-2], query.device)
         return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
                                       is_causal=is_causal, **kwargs)
-    if query.shape[2] == 1 and attention_mask is None and dropout == 0.0 and query.dtype == torch.float16:
-        out = cache.attend(query.contiguous(), scale=scaling)
+    if attention_mask is None and dropout == 0.0 and query.dtype == torch.float16 and \
+            (ql == 1 or (causal and cache.newest_in_buffer(ql))):
+        out = cache.attend(query.contiguous(), scale=scaling, causal=ql > 1)
         return out.transpose(1, 2).contiguous(), None
     K, V = cache.get_all_keys_values()
-    return sdpa_attention_forward(module, query, K.to(query.dtype), V.to(query.dtype), attention_mask,
-                                  dropout=dropout, scaling=scaling, is_causal=is_causal, **kwargs)
+    K, V = K.to(query.dtype), V.to(query.dtype)
+    if attention_mask is None and causal and 1 < ql < K.shape[-2]:
+        # SDPA's is_causal is top-left aligned; queries after a cached prefix need bottom-right
+        attention_mask = _bottom_right_causal(ql, K.shape[-2], query.device)
+    return sdpa_attention_forward(module, query, K, V, attention_mask, dropout=dropout, scaling=scaling,
+                                  is_causal=is_causal, **kwargs)
+
+
+def argus_mask(batch_size, q_length, kv_length, q_offset=0, kv_offset=0, mask_function=None, attention_mask=None,
+               local_size=None, allow_is_causal_skip=True, **kwargs):
+    """Mask builder registered with "argus": a plain causal mask without padding is left to the
+    attention function (None), which knows the cached length and aligns the causal mask to its
+    end; anything else is transformers' SDPA mask."""
+    from transformers.masking_utils import causal_mask_function, sdpa_mask
+    if mask_function is None:
+        mask_function = causal_mask_function
+    if mask_function is causal_mask_function and local_size is None and allow_is_causal_skip and \
+            (attention_mask is None or bool(attention_mask.all())):
+        return None
+    return sdpa_mask(batch_size, q_length, kv_length, q_offset=q_offset, kv_offset=kv_offset,
+                     mask_function=mask_function, attention_mask=attention_mask, local_size=local_size,
+                     allow_is_causal_skip=allow_is_causal_skip, **kwargs)
 
 
 def _register():
     try:
-        from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+        from transformers.masking_utils import AttentionMaskInterface
         from transformers.modeling_utils import AttentionInterface
     except ImportError:
         return
     AttentionInterface.register("argus", argus_attention_forward)
-    AttentionMaskInterface.register("argus", sdpa_mask)
+    AttentionMaskInterface.register("argus", argus_mask)
 
 
 _register()

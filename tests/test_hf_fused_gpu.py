@@ -128,3 +128,74 @@ def test_attend_follows_single_token_appends(tmp_path, monkeypatch):
     assert same > 20 and reused == same
     assert any(pg.get("key_out_indices") is not None and pg["key_out_indices"].numel()
                for _, lst in cache._compressed_order() for pg in lst)
+
+
+def test_attend_causal_queries_of_the_newest_tokens(tmp_path, monkeypatch):
+    """attend(causal=True) for steps of several tokens: query i sees the cached tokens up to its
+    own (bottom-right causal mask over the rebuilt K/V), through page formation and demotions."""
+    import oracle
+    from argus_b200.core.memory_manager import PagedDynamicKVCache
+    monkeypatch.setenv("ARGUS_LOG_LEVEL", "quiet")
+    monkeypatch.chdir(tmp_path)
+    B, H, G, D = 2, 2, 4, 64
+    cache = PagedDynamicKVCache(page_size=32, max_active_pages=1, max_fp8_pages=1, max_int8_pages=1,
+                                max_int4_pages=1, max_int2_pages=1, max_one_bit_pages=1, sink_tokens=4)
+    g = torch.Generator().manual_seed(11)
+    kv = lambda n: (torch.randn(B, H, n, D, generator=g) * 1.5).half().cuda()  # noqa: E731
+    scale = 1.0 / math.sqrt(D)
+    checked = 0
+    for pushes in ([200, 3], [200, 5, 4], [30, 40], [6]):
+        for n in pushes:
+            cache.push_new_tokens(kv(n), kv(n))
+        ql = pushes[-1]
+        q = (torch.randn(B, H * G, ql, D, generator=g) / 8).half()
+        out = host(cache.attend(q.cuda(), causal=True)).astype(np.float64)
+        K, V = (host(t) for t in cache.get_all_keys_values())
+        L = K.shape[-2]
+        ref = np.stack([oracle.sdpa_f64(q.numpy()[:, :, i:i + 1], K[:, :, :L - ql + i + 1], V[:, :, :L - ql + i + 1],
+                                        scale)[:, :, 0] for i in range(ql)], axis=2)
+        bar = 2e-3 + np.abs(ref) * 2.0 ** -10
+        assert (np.abs(out - ref) <= bar).all(), (pushes, np.abs(out - ref).max())
+        checked += 1
+        # a decode step after the causal one sees every cached token
+        q1 = (torch.randn(B, H * G, 1, D, generator=g) / 8).half()
+        out1 = host(cache.attend(q1.cuda())).astype(np.float64)
+        ref1 = oracle.sdpa_f64(q1.numpy(), K, V, scale)
+        assert (np.abs(out1 - ref1) <= 2e-3 + np.abs(ref1) * 2.0 ** -11).all()
+    assert checked == 4
+
+
+def test_fused_steps_of_several_tokens_match_materializing_adapter(tmp_path, monkeypatch):
+    """Chunked decode (3 tokens a step) through the "argus" attention: steps whose tokens are in
+    the staging buffer run fused without rebuilding K/V and match the materializing adapter."""
+    from argus_b200.core.memory_manager import PagedDynamicKVCache
+    monkeypatch.setenv("ARGUS_LOG_LEVEL", "quiet")
+    monkeypatch.chdir(tmp_path)
+    ref_model, fused_model = _models(1, 256, 8, 2, 32)
+    ref_cache, fused_cache = _cache(False), _cache(True)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ids = torch.randint(0, 256, (1, 120), device="cuda", generator=g)
+    steps = torch.randint(0, 256, (1, 24), device="cuda", generator=g)
+    rebuilt = []
+    real = PagedDynamicKVCache.get_all_keys_values
+
+    def counting(self):
+        rebuilt.append(1)
+        return real(self)
+
+    fused_steps, worst = 0, 0.0
+    with torch.no_grad():
+        a = ref_model(ids, past_key_values=ref_cache, use_cache=True).logits
+        b = fused_model(ids, past_key_values=fused_cache, use_cache=True).logits
+        assert (a.float() - b.float()).abs().max() <= 1e-3
+        monkeypatch.setattr(PagedDynamicKVCache, "get_all_keys_values", counting)
+        for t in range(0, steps.shape[1], 3):
+            tok = steps[:, t:t + 3]
+            a = ref_model(tok, past_key_values=ref_cache, use_cache=True).logits
+            n_before = len(rebuilt)
+            b = fused_model(tok, past_key_values=fused_cache, use_cache=True).logits
+            fused_steps += len(rebuilt) == n_before
+            worst = max(worst, float((a.float() - b.float()).abs().max()))
+    assert fused_cache.get_seq_length(0) == ref_cache.get_seq_length(0) == 144
+    assert fused_steps >= 4, fused_steps
+    assert worst <= 1e-2, worst

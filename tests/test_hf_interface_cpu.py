@@ -36,3 +36,28 @@ def test_mask_sizes_count_cached_tokens():
     c = PagedDynamicQuantizedCache(page_size=16)
     assert c.get_mask_sizes(5, 0) == (5, 0)
     assert c.get_mask_sizes(torch.arange(3), 0) == (3, 0)
+
+
+def test_argus_chunks_after_a_cached_prefix_match_sdpa():
+    """Several new tokens after a cached prefix (chunked prefill / speculative steps) on a plain
+    DynamicCache: the "argus" mask leaves the causal mask to the attention function, which aligns
+    it to the end of the cache exactly as transformers' SDPA mask does."""
+    transformers = pytest.importorskip("transformers")
+    from transformers import DynamicCache
+
+    from argus_b200.models import attention_wrapper  # noqa: F401
+    cfg = transformers.LlamaConfig(vocab_size=64, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=128)
+    torch.manual_seed(0)
+    ref = transformers.LlamaForCausalLM(cfg).eval()
+    cfg2 = transformers.LlamaConfig(**cfg.to_dict())
+    cfg2._attn_implementation = "argus"
+    ours = transformers.LlamaForCausalLM(cfg2).eval()
+    ours.load_state_dict(ref.state_dict())
+    ids = torch.randint(0, 64, (1, 17))
+    ca, cb = DynamicCache(), DynamicCache()
+    with torch.no_grad():
+        for s, e in ((0, 9), (9, 12), (12, 17)):
+            a = ref(ids[:, s:e], past_key_values=ca, use_cache=True).logits
+            b = ours(ids[:, s:e], past_key_values=cb, use_cache=True).logits
+            assert torch.allclose(a, b, atol=1e-5), (s, e, (a - b).abs().max())
