@@ -214,21 +214,51 @@ def chunk_capacity(arena, head_dim):
     return _bind().argus_decode_attention_chunk_tiles(arena.tier, arena.layout, arena.page_tokens, head_dim)
 
 
+# Relative cost of one token of each tier in the fused kernel, measured on B200 with each tier alone
+# over a 32K-token Llama-3-8B layer (B 8, 8 KV heads, D 128): a staged tile costs about the same
+# whatever its bytes (the low-bit tiers are bound by instruction latency), except fp16, whose
+# tiles stream at the HBM rate.
+TIER_TOKEN_COST = {TIER_1BIT: 0.69, TIER_INT2: 0.93, TIER_INT4: 0.96, TIER_INT8: 1.06, TIER_FP8SIM: 1.06,
+                   TIER_FP16: 2.0}
+
+# The kernel deals a split's chunks to its 4 warps by position: chunk i goes to warp pair i % 2, and
+# within the pair to warp (i // 2) % 2.
+CTA_WARPS = 4
+
+
 def _tile_cost(tier, head_dim, ntok):
-    """Estimated cost of tokens of one tier for split balancing.  The fused kernel spends its time
-    rebuilding and contracting tokens (every tier costs about the same per token once staged), so
-    the estimate is the token count; measured on B200 it balances splits far better than bytes."""
-    return float(ntok) * head_dim / 128
+    """Estimated cost of ntok tokens of one tier, for balancing splits and warps."""
+    return float(ntok) * head_dim / 128 * TIER_TOKEN_COST[tier]
+
+
+def _balance_warps(part, cost):
+    """Reorders one split's chunk list so that the kernel's positional dealing (position i to warp
+    class i % CTA_WARPS) gives its warps nearly equal costs: the heaviest chunks first, each to the
+    lightest class that still has a position free, then each class's chunks in their original
+    (arena) order, so every warp still moves through the tiers in the same order."""
+    n = len(part)
+    cap = [len(range(c, n, CTA_WARPS)) for c in range(CTA_WARPS)]
+    load = [0.0] * CTA_WARPS
+    members = [[] for _ in range(CTA_WARPS)]
+    for k in sorted(range(n), key=lambda k: -cost[part[k]]):
+        c = min((c for c in range(CTA_WARPS) if len(members[c]) < cap[c]), key=lambda c: load[c])
+        members[c].append(k)
+        load[c] += cost[part[k]]
+    for m in members:
+        m.sort()
+    return [part[members[i % CTA_WARPS][i // CTA_WARPS]] for i in range(n)]
 
 
 def _deal_chunks(chunk_arena, cost, n_splits):
     """Orders the chunks for n_splits split-K slices and returns (order, bounds): slice s runs
     chunks order[bounds[s]:bounds[s+1]].
 
-    Every slice takes a contiguous share of EVERY arena's chunks, and lists its shares in the
-    same arena order, so all CTAs move through the tiers together and the SMs' instruction caches
-    hold one tier's code at a time.  Shares are cut by cost, and the rounding error of each cut is
-    carried into the next arena's cut so the slices' total costs stay within about one chunk."""
+    Every slice takes a contiguous share of EVERY arena's chunks, and each of its warps meets its
+    shares in the same arena order, so all CTAs move through the tiers together and the SMs'
+    instruction caches hold one tier's code at a time.  Shares are cut by cost, and the rounding
+    error of each cut is carried into the next arena's cut so the slices' total costs stay within
+    about one chunk; within a slice the chunks are placed so its warps' costs are balanced
+    (_balance_warps)."""
     n = len(cost)
     if n == 0:
         return [], np.zeros(n_splits + 1, np.int32)
@@ -248,8 +278,10 @@ def _deal_chunks(chunk_arena, cost, n_splits):
         cuts.append((idx, b))
     order, bounds = [], [0]
     for s in range(n_splits):
+        part = []
         for idx, b in cuts:
-            order += idx[b[s]:b[s + 1]]
+            part += idx[b[s]:b[s + 1]]
+        order += _balance_warps(part, cost)
         bounds.append(len(order))
     return order, np.asarray(bounds, np.int32)
 

@@ -40,8 +40,9 @@ def test_large_pages_tile_within_a_slot():
     plan = A.AttentionPlan([a], [(0, 0, 80), (0, 1, 80)], batch=2, heads_kv=2, group=4, head_dim=128, n_splits=1)
     cap = A.chunk_capacity(a, 128)
     assert cap == 2
-    assert chunks_of(plan) == [(0, 0, 0, 2, 16), (0, 32, 0, 2, 16), (0, 64, 0, 1, 16),
-                               (1, 0, 0, 2, 16), (1, 32, 0, 2, 16), (1, 64, 0, 1, 16)]
+    # (the plan may place the chunks in any order to balance its warps)
+    assert sorted(chunks_of(plan)) == [(0, 0, 0, 2, 16), (0, 32, 0, 2, 16), (0, 64, 0, 1, 16),
+                                       (1, 0, 0, 2, 16), (1, 32, 0, 2, 16), (1, 64, 0, 1, 16)]
 
 
 def test_split_fp16_partial_closes_chunk():
@@ -74,7 +75,8 @@ def test_splits_take_a_share_of_every_arena_in_the_same_order():
     for s in range(7):
         part = plan.chunks[b[s]:b[s + 1]]
         seq = [c[2] for c in part]
-        assert seq == sorted(seq)  # arenas in the same order in every split
+        for w in range(A.CTA_WARPS):  # each warp meets the arenas in the same order
+            assert seq[w::A.CTA_WARPS] == sorted(seq[w::A.CTA_WARPS])
         assert set(seq) == {0, 1, 2, 3}  # a share of every arena
         costs.append(sum(A._tile_cost(arenas[c[2]].tier, 128, 16 * c[3]) for c in part))
     assert max(costs) - min(costs) <= max(A._tile_cost(t, 128, 16 * 16) for t in range(6))
@@ -95,3 +97,20 @@ def test_record_views_share_storage():
     rec = A.record_bytes(A.TIER_INT4, 16, 64)
     assert (raw[:, 1, :512] == 7).all() and (raw[:, 0] == 0).all() and (raw[:, 2] == 0).all()
     assert (raw[:, 1, 1024:1056].view(torch.float16) == 1.5).all() and rec == 1024 + 128
+
+
+def test_warps_of_a_split_get_balanced_costs():
+    """The kernel deals a split's chunks to its warps by position (i % 4); the plan places them so
+    the warps' costs differ by at most one chunk's, on a layer with every tier (chunk capacities
+    from 15 one-bit tiles down to one fp16 tile)."""
+    tiers = [(A.TIER_1BIT, 512), (A.TIER_INT2, 512), (A.TIER_INT4, 512), (A.TIER_INT8, 256), (A.TIER_FP8SIM, 192),
+             (A.TIER_FP16, 64)]
+    arenas = [arena(t, n) for t, n in tiers]
+    pages = [(i, s, 16) for i, (_, n) in enumerate(tiers) for s in range(n)]
+    plan = A.AttentionPlan(arenas, pages, batch=1, heads_kv=1, group=8, head_dim=128, n_splits=9)
+    b = plan.splits_dev.numpy()
+    for s in range(9):
+        part = plan.chunks[b[s]:b[s + 1]]
+        cost = [A._tile_cost(arenas[c[2]].tier, 128, 16 * c[3]) for c in part]
+        warps = [sum(cost[w::A.CTA_WARPS]) for w in range(A.CTA_WARPS)]
+        assert max(warps) - min(warps) <= max(cost) + 1e-9, warps
