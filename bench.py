@@ -618,11 +618,13 @@ def run_70b_heads(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        run()
-    e1.record()
-    torch.cuda.synchronize(device)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    with ClockSampler(vis.split(",")[local_rank] if vis else str(local_rank)) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1) / args.steps
     if world > 1:
         t = torch.tensor([ms], device=device)
@@ -642,7 +644,8 @@ def run_70b_heads(args, rank, world, local_rank):
                       "roofline": {"bound": "hbm", "achieved_per_gpu": layer_bytes / world / (ms * 1e-3) / 1e9,
                                    "peak": hbm, "unit": "GB/s",
                                    "frac": layer_bytes / world / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
-                                   "algorithmic_bytes_per_step": layer_bytes}}), flush=True)
+                                   "algorithmic_bytes_per_step": layer_bytes},
+                      "clocks": clk.summary()}), flush=True)
 
 
 def run_cascade(args):
