@@ -395,15 +395,40 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(Rows src, Rows dst, int6
         float sa[per], sb[per], sr[per];
 #pragma unroll
         for (int i = 0; i < per; ++i) {
-            const __half* hv = reinterpret_cast<const __half*>(raw[i]);
             bool nan = false;
             float m = 0.0f, lo = INFINITY, hi = -INFINITY;
+            if constexpr (C % 2 == 0) {
+                // column pairs in half2 lanes (exact: min, max and |x| do not round); the
+                // NaN-propagating max marks rows holding a NaN
+                const __half2* hv2 = reinterpret_cast<const __half2*>(raw[i]);
+                if constexpr (MODE == Q_INT8 || MODE == Q_FP8SIM) {
+                    __half2 a2 = __habs2(hv2[0]);
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-                const float v = h2f(hv[c]);
-                nan |= (v != v);
-                if (MODE == Q_INT8 || MODE == Q_FP8SIM) m = fmaxf(m, fabsf(v));
-                else { lo = fminf(lo, v); hi = fmaxf(hi, v); }
+                    for (int k = 1; k < C / 2; ++k) a2 = __hmax2_nan(a2, __habs2(hv2[k]));
+                    const float2 af = __half22float2(a2);
+                    nan = (af.x != af.x) || (af.y != af.y);
+                    m = fmaxf(af.x, af.y);
+                } else {
+                    __half2 l2 = hv2[0], u2 = hv2[0];
+#pragma unroll
+                    for (int k = 1; k < C / 2; ++k) {
+                        l2 = __hmin2(l2, hv2[k]);
+                        u2 = __hmax2_nan(u2, hv2[k]);
+                    }
+                    const float2 lf = __half22float2(l2), uf = __half22float2(u2);
+                    nan = (uf.x != uf.x) || (uf.y != uf.y);
+                    lo = fminf(lf.x, lf.y);
+                    hi = fmaxf(uf.x, uf.y);
+                }
+            } else {
+                const __half* hv = reinterpret_cast<const __half*>(raw[i]);
+#pragma unroll
+                for (int c = 0; c < C; ++c) {
+                    const float v = h2f(hv[c]);
+                    nan |= (v != v);
+                    if (MODE == Q_INT8 || MODE == Q_FP8SIM) m = fmaxf(m, fabsf(v));
+                    else { lo = fminf(lo, v); hi = fmaxf(hi, v); }
+                }
             }
 #pragma unroll
             for (int o = 1; o < 8; o <<= 1) {

@@ -673,19 +673,21 @@ def run_cascade(args):
     hbm, peak_kind = peaks()
     xbytes = x.numel() * 2
     per_tier, tot_bytes, tot_ms = {}, 0, 0.0
-    for name, qf, df in tiers:
-        coded = qf(x)
-        cbytes = sum(t.numel() * t.element_size() for t in coded)
-        ms_p = _timed(lambda: qf(x), args.steps, args.warmup)
-        ms_u = _timed(lambda: df(*coded), args.steps, args.warmup)
-        nb = xbytes + cbytes
-        per_tier[name] = {"pack_ms": ms_p, "unpack_ms": ms_u, "pack_GBs": nb / ms_p / 1e6, "unpack_GBs": nb / ms_u / 1e6,
-                          "pack_frac": nb / ms_p / 1e6 / hbm, "unpack_frac": nb / ms_u / 1e6 / hbm,
-                          "coded_bytes": cbytes}
-        tot_bytes += 2 * nb
-        tot_ms += ms_p + ms_u
-        del coded
-        torch.cuda.empty_cache()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    with ClockSampler(vis.split(",")[0] if vis else "0") as clk:
+        for name, qf, df in tiers:
+            coded = qf(x)
+            cbytes = sum(t.numel() * t.element_size() for t in coded)
+            ms_p = _timed(lambda: qf(x), args.steps, args.warmup)
+            ms_u = _timed(lambda: df(*coded), args.steps, args.warmup)
+            nb = xbytes + cbytes
+            per_tier[name] = {"pack_ms": ms_p, "unpack_ms": ms_u, "pack_GBs": nb / ms_p / 1e6,
+                              "unpack_GBs": nb / ms_u / 1e6, "pack_frac": nb / ms_p / 1e6 / hbm,
+                              "unpack_frac": nb / ms_u / 1e6 / hbm, "coded_bytes": cbytes}
+            tot_bytes += 2 * nb
+            tot_ms += ms_p + ms_u
+            del coded
+            torch.cuda.empty_cache()
     value = tot_bytes / tot_ms / 1e6
     line = {"metric": "quantize/pack cascade microbench, pack+unpack GB/s over all tiers", "value": value,
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms,
@@ -694,7 +696,7 @@ def run_cascade(args):
                        "outliers": "1% Laplace(0,4)", "l2": "inputs larger than L2 (2 GiB), no flush"},
             "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s", "frac": value / hbm,
                          "peak_kind": peak_kind, "algorithmic_bytes_per_step": tot_bytes},
-            "tiers": per_tier}
+            "tiers": per_tier, "clocks": clk.summary()}
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = _cascade_cpu()
     print(json.dumps(line), flush=True)
