@@ -370,10 +370,15 @@ def run_jl_archive(args):
     q = (torch.randn(Bj, HQj, 1, Dj, device=dev, generator=g) / math.sqrt(Dj)).half()
     out = torch.empty_like(q)
     lse = torch.empty(Bj, HQj, 1, device=dev)
-    ms = _timed(lambda: att.run(q, yk, yv, out=out, lse=lse), args.steps, args.warmup)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    with ClockSampler(vis.split(",")[0] if vis else "0") as clk:
+        ms = _timed(lambda: att.run(q, yk, yv, out=out, lse=lse), args.steps, args.warmup)
     hbm, peak_kind = peaks()
     ybytes = 2 * yk.numel() * 2
     tokens = Bj * NB * N
+    extra = {"clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        extra["cpu_baseline"] = _jl_cpu(R.cpu().numpy(), yk, yv, q, HQj // HKVj)
     print(json.dumps({"metric": "JL-archive decode attention, archived KV tokens/s", "value": tokens / (ms * 1e-3),
                       "unit": "KV tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
                       "ms_per_step": ms, "higher_is_better": True, "dtype": "fp16", "data": "synthetic",
@@ -381,7 +386,38 @@ def run_jl_archive(args):
                                  "head_dim": Dj, "blocks": NB, "block_tokens": N, "block_rows": MJ},
                       "roofline": {"bound": "hbm", "achieved": ybytes / (ms * 1e-3) / 1e9, "peak": hbm,
                                    "unit": "GB/s", "frac": ybytes / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
-                                   "algorithmic_bytes_per_launch": ybytes}}), flush=True)
+                                   "algorithmic_bytes_per_launch": ybytes}, **extra}), flush=True)
+
+
+def _jl_cpu(R, yk, yv, q, G, min_seconds=10.0):
+    """The reference's path for archived blocks on the host: every block rebuilt as K = R Yk,
+    V = R Yv (the oracle's float64 product rounded to fp16), then softmax attention of the (b, kv
+    head)'s G queries over all its rebuilt tokens; (b, kv head) pairs in turn until min_seconds."""
+    import numpy as np
+
+    import oracle
+
+    Bj, Hk, NB, MJ, Dj = yk.shape
+    N = R.shape[0]
+    qn = q.float().cpu().numpy()
+    scale = 1.0 / math.sqrt(Dj)
+    pairs, t0 = 0, time.perf_counter()
+    while True:
+        b, h = divmod(pairs % (Bj * Hk), Hk)
+        ykh = yk[b, h].cpu().numpy()
+        yvh = yv[b, h].cpu().numpy()
+        kv = [oracle.page_kv("jl", {"key_proj": ykh[j], "value_proj": yvh[j]}, R) for j in range(NB)]
+        K = np.concatenate([k for k, _ in kv])
+        V = np.concatenate([v for _, v in kv])
+        oracle.sdpa_f64(qn[b:b + 1, h * G:(h + 1) * G], K[None, None], V[None, None], scale)
+        pairs += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    tokens = pairs * NB * N / Hk  # a KV token covers all of a sequence's KV heads
+    return {"value": tokens / dt, "unit": "KV tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{pairs} (batch, kv head) pairs of {NB} blocks x {N} tokens rebuilt and attended "
+                      f"({dt:.1f} s)"}
 
 
 def run_70b_spill(args):
@@ -402,17 +438,24 @@ def run_70b_spill(args):
     host = spill.arenas_to_host([plan_all.arenas[0]])[0]
     st = spill.StreamedArenaAttention(host, group=HQ // HKV, chunk_slots=512)
     lse_r = torch.empty(B, HQ, 1, device=dev)
-    ms_resident_all = _timed(lambda: plan_all.run(q), args.steps, args.warmup)
-    ms_res = _timed(lambda: plan_res.run(q, lse=lse_r), args.steps, args.warmup)
-
     def layer():
         o_r = plan_res.run(q, lse=lse_r)
         o_s, l_s = st.run(q)
         return jl.merge_attention(o_r, lse_r, o_s, l_s)
 
-    ms = _timed(layer, max(3, args.steps // 10), 2)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    with ClockSampler(vis.split(",")[0] if vis else "0") as clk:
+        ms_resident_all = _timed(lambda: plan_all.run(q), args.steps, args.warmup)
+        ms_res = _timed(lambda: plan_res.run(q, lse=lse_r), args.steps, args.warmup)
+        ms = _timed(layer, max(3, args.steps // 10), 2)
     hbm, peak_kind = peaks()
     spilled = host.k.numel()
+    extra = {"clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        value, dt, cpu_steps = time_cpu(1, 0, os.cpu_count() or 1, min_seconds=10.0)
+        extra["cpu_baseline"] = {"value": value, "unit": "KV tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                                 "sample": f"1 sequence x {HKV} KV heads x {L} tokens per step (every tier resident), "
+                                           f"{cpu_steps} timed steps ({cpu_steps * dt:.1f} s of CPU work)"}
     print(json.dumps({"metric": "Llama-3-70B layer decode with the 1-bit tier spilled to host, KV tokens/s",
                       "value": B * L / (ms * 1e-3), "unit": "KV tokens/s", "n_gpus": 1, "ms_per_step": ms,
                       "higher_is_better": True, "dtype": "fp16", "data": "synthetic",
@@ -423,7 +466,7 @@ def run_70b_spill(args):
                                        "frac_of_hbm": plan_all.compressed_bytes / ms_resident_all / 1e6 / hbm,
                                        "peak_kind": peak_kind},
                       "resident_tiers_ms": ms_res,
-                      "host_link": {"spilled_bytes": spilled, "GB/s": spilled / ms / 1e6}}), flush=True)
+                      "host_link": {"spilled_bytes": spilled, "GB/s": spilled / ms / 1e6}, **extra}), flush=True)
 
 
 def _tinyllama_pages(device, seed=0):
