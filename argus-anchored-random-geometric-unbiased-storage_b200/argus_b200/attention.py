@@ -221,6 +221,9 @@ def chunk_capacity(arena, head_dim):
 TIER_TOKEN_COST = {TIER_1BIT: 0.69, TIER_INT2: 0.93, TIER_INT4: 0.96, TIER_INT8: 1.06, TIER_FP8SIM: 1.06,
                    TIER_FP16: 2.0}
 
+# CUDA graphs AttentionPlan.run_host keeps (one per pair of host buffers and scale).
+RUN_HOST_GRAPHS = 4
+
 # The kernel deals a split's chunks to its 4 warps by position: chunk i goes to warp pair i % 2, and
 # within the pair to warp (i // 2) % 2.
 CTA_WARPS = 4
@@ -437,10 +440,11 @@ class AttentionPlan:
     def run_host(self, q_host, out_host, scale=None):
         """One decode step for a host-resident query and output (pinned CPU tensors of q's shape):
         copy q in, run the fused kernel, copy the output back, replayed as one CUDA graph captured on
-        the first call for this pair of buffers and this scale.  Returns out_host once the copy-back
-        has been queued on the current stream (synchronize before reading it)."""
+        the first call for this pair of buffers and this scale (the RUN_HOST_GRAPHS most recently
+        used pairs keep theirs).  Returns out_host once the copy-back has been queued on the
+        current stream (synchronize before reading it)."""
         key = (q_host.data_ptr(), out_host.data_ptr(), scale)
-        entry = self._graphs.get(key)
+        entry = self._graphs.pop(key, None)
         if entry is None:
             exp = (self.B, self.Hkv * self.G, self.qlen, self.D)
             if tuple(q_host.shape) != exp or tuple(out_host.shape) != exp:
@@ -464,7 +468,9 @@ class AttentionPlan:
                 self.run(q_dev, scale=scale, out=out_dev)
                 out_host.copy_(out_dev, non_blocking=True)
             entry = (graph, q_dev, out_dev, q_host, out_host)
-            self._graphs[key] = entry
+            while len(self._graphs) >= RUN_HOST_GRAPHS:
+                self._graphs.pop(next(iter(self._graphs)))  # least recently used
+        self._graphs[key] = entry  # (re)inserted last: most recently used
         entry[0].replay()
         return out_host
 

@@ -139,4 +139,12 @@ def test_run_host_graph_matches_run():
         ref = plan.run(q.cuda())
         torch.cuda.synchronize()
         assert torch.equal(out_host.view(torch.int16), ref.cpu().view(torch.int16)), step
+    # more buffer pairs than the plan keeps graphs for: the least recently used graphs are dropped
+    for step in range(A.RUN_HOST_GRAPHS + 2):
+        qh = torch.from_numpy((rng.standard_normal((B, Hkv * G, 1, D)) / 8).astype(np.float16)).pin_memory()
+        oh = torch.empty_like(qh).pin_memory()
+        plan.run_host(qh, oh)
+        torch.cuda.synchronize()
+        assert torch.equal(oh.view(torch.int16), plan.run(qh.cuda()).cpu().view(torch.int16)), step
+        assert len(plan._graphs) <= A.RUN_HOST_GRAPHS
     assert A.device_status() == 0
