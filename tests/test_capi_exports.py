@@ -36,3 +36,62 @@ def test_status_strings():
     from argus_b200 import _lib
     assert _lib.status_string(0) == "ok"
     assert "misaligned" in _lib.status_string(_lib.ERR_MISALIGNED)
+
+
+def test_decode_attention_refuses_bad_arguments_before_touching_the_device():
+    """argus_decode_attention validates its arguments on the host and returns the status codes
+    the header documents (no CUDA call is reached for any of these)."""
+    from argus_b200 import _lib
+    from argus_b200 import attention as A
+
+    L = A._bind()
+    buf = (ctypes.c_uint8 * 4096)()
+    base = (ctypes.addressof(buf) + 15) & ~15  # 16-byte aligned host scratch standing in for q / out
+    split = (ctypes.c_int32 * 2)(0, 0)
+    arenas = (A.ArenaC * A.MAX_ARENAS)()
+
+    def call(shape, chunks=None, q=base, out=base + 1024, arena_ptr=arenas, s_ptr=True):
+        return L.argus_decode_attention(ctypes.byref(shape) if s_ptr else None, arena_ptr, chunks, split, q, out,
+                                        None, None, None, None)
+
+    def shape(**kw):
+        f = dict(batch=1, heads_kv=1, group=4, q_len=1, head_dim=128, n_splits=1, n_arenas=1, n_chunks=0,
+                 scale=0.088, flags=0)
+        f.update(kw)
+        return A.ShapeC(**f)
+
+    assert call(shape(), s_ptr=False) == _lib.ERR_INVALID_ARGUMENT
+    assert call(shape(), q=None) == _lib.ERR_INVALID_ARGUMENT
+    assert call(shape(batch=0)) == _lib.ERR_INVALID_ARGUMENT
+    assert call(shape(n_splits=0)) == _lib.ERR_INVALID_ARGUMENT
+    assert call(shape(n_arenas=0)) == _lib.ERR_INVALID_ARGUMENT
+    assert call(shape(n_arenas=A.MAX_ARENAS + 1)) == _lib.ERR_INVALID_ARGUMENT
+    assert call(shape(n_chunks=1)) == _lib.ERR_INVALID_ARGUMENT  # chunks missing
+    assert call(shape(head_dim=48)) == _lib.ERR_UNSUPPORTED
+    assert call(shape(batch=256, heads_kv=256)) == _lib.ERR_UNSUPPORTED  # B * H_kv above 65535
+    assert call(shape(), q=base + 2) == _lib.ERR_MISALIGNED
+    assert call(shape(), out=base + 1026) == _lib.ERR_MISALIGNED
+    assert "alignment" in _lib.lib().argus_last_error().decode()
+
+
+def test_codec_entry_points_refuse_bad_arguments():
+    """The quantizers refuse null buffers, head dims that are not a multiple of 8 and sequence
+    lengths that are not a multiple of the tier's packing factor (the reference asserts the last,
+    core/quantization.py:41,79,183), on the host, before any launch."""
+    from argus_b200 import _lib
+
+    L = _lib.lib()  # argument types bound from _lib.SIGNATURES
+    buf = (ctypes.c_uint8 * 4096)()
+    p = ctypes.addressof(buf)
+    for name in ("argus_quant_int8", "argus_quant_fp8sim"):
+        fn = getattr(L, name)
+        assert fn(None, 4, 64, p, p, None) == _lib.ERR_INVALID_ARGUMENT
+        assert fn(p, 4, 64, p, None, None) == _lib.ERR_INVALID_ARGUMENT
+        assert fn(p, 4, 60, p, p, None) == _lib.ERR_UNSUPPORTED
+    for name, per in (("argus_quant_int4", 2), ("argus_quant_int2", 4), ("argus_quant_1bit", 8)):
+        fn = getattr(L, name)
+        extra = (p,) if name != "argus_quant_1bit" else ()
+        assert fn(p, per + 1, 64, p, p, *extra, None) == _lib.ERR_INVALID_ARGUMENT
+        assert "packing factor" in L.argus_last_error().decode()
+        assert fn(p, -per, 64, p, p, *extra, None) == _lib.ERR_INVALID_ARGUMENT
+        assert fn(p, per, 64, p, None, *extra, None) == _lib.ERR_INVALID_ARGUMENT
