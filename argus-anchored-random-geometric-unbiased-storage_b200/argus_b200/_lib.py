@@ -46,6 +46,7 @@ SIGNATURES = {
     "argus_scatter_coo": [_p, _i64, _i64, _i32, _i32, _i32, _i32, _p, _p, _i64, _p],
     "argus_outliers_to_coo": [_p, _p, _i32, _i32, _i32, _i32, _p, _p, _i64, _p, _p],
     "argus_selftest_fp16_quotients": [_p, _p],
+    "argus_selftest_wait_timeout": [_i64, _p, _p],
 }
 
 

@@ -138,9 +138,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: false after kSpinLimit polls (the caller records a timeout and stops).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
-    for (long long i = 0; i < kSpinLimit; ++i)
+// Bounded wait: false after `polls` polls (the caller records a timeout and stops).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, long long polls = kSpinLimit) {
+    for (long long i = 0; i < polls; ++i)
         if (mbar_try_wait(bar, phase)) return true;
     return false;
 }
@@ -1327,6 +1327,25 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
     }
 }
 
+// Self-test of the bounded waits (argus_selftest_wait_timeout): the CTA waits, through the same
+// mbar_wait the ring consumers use, on an mbarrier that no copy and no thread ever completes, gives
+// up after `polls` polls and records ARGUS_ERR_TIMEOUT in the status word as a ring consumer does.
+__device__ int g_selftest_gave_up = 0;
+
+__global__ void wait_timeout_selftest_kernel(long long polls) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const bool done = mbar_wait(&bar, 0u, polls);
+    if (threadIdx.x == 0) {
+        if (!done) atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
+        g_selftest_gave_up = done ? 0 : 1;
+    }
+}
+
 template <int D>
 int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
     bool side = false;
@@ -1459,6 +1478,17 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
         case 128: return da::launch<128>(prm, s->n_splits, precise, st);
         default: return da::launch<256>(prm, s->n_splits, precise, st);
     }
+}
+
+int argus_selftest_wait_timeout(int64_t polls, int* gave_up, argus_stream_t stream) {
+    if (!gave_up) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null result");
+    if (polls <= 0 || polls > (int64_t)1 << 20) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "polls out of range");
+    cudaStream_t st = (cudaStream_t)stream;
+    da::wait_timeout_selftest_kernel<<<1, 32, 0, st>>>((long long)polls);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbolAsync(gave_up, da::g_selftest_gave_up, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return e == cudaSuccess ? ARGUS_OK : argus_set_cuda_error(e);
 }
 
 int argus_device_status(int* status, argus_stream_t stream) {

@@ -378,6 +378,13 @@ int64_t argus_decode_attention_noalloc_capacity(void);
  * reference. */
 int argus_selftest_fp16_quotients(unsigned long long* mismatches, argus_stream_t stream);
 
+/* Self-test of the bounded device waits: one CTA waits, with the wait the decode kernel's staging
+ * rings use, on an mbarrier that nothing ever completes, gives up after `polls` polls (1 .. 2^20)
+ * and sets the status word to ARGUS_ERR_TIMEOUT as a timed-out ring consumer does; *gave_up (host)
+ * receives 1.  The status stays set for argus_device_status to read; the context stays usable.
+ * Synchronises `stream`.  No counterpart in the reference. */
+int argus_selftest_wait_timeout(int64_t polls, int* gave_up, argus_stream_t stream);
+
 /* Reads (and clears) the device-side status words that bounded waits in the kernels set on a
  * timeout, and argus_outlier_corrections on a bad sidecar; writes ARGUS_OK, ARGUS_ERR_TIMEOUT or
  * ARGUS_ERR_INVALID_ARGUMENT to *status after synchronising `stream`. */

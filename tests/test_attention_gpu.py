@@ -169,3 +169,25 @@ def test_llama8b_layer_full_size_sampled_heads():
         ref = U.f64_attention(q[b:b + 1, h * G:(h + 1) * G], K, V)
         got = out[b:b + 1, h * G:(h + 1) * G]
         assert within(got, ref).all(), ((b, h), np.abs(got - ref).max())
+
+
+def test_bounded_wait_times_out_and_the_context_stays_usable():
+    """A device wait that nothing completes (the bounded mbarrier wait the decode kernel's staging
+    rings use) gives up after its poll limit and reports ARGUS_ERR_TIMEOUT through
+    argus_device_status, without a fault; launches afterwards run normally."""
+    import ctypes
+
+    from argus_b200 import _lib
+    from argus_b200 import attention as A
+    gave_up = ctypes.c_int(0)
+    _lib.call("argus_selftest_wait_timeout", 1000, ctypes.byref(gave_up), _lib.stream_handle())
+    assert gave_up.value == 1
+    assert A.device_status() == _lib.ERR_TIMEOUT
+    assert A.device_status() == 0  # read once, then cleared
+    B, Hkv, G, D, P = 1, 2, 4, 64, 16
+    rng = np.random.default_rng(5)
+    pages = U.random_pages(rng, [("int4", 32), ("fp16", 16)], B, Hkv, D, P)
+    q = (rng.standard_normal((B, Hkv * G, 1, D)) / 8).astype(np.float16)
+    out, _ = run_plan(pages, B, Hkv, G, D, q)
+    K, V = U.reference_kv(pages)
+    assert within(out, U.f64_attention(q, K, V)).all()

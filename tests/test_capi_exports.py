@@ -95,3 +95,13 @@ def test_codec_entry_points_refuse_bad_arguments():
         assert "packing factor" in L.argus_last_error().decode()
         assert fn(p, -per, 64, p, p, *extra, None) == _lib.ERR_INVALID_ARGUMENT
         assert fn(p, per, 64, p, None, *extra, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_wait_timeout_selftest_refuses_bad_arguments():
+    from argus_b200 import _lib
+
+    L = _lib.lib()
+    g = ctypes.c_int(0)
+    assert L.argus_selftest_wait_timeout(0, ctypes.byref(g), None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.argus_selftest_wait_timeout((1 << 20) + 1, ctypes.byref(g), None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.argus_selftest_wait_timeout(10, None, None) == _lib.ERR_INVALID_ARGUMENT
