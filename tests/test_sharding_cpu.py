@@ -102,3 +102,40 @@ def test_head_sharded_gather_matches_full_attention_world2(tmp_path):
     mp.start_processes(_rank_main, args=(2, _free_port(), path), nprocs=2, join=True, start_method="spawn")
     with open(path) as f:
         assert f.read() == "ok"
+
+
+def _rank_leaves_main(rank, world, port, result_path):
+    """Both ranks run one sharded step; rank 1 then leaves between steps (no collective in flight)
+    and rank 0's next step must end with an error within the process group's short timeout."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import time
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    rng = np.random.default_rng(3)
+    B, Hkv, G, L, D = 1, 2, 2, 24, 16
+    K = rng.standard_normal((B, Hkv, L, D))
+    V = rng.standard_normal((B, Hkv, L, D))
+    q = torch.from_numpy(rng.standard_normal((B, Hkv * G, 1, D)))
+    h0, h1 = sharding.head_range(Hkv, world, rank)
+    step = sharding.HeadShardedDecode(_OraclePlan(K[:, h0:h1], V[:, h0:h1]), Hkv)
+    step(q)
+    if rank == 1:
+        return  # leaves without joining the next step
+    t0 = time.monotonic()
+    try:
+        step(q)
+        outcome = "completed"
+    except Exception as e:  # gloo reports the lost peer or the timeout
+        outcome = f"raised {type(e).__name__} after {time.monotonic() - t0:.1f} s"
+    with open(result_path, "w") as f:
+        f.write(outcome)
+
+
+def test_a_rank_leaving_between_steps_ends_the_next_step_with_an_error(tmp_path):
+    path = str(tmp_path / "result.txt")
+    mp.start_processes(_rank_leaves_main, args=(2, _free_port(), path), nprocs=2, join=True, start_method="spawn")
+    with open(path) as f:
+        outcome = f.read()
+    assert outcome.startswith("raised"), outcome
+    assert float(outcome.split()[-2]) < 30.0
