@@ -141,10 +141,15 @@ __device__ __forceinline__ void decode8(const Rows& s, int64_t g, int pr, int c8
         const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
         const __half* sp = s.scales + g * s.sgroup_stride + s.row0 + t0;
         if constexpr (SRC == Q_INT8 || SRC == Q_FP8SIM) {
+            // code pairs to fp16 without conversions: the sign-flipped byte under the exponent of
+            // 1024 reads as 1024 + q + 128, so subtracting 1152 leaves q exactly; then fp16(q * s)
             const __half2 s2 = __half2half2(sp[0]);
+            const uint32_t w[2] = {raw.x ^ 0x80808080u, raw.y ^ 0x80808080u};
+            const __half2 bias = __float2half2_rn(1152.0f);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const __half2 v = __hmul2_rn(__halves2half2(__short2half_rn((int8_t)b[2 * e]), __short2half_rn((int8_t)b[2 * e + 1])), s2);
+                const uint32_t hv = __byte_perm(w[e >> 1], 0x64646464u, (e & 1) ? 0x5342 : 0x5140);
+                const __half2 v = __hmul2_rn(__hsub2(*reinterpret_cast<const __half2*>(&hv), bias), s2);
                 out[0][2 * e] = __low2half(v);
                 out[0][2 * e + 1] = __high2half(v);
             }
@@ -152,13 +157,19 @@ __device__ __forceinline__ void decode8(const Rows& s, int64_t g, int pr, int c8
             constexpr int BITS = 8 / per;
             constexpr uint32_t m = (1u << BITS) - 1u;
             const __half* mp = s.mins + g * s.sgroup_stride + s.row0 + t0;
+            // columns 2e, 2e+1 as the low bytes of two halves; row i's codes shifted down, masked and
+            // put under the exponent of 1024 read as 1024 + u, so subtracting 1024 leaves u exactly
+            uint32_t pairs[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pairs[e] = __byte_perm((e < 2) ? raw.x : raw.y, 0u, (e & 1) ? 0x4342 : 0x4140);
+            const __half2 base = __float2half2_rn(1024.0f);
 #pragma unroll
             for (int i = 0; i < per; ++i) {
                 const __half2 s2 = __half2half2(sp[i]), m2 = __half2half2(mp[i]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const __half2 u = __halves2half2(__uint2half_rn((b[2 * e] >> (BITS * i)) & m),
-                                                     __uint2half_rn((b[2 * e + 1] >> (BITS * i)) & m));
+                    const uint32_t hv = ((pairs[e] >> (BITS * i)) & (m | (m << 16))) | 0x64006400u;
+                    const __half2 u = __hsub2(*reinterpret_cast<const __half2*>(&hv), base);
                     const __half2 v = __hadd2_rn(__hmul2_rn(u, s2), m2);
                     out[i][2 * e] = __low2half(v);
                     out[i][2 * e + 1] = __high2half(v);
