@@ -536,7 +536,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(Rows src, Rows dst, int6
 // order (lane l sums columns 8c + l), so each row passes through a small per-group shared-memory
 // buffer where the 8 lanes read it strided; the sign bits come from the lane's own registers.
 template <int D>
-__global__ void __launch_bounds__(256) pack_sign_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows) {
+__global__ void __launch_bounds__(256, D >= 256 ? 2 : (D >= 128 ? 3 : 4)) pack_sign_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows) {
     constexpr int C = D / 8;
     constexpr int LW = (C * 2 + 3) / 4;
     constexpr int OW = (C + 3) / 4;
@@ -549,43 +549,51 @@ __global__ void __launch_bounds__(256) pack_sign_kernel(Rows src, Rows dst, int6
     const int64_t stride = ((int64_t)gridDim.x * blockDim.x) >> 3;
     // every lane runs the same number of iterations (the shuffles and warp barriers need the whole warp)
     const int64_t first = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >> 3;
+    const __half2 zero2 = __float2half2_rn(0.0f);
     for (int64_t base = first; base < total; base += stride) {
         const int64_t pr = base + ((threadIdx.x & 31) >> 3);
         const bool live = pr < total;
         const int64_t g = live ? pr / prg : 0;
         const int prl = live ? (int)(pr - g * prg) : 0;
-        uint32_t raw[8][LW];
+        const unsigned char* rows = src.payload + g * src.group_stride + (int64_t)(src.row0 + prl * 8) * D * 2 + lane8 * C * 2;
+        // the 8 token rows stream through: row i+1 loads while row i is summed and its sign bits taken
+        uint32_t cur[LW], nxt[LW];
+        if (live) ld_bytes<C * 2>(rows, cur);
+        else
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (live)
-                ld_bytes<C * 2>(src.payload + g * src.group_stride + (int64_t)(src.row0 + prl * 8 + i) * D * 2 + lane8 * C * 2,
-                                raw[i]);
-            else
+            for (int w = 0; w < LW; ++w) cur[w] = 0u;
+        uint32_t pairw[C / 2];  // bit i of bytes 0 / 2: x >= 0 for row i, columns 2k / 2k+1 (NaN: 0, -0: 1)
 #pragma unroll
-                for (int w = 0; w < LW; ++w) raw[i][w] = 0u;
-        }
+        for (int k = 0; k < C / 2; ++k) pairw[k] = 0u;
         float sa[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
+            if (i < 7) {
+                if (live) ld_bytes<C * 2>(rows + (int64_t)(i + 1) * D * 2, nxt);
+                else
 #pragma unroll
-            for (int w = 0; w < LW; ++w) reinterpret_cast<uint32_t*>(buf + lane8 * C)[w] = raw[i][w];
+                    for (int w = 0; w < LW; ++w) nxt[w] = 0u;
+            }
+#pragma unroll
+            for (int w = 0; w < LW; ++w) reinterpret_cast<uint32_t*>(buf + lane8 * C)[w] = cur[w];
             __syncwarp();
             const float lane_sum = cascade_lane_sum<true>(buf, D / 8, lane8);
             sa[i] = rh(__fdiv_rn(cascade_combine(lane_sum), (float)D));  // fp16(sum |x| / D)
             __syncwarp();
+#pragma unroll
+            for (int k = 0; k < C / 2; ++k)
+                pairw[k] |= __hge2_mask(reinterpret_cast<const __half2*>(cur)[k], zero2) & (0x00010001u << i);
+            if (i < 7)
+#pragma unroll
+                for (int w = 0; w < LW; ++w) cur[w] = nxt[w];
         }
         uint32_t out[OW];
 #pragma unroll
         for (int w = 0; w < OW; ++w) out[w] = 0u;
-        const __half2 zero2 = __float2half2_rn(0.0f);
 #pragma unroll
         for (int k = 0; k < C / 2; ++k) {
-            uint32_t pairw = 0u;  // bit i of bytes 0 / 2: x >= 0 for row i, columns 2k / 2k+1 (NaN: 0, -0: 1)
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                pairw |= __hge2_mask(reinterpret_cast<const __half2*>(raw[i])[k], zero2) & (0x00010001u << i);
-            if (k & 1) out[k >> 1] |= __byte_perm(pairw, 0u, 0x2044) & 0xFFFF0000u;
-            else       out[k >> 1] |= __byte_perm(pairw, 0u, 0x4420) & 0x0000FFFFu;
+            if (k & 1) out[k >> 1] |= __byte_perm(pairw[k], 0u, 0x2044) & 0xFFFF0000u;
+            else       out[k >> 1] |= __byte_perm(pairw[k], 0u, 0x4420) & 0x0000FFFFu;
         }
         if (live) {
             st_bytes<C>(dst.payload + g * dst.group_stride + (int64_t)((dst.row0 + prl * 8) / 8) * D + lane8 * C, out);
