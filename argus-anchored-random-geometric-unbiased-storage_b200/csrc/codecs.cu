@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(Rows src, Rows dst, int6
     const int64_t total = n_groups * prg;
     for (int64_t pr = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3; pr < total;
          pr += ((int64_t)gridDim.x * blockDim.x) >> 3) {
-        const int64_t g = pr / prg;
+        const int64_t g = n_groups == 1 ? 0 : pr / prg;  // one group (flat tensors): no division
         const int prl = (int)(pr - g * prg);
         uint32_t raw[per][LW];
 #pragma unroll
@@ -553,7 +553,7 @@ __global__ void __launch_bounds__(256, D >= 256 ? 2 : (D >= 128 ? 3 : 4)) pack_s
     for (int64_t base = first; base < total; base += stride) {
         const int64_t pr = base + ((threadIdx.x & 31) >> 3);
         const bool live = pr < total;
-        const int64_t g = live ? pr / prg : 0;
+        const int64_t g = (live && n_groups > 1) ? pr / prg : 0;  // one group (flat tensors): no division
         const int prl = live ? (int)(pr - g * prg) : 0;
         const unsigned char* rows = src.payload + g * src.group_stride + (int64_t)(src.row0 + prl * 8) * D * 2 + lane8 * C * 2;
         // the 8 token rows stream through: row i+1 loads while row i is summed and its sign bits taken
@@ -623,11 +623,25 @@ __global__ void dequant_kernel(Rows src, Rows dst, int64_t n_groups, int group_r
     constexpr int per = mode_per(SRC);
     const int c8n = D / 8;
     const int prg = group_rows / per;
-    const int64_t items = n_groups * prg * c8n;
+    const int64_t per_group = (int64_t)prg * c8n;
+    const int64_t items = n_groups * per_group;
+    // one group whose items fit 32 bits and a power-of-two column count (the usual flat tensors):
+    // the item index splits with a shift and a mask instead of 64-bit divisions
+    const bool flat32 = n_groups == 1 && per_group < ((int64_t)1 << 31) && (c8n & (c8n - 1)) == 0;
+    const int sh = __ffs(c8n) - 1;
     for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < items; w += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t g = w / ((int64_t)prg * c8n);
-        const int rem = (int)(w - g * prg * c8n);
-        const int pr = rem / c8n, c8 = rem - pr * c8n;
+        int64_t g;
+        int pr, c8;
+        if (flat32) {
+            g = 0;
+            pr = (int)((uint32_t)w >> sh);
+            c8 = (int)((uint32_t)w & (uint32_t)(c8n - 1));
+        } else {
+            g = w / per_group;
+            const int64_t rem = w - g * per_group;
+            pr = (int)(rem / c8n);
+            c8 = (int)(rem - (int64_t)pr * c8n);
+        }
         __half v[8][8];
         decode8<SRC>(src, g, pr, c8, D, v);
 #pragma unroll
