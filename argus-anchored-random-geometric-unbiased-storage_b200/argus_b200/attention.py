@@ -485,45 +485,3 @@ def device_status(stream=None):
         raise _lib.ArgusError("argus_device_status", rc, L.argus_last_error().decode())
     return v.value
 
-
-def smoke_check():
-    """One small mixed-tier attention on cuda:0 checked against a float64 reference built from
-    the CPU oracle's dequantization of the same pages."""
-    import oracle
-    from .core import quantization as Q
-
-    torch.manual_seed(0)
-    B, Hkv, G, D, P = 1, 2, 4, 128, 16
-    dev = "cuda:0"
-    arenas, refs = [], []
-    for tier in (TIER_FP16, TIER_INT8, TIER_INT4, TIER_1BIT):
-        k = torch.randn(1, B, Hkv, P, D, device=dev).half()
-        v = torch.randn(1, B, Hkv, P, D, device=dev).half()
-        a = KVArena.allocate(tier, B, Hkv, 1, P, D, dev)
-        kn, vn = k[0].cpu().numpy(), v[0].cpu().numpy()
-        if tier == TIER_FP16:
-            a.write_pages(0, k, v)
-            refs.append((kn, vn))
-        elif tier == TIER_INT8:
-            (kq, ks), (vq, vs) = Q.quantize_to_int8(k), Q.quantize_to_int8(v)
-            a.write_pages(0, kq, vq, ks, vs)
-            refs.append(tuple(oracle.dequantize_from_int8(*oracle.quantize_to_int8(x)) for x in (kn, vn)))
-        elif tier == TIER_INT4:
-            (kp, ks, km), (vp, vs, vm) = Q.quantize_to_int4_packed(k), Q.quantize_to_int4_packed(v)
-            a.write_pages(0, kp, vp, ks, vs, km, vm)
-            refs.append(tuple(oracle.dequantize_from_int4_packed(*oracle.quantize_to_int4_packed(x)) for x in (kn, vn)))
-        else:
-            (kp, ks), (vp, vs) = Q.quantize_to_1bit_packed(k), Q.quantize_to_1bit_packed(v)
-            a.write_pages(0, kp, vp, ks, vs)
-            refs.append(tuple(oracle.dequantize_from_1bit_packed(*oracle.quantize_to_1bit_packed(x)) for x in (kn, vn)))
-        arenas.append(a)
-    plan = AttentionPlan(arenas, [(i, 0, P) for i in range(len(arenas))], batch=B, heads_kv=Hkv, group=G,
-                         head_dim=D, n_splits=2)
-    q = torch.randn(B, Hkv * G, 1, D, device=dev).half()
-    out = plan.run(q)
-    K = np.concatenate([r[0] for r in refs], axis=2)
-    V = np.concatenate([r[1] for r in refs], axis=2)
-    ref = oracle.sdpa_f64(q.cpu().numpy(), K, V, 1.0 / math.sqrt(D))
-    err = np.abs(out.cpu().numpy().astype(np.float64) - ref).max()
-    assert err < 2e-3, f"decode attention smoke: max abs err {err}"
-    assert device_status() == 0

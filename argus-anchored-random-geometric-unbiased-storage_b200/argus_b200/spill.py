@@ -55,6 +55,9 @@ def arenas_to_device(host_arenas, device, event_out=None):
         return []
     device = torch.device(device)
     st = side_stream(device)
+    # the new buffers come from the compute stream's pool: a block it freed may still have reads or
+    # writes queued there, so the copies start after the compute stream's pending work
+    st.wait_stream(torch.cuda.current_stream(device))
     out = []
     for a in host_arenas:
         buf = torch.empty(a.k.shape, dtype=torch.uint8, device=device)
@@ -96,6 +99,10 @@ class StreamedArenaAttention:
         self._plans = {}
         self.copied = [torch.cuda.Event() for _ in range(2)]
         self.released = [torch.cuda.Event() for _ in range(2)]
+        # the staging buffers were allocated on the current stream (whose earlier work may still use
+        # their blocks): the first copies into them wait for it through these events
+        for ev in self.released:
+            ev.record(torch.cuda.current_stream(self.device))
 
     def _plan(self, buf, ns, q_len):
         from .attention import AttentionPlan

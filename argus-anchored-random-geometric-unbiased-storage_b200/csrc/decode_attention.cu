@@ -16,8 +16,8 @@
 //   K (A operand) thread (g, t) holds tokens 2g, 2g+1 and dims t*D/4 .. t*D/4 + D/4 - 1;
 //   V (A operand) thread (g, t) holds tokens 4t .. 4t+3 and dims g*D/8 .. g*D/8 + D/8 - 1.
 // The score tile is moved into the PV operand layout with movmatrix (8x8 transpose).  Online
-// softmax runs in the log2 domain; warps merge in shared memory; splits merge in a second kernel
-// (log-sum-exp combine).
+// softmax runs in the log2 domain; warps merge in shared memory; the last CTA of each (batch,
+// kv_head, query group) to finish merges the split-K partials by log-sum-exp inside this kernel.
 #include <mutex>
 
 #include "common.cuh"
@@ -1157,16 +1157,17 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
             }
         }
         {
-            // bounded: chunk j is issued by whichever warp finishes chunk j - kStages
+            // bounded: chunk j is issued by whichever warp finishes chunk j - kStages.  Both waits are
+            // voted over the warp, so its lanes leave the loop together.
             long long spin = 0;
             while (*reinterpret_cast<volatile int*>(&issued[pair][stage]) != j && spin < kSpinLimit) ++spin;
-            if (spin >= kSpinLimit) {
+            if (__any_sync(0xffffffffu, spin >= kSpinLimit)) {
                 failed = true;
                 break;
             }
             __threadfence_block();
         }
-        if (!mbar_wait(&mbar[pair][stage], (uint32_t)((j / kStages) & 1))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&mbar[pair][stage], (uint32_t)((j / kStages) & 1)))) {
             failed = true;
             break;
         }
@@ -1244,8 +1245,12 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
     }
     if (failed) {
         if (lane == 0) atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
-        // let copies still in flight land before the shared memory is released (bounded again)
-        for (int s = 0; s < kStages; ++s) (void)mbar_wait(&mbar[pair][s], 0u);
+        // let copies still in flight land before the shared memory is released (bounded again): each
+        // slot's last issued chunk j' completes phase j' / kStages of the slot's barrier
+        for (int s = 0; s < kStages; ++s) {
+            const int jl = *reinterpret_cast<volatile int*>(&issued[pair][s]);
+            if (jl >= 0) (void)mbar_wait(&mbar[pair][s], (uint32_t)((jl / kStages) & 1));
+        }
     }
 
     // ---- finish this warp: reduce l over the 8 token lanes
@@ -1400,9 +1405,16 @@ int64_t argus_decode_attention_workspace_size(const argus_attn_shape* s) {
     return ((groups * 4 + 255) & ~255LL) + groups * s->n_splits * da::kQ * ((int64_t)s->head_dim + 1) * (int64_t)sizeof(float) + 256;
 }
 
-int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
-                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, float* tile_lse,
-                           void* workspace, argus_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// Checks every argument of a decode-attention call but the split-K workspace and fills the launch
+// parameters.  Returns ARGUS_OK or an error status (argus_last_error has the text); nothing is
+// queued on the device either way.
+int prepare_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
+                      const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, float* tile_lse,
+                      da::Params& prm) {
     if (!s || !arenas || !split_chunk0 || !q || !out)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
     if (s->batch <= 0 || s->heads_kv <= 0 || s->group <= 0 || s->q_len <= 0 || s->n_splits <= 0)
@@ -1414,7 +1426,6 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
     const int D = s->head_dim;
     if (!valid_head_dim(D)) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "head_dim must be 16, 32, 64, 128 or 256");
     if (!argus_aligned(q, 16) || !argus_aligned(out, 16)) return argus_set_error(ARGUS_ERR_MISALIGNED, "q/out alignment");
-    da::Params prm;
     memset(&prm, 0, sizeof(prm));
     for (int i = 0; i < s->n_arenas; ++i) {
         const argus_kv_arena& a = arenas[i];
@@ -1461,6 +1472,12 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
     prm.scale_log2 = s->scale * 1.4426950408889634f;
     if ((int64_t)(s->n_splits + 2) * da::kQ * 4 > (int64_t)da::kPairs * da::kStages * da::stage_bytes(D))
         return argus_set_error(ARGUS_ERR_UNSUPPORTED, "too many splits for the split merge");
+    return ARGUS_OK;
+}
+
+// Launches a prepared call with its split-K workspace (unused when n_splits == 1).
+int launch_prepared(const argus_attn_shape* s, da::Params& prm, void* workspace, argus_stream_t stream) {
+    const int D = s->head_dim;
     if (s->n_splits > 1) {
         if (!workspace || !argus_aligned(workspace, 16))
             return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "split-K needs a 16-byte aligned workspace");
@@ -1478,6 +1495,19 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
         case 128: return da::launch<128>(prm, s->n_splits, precise, st);
         default: return da::launch<256>(prm, s->n_splits, precise, st);
     }
+}
+
+}  // namespace
+
+extern "C" {
+
+int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
+                           const int32_t* split_chunk0, const uint16_t* q, uint16_t* out, float* lse, float* tile_lse,
+                           void* workspace, argus_stream_t stream) {
+    da::Params prm;
+    const int rc = prepare_attention(s, arenas, chunks, split_chunk0, q, out, lse, tile_lse, prm);
+    if (rc != ARGUS_OK) return rc;
+    return launch_prepared(s, prm, workspace, stream);
 }
 
 int argus_selftest_wait_timeout(int64_t polls, int* gave_up, argus_stream_t stream) {
@@ -1554,6 +1584,11 @@ extern "C" int argus_decode_attention_noalloc(const argus_attn_shape* s, const a
         return argus_set_error(ARGUS_ERR_CAPACITY,
                                "split-K partials exceed the 8 MiB built-in scratch: use fewer splits or "
                                "argus_decode_attention with a caller workspace");
+    // every other argument is checked before anything touches the shared scratch, so a refused call
+    // leaves the counters of a call still in flight alone
+    da::Params prm;
+    const int prc = prepare_attention(s, arenas, chunks, split_chunk0, q, out, lse, tile_lse, prm);
+    if (prc != ARGUS_OK) return prc;
     void* scratch = nullptr;
     if (need > 0) {
         const int rc = noalloc_scratch(&scratch);
@@ -1564,5 +1599,5 @@ extern "C" int argus_decode_attention_noalloc(const argus_attn_shape* s, const a
         const cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)((groups * 4 + 255) & ~255LL), (cudaStream_t)stream);
         if (e != cudaSuccess) return argus_set_cuda_error(e);
     }
-    return argus_decode_attention(s, arenas, chunks, split_chunk0, q, out, lse, tile_lse, scratch, stream);
+    return launch_prepared(s, prm, scratch, stream);
 }

@@ -99,10 +99,19 @@ __global__ void __launch_bounds__(kThreads) jl_apply_tc_kernel(const __half* __r
     const uint32_t idesc = instr_desc(kM, N);
     const int nk = K / kKT;
     const int xchunks = N / 8;  // 16-byte chunks per staging row
+    // Every wait's outcome is voted over the CTA (__syncthreads_and), so all threads leave the k-loop
+    // on the same iteration and the barriers, the warp-collective tensor-memory loads and the
+    // deallocation below are reached by whole warps.  `pending`: parity of the last committed MMA
+    // group not yet seen complete (-1: none).
     bool ok = true;
-    for (int kt = 0; kt < nk && ok; ++kt) {
-        if (kt > 0) ok = mbar_wait(bar, (uint32_t)((kt - 1) & 1));  // previous MMAs done with the tiles
-        if (!ok) break;
+    int pending = -1;
+    for (int kt = 0; kt < nk; ++kt) {
+        if (kt > 0) {
+            // previous MMAs done with the tiles
+            ok = __syncthreads_and(mbar_wait(bar, (uint32_t)((kt - 1) & 1)) ? 1 : 0) != 0;
+            if (!ok) break;
+            pending = -1;
+        }
         // A tile: row m, 8-element group g -> core matrix (m / 8, g) row m % 8
         for (int idx = tid; idx < kM * (kKT / 8); idx += kThreads) {
             const int m = idx >> 3, g = idx & 7;
@@ -149,8 +158,12 @@ __global__ void __launch_bounds__(kThreads) jl_apply_tc_kernel(const __half* __r
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                          : "memory");
         }
+        pending = kt & 1;
     }
-    if (ok) ok = mbar_wait(bar, (uint32_t)((nk - 1) & 1));
+    if (ok) {
+        ok = __syncthreads_and(mbar_wait(bar, (uint32_t)((nk - 1) & 1)) ? 1 : 0) != 0;
+        if (ok) pending = -1;
+    }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
         // epilogue: warp w reads tensor-memory lanes 32w .. 32w+31 (rows), 32 columns at a time
@@ -176,8 +189,10 @@ __global__ void __launch_bounds__(kThreads) jl_apply_tc_kernel(const __half* __r
                 *reinterpret_cast<uint4*>(crow + c0 + j) = w;
             }
         }
-    } else if (tid == 0) {
-        atomicExch(&g_jl_status, (int)ARGUS_ERR_TIMEOUT);
+    } else {
+        if (tid == 0) atomicExch(&g_jl_status, (int)ARGUS_ERR_TIMEOUT);
+        // MMAs still in flight write tensor memory: give them one more bounded wait before it is freed
+        if (pending >= 0) (void)__syncthreads_and(mbar_wait(bar, (uint32_t)pending) ? 1 : 0);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();

@@ -196,6 +196,9 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
     const int64_t x_end = ((c + 1) * T + C - 1) / C;
     bool ok = true;
     int it = 0;
+    // parity of each buffer's issued copy not yet seen complete (-1: none); kept alike by every
+    // thread, so that after a timed-out wait the CTA waits (bounded) for exactly the copies in flight
+    int yk_pend = -1, yv_pend = -1;
     for (int64_t xs = (c * T + C - 1) / C; xs < x_end && ok;) {
     const int64_t bh = xs / PP;
     const int64_t xe = (x_end < (bh + 1) * PP) ? x_end : (bh + 1) * PP;
@@ -226,10 +229,13 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         lrun[tid] = 0.f;
     }
     __syncthreads();
-    if (tid == 0 && j0 < j1) {
-        const int nb = (j1 - j0) < PACK ? (j1 - j0) : PACK;
-        issue_blocks(&p.tmk, bh, j0, nb, ykbuf, ykbar);
-        issue_blocks(&p.tmv, bh, j0, nb, yvbuf, yvbar);
+    if (j0 < j1) {
+        if (tid == 0) {
+            const int nb = (j1 - j0) < PACK ? (j1 - j0) : PACK;
+            issue_blocks(&p.tmk, bh, j0, nb, ykbuf, ykbar);
+            issue_blocks(&p.tmv, bh, j0, nb, yvbuf, yvbar);
+        }
+        yk_pend = yv_pend = it & 1;
     }
 
     float oacc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 16*warp + g (+8), columns 2t, 2t+1
@@ -237,6 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         const bool hasB = PACK == 2 && j + 1 < j1;
         ok = __syncthreads_and(mbar_wait(ykbar, (uint32_t)(it & 1)));
         if (!ok) break;
+        yk_pend = -1;
         // ---- u = Yk . q^T: rows 16*warp .. +15, block A in columns 0..3 (or 0..7), block B in 4..7
         {
             float u[4] = {0.f, 0.f, 0.f, 0.f}, u2[4] = {0.f, 0.f, 0.f, 0.f};  // two independent chains
@@ -266,9 +273,12 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             }
         }
         __syncthreads();
-        if (tid == 0 && j + PACK < j1) {  // Yk buffer consumed: bring the next pair
-            const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
-            issue_blocks(&p.tmk, bh, j + PACK, nb, ykbuf, ykbar);
+        if (j + PACK < j1) {  // Yk buffer consumed: bring the next pair
+            if (tid == 0) {
+                const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
+                issue_blocks(&p.tmk, bh, j + PACK, nb, ykbuf, ykbar);
+            }
+            yk_pend = (it + 1) & 1;
         }
         // ---- scores, softmax and w over this warp's token tiles
         uint32_t ub[KM][2][2];
@@ -408,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
         __syncthreads();
         ok = __syncthreads_and(mbar_wait(yvbar, (uint32_t)(it & 1)));
         if (!ok) break;
+        yv_pend = -1;
         // ---- o += Yv^T . w for dims 16*warp .. +15
         {
             const float a0 = alpha[2 * t], a1 = alpha[2 * t + 1];
@@ -435,15 +446,19 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_const
             for (int c = 0; c < 4; ++c) oacc[c] += olo[c];
         }
         __syncthreads();
-        if (tid == 0 && j + PACK < j1) {  // Yv buffer consumed
-            const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
-            issue_blocks(&p.tmv, bh, j + PACK, nb, yvbuf, yvbar);
+        if (j + PACK < j1) {  // Yv buffer consumed
+            if (tid == 0) {
+                const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
+                issue_blocks(&p.tmv, bh, j + PACK, nb, yvbuf, yvbar);
+            }
+            yv_pend = (it + 1) & 1;
         }
     }
     if (!ok) {
         if (tid == 0) atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
-        (void)mbar_wait(ykbar, 0u);  // let copies in flight land before the CTA exits (bounded)
-        (void)mbar_wait(yvbar, 0u);
+        // let copies in flight land before the CTA exits (bounded)
+        if (yk_pend >= 0) (void)mbar_wait(ykbar, (uint32_t)yk_pend);
+        if (yv_pend >= 0) (void)mbar_wait(yvbar, (uint32_t)yv_pend);
         break;
     }
     __syncthreads();

@@ -7,9 +7,16 @@ Llama-3-8B-shaped layer, batch 8 per GPU, 32 query heads, 8 KV heads, head_dim 1
 tier codecs; queries N(0,1)/sqrt(128); softmax scale 1/sqrt(128).  The compressed cache is
 280.8 MB per GPU, larger than the 126 MB L2, so every step streams it from HBM.
 
-Multi-GPU: one process per GPU (torchrun); each rank holds its own batch of 8 sequences (batch
-sharding: no exchange in the data path), so per-GPU work is fixed ("weak" scaling) and `value`
-is the whole-job KV tokens/s (ranks x 8 x 32768 / max-over-ranks step time).
+Multi-GPU: one process per GPU (torchrun), the layer sharded by KV head.  The batch grows with the
+ranks (8 x N sequences) and rank r holds KV heads [8r/N, 8(r+1)/N) of every sequence and page, so
+each GPU streams the same 280.8 MB per step ("weak" scaling); a step is the fused kernel on the
+rank's heads plus one NCCL all-gather of the per-head outputs into [8N, 32, 1, 128]
+(sharding.HeadShardedDecode).  `value` is the whole-job KV tokens/s (8N x 32768 / max-over-ranks
+step time).  At N = 1 there is nothing to gather and the step is the kernel alone.
+
+Timing: W untimed steps, then windows of exactly K steps (CUDA events on the launching stream,
+barrier + synchronize around each) repeated until at least one second of device time has passed,
+so the clock sampler sees the kernel under load; the reported step time is the median window.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -54,11 +61,13 @@ SPLIT = [("one_bit", 8192), ("int2", 8192), ("int4", 8192), ("int8", 4096), ("fp
 WORKLOAD = "llama3-8b-layer-mixed-tier-decode"
 
 
-def config(parallelism):
-    return {"workload": WORKLOAD, "batch_per_gpu": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+def config(world):
+    par = "single GPU" if world == 1 else f"kv-head sharded x{world} ({HKV // world} KV heads per GPU), NCCL all-gather of outputs"
+    return {"workload": WORKLOAD, "global_batch": B * world, "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
             "context": L, "page_size": P, "tiers_oldest_first": dict(SPLIT),
+            "bytes_per_gpu": "280.8 MB compressed (8 sequences x 8 KV heads' worth)",
             "l2": "inputs larger than L2 (280.8 MB compressed per GPU vs 126 MB L2), no flush",
-            "parallelism": parallelism}
+            "parallelism": par}
 
 
 def peaks():
@@ -82,19 +91,27 @@ def traffic_from_profile():
 
 
 # ------------------------------------------------------------------------------ workload
-def build_cache(device, seed):
+def build_cache(device, seed, batch=None, heads_kv=None, sample=None):
+    """The tiered cache of `batch` sequences x `heads_kv` KV heads (default: the module's B, HKV),
+    quantized on the device by the tier codecs, its AttentionPlan, and N(0,1)/sqrt(D) queries for
+    the group of query heads of those KV heads.  With `sample` (a list of (b, h) pairs) also returns
+    host copies of those pairs' fp16 K/V before quantization: {tier: (k, v)} of [pages, P, D] each."""
     import torch
 
     from argus_b200 import attention as A
     from argus_b200.core import quantization as Q
 
+    Bc = B if batch is None else batch
+    Hc = HKV if heads_kv is None else heads_kv
     g = torch.Generator(device=device).manual_seed(seed)
-    arenas, pages = [], []
+    arenas, pages, src = [], [], {}
     for tier, ntok in SPLIT:
         n = ntok // P
-        k = torch.randn(n, B, HKV, P, D, device=device, generator=g).half()
-        v = torch.randn(n, B, HKV, P, D, device=device, generator=g).half()
-        a = A.KVArena.allocate(A.TIER_NAMES[tier], B, HKV, n, P, D, device)
+        k = torch.randn(n, Bc, Hc, P, D, device=device, generator=g).half()
+        v = torch.randn(n, Bc, Hc, P, D, device=device, generator=g).half()
+        if sample is not None:
+            src[tier] = {bh: (k[:, bh[0], bh[1]].cpu().numpy(), v[:, bh[0], bh[1]].cpu().numpy()) for bh in sample}
+        a = A.KVArena.allocate(A.TIER_NAMES[tier], Bc, Hc, n, P, D, device)
         if tier == "fp16":
             a.write_pages(0, k, v)
         elif tier in ("int8", "fp8"):
@@ -113,9 +130,9 @@ def build_cache(device, seed):
         arenas.append(a)
         pages += [(ai, j, P) for j in range(n)]
     torch.cuda.synchronize(device)
-    plan = A.AttentionPlan(arenas, pages, batch=B, heads_kv=HKV, group=HQ // HKV, head_dim=D)
-    q = (torch.randn(B, HQ, 1, D, device=device, generator=g) / math.sqrt(D)).half()
-    return plan, q
+    plan = A.AttentionPlan(arenas, pages, batch=Bc, heads_kv=Hc, group=HQ // HKV, head_dim=D)
+    q = (torch.randn(Bc, Hc * (HQ // HKV), 1, D, device=device, generator=g) / math.sqrt(D)).half()
+    return (plan, q, src) if sample is not None else (plan, q)
 
 
 class ClockSampler:
@@ -222,116 +239,205 @@ def cpu_sample(seed=0):
     return pages, q
 
 
-def time_cpu(steps, warmup, threads, min_seconds=0.0):
-    """Seconds per step of the CPU path; runs at least `steps` steps and at least `min_seconds`.
-    Returns (KV tokens/s, seconds per step, steps run)."""
+CPU_PORT_SCOPE = ("the oracle port of the reference's reconstruct-then-attend path: every page dequantized with the "
+                  "reference's codecs bit for bit (C), concatenated, then fp32 torch softmax attention per GQA group; "
+                  "it leaves out the reference's per-page Python dict walk, prefetch-cache lookups, per-page .item() "
+                  "syncs and importance/resurrection bookkeeping, so the reference itself is slower")
+
+
+def time_cpu(steps, warmup, threads, min_seconds=0.0, nseq=1):
+    """Seconds per step of the CPU path over `nseq` distinct sequences per step; runs at least
+    `steps` steps and at least `min_seconds`.  Returns (KV tokens/s, seconds per step, steps run)."""
     import torch
 
     torch.set_num_threads(threads)
-    pages, q = cpu_sample()
+    samples = [cpu_sample(seed) for seed in range(nseq)]
+
+    def step():
+        for pages, q in samples:
+            cpu_reference_step(pages, q, threads)
+
     for _ in range(warmup):
-        cpu_reference_step(pages, q, threads)
+        step()
     t0 = time.perf_counter()
     n = 0
     while n < steps or time.perf_counter() - t0 < min_seconds:
-        cpu_reference_step(pages, q, threads)
+        step()
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return L / dt, dt, n
+    return nseq * L / dt, dt, n
+
+
+def cpu_baselines(min_seconds=10.0):
+    """The cpu_baseline object: the oracle port on all host threads (one sequence per step for at
+    least min_seconds) and on one thread (at least one step)."""
+    threads = os.cpu_count() or 1
+    value, dt, n = time_cpu(3, 1, threads, min_seconds=min_seconds)
+    v1, dt1, n1 = time_cpu(1, 0, 1, min_seconds=min_seconds / 2)
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"1 sequence x {HKV} KV heads x {L} tokens per step (one of the {B} sequences of a GPU's share), "
+                      f"{n} timed steps ({n * dt:.1f} s of CPU work) on {threads} threads",
+            "one_thread": {"value": v1, "unit": UNIT, "cores": 1, "steps": n1, "seconds": round(n1 * dt1, 1)},
+            "scope": CPU_PORT_SCOPE}
 
 
 def run_reference(args, rank):
+    """The reference arm: the CPU path on all host threads, rank 0 only.  Each step attends as many
+    of the workload's 8 sequences (all KV heads, full context) as keep the whole run within about
+    two and a half minutes."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    value, dt, _ = time_cpu(args.steps, args.warmup, threads)
-    sample = f"1 sequence x {HKV} KV heads x {L} tokens per step (one of the {B} sequences of the workload)"
+    _, t_seq, _ = time_cpu(1, 0, threads)
+    nseq = int(max(1, min(B, 150.0 / max(1e-3, (args.steps + args.warmup) * t_seq))))
+    value, dt, _ = time_cpu(args.steps, args.warmup, threads, nseq=nseq)
+    sample = (f"{nseq} of the {B} sequences of the workload x {HKV} KV heads x {L} tokens per step, "
+              f"{threads} host threads")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": config(f"cpu, {threads} host threads"),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "config": config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+                             "scope": CPU_PORT_SCOPE},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # ----------------------------------------------------------------------------- our arm
-def run_ours(args, rank, world, local_rank):
+def _windows(fn, steps, world, device, min_seconds=1.0, max_windows=4000):
+    """Device milliseconds per step of windows of exactly `steps` calls of fn, each window bracketed
+    by a barrier and a synchronize on both sides and timed with CUDA events on the current stream,
+    repeated until min_seconds of device time (every rank runs the same number of windows).
+    Returns the per-window times, each the max over ranks."""
     import torch
     import torch.distributed as dist
 
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    plan, q = build_cache(device, seed=1234 + rank)
     stream = torch.cuda.current_stream(device)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # device-resident timing
+    def window():
+        torch.cuda.synchronize(device)
+        barrier()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        return e0.elapsed_time(e1) / steps
+
+    first = window()
+    t = torch.tensor([first], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    n = int(min(max_windows, max(1, math.ceil(min_seconds * 1e3 / max(1e-6, float(t.item()) * steps)))))
+    ms = [first] + [window() for _ in range(n - 1)]
+    t = torch.tensor(ms, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from argus_b200 import sharding
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if HKV % world:
+        raise SystemExit(f"{HKV} KV heads do not split over {world} ranks")
+    hl = HKV // world
+    Bg = B * world  # global batch: every GPU holds B x HKV (batch, kv_head) pairs' worth of pages
+    plan, _ = build_cache(device, seed=1234 + rank, batch=Bg, heads_kv=hl)
+    gq = torch.Generator(device=device).manual_seed(99)  # the same queries on every rank
+    q_full = (torch.randn(Bg, HQ, 1, D, device=device, generator=gq) / math.sqrt(D)).half()
+    stream = torch.cuda.current_stream(device)
+    if world > 1:
+        step_api = sharding.HeadShardedDecode(plan, HKV)
+        step = lambda: step_api(q_full)  # noqa: E731
+    else:
+        step = lambda: plan.run(q_full)  # noqa: E731
+
     for _ in range(args.warmup):
-        plan.run(q)
-    torch.cuda.synchronize(device)
-    barrier()
-    torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        step()
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
     with ClockSampler(smi_index) as clk:
-        e0.record(stream)
-        for _ in range(args.steps):
-            plan.run(q)
-        e1.record(stream)
-        torch.cuda.synchronize(device)
-    barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    # end-to-end through the public API: q from pinned host memory, output back to host, every
-    # step (AttentionPlan.run_host: the copy in, the kernel and the copy out as one CUDA graph)
-    q_host = q.cpu().pin_memory()
-    o_host = torch.empty_like(q_host).pin_memory()
-    for _ in range(args.warmup):
-        plan.run_host(q_host, o_host)
-    torch.cuda.synchronize(device)
-    barrier()
-    torch.cuda.synchronize(device)
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(args.steps):
-        plan.run_host(q_host, o_host)
-    f1.record(stream)
-    torch.cuda.synchronize(device)
-    barrier()
-    e2e_ms = f0.elapsed_time(f1) / args.steps
+        wins = _windows(step, args.steps, world, device, min_seconds=args.min_seconds)
+    ms = statistics.median(wins)
+
+    # per-step breakdown at N > 1: the kernel on this rank's heads, then the all-gather (+ head-order
+    # copy), from events recorded between them in one window of K steps
+    kernel_ms, gather_ms = ms, 0.0
     if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = t.tolist()
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        for e in evs:
+            e[0].record(stream)
+            buf = step_api.local(q_full)
+            e[1].record(stream)
+            step_api.all_gather(buf)
+            step_api.to_head_order(buf, step_api._out)
+            e[2].record(stream)
+        torch.cuda.synchronize(device)
+        kg = torch.tensor([statistics.median([e[0].elapsed_time(e[1]) for e in evs]),
+                           statistics.median([e[1].elapsed_time(e[2]) for e in evs])], device=device)
+        dist.all_reduce(kg, op=dist.ReduceOp.MAX)
+        kernel_ms, gather_ms = kg.tolist()
+
+    # end-to-end through the public API: the full query batch from pinned host memory, the step,
+    # the (gathered) output back to host, every step
+    q_host = q_full.cpu().pin_memory()
+    o_host = torch.empty_like(q_host).pin_memory()
+    if world > 1:
+        q_dev = torch.empty_like(q_full)
+
+        def e2e_step():
+            q_dev.copy_(q_host, non_blocking=True)
+            o_host.copy_(step_api(q_dev), non_blocking=True)
+        e2e_path = ("HeadShardedDecode: pinned host q in, fused kernel on this rank's heads, NCCL all-gather, "
+                    "gathered output out, every step")
+    else:
+        e2e_step = lambda: plan.run_host(q_host, o_host)  # noqa: E731
+        e2e_path = "AttentionPlan.run_host: pinned host q in, fused kernel, output out, one CUDA graph per step"
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_wins = _windows(e2e_step, args.steps, world, device, min_seconds=args.min_seconds / 4)
+    e2e_ms = statistics.median(e2e_wins)
     if rank != 0:
         return
-    tokens = world * B * L
+    tokens = Bg * L
     hbm, peak_kind = peaks()
-    achieved = plan.compressed_bytes / (ms * 1e-3) / 1e9
-    launches_per_step = 1  # the split-K combine runs inside the decode kernel (last CTA per group)
+    achieved = plan.compressed_bytes / (kernel_ms * 1e-3) / 1e9
     line = {"metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": config(f"batch-sharded x{world}" if world > 1 else "single GPU"),
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic", "config": config(world),
+            "timing": {"windows": len(wins), "steps_per_window": args.steps, "statistic": "median window",
+                       "window_ms_per_step_min_max": [min(wins), max(wins)],
+                       "timed_device_seconds": round(sum(wins) * args.steps / 1e3, 3)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_kind": peak_kind, "traffic": traffic_from_profile(),
                          "algorithmic_bytes_per_launch": plan.compressed_bytes,
                          "timed": "decode kernel (split-K combine fused), CUDA events"},
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": q.numel() * 2,
-                    "d2h_bytes_per_step": q.numel() * 2,
-                    "path": "AttentionPlan.run_host: pinned host q in, fused kernel, output out, one CUDA graph per step"},
-            "gpu_launches": launches_per_step * args.steps,
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": q_full.numel() * 2,
+                    "d2h_bytes_per_step": q_full.numel() * 2, "path": e2e_path},
+            "gpu_launches": args.steps,
             "clocks": clk.summary(),
             "splits": plan.n_splits}
-    if not args.no_cpu_baseline:
-        value, dt, cpu_steps = time_cpu(3, 1, os.cpu_count() or 1, min_seconds=10.0)
-        line["cpu_baseline"] = {"value": value, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
-                                "sample": f"1 sequence x {HKV} KV heads x {L} tokens per step, {cpu_steps} timed steps "
-                                          f"({cpu_steps * dt:.1f} s of CPU work)"}
+    if world > 1:
+        line["step_breakdown_ms"] = {"kernel": kernel_ms, "all_gather_and_reorder": gather_ms,
+                                     "gather_bytes_per_rank": q_full.numel() * 2 // world,
+                                     "limiting": "kernel" if kernel_ms >= gather_ms else "all-gather"}
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baselines()
     print(json.dumps(line), flush=True)
 
 
@@ -782,6 +888,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--min-seconds", type=float, default=1.0,
+                    help="repeat the K-step timed window until this much device time has passed")
     ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b-spill", "tinyllama-sidecars",
                                            "cascade", "llama3-70b-heads"), default="llama3-8b-layer")
     args = ap.parse_args()

@@ -58,11 +58,15 @@ class _OraclePlan:
     def __init__(self, K, V):
         self.K, self.V = K, V
 
-    def run(self, q, scale=None):
+    def run(self, q, scale=None, out=None):
         import oracle
         D = q.shape[-1]
-        out = oracle.sdpa_f64(q.numpy(), self.K, self.V, 1.0 / math.sqrt(D) if scale is None else scale)
-        return torch.from_numpy(np.ascontiguousarray(out))
+        res = oracle.sdpa_f64(q.numpy(), self.K, self.V, 1.0 / math.sqrt(D) if scale is None else scale)
+        res = torch.from_numpy(np.ascontiguousarray(res))
+        if out is None:
+            return res
+        out.copy_(res)  # like AttentionPlan.run: the output lands in the caller's buffer
+        return out
 
 
 def _free_port():
@@ -84,8 +88,8 @@ def _rank_main(rank, world, port, result_path):
         q = torch.from_numpy(rng.standard_normal((B, Hkv * G, 1, D)))
         h0, h1 = sharding.head_range(Hkv, world, rank)
         step = sharding.HeadShardedDecode(_OraclePlan(K[:, h0:h1], V[:, h0:h1]), Hkv)
-        out = step(q)
-        out2 = step(q)  # the gather buffer is reused
+        out = step(q).clone()
+        out2 = step(q)  # the gather buffers are reused
         if rank == 0:
             import oracle
             ref = oracle.sdpa_f64(q.numpy(), K, V, 1.0 / math.sqrt(D))

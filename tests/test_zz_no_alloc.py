@@ -25,7 +25,7 @@ def within(out, ref):
     return np.abs(out - ref) <= ATOL + np.abs(ref) * 2.0 ** -11
 
 
-def make_plan(seed, B, Hkv, G, D, P, qlen, tiers, n_splits):
+def make_plan(seed, B, Hkv, G, D, P, qlen, tiers, n_splits, with_pages=False):
     from argus_b200 import attention as A
     rng = np.random.default_rng(seed)
     pages = U.random_pages(rng, tiers, B, Hkv, D, P)
@@ -33,7 +33,7 @@ def make_plan(seed, B, Hkv, G, D, P, qlen, tiers, n_splits):
     plan = A.AttentionPlan(arenas, plist, batch=B, heads_kv=Hkv, group=G, head_dim=D, q_len=qlen,
                            n_splits=n_splits)
     q = torch.from_numpy(rng.standard_normal((B, Hkv * G, qlen, D)).astype(np.float16)).cuda()
-    return plan, q
+    return (plan, q, pages) if with_pages else (plan, q)
 
 
 def call_noalloc(plan, q):
@@ -94,3 +94,18 @@ def test_noalloc_rejects_oversized_partials():
                                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == CAPACITY_ERROR
     assert "scratch" in L.argus_last_error().decode()
+
+
+def test_noalloc_matches_the_float64_oracle_twice():
+    """The same two calls against float64 softmax attention over the K/V the CPU oracle rebuilds from
+    the same pages (the reference's dequantization, bit for bit)."""
+    from argus_b200 import attention as A
+    runs = [make_plan(*c, with_pages=True) for c in CASES]
+    for plan, q, pages in runs:
+        out_n, _ = call_noalloc(plan, q)
+        torch.cuda.synchronize()
+        assert A.device_status() == 0
+        K, V = U.reference_kv(pages)
+        ref = U.f64_attention(q.cpu().numpy(), K, V)
+        got = out_n.cpu().numpy().astype(np.float64)
+        assert within(got, ref).all(), np.abs(got - ref).max()
