@@ -7,8 +7,14 @@
 // Work decomposition: one CTA per (split, batch*kv_head, query group of 8).  The CTA's four warps
 // each stream their own chunks of compressed tiles (<= 16 tokens each) from HBM into a private
 // two-stage shared-memory ring with cp.async.bulk (TMA bulk copies) completed on an mbarrier.
-// A warp rebuilds each staged tile in registers as the exact fp16 values the reference's
-// dequantizers produce (fp16(fp16(u*s) + min), fp16(q*s), +-s) and feeds them to mma.sync m16n8k16:
+// A warp rebuilds each staged tile in registers and feeds it to mma.sync m16n8k16.  V is rebuilt as
+// the exact fp16 values the reference's dequantizers produce (fp16(fp16(u*s) + min), fp16(q*s), +-s).
+// Scores are linear in K, so the key side keeps a per-token affine step out of the fragments and
+// applies it to the 16 x 8 score tile in fp32 instead: INT8 / FP8-sim keys enter the MMA as their
+// codes (1152 + q, exact in fp16) and the score is s * (S - 1152 * sum(q)); INT4 / INT2 keys enter as
+// fp16(u*s) (the reference's first rounding, exact) and min * sum(q) is added to the score.  The
+// scores therefore skip the reference's fp16 rounding of q*s and of fp16(u*s) + min (a relative
+// 2^-11 change per key value, inside the attention tolerance).
 //   S^T[16 tokens x 8 queries] = K[16 x D] . Q^T        (tokens on M, queries on N)
 //   O^T[D x 8 queries]        += V^T[D x 16] . P^T      (P = unnormalised softmax weights as an
 //                                                        fp16 hi + lo pair, two MMAs)
@@ -261,6 +267,8 @@ struct TokScale {
     __half2 c[2];   // -2^(10-p) * s * 2^-k   (p: mantissa bit the token's codes sit at)
     __half2 f[2];   // 2^k
     __half2 mn[2];  // min
+    // key side only: score = (S + kz * sum(q)) * kw * scale, S the MMA over the key fragments
+    float kz[2], kw[2];
 };
 
 // Fills b, c, f from s and the codes' base 2^(10-p) per half: k = 10 where s >= 64 (so the addend
@@ -302,11 +310,11 @@ __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4,
 #pragma unroll
         for (int c = 0; c < KC; ++c) {
             const uint32_t wa = ra[c] ^ 0x80808080u, wb = rb[c] ^ 0x80808080u;
-            // fp16(q * s): exact code (bias removed) times the token's scale
-            a[c][0] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7270), kMagic1152)), ts.s[0]));
-            a[c][2] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wa, kMagic1024, 0x7371), kMagic1152)), ts.s[0]));
-            a[c][1] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7270), kMagic1152)), ts.s[1]));
-            a[c][3] = h2u(__hmul2_rn(u2h(hsub2u(prmt(wb, kMagic1024, 0x7371), kMagic1152)), ts.s[1]));
+            // 1024 + (q + 128) = 1152 + q, exact; the scale and the bias are applied to the scores
+            a[c][0] = prmt(wa, kMagic1024, 0x7270);
+            a[c][2] = prmt(wa, kMagic1024, 0x7371);
+            a[c][1] = prmt(wb, kMagic1024, 0x7270);
+            a[c][3] = prmt(wb, kMagic1024, 0x7371);
         }
     } else if constexpr (TIER == ARGUS_TIER_INT4 || TIER == ARGUS_TIER_INT2) {
         // codes of token 2g at mantissa bit pA of each byte, of token 2g+1 at pB
@@ -324,10 +332,11 @@ __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4,
 #pragma unroll
         for (int c = 0; c < KC; ++c) {
             const uint32_t r8 = r[c] >> 8;  // bytes 1 and 3 moved to 0 and 2
-            a[c][0] = deq_u(lop_and_or(r[c], mA, gA), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[c][1] = deq_u(lop_and_or(r[c], mB, gB), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
-            a[c][2] = deq_u(lop_and_or(r8, mA, gA), ts.b[0], ts.c[0], ts.f[0], ts.mn[0]);
-            a[c][3] = deq_u(lop_and_or(r8, mB, gB), ts.b[1], ts.c[1], ts.f[1], ts.mn[1]);
+            // fp16(u * s) * 2^-k, one rounding (see deq_u); the min is added to the scores
+            a[c][0] = h2u(__hfma2(u2h(lop_and_or(r[c], mA, gA)), ts.b[0], ts.c[0]));
+            a[c][1] = h2u(__hfma2(u2h(lop_and_or(r[c], mB, gB)), ts.b[1], ts.c[1]));
+            a[c][2] = h2u(__hfma2(u2h(lop_and_or(r8, mA, gA)), ts.b[0], ts.c[0]));
+            a[c][3] = h2u(__hfma2(u2h(lop_and_or(r8, mB, gB)), ts.b[1], ts.c[1]));
         }
     } else {  // 1-bit: b ? +s : -s, the sign bit taken from the packed bit moved to bit 15 / 31
         uint32_t r[KC];
@@ -451,6 +460,11 @@ constexpr float kNoMax = -1.0e30f;
 #endif
 constexpr float kRescaleSlack = ARGUS_DA_RESCALE_SLACK;
 
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ __half2 load_h2(const __half* p) { return *reinterpret_cast<const __half2*>(p); }
 
 // Pointers of one staged tile.
@@ -463,10 +477,19 @@ struct TilePtr {
 
 template <int TIER>
 __device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t4, TokScale& tk, TokScale& tv) {
+    // key-side score terms (see TokScale): fp16 and 1-bit keys enter the MMA as their values
+    tk.kz[0] = tk.kz[1] = 0.f;
+    tk.kw[0] = tk.kw[1] = 1.f;
     if constexpr (TIER != ARGUS_TIER_FP16) {
         const __half2 k2 = load_h2(tp.ks + 2 * g4);
         tk.s[0] = __low2half2(k2);
         tk.s[1] = __high2half2(k2);
+        if constexpr (TIER == ARGUS_TIER_INT8 || TIER == ARGUS_TIER_FP8SIM) {
+            // codes 1152 + q: score = s * (S - 1152 * sum(q))
+            tk.kz[0] = tk.kz[1] = -1152.f;
+            tk.kw[0] = __low2float(k2);
+            tk.kw[1] = __high2float(k2);
+        }
         const uint2 v4 = *reinterpret_cast<const uint2*>(tp.vs + 4 * t4);
         tv.s[0] = u2h(prmt(v4.x, v4.y, 0x5410));
         tv.s[1] = u2h(prmt(v4.x, v4.y, 0x7632));
@@ -497,9 +520,17 @@ __device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t
                 tk.b[1] = tk.s[1]; tk.c[1] = __hmul2(tk.s[1], __hneg2(bk1)); tk.f[1] = one;
                 tv.b[0] = tv.s[0]; tv.c[0] = __hmul2(tv.s[0], __hneg2(bv0)); tv.f[0] = one;
                 tv.b[1] = tv.s[1]; tv.c[1] = __hmul2(tv.s[1], __hneg2(bv1)); tv.f[1] = one;
+                // key values fp16(u * s): score = S + min * sum(q)
+                tk.kz[0] = __low2float(m2);
+                tk.kz[1] = __high2float(m2);
             } else {
                 scale_terms(tk, 0, bk0); scale_terms(tk, 1, bk1);
                 scale_terms(tv, 0, bv0); scale_terms(tv, 1, bv1);
+                // key values fp16(u * s) * 2^-k: score = (S + min * 2^-k * sum(q)) * 2^k
+                tk.kw[0] = __low2float(tk.f[0]);
+                tk.kw[1] = __low2float(tk.f[1]);
+                tk.kz[0] = __low2float(m2) / tk.kw[0];
+                tk.kz[1] = __high2float(m2) / tk.kw[1];
             }
         }
     }
@@ -529,42 +560,50 @@ __device__ __forceinline__ void load_qfrags(uint32_t qs, int lane, uint32_t (&qf
 
 // Scores of one tile in the log2 domain: x[0..3] = (token 2g, query 2t), (2g, 2t+1), (2g+1, 2t),
 // (2g+1, 2t+1); tokens past the tile's end are -inf.
+// qsum: sums over d of queries 2t and 2t+1 (fp32), for the key-side score terms.
 template <int D, int TIER>
 __device__ __forceinline__ void tile_scores(const TilePtr& tp, int g4, int t4, const TokScale& tk,
-                                            uint32_t qs, float scale_log2, float (&x)[4]) {
+                                            uint32_t qs, float scale_log2, float2 qsum, float (&x)[4]) {
     constexpr int KC = D / 16;
     uint32_t a[KC][4];
     k_frags<D, TIER>(tp.k, g4, t4, tk, a);
     uint32_t qf[KC][2];
     load_qfrags<D>(qs, threadIdx.x & 31, qf);
-    float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+    // the first chain starts from the key-side offsets kz * sum(q) (zero for fp16 and 1-bit keys)
+    float s[4] = {tk.kz[0] * qsum.x, tk.kz[0] * qsum.y, tk.kz[1] * qsum.x, tk.kz[1] * qsum.y};
+    float s2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < KC; c += 2) {
         mma16816(s, a[c], qf[c][0], qf[c][1]);
         if (c + 1 < KC) mma16816(s2, a[c + 1], qf[c + 1][0], qf[c + 1][1]);
     }
     const bool va = 2 * g4 < tp.ntok, vb = 2 * g4 + 1 < tp.ntok;
-    x[0] = va ? (s[0] + s2[0]) * scale_log2 : -INFINITY;
-    x[1] = va ? (s[1] + s2[1]) * scale_log2 : -INFINITY;
-    x[2] = vb ? (s[2] + s2[2]) * scale_log2 : -INFINITY;
-    x[3] = vb ? (s[3] + s2[3]) * scale_log2 : -INFINITY;
+    const float w0 = tk.kw[0] * scale_log2, w1 = tk.kw[1] * scale_log2;
+    x[0] = va ? (s[0] + s2[0]) * w0 : -INFINITY;
+    x[1] = va ? (s[1] + s2[1]) * w0 : -INFINITY;
+    x[2] = vb ? (s[2] + s2[2]) * w1 : -INFINITY;
+    x[3] = vb ? (s[3] + s2[3]) * w1 : -INFINITY;
 }
 
-// O^T += V^T . P^T for one tile, P given as the two movmatrix-transposed fp16 fragments.
-template <int D, int TIER, bool PRECISE>
-__device__ __forceinline__ void tile_pv(const TilePtr& tp, int g4, int t4, const TokScale& tv, uint32_t b01,
-                                        uint32_t b23, uint32_t c01, uint32_t c23, float (&o)[D / 16][4]) {
+// V^T fragments of one tile (tokens past the tile's end zeroed: they may hold non-finite garbage).
+template <int D, int TIER>
+__device__ __forceinline__ void tile_vfrags(const TilePtr& tp, int g4, int t4, const TokScale& tv, uint32_t (&av)[D / 16][4]) {
     constexpr int KC = D / 16;
-    uint32_t av[KC][4];
     v_frags<D, TIER>(tp.v, g4, t4, tv, av);
     if (tp.ntok < 16) {
-        // tokens past the tile's end may hold non-finite garbage: zero their V values
         const int nt = tp.ntok;
         const uint32_t m01 = (4 * t4 < nt ? 0x0000FFFFu : 0u) | (4 * t4 + 2 < nt ? 0xFFFF0000u : 0u);
         const uint32_t m23 = (4 * t4 + 1 < nt ? 0x0000FFFFu : 0u) | (4 * t4 + 3 < nt ? 0xFFFF0000u : 0u);
 #pragma unroll
         for (int t = 0; t < KC; ++t) { av[t][0] &= m01; av[t][1] &= m01; av[t][2] &= m23; av[t][3] &= m23; }
     }
+}
+
+// O^T += V^T . P^T for one tile, P given as the two movmatrix-transposed fp16 fragments.
+template <int D, bool PRECISE>
+__device__ __forceinline__ void tile_pv(const uint32_t (&av)[D / 16][4], uint32_t b01, uint32_t b23, uint32_t c01,
+                                        uint32_t c23, float (&o)[D / 16][4]) {
+    constexpr int KC = D / 16;
 #pragma unroll
     for (int t = 0; t < KC; ++t) {
         mma16816(o[t], av[t], b01, b23);
@@ -595,7 +634,7 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
         }
         const float n0 = fmaxf(st.m[0], mx0), n1 = fmaxf(st.m[1], mx1);
-        const float f0 = exp2f(st.m[0] - n0), f1 = exp2f(st.m[1] - n1);  // kNoMax - finite -> 0
+        const float f0 = ex2(st.m[0] - n0), f1 = ex2(st.m[1] - n1);  // kNoMax - finite -> 0
 #pragma unroll
         for (int t = 0; t < KC; ++t) { o[t][0] *= f0; o[t][2] *= f0; o[t][1] *= f1; o[t][3] *= f1; }
         st.l[0] *= f0; st.l[1] *= f1;
@@ -604,8 +643,8 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
     const float m0 = st.m[0], m1 = st.m[1];
 #pragma unroll
     for (int i = 0; i < NT; ++i) {
-        const float p0 = exp2f(x[i][0] - m0), p1 = exp2f(x[i][1] - m1);
-        const float p2 = exp2f(x[i][2] - m0), p3 = exp2f(x[i][3] - m1);
+        const float p0 = ex2(x[i][0] - m0), p1 = ex2(x[i][1] - m1);
+        const float p2 = ex2(x[i][2] - m0), p3 = ex2(x[i][3] - m1);
         st.l[0] += p0 + p2;
         st.l[1] += p1 + p3;
         if constexpr (MASS) {
@@ -915,24 +954,28 @@ __device__ __forceinline__ OutlierTile outlier_tile(unsigned long long blk, int 
 
 // Processes one staged tile: scores, online softmax, PV (OUT: with the page's outlier corrections).
 template <int D, int TIER, bool PRECISE, bool MASS, bool OUT>
-__device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, uint32_t qs, float scale_log2,
+__device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, uint32_t qs, float scale_log2, float2 qsum,
                                              SoftmaxState& st, float (&o)[D / 16][4], float* mass_out,
                                              const OutlierTile& ot) {
     TokScale tk[1], tv[1];
     float x[1][4];
     load_tok_scales<TIER>(tp, g4, t4, tk[0], tv[0]);
-    tile_scores<D, TIER>(tp, g4, t4, tk[0], qs, scale_log2, x[0]);
+    tile_scores<D, TIER>(tp, g4, t4, tk[0], qs, scale_log2, qsum, x[0]);
     if constexpr (OUT) {
         if constexpr (side_dense(D)) dense_k_outliers<D>(ot, qs, scale_log2, tp.ntok, x[0]);
         else walk_k_outliers<D>(ot, g4, t4, qs, scale_log2, tp.ntok, x[0]);
     }
+    // the V fragments do not depend on the scores: built here, their dequantization overlaps the
+    // score MMAs' latency and the softmax's exponentials
+    uint32_t av[D / 16][4];
+    tile_vfrags<D, TIER>(tp, g4, t4, tv[0], av);
     uint32_t b01[1], b23[1], c01[1], c23[1];
     softmax_update<D / 16, 1, PRECISE, MASS>(x, st, o, b01, b23, c01, c23, mass_out);
     if constexpr (OUT) {
         if constexpr (side_dense(D)) dense_v_outliers<D, PRECISE>(ot, tp.ntok, b01[0], b23[0], c01[0], c23[0], o);
         else walk_v_outliers<D>(ot, g4, t4, tp.ntok, st, x[0], o);
     }
-    tile_pv<D, TIER, PRECISE>(tp, g4, t4, tv[0], b01[0], b23[0], c01[0], c23[0], o);
+    tile_pv<D, PRECISE>(av, b01[0], b23[0], c01[0], c23[0], o);
 }
 
 // Merges the split partials of one (batch, kv_head, query group): out = sum_s 2^(lse_s - LSE) O_s,
@@ -1000,6 +1043,7 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
     // even landed; an mbarrier parity test would then match the previous, completed phase.  Waiters
     // first see their chunk issued here, then test the parity.
     __shared__ int issued[kPairs][kStages];
+    __shared__ float qsum_s[kQ];  // sum over d of each query of the group (key-side score terms)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g4 = lane >> 2, t4 = lane & 3;
@@ -1107,6 +1151,7 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
             const int gi = n / p.qlen, qi = n - gi * p.qlen;
             qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
         }
+        float qsum = 0.f;
 #pragma unroll
         for (int c = 0; c < KC; ++c) {
             uint32_t f0 = 0u, f1 = 0u;
@@ -1115,14 +1160,21 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
                 const uint32_t q23 = *reinterpret_cast<const uint32_t*>(qrow + 4 * c + 2);
                 f0 = prmt(q01, q23, 0x5410);  // dims 4c, 4c+2
                 f1 = prmt(q01, q23, 0x7632);  // dims 4c+1, 4c+3
+                const float2 a01 = __half22float2(u2h(q01)), a23 = __half22float2(u2h(q23));
+                qsum += (a01.x + a01.y) + (a23.x + a23.y);
             }
             const int j0 = 2 * c, j1 = 2 * c + 1;
             qsw[((j0 / V) * 32 + lane) * V + j0 % V] = f0;
             qsw[((j1 / V) * 32 + lane) * V + j1 % V] = f1;
         }
+        // lanes 4n .. 4n+3 hold query n's four dim ranges
+        qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+        qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+        if (t4 == 0) qsum_s[g4] = qsum;
     }
 
     __syncthreads();  // rings initialised, first copies issued, query fragments in place
+    const float2 qsum = make_float2(qsum_s[2 * t4], qsum_s[2 * t4 + 1]);
 
     bool failed = false;
     argus_kv_chunk nch;  // descriptor of this warp's next chunk, loaded one chunk ahead
@@ -1195,7 +1247,7 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
                 tp.ntok = 16;                                                                                     \
                 OutlierTile ot;                                                                                   \
                 if constexpr (OUT) ot = outlier_tile(cblk, ck0, ck1, cv0, cv1, i, 0, 1, sbuf);                  \
-                process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, st, o,                       \
+                process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, qsum, st, o,                       \
                                                        mass_base ? mass_base + i * kQ : nullptr, ot);             \
             }                                                                                                     \
         } else {                                                                                                  \
@@ -1213,7 +1265,7 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
                 OutlierTile ot;                                                                                   \
                 if constexpr (OUT) /* whole records: tile i is page slot0 + i; else tokens tok0 + 16 i .. */    \
                     ot = outlier_tile(cblk, ck0, ck1, cv0, cv1, i, cwhole ? 0 : (ch.tok0 >> 4) + i, cnt, sbuf);   \
-                process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, st, o,                       \
+                process_tile<D, T, PRECISE, MASS, OUT>(tp, g4, t4, qs, p.scale_log2, qsum, st, o,                       \
                                                        mass_base ? mass_base + i * kQ : nullptr, ot);             \
             }                                                                                                     \
         }
