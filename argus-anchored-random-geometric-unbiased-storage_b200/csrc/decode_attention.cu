@@ -89,6 +89,7 @@ struct Params {
     float* tile_lse;  // optional [B*Hkv*NQG][n_chunks][16][8]: log2-sum-exp of each tile's scores
     int B, Hkv, G, qlen, S, nqg, n_chunks;
     float scale_log2;
+    argus_peer_gather gat;  // gat.world > 0: outputs go to every rank (argus_decode_attention_gather)
 };
 
 // Where the pieces of tile i of a staged chunk sit in shared memory (uniform across the warp).
@@ -978,12 +979,41 @@ __device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, 
     tile_pv<D, PRECISE>(av, b01[0], b23[0], c01[0], c23[0], o);
 }
 
+// Gather mode: shared memory past the merge buffers where a group's output rows are staged as fp16
+// [kQ][D] before they go to the ranks.
+template <int D>
+__device__ __forceinline__ __half* gather_stage(unsigned char* smem) {
+    return reinterpret_cast<__half*>(smem + (size_t)kPairs * kStages * stage_bytes(D) - (size_t)kQ * D * 2);
+}
+
+// Gather mode: copies the staged rows of group (b, h, qg) into every rank's output buffer at their
+// rows of the full layout (16-byte stores, peers through their IPC mappings).  No fence here: the
+// arrival signal comes from gather_signal_wait_kernel, queued after this kernel on the same stream.
+template <int D>
+__device__ __forceinline__ void gather_rows(const Params& p, int b, int h, int qg, const __half* ost) {
+    constexpr int V = D / 8;  // 16-byte vectors per row
+    const int NQ = p.G * p.qlen;
+    const int hg = p.gat.rank * p.Hkv + h;
+    const int64_t half_elems = (int64_t)p.B * p.gat.heads_kv_total * p.G * p.qlen * D;
+    for (int e = threadIdx.x; e < p.gat.world * kQ * V; e += kThreads) {
+        const int r = e / (kQ * V), rem = e - r * (kQ * V);
+        const int n = rem / V, v = rem - n * V;
+        const int ng = qg * kQ + n;
+        if (ng >= NQ) continue;
+        const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
+        const int64_t row = (((int64_t)b * p.gat.heads_kv_total + hg) * p.G + gi) * p.qlen + qi;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.gat.out[r]) + p.gat.parity * half_elems + row * D);
+        dst[v] = reinterpret_cast<const uint4*>(ost + n * D)[v];
+    }
+}
+
 // Merges the split partials of one (batch, kv_head, query group): out = sum_s 2^(lse_s - LSE) O_s,
 // LSE = log2 sum_s 2^lse_s.  Run by the group's last CTA to finish (all its threads); the other
 // CTAs' partials are read through L2.  The per-(split, query) weights are formed once in shared
 // memory (wbuf: S*8 + 16 floats), then every output element sums its S partials eight at a time.
 template <int D>
-__device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int b, int h, int qg, float* wbuf) {
+__device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int b, int h, int qg, float* wbuf,
+                                              __half* ost) {
     const int NQ = p.G * p.qlen, S = p.S;
     float* Ms = wbuf;           // [kQ] max lse per query
     float* Ws = wbuf + kQ;      // [kQ] sum of weights per query
@@ -1024,8 +1054,14 @@ __device__ __forceinline__ void combine_group(const Params& p, int64_t grp, int 
         const float W = Ws[n], M = Ms[n];
         const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
         const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
-        p.out[row * D + d] = __float2half_rn(W > 0.f ? sum / W : 0.f);
+        const __half val = __float2half_rn(W > 0.f ? sum / W : 0.f);
+        if (p.gat.world > 0) ost[n * D + d] = val;
+        else p.out[row * D + d] = val;
         if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
+    }
+    if (p.gat.world > 0) {
+        __syncthreads();
+        gather_rows<D>(p, b, h, qg, ost);
     }
 }
 
@@ -1148,8 +1184,11 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
         const bool live = n < NQ;
         const __half* qrow = p.q;
         if (live) {
+            // gather mode reads the full query [B][H_q total][q_len][D]: this rank's heads start at rank * Hkv
             const int gi = n / p.qlen, qi = n - gi * p.qlen;
-            qrow = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
+            const int hq = p.gat.world > 0 ? p.gat.heads_kv_total : p.Hkv;
+            const int hh = p.gat.world > 0 ? p.gat.rank * p.Hkv + h : h;
+            qrow = p.q + (((int64_t)b * hq * p.G + (int64_t)hh * p.G + gi) * p.qlen + qi) * D + t4 * (D / 4);
         }
         float qsum = 0.f;
 #pragma unroll
@@ -1357,7 +1396,9 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
             if (ng < NQ) {
                 const int gi = ng / p.qlen, qi = ng - gi * p.qlen;
                 const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
-                p.out[row * D + d] = __float2half_rn(L > 0.f ? acc / L : 0.f);
+                const __half val = __float2half_rn(L > 0.f ? acc / L : 0.f);
+                if (p.gat.world > 0) gather_stage<D>(smem)[n * D + d] = val;
+                else p.out[row * D + d] = val;
                 if (p.lse && d == 0) p.lse[row] = (L > 0.f) ? (M + log2f(L)) * 0.69314718055994530942f : -INFINITY;
             }
         } else {
@@ -1365,6 +1406,10 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
             po[d] = L > 0.f ? acc / L : 0.f;
             if (d == 0) p.part_lse[(grp * p.S + split) * kQ + n] = (L > 0.f) ? M + log2f(L) : -INFINITY;
         }
+    }
+    if (p.S == 1 && p.gat.world > 0) {
+        __syncthreads();
+        gather_rows<D>(p, b, h, qg, gather_stage<D>(smem));
     }
     if (p.S > 1) {
         // the group's last CTA to arrive merges the splits (and resets the counter for the next launch)
@@ -1379,7 +1424,7 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
         __syncthreads();
         if (last) {
             __threadfence();
-            combine_group<D>(p, grp, b, h, qg, reinterpret_cast<float*>(smem));
+            combine_group<D>(p, grp, b, h, qg, reinterpret_cast<float*>(smem), gather_stage<D>(smem));
         }
     }
 }
@@ -1403,14 +1448,37 @@ __global__ void wait_timeout_selftest_kernel(long long polls) {
     }
 }
 
+// One thread signals every rank, then waits (bounded, ~0.25 us between polls) until this rank's
+// arrival counter reaches target.  The attention kernel before it on the stream stored this rank's
+// rows into every rank's buffer: stream order puts those stores before the system-scope fence and
+// the release adds here, so a rank whose acquire load sees every signal of a step also sees every
+// row of it, and so do the kernels queued after this one.
+__global__ void gather_signal_wait_kernel(argus_peer_gather g, unsigned long long target, long long polls) {
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    for (int r = 0; r < g.world; ++r)
+        asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(g.arrivals[r]), "l"(1ull) : "memory");
+    const unsigned long long* arrivals = static_cast<const unsigned long long*>(g.arrivals[g.rank]);
+    for (long long i = 0;; ++i) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(arrivals) : "memory");
+        if (v >= target) return;
+        if (i >= polls) {
+            atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
+            return;
+        }
+        __nanosleep(256);
+    }
+}
+
 template <int D>
 int launch(const Params& prm, int n_splits, bool precise, cudaStream_t st) {
     bool side = false;
     for (int i = 0; i < ARGUS_MAX_ARENAS; ++i) side |= prm.arenas[i].outlier_dir != nullptr;
     // kernels with outlier sidecars also hold one correction buffer per warp
     const size_t smem = (size_t)kPairs * kStages * stage_bytes(D) + stage_slack(D) + (side ? kWarps * side_warp_bytes(D) : 0);
-    static_assert((size_t)kWarps * kQ * (D + 2) * 4 <= (size_t)kPairs * kStages * stage_bytes(D),
-                  "merge buffer must fit in the stage memory");
+    static_assert((size_t)kWarps * kQ * (D + 2) * 4 + (size_t)kQ * D * 2 <= (size_t)kPairs * kStages * stage_bytes(D),
+                  "merge buffer and gather staging must fit in the stage memory");
     const bool mass = prm.tile_lse != nullptr;
     auto kern = side ? (precise ? (mass ? decode_attn_kernel<D, true, true, true> : decode_attn_kernel<D, true, false, true>)
                                 : (mass ? decode_attn_kernel<D, false, true, true> : decode_attn_kernel<D, false, false, true>))
@@ -1560,6 +1628,86 @@ int argus_decode_attention(const argus_attn_shape* s, const argus_kv_arena* aren
     const int rc = prepare_attention(s, arenas, chunks, split_chunk0, q, out, lse, tile_lse, prm);
     if (rc != ARGUS_OK) return rc;
     return launch_prepared(s, prm, workspace, stream);
+}
+
+int64_t argus_gather_arrivals_per_step(int world) { return world > 0 ? world : 0; }
+
+int argus_decode_attention_gather(const argus_attn_shape* s, const argus_kv_arena* arenas, const argus_kv_chunk* chunks,
+                                  const int32_t* split_chunk0, const uint16_t* q, const argus_peer_gather* g, float* lse,
+                                  float* tile_lse, void* workspace, argus_stream_t stream) {
+    if (!s || !g) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    if (g->world < 1 || g->world > ARGUS_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "world / rank out of range");
+    if ((int64_t)g->heads_kv_total != (int64_t)s->heads_kv * g->world)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "heads_kv_total must be heads_kv * world");
+    if (g->parity != 0 && g->parity != 1) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "parity must be 0 or 1");
+    for (int r = 0; r < g->world; ++r) {
+        if (!g->out[r] || !g->arrivals[r]) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null peer buffer");
+        if (!argus_aligned(g->out[r], 16) || !argus_aligned(g->arrivals[r], 8))
+            return argus_set_error(ARGUS_ERR_MISALIGNED, "peer output 16-byte / counter 8-byte alignment");
+    }
+    const int D = s->head_dim;
+    if (valid_head_dim(D) && (int64_t)(s->n_splits + 2) * da::kQ * 4 + (int64_t)da::kQ * D * 2 >
+                                 (int64_t)da::kPairs * da::kStages * da::stage_bytes(D))
+        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "too many splits for the split merge with gather staging");
+    da::Params prm;
+    // the local half of this rank's own buffer stands in for `out` in the common checks
+    const int rc = prepare_attention(s, arenas, chunks, split_chunk0, q, static_cast<uint16_t*>(g->out[g->rank]), lse,
+                                     tile_lse, prm);
+    if (rc != ARGUS_OK) return rc;
+    prm.gat = *g;
+    return launch_prepared(s, prm, workspace, stream);
+}
+
+int argus_gather_wait(const argus_peer_gather* g, uint64_t target, int64_t max_polls, argus_stream_t stream) {
+    if (!g || g->world < 1 || g->world > ARGUS_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad gather spec");
+    for (int r = 0; r < g->world; ++r)
+        if (!g->arrivals[r] || !argus_aligned(g->arrivals[r], 8))
+            return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad arrival counter");
+    if (max_polls <= 0) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "max_polls must be positive");
+    da::gather_signal_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*g, (unsigned long long)target,
+                                                                     (long long)max_polls);
+    ARGUS_CHECK_LAUNCH();
+    return ARGUS_OK;
+}
+
+int argus_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle) {
+    if (bytes <= 0 || !ptr || !ipc_handle) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad argument");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+    if (e != cudaSuccess) return argus_set_cuda_error(e);
+    e = cudaMemset(p, 0, (size_t)bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return argus_set_cuda_error(e);
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+    memcpy(ipc_handle, &h, sizeof(h));
+    *ptr = p;
+    return ARGUS_OK;
+}
+
+int argus_peer_open(const void* ipc_handle, void** ptr) {
+    if (!ipc_handle || !ptr) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? ARGUS_OK : argus_set_cuda_error(e);
+}
+
+int argus_peer_close(void* ptr) {
+    if (!ptr) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? ARGUS_OK : argus_set_cuda_error(e);
+}
+
+int argus_peer_free(void* ptr) {
+    if (!ptr) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
+    const cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? ARGUS_OK : argus_set_cuda_error(e);
 }
 
 int argus_selftest_wait_timeout(int64_t polls, int* gave_up, argus_stream_t stream) {

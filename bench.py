@@ -9,10 +9,13 @@ tier codecs; queries N(0,1)/sqrt(128); softmax scale 1/sqrt(128).  The compresse
 
 Multi-GPU: one process per GPU (torchrun), the layer sharded by KV head.  The batch grows with the
 ranks (8 x N sequences) and rank r holds KV heads [8r/N, 8(r+1)/N) of every sequence and page, so
-each GPU streams the same 280.8 MB per step ("weak" scaling); a step is the fused kernel on the
-rank's heads plus one NCCL all-gather of the per-head outputs into [8N, 32, 1, 128]
-(sharding.HeadShardedDecode).  `value` is the whole-job KV tokens/s (8N x 32768 / max-over-ranks
-step time).  At N = 1 there is nothing to gather and the step is the kernel alone.
+each GPU streams the same 280.8 MB per step ("weak" scaling); a step is the attention over the
+rank's heads with the all-gather of the per-head outputs into [8N, 32, 1, 128] fused in
+(sharding.FusedHeadShardedDecode: the kernel writes its output rows straight into every rank's
+output buffer in peer memory, and a one-thread wait kernel completes the step).  The NCCL path
+(kernel, all_gather_into_tensor, head-order copy; sharding.HeadShardedDecode) is timed beside it.
+`value` is the whole-job KV tokens/s (8N x 32768 / max-over-ranks step time).  At N = 1 there is
+nothing to gather and the step is the kernel alone.
 
 Timing: W untimed steps, then windows of exactly K steps (CUDA events on the launching stream,
 barrier + synchronize around each) repeated until at least one second of device time has passed,
@@ -360,8 +363,11 @@ def run_ours(args, rank, world, local_rank):
     q_full = (torch.randn(Bg, HQ, 1, D, device=device, generator=gq) / math.sqrt(D)).half()
     stream = torch.cuda.current_stream(device)
     if world > 1:
+        # the product path: the all-gather runs inside the attention kernel (peer stores + arrival
+        # counters); the NCCL path is timed beside it for comparison
+        fused = sharding.FusedHeadShardedDecode(plan, HKV)
+        step = lambda: fused(q_full)  # noqa: E731
         step_api = sharding.HeadShardedDecode(plan, HKV)
-        step = lambda: step_api(q_full)  # noqa: E731
     else:
         step = lambda: plan.run(q_full)  # noqa: E731
 
@@ -373,25 +379,33 @@ def run_ours(args, rank, world, local_rank):
         wins = _windows(step, args.steps, world, device, min_seconds=args.min_seconds)
     ms = statistics.median(wins)
 
-    # per-step breakdown at N > 1: the kernel on this rank's heads, then the all-gather (+ head-order
-    # copy), from events recorded between them in one window of K steps
-    kernel_ms, gather_ms = ms, 0.0
+    # per-step breakdown at N > 1: the plain kernel on this rank's heads (no gather) for the roofline,
+    # the fused step's wait for the peers' rows, and the NCCL path (kernel, then all-gather and
+    # head-order copy) for comparison, each from events in one window of K steps
+    kernel_ms, gather_ms, nccl = ms, 0.0, None
     if world > 1:
+        q_local = sharding.shard_queries(q_full, HKV, world, rank)
+        kernel_ms = statistics.median(_windows(lambda: plan.run(q_local), args.steps, world, device,
+                                               min_seconds=0.2))
         evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
         torch.cuda.synchronize(device)
         dist.barrier()
         for e in evs:
             e[0].record(stream)
-            buf = step_api.local(q_full)
+            fused.local(q_full)
             e[1].record(stream)
-            step_api.all_gather(buf)
-            step_api.to_head_order(buf, step_api._out)
+            fused.wait()
             e[2].record(stream)
         torch.cuda.synchronize(device)
+        for _ in range(args.warmup):
+            step_api(q_full)
+        nccl_ms = statistics.median(_windows(lambda: step_api(q_full), args.steps, world, device, min_seconds=0.2))
         kg = torch.tensor([statistics.median([e[0].elapsed_time(e[1]) for e in evs]),
-                           statistics.median([e[1].elapsed_time(e[2]) for e in evs])], device=device)
+                           statistics.median([e[1].elapsed_time(e[2]) for e in evs]), nccl_ms], device=device)
         dist.all_reduce(kg, op=dist.ReduceOp.MAX)
-        kernel_ms, gather_ms = kg.tolist()
+        fused_kernel_ms, gather_ms, nccl_ms = kg.tolist()
+        nccl = {"ms_per_step": nccl_ms, "value": Bg * L / (nccl_ms * 1e-3),
+                "path": "HeadShardedDecode: kernel, NCCL all_gather_into_tensor in place, head-order copy"}
 
     # end-to-end through the public API: the full query batch from pinned host memory, the step,
     # the (gathered) output back to host, every step
@@ -402,9 +416,9 @@ def run_ours(args, rank, world, local_rank):
 
         def e2e_step():
             q_dev.copy_(q_host, non_blocking=True)
-            o_host.copy_(step_api(q_dev), non_blocking=True)
-        e2e_path = ("HeadShardedDecode: pinned host q in, fused kernel on this rank's heads, NCCL all-gather, "
-                    "gathered output out, every step")
+            o_host.copy_(fused(q_dev), non_blocking=True)
+        e2e_path = ("FusedHeadShardedDecode: pinned host q in, attention with the all-gather fused in (peer "
+                    "stores), gathered output out, every step")
     else:
         e2e_step = lambda: plan.run_host(q_host, o_host)  # noqa: E731
         e2e_path = "AttentionPlan.run_host: pinned host q in, fused kernel, output out, one CUDA graph per step"
@@ -412,6 +426,8 @@ def run_ours(args, rank, world, local_rank):
         e2e_step()
     e2e_wins = _windows(e2e_step, args.steps, world, device, min_seconds=args.min_seconds / 4)
     e2e_ms = statistics.median(e2e_wins)
+    if world > 1:
+        fused.close()  # every rank: unmaps the peers' buffers (barriers inside)
     if rank != 0:
         return
     tokens = Bg * L
@@ -433,9 +449,11 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "splits": plan.n_splits}
     if world > 1:
-        line["step_breakdown_ms"] = {"kernel": kernel_ms, "all_gather_and_reorder": gather_ms,
+        line["step_breakdown_ms"] = {"kernel_alone": kernel_ms, "fused_kernel": fused_kernel_ms,
+                                     "wait_for_peers": gather_ms,
                                      "gather_bytes_per_rank": q_full.numel() * 2 // world,
-                                     "limiting": "kernel" if kernel_ms >= gather_ms else "all-gather"}
+                                     "limiting": "kernel" if kernel_ms >= 0.5 * ms else "gather"}
+        line["nccl_all_gather_path"] = nccl
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baselines()
     print(json.dumps(line), flush=True)

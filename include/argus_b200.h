@@ -370,6 +370,54 @@ int argus_decode_attention_noalloc(const argus_attn_shape* shape, const argus_kv
 /* Bytes of the built-in scratch of argus_decode_attention_noalloc. */
 int64_t argus_decode_attention_noalloc_capacity(void);
 
+/* ---- KV-head-sharded decode with the output all-gather fused into the attention kernel ----
+ * Rank r of `world` GPUs (one process each) holds KV heads [r*Hl, (r+1)*Hl) of every page
+ * (Hl = shape.heads_kv; the reference lays a page out as one [B, H_kv, P, D] block per tier,
+ * core/memory_manager.py:333-379, so every rank keeps the same page table).  The kernel that
+ * finishes a (batch, kv_head, query group) writes its output rows straight into every rank's output
+ * buffer at their place in the full [B][H_q total][q_len][D] layout (plain 16-byte stores to peer
+ * memory mapped with CUDA IPC); argus_gather_wait, queued after it on the same stream, then adds one
+ * to every rank's arrival counter (after a system-scope fence, with release semantics) and holds the
+ * stream until every rank has signalled the step.  This replaces the local attention + NCCL
+ * all-gather + head-order copy of a head-sharded step; the reference has no multi-GPU path. */
+#define ARGUS_MAX_PEERS 8
+typedef struct argus_peer_gather {
+    int32_t world;                   /* ranks, 1 .. ARGUS_MAX_PEERS */
+    int32_t rank;                    /* this rank */
+    int32_t heads_kv_total;          /* H_kv of the whole layer: shape.heads_kv * world */
+    int32_t parity;                  /* half of every rank's output pair this step writes: 0 or 1 */
+    void* out[ARGUS_MAX_PEERS];      /* per rank, mapped in this process: fp16 [2][B][H_q total][q_len][D] */
+    void* arrivals[ARGUS_MAX_PEERS]; /* per rank, mapped in this process: one uint64 arrival counter */
+} argus_peer_gather;
+
+/* argus_decode_attention for rank g->rank of a head-sharded layer, the output going to every rank
+ * (see above) instead of a local `out`.  q is the full query [B][H_q total][q_len][D] (the same on
+ * every rank; this rank reads its own heads' rows); lse, tile_lse and workspace stay local (this
+ * rank's heads).
+ * Follow each call with argus_gather_wait on the same stream.  Consecutive steps alternate `parity`,
+ * so a rank one step ahead never overwrites rows its peers may still be reading.  The caller keeps
+ * every rank's calls in the same order. */
+int argus_decode_attention_gather(const argus_attn_shape* shape, const argus_kv_arena* arenas,
+                                  const argus_kv_chunk* chunks, const int32_t* split_chunk0, const uint16_t* q,
+                                  const argus_peer_gather* g, float* lse, float* tile_lse, void* workspace,
+                                  argus_stream_t stream);
+/* Arrivals every rank's counter receives per step (one signal from each rank): world. */
+int64_t argus_gather_arrivals_per_step(int world);
+/* Queues a one-thread kernel on `stream` that signals every rank of g (the step's rows of this rank
+ * are stored) and then waits until this rank's counter reaches `target` (steps so far times
+ * argus_gather_arrivals_per_step), polling at most max_polls times about 0.25 us apart; on timeout
+ * it records ARGUS_ERR_TIMEOUT in the status word read by argus_device_status and returns. */
+int argus_gather_wait(const argus_peer_gather* g, uint64_t target, int64_t max_polls, argus_stream_t stream);
+/* Device memory another process can map: `bytes` zero-filled bytes (cudaMalloc) and their 64-byte
+ * CUDA IPC handle in ipc_handle. */
+int argus_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+/* Maps a peer's argus_peer_alloc memory into this process (peer access enabled lazily). */
+int argus_peer_open(const void* ipc_handle, void** ptr);
+/* Unmaps memory mapped by argus_peer_open. */
+int argus_peer_close(void* ptr);
+/* Frees memory from argus_peer_alloc (after every peer has closed its mapping). */
+int argus_peer_free(void* ptr);
+
 /* Self-test of the quantizers' fast exact quotient: for every finite fp16 x and positive finite
  * fp16 s, the quotient computed from the correctly rounded reciprocal of s with one FMA correction
  * is compared with the IEEE-rounded fp32 divide (equal values; a zero quotient may differ in sign,

@@ -24,10 +24,11 @@ def test_library_exports_header_symbols():
 
 
 def test_python_binding_covers_header():
-    from argus_b200 import _lib, attention, paged
+    from argus_b200 import _lib, attention, paged, sharding
     from argus_b200.core import jl
     declared = set(declared_symbols())
     bound = (set(_lib.SIGNATURES) | set(attention.BOUND_SYMBOLS) | set(paged.BOUND_SYMBOLS) | set(jl.BOUND_SYMBOLS)
+             | set(sharding.BOUND_SYMBOLS)
              | {"argus_status_string", "argus_last_error", "argus_version"})
     assert declared <= bound, sorted(declared - bound)
 
