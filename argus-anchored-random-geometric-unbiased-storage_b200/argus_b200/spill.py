@@ -80,9 +80,12 @@ class StreamedArenaAttention:
     fp32.  The reference instead moves every spilled tensor back synchronously before attending
     (core/memory_manager.py:1163, 1686-1713)."""
 
-    def __init__(self, host_arena: KVArena, *, group, chunk_slots=256, n_slots=None, device="cuda"):
-        if host_arena.k.is_cuda or not host_arena.k.is_pinned():
-            raise ValueError("the arena must live in pinned host memory")
+    def __init__(self, host_arena: KVArena, *, group, chunk_slots=256, n_slots=None, device="cuda", n_splits=None):
+        """host_arena: the spilled arena, in pinned host memory (a device arena is accepted too: the
+        runs are then copied device to device, which computes the same result from resident memory).
+        n_splits: split-K partitions of every run's launch (default: the plan's own choice)."""
+        if not host_arena.k.is_cuda and not host_arena.k.is_pinned():
+            raise ValueError("a host arena must live in pinned memory")
         from .attention import LAYOUT_RECORD
         if host_arena.layout != LAYOUT_RECORD:
             raise ValueError("only record arenas stream")
@@ -97,6 +100,7 @@ class StreamedArenaAttention:
                                record_bytes=a.record_bytes, page_tokens=a.page_tokens, head_dim=a.D, batch=a.B,
                                heads=a.H, slots=self.chunk) for b in self.bufs]
         self._plans = {}
+        self.n_splits = n_splits
         self.copied = [torch.cuda.Event() for _ in range(2)]
         self.released = [torch.cuda.Event() for _ in range(2)]
         # the staging buffers were allocated on the current stream (whose earlier work may still use
@@ -110,7 +114,8 @@ class StreamedArenaAttention:
         if key not in self._plans:
             a = self.h
             self._plans[key] = AttentionPlan([self.arenas[buf]], [(0, j, a.page_tokens) for j in range(ns)], batch=a.B,
-                                             heads_kv=a.H, group=self.G, head_dim=a.D, q_len=q_len)
+                                             heads_kv=a.H, group=self.G, head_dim=a.D, q_len=q_len,
+                                             n_splits=self.n_splits)
         return self._plans[key]
 
     def _copy(self, run, s0, ns, stream):
@@ -149,3 +154,51 @@ class StreamedArenaAttention:
                 self._copy(i + 2, *runs[i + 2], copy)
                 self.copied[i % 2].record(copy)
         return acc_o.to(torch.float16), acc_lse
+
+
+class SpilledLayerDecode:
+    """Decode attention over a layer whose oldest tier lives in pinned host memory: the resident
+    tiers in one fused launch (with their log-sum-exp), the spilled arena streamed in runs on a side
+    stream while the resident launch runs (StreamedArenaAttention), the two results joined by LSE.
+    The reference instead swaps the whole spilled cache back before attending
+    (core/memory_manager.py:1163, 1345, 1686-1713).
+
+    resident_plan: AttentionPlan over the resident arenas; spilled: the spilled record arena (pinned
+    host, or a device arena for a resident run of the same computation)."""
+
+    def __init__(self, resident_plan, spilled, *, chunk_slots=512, n_splits=None):
+        self.plan = resident_plan
+        self.stream = StreamedArenaAttention(spilled, group=resident_plan.G, chunk_slots=chunk_slots,
+                                             device=resident_plan.device, n_splits=n_splits)
+        self._lse = None
+
+    def __call__(self, q, scale=None, out=None):
+        from .core import jl
+        shape = q.shape[:3]
+        if self._lse is None or tuple(self._lse.shape) != tuple(shape) or self._lse.device != q.device:
+            self._lse = torch.empty(shape, dtype=torch.float32, device=q.device)
+        o_r = self.plan.run(q, scale=scale, lse=self._lse)
+        o_s, l_s = self.stream.run(q, scale=scale)
+        return jl.merge_attention(o_r, self._lse, o_s, l_s, out=out)
+
+
+def numa_local_cpus(device):
+    """CPU ids close to the GPU (NVML's CPU affinity of the device; a read-only query), or None when
+    unknown.  A process pinned to them allocates its pinned host buffers on the GPU's NUMA node
+    (first touch)."""
+    import os
+    try:
+        import pynvml
+        idx = torch.device(device).index or 0
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        phys = int(vis.split(",")[idx]) if vis else idx
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+        return cpus & set(range(os.cpu_count())) or None
+    except Exception:
+        return None

@@ -23,22 +23,23 @@ so the clock sampler sees the kernel under load; the reported step time is the m
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Two further single-GPU workloads (not the headline line) are measured by the same script:
+Further workloads (not the headline line) are measured by the same script:
 
     python bench.py --workload jl-archive          # attention over the JL archive: B 4, H_q 32,
                                                    # H_kv 8, D 128, 64 blocks of 1024 tokens -> 128 rows
-    python bench.py --workload llama3-70b-spill    # Llama-3-70B layer on one GPU: B 64, H_q 64, H_kv 8,
-                                                   # context 131072 (the 8B tier ratios x4); the 1-bit
-                                                   # tier (oldest 25%) in pinned host memory, streamed
+    torchrun --nproc-per-node N bench.py --workload llama3-70b --gpus N   (or N = 1 without torchrun)
+                                                   # Llama-3-70B layer: B 64, H_q 64, H_kv 8, context
+                                                   # 131072 (the 8B tier ratios x4), KV-head sharded over
+                                                   # N GPUs; each rank's 1-bit share (oldest 25%) in
+                                                   # pinned host memory, streamed under the resident tiers
     python bench.py --workload tinyllama-sidecars  # TinyLlama-shaped layer: H_q 32, H_kv 4, D 64, 4096
                                                    # tokens, 3840 in INT8 pages with outlier sidecars
     python bench.py --workload cascade             # pack/unpack of every tier, 1M tokens x 8 heads x 128
-    torchrun --nproc-per-node N bench.py --workload llama3-70b-heads --gpus N
-                                                   # the 70B layer sharded by KV head over N GPUs
 
 --impl reference times the CPU restatement of the reference's path (dequantize every page, then
 softmax attention over the reconstructed K/V; argus_cache core/memory_manager.py:1157-1315 +
-1424-1430) on the host cores, on a bounded sample (one sequence, all KV heads, full context).
+1424-1430) on the host cores, on a bounded sample (as many of the sequences as fit about 2.5 minutes, all KV
+heads, full context).
 """
 import argparse
 import json
@@ -544,55 +545,6 @@ def _jl_cpu(R, yk, yv, q, G, min_seconds=10.0):
                       f"({dt:.1f} s)"}
 
 
-def run_70b_spill(args):
-    import torch
-
-    from argus_b200 import attention as A
-    from argus_b200 import spill
-    from argus_b200.core import jl
-
-    global B, HQ, L, SPLIT
-    B, HQ, L = 64, 64, 131072
-    SPLIT = [(t, 4 * n) for t, n in SPLIT]
-    dev = torch.device("cuda", 0)
-    plan_all, q = build_cache(dev, seed=77)
-    res = plan_all.arenas[1:]  # SPLIT starts with the 1-bit tier: it is the spilled one
-    plan_res = A.AttentionPlan(res, [(ai, j, P) for ai, a in enumerate(res) for j in range(a.slots)], batch=B,
-                               heads_kv=HKV, group=HQ // HKV, head_dim=D)
-    host = spill.arenas_to_host([plan_all.arenas[0]])[0]
-    st = spill.StreamedArenaAttention(host, group=HQ // HKV, chunk_slots=512)
-    lse_r = torch.empty(B, HQ, 1, device=dev)
-    def layer():
-        o_r = plan_res.run(q, lse=lse_r)
-        o_s, l_s = st.run(q)
-        return jl.merge_attention(o_r, lse_r, o_s, l_s)
-
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    with ClockSampler(vis.split(",")[0] if vis else "0") as clk:
-        ms_resident_all = _timed(lambda: plan_all.run(q), args.steps, args.warmup)
-        ms_res = _timed(lambda: plan_res.run(q, lse=lse_r), args.steps, args.warmup)
-        ms = _timed(layer, max(3, args.steps // 10), 2)
-    hbm, peak_kind = peaks()
-    spilled = host.k.numel()
-    extra = {"clocks": clk.summary()}
-    if not args.no_cpu_baseline:
-        value, dt, cpu_steps = time_cpu(1, 0, os.cpu_count() or 1, min_seconds=10.0)
-        extra["cpu_baseline"] = {"value": value, "unit": "KV tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
-                                 "sample": f"1 sequence x {HKV} KV heads x {L} tokens per step (every tier resident), "
-                                           f"{cpu_steps} timed steps ({cpu_steps * dt:.1f} s of CPU work)"}
-    print(json.dumps({"metric": "Llama-3-70B layer decode with the 1-bit tier spilled to host, KV tokens/s",
-                      "value": B * L / (ms * 1e-3), "unit": "KV tokens/s", "n_gpus": 1, "ms_per_step": ms,
-                      "higher_is_better": True, "dtype": "fp16", "data": "synthetic",
-                      "config": {"workload": "llama3-70b-spill", "batch": B, "q_heads": HQ, "kv_heads": HKV,
-                                 "head_dim": D, "context": L, "tiers_oldest_first": dict(SPLIT),
-                                 "spilled": "one_bit (pinned host, streamed in runs of 512 slots)"},
-                      "all_resident": {"ms": ms_resident_all, "GB/s": plan_all.compressed_bytes / ms_resident_all / 1e6,
-                                       "frac_of_hbm": plan_all.compressed_bytes / ms_resident_all / 1e6 / hbm,
-                                       "peak_kind": peak_kind},
-                      "resident_tiers_ms": ms_res,
-                      "host_link": {"spilled_bytes": spilled, "GB/s": spilled / ms / 1e6}, **extra}), flush=True)
-
-
 def _tinyllama_pages(device, seed=0):
     """The TinyLlama-shaped layer: B 1, H_kv 4, D 64, 4096 tokens of N(0,1) K/V with 4 outlier
     channels per head scaled x8; the oldest 3840 tokens as 240 INT8 pages of 16 tokens whose
@@ -747,72 +699,93 @@ def _tinyllama_cpu(k, v, q, Pt, HQt, min_seconds=10.0):
                       f"({n * dt:.1f} s of CPU work)"}
 
 
-def run_70b_heads(args, rank, world, local_rank):
-    """Llama-3-70B layer sharded by KV head (strong scaling): B 64, H_q 64, H_kv 8, D 128, context
-    131072 with the 8B tier ratios x4 (8.98 GB compressed per layer), every tier resident; rank r of
-    N holds KV heads [8r/N, 8(r+1)/N) of every page and their query heads, runs the fused kernel on
-    them and all-gathers the per-head outputs over NCCL (sharding.HeadShardedDecode).  Value = the
-    layer's KV tokens (B x L) / the max-over-ranks step time."""
+def run_70b(args, rank, world, local_rank):
+    """Llama-3-70B layer: B 64, H_q 64, H_kv 8, D 128, context 131072 with the 8B tier ratios x4
+    (8.98 GB compressed).  Sharded by KV head over the ranks (rank r holds heads [8r/N, 8(r+1)/N) of
+    every page: the layer's bytes split N ways, "strong" scaling).  Each rank's share of the oldest
+    25% of the pages (its slice of the 1-bit tier) lives in pinned host memory allocated from a
+    thread pinned to the GPU's NUMA node, and is streamed in runs of 512 slots on a side stream while
+    the resident tiers are attended (spill.SpilledLayerDecode); the two results are joined by LSE and
+    the per-head outputs all-gathered (NCCL).  value = B x L / max-over-ranks step time; also the
+    resident tiers' kernel against the HBM roof and the host link's GB/s per rank."""
     import torch
     import torch.distributed as dist
 
     from argus_b200 import attention as A
-    from argus_b200 import sharding
+    from argus_b200 import sharding, spill
 
-    global B, HQ, HKV, L, SPLIT
+    global B, HQ, L, SPLIT
     B, HQ, L = 64, 64, 131072
-    n_kv = HKV
     SPLIT = [(t, 4 * n) for t, n in SPLIT]
-    if n_kv % world:
-        raise SystemExit(f"{n_kv} KV heads do not split over {world} ranks")
-    HKV = n_kv // world  # this rank's heads (the cache is built for them only)
-    HQ = HQ // world
+    if HKV % world:
+        raise SystemExit(f"{HKV} KV heads do not split over {world} ranks")
+    hl = HKV // world
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    plan, q_local = build_cache(device, seed=4242 + rank)
-    HKV, HQ = n_kv, HQ * world
-    q_full = torch.empty(B, HQ, 1, D, dtype=torch.float16, device=device)
-    q_full.view(B, world, HQ // world, 1, D)[:, rank].copy_(q_local)
+    cpus = spill.numa_local_cpus(device)
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    plan_all, _ = build_cache(device, seed=4242 + rank, batch=B, heads_kv=hl)
+    gq = torch.Generator(device=device).manual_seed(99)
+    q_full = (torch.randn(B, HQ, 1, D, device=device, generator=gq) / math.sqrt(D)).half()
+    q_local = sharding.shard_queries(q_full, HKV, world, rank)
+    res = plan_all.arenas[1:]  # SPLIT starts with the 1-bit tier: it is the spilled one
+    plan_res = A.AttentionPlan(res, [(ai, j, P) for ai, a in enumerate(res) for j in range(a.slots)], batch=B,
+                               heads_kv=hl, group=HQ // HKV, head_dim=D)
+    host = spill.arenas_to_host([plan_all.arenas[0]])[0]
+    layer = spill.SpilledLayerDecode(plan_res, host, chunk_slots=512)
     if world > 1:
-        step = sharding.HeadShardedDecode(plan, n_kv)
-        run = lambda: step(q_full)  # noqa: E731
+        gather = sharding.HeadShardedDecode(plan_res, HKV)
+        buf, out_full = gather._buffers(q_local.shape, q_local.dtype, device)
+
+        def step():
+            layer(q_local, out=buf[rank])
+            gather.all_gather(buf)
+            gather.to_head_order(buf, out_full)
     else:
-        run = lambda: plan.run(q_local)  # noqa: E731
+        step = lambda: layer(q_local)  # noqa: E731
     for _ in range(args.warmup):
-        run()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        step()
+    lse_r = torch.empty(B, hl * (HQ // HKV), 1, device=device)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     with ClockSampler(vis.split(",")[local_rank] if vis else str(local_rank)) as clk:
-        e0.record()
-        for _ in range(args.steps):
-            run()
-        e1.record()
-        torch.cuda.synchronize(device)
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        wins = _windows(step, args.steps, world, device, min_seconds=args.min_seconds)
+        res_ms = statistics.median(_windows(lambda: plan_res.run(q_local, lse=lse_r), args.steps, world, device,
+                                            min_seconds=0.2))
+        all_ms = statistics.median(_windows(lambda: plan_all.run(q_local), args.steps, world, device,
+                                            min_seconds=0.2))
+    ms = statistics.median(wins)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        value, dt, cpu_steps = time_cpu(1, 0, os.cpu_count() or 1, min_seconds=10.0)
+        cpu = {"value": value, "unit": "KV tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"1 sequence x {HKV} KV heads x {L} tokens per step (every tier resident), "
+                         f"{cpu_steps} timed steps ({cpu_steps * dt:.1f} s of CPU work)", "scope": CPU_PORT_SCOPE}
     if rank != 0:
         return
     hbm, peak_kind = peaks()
-    layer_bytes = plan.compressed_bytes * world
-    print(json.dumps({"metric": "Llama-3-70B layer decode, KV-head sharded, KV tokens/s", "value": B * L / (ms * 1e-3),
-                      "unit": "KV tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                      "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "dtype": "fp16",
-                      "data": "synthetic",
-                      "config": {"workload": "llama3-70b-heads", "batch": B, "q_heads": HQ, "kv_heads": n_kv,
+    spilled = host.k.numel()
+    print(json.dumps({"metric": "Llama-3-70B layer decode, KV-head sharded, oldest 25% spilled to host, KV tokens/s",
+                      "value": B * L / (ms * 1e-3), "unit": "KV tokens/s", "n_gpus": world, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                      "dtype": "fp16", "data": "synthetic",
+                      "config": {"workload": "llama3-70b", "batch": B, "q_heads": HQ, "kv_heads": HKV,
                                  "head_dim": D, "context": L, "tiers_oldest_first": dict(SPLIT),
-                                 "parallelism": f"kv-head sharded x{world}, NCCL all-gather of outputs"},
-                      "roofline": {"bound": "hbm", "achieved_per_gpu": layer_bytes / world / (ms * 1e-3) / 1e9,
-                                   "peak": hbm, "unit": "GB/s",
-                                   "frac": layer_bytes / world / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
-                                   "algorithmic_bytes_per_step": layer_bytes},
-                      "clocks": clk.summary()}), flush=True)
+                                 "spilled": "one_bit (25% of the tokens): pinned host memory of the GPU's NUMA node, "
+                                            "streamed in runs of 512 slots",
+                                 "parallelism": f"kv-head sharded x{world} ({hl} KV heads per GPU)" +
+                                                (", NCCL all-gather of outputs" if world > 1 else "")},
+                      "timing": {"windows": len(wins), "steps_per_window": args.steps, "statistic": "median window"},
+                      "per_rank": {"compressed_bytes": plan_all.compressed_bytes, "spilled_bytes": spilled,
+                                   "host_link_GBs": spilled / (ms * 1e-3) / 1e9,
+                                   "resident_tiers_ms": res_ms,
+                                   "resident_tiers_frac_of_hbm": plan_res.compressed_bytes / (res_ms * 1e-3) / 1e9 / hbm,
+                                   "all_resident_ms": all_ms,
+                                   "all_resident_frac_of_hbm": plan_all.compressed_bytes / (all_ms * 1e-3) / 1e9 / hbm,
+                                   "peak_kind": peak_kind, "numa_local_cpus": len(cpus) if cpus else None},
+                      "limiting": "host link (the spilled tier's copies)" if ms > 1.5 * res_ms else
+                                  "HBM (the resident tiers' kernel)",
+                      "clocks": clk.summary(), "cpu_baseline": cpu}), flush=True)
 
 
 def run_cascade(args):
@@ -908,15 +881,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the K-step timed window until this much device time has passed")
-    ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b-spill", "tinyllama-sidecars",
-                                           "cascade", "llama3-70b-heads"), default="llama3-8b-layer")
+    ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b", "tinyllama-sidecars",
+                                           "cascade"), default="llama3-8b-layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "jl-archive":
         run_jl_archive(args)
-        return
-    if args.workload == "llama3-70b-spill":
-        run_70b_spill(args)
         return
     if args.workload == "tinyllama-sidecars":
         run_tinyllama_sidecars(args)
@@ -930,8 +900,8 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    if args.workload == "llama3-70b-heads" and world == 1:
-        run_70b_heads(args, 0, 1, local_rank)
+    if args.workload == "llama3-70b" and world == 1:
+        run_70b(args, 0, 1, local_rank)
         return
     if world > 1:
         import datetime
@@ -942,8 +912,8 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
-        if args.workload == "llama3-70b-heads":
-            run_70b_heads(args, rank, world, local_rank)
+        if args.workload == "llama3-70b":
+            run_70b(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
