@@ -50,7 +50,7 @@ class ArenaC(ctypes.Structure):
     _fields_ = [("tier", ctypes.c_int32), ("layout", ctypes.c_int32), ("k", ctypes.c_void_p),
                 ("v", ctypes.c_void_p), ("bh_stride", ctypes.c_int64), ("record_bytes", ctypes.c_int32),
                 ("page_tokens", ctypes.c_int32), ("outlier_dir", ctypes.c_void_p), ("dir_slots", ctypes.c_int32),
-                ("reserved", ctypes.c_int32)]
+                ("reserved", ctypes.c_int32), ("slot_live", ctypes.c_void_p)]
 
 
 class ChunkC(ctypes.Structure):
@@ -114,6 +114,8 @@ class KVArena:
         # the blocks of each slot kept referenced while the directory points at them
         self.outlier_dir = None
         self._outlier_blocks = {}
+        # optional device occupancy [slots] uint8 (nonzero = live page), read by the kernel per tile
+        self.slot_live = None
 
     # ---------------------------------------------------------------- record arenas
     @classmethod
@@ -204,10 +206,10 @@ class KVArena:
             self._outlier_blocks.pop(slot, None)
 
     def c_struct(self):
-        d = self.outlier_dir
+        d, live = self.outlier_dir, self.slot_live
         return ArenaC(self.tier, self.layout, self.k.data_ptr(), self.v.data_ptr() if self.v is not None else None,
                       self.bh_stride, self.record_bytes, self.page_tokens, d.data_ptr() if d is not None else None,
-                      self.slots if d is not None else 0, 0)
+                      self.slots if d is not None else 0, 0, live.data_ptr() if live is not None else None)
 
 
 def chunk_capacity(arena, head_dim):
@@ -296,7 +298,9 @@ class AttentionPlan:
     longer record pages and split-fp16 slots may end short."""
 
     def __init__(self, arenas, pages, *, batch, heads_kv, group, head_dim, q_len=1, n_splits=None, device=None,
-                 precise_pv=False):
+                 precise_pv=False, single_tile=()):
+        """single_tile: indices of split fp16 arenas whose 16-token slots each get a chunk of their own,
+        so that any slot's token count can be patched later (patch_tokens)."""
         if not 0 < len(arenas) <= MAX_ARENAS:
             raise ValueError(f"1..{MAX_ARENAS} arenas supported")
         self.arenas = list(arenas)
@@ -346,7 +350,8 @@ class AttentionPlan:
             else:  # split fp16: slot = 16-token block
                 if ntok > 16:
                     raise ValueError("split fp16 slots hold at most 16 tokens")
-                if cur is not None and cur[2] == ai and cur[5] == slot and cur[3] < caps[ai] and cur[4] == 16:
+                if (cur is not None and cur[2] == ai and cur[5] == slot and cur[3] < caps[ai] and cur[4] == 16
+                        and ai not in single_tile):
                     cur[3] += 1
                     cur[4] = ntok
                     cur[5] += 1
@@ -406,6 +411,19 @@ class AttentionPlan:
             if tier != TIER_FP16:
                 total += 2 * 2 * int(n) * (2 if tier in (TIER_INT4, TIER_INT2) else 1)
         return total * self.B * self.Hkv
+
+    def refresh_arenas(self):
+        """Re-reads the arenas' device pointers (outlier directories, occupancy) into the launch."""
+        self._arena_c = (ArenaC * MAX_ARENAS)(*[a.c_struct() for a in self.arenas])
+        self._outlier_dirs = [a.outlier_dir for a in self.arenas]
+
+    def patch_tokens(self, chunk, ntok):
+        """Sets the token count of a single-tile chunk's tile (1..16) in the device chunk table."""
+        slot, tok0, ai, nt, _ = self.chunks[chunk]
+        if nt != 1 or not 1 <= ntok <= 16:
+            raise ValueError("only single-tile chunks are patched")
+        self.chunks[chunk] = (slot, tok0, ai, nt, int(ntok))
+        self.chunks_dev[chunk * ctypes.sizeof(ChunkC) + 8] = int(ntok)  # ntok_last: byte 8 of argus_kv_chunk
 
     def tile_lse_shape(self):
         nqg = (self.G * self.qlen + 7) // 8

@@ -28,6 +28,7 @@ import math
 import os
 import time
 
+import numpy as np
 import torch
 
 from .. import _lib
@@ -202,6 +203,16 @@ class PagedDynamicKVCache:
         self._plan = None
         self._plan_key = None
         self._plan_base_cache = None
+        # occupancy of the pools' slots (see _attention_plan): host mirrors, what changed since the
+        # last upload, and how many times the launch tables were built
+        self._live_host = {}
+        self._live_dirty = False
+        self._tiers_dirty = set()
+        self._tiers_dirty_all = False
+        self._buf_live = None
+        self._buf_live_host = None
+        self._jl_ops = None
+        self.plan_builds = 0
         # attend JL pages without rebuilding them (argus_b200.core.jl.JLAttention) when their shape
         # allows it (128-row blocks, i.e. 512-token pages, head_dim 128, <= 8 queries per kv head)
         self.fused_jl_attention = True
@@ -269,6 +280,11 @@ class PagedDynamicKVCache:
         for name, (attr, tier) in _TIERS.items():
             slots = getattr(self, f"max_{attr[:-6]}_pages")
             self.arenas[name] = A.KVArena.allocate(tier, B, H, max(1, slots), P, D, dev)
+        # per pool: which slots hold live pages (host mirror, device array read by the kernel)
+        self._live_host = {}
+        for name, a in self.arenas.items():
+            self._live_host[name] = np.zeros(a.slots, np.uint8)
+            a.slot_live = torch.zeros(a.slots, dtype=torch.uint8, device=dev)
         self._pools_allocated = True
         self._invalidate()
 
@@ -349,10 +365,10 @@ class PagedDynamicKVCache:
         # the attention plan reads the static buffer in place and tracks buffer_length itself
         P = self.page_size
         while self.buffer_length >= P:
-            self._invalidate()
             if len(self.active_pages) >= self.max_active_pages:
                 self.manage_memory_lifecycle()
             idx = self._get_free_pool_idx(self.active_pages, self.max_active_pages)
+            self._slot("fp16", idx, True)
             self.arenas["fp16"].view("k", idx).copy_(self.static_k_buffer[..., :P, :])
             self.arenas["fp16"].view("v", idx).copy_(self.static_v_buffer[..., :P, :])
             remaining = self.buffer_length - P
@@ -454,7 +470,7 @@ class PagedDynamicKVCache:
 
     def _demote_active_to_fp8(self, page):
         """Outlier isolation + simulated-FP8 quantization of an active page (memory_manager.py:944-987)."""
-        self._invalidate()
+        self._slot("fp16", page["pool_idx"], False)
         k = page["key"].contiguous()
         v = page["value"].contiguous()
         k_norm, k_out, k_mask = isolate_outliers(k, self.threshold_sigma)
@@ -465,6 +481,7 @@ class PagedDynamicKVCache:
             self.fp8_pages.sort(key=lambda p: p.get("importance_score", 0.0))
             self._demote_fp8_to_int8(self.fp8_pages.pop(0))
         idx = self._get_free_pool_idx(self.fp8_pages, self.max_fp8_pages)
+        self._slot("fp8", idx, True)
         paged.quantize_page(self.arenas["fp8"], idx, k_norm, v_norm)
         entry = self._page_views("fp8", idx)
         entry.update({"key_out_indices": k_idx, "key_out_values": k_vals, "value_out_indices": v_idx,
@@ -486,7 +503,7 @@ class PagedDynamicKVCache:
         """Shared body of the FP8->INT8, INT8->INT4, INT4->INT2 and INT2->1-bit demotions
         (memory_manager.py:989-1123): make room in `dst` (recursively), then one fused kernel
         re-quantizes the page in place.  The V sidecar carries the K sidecar, as in the reference."""
-        self._invalidate()
+        self._slot(src, old["pool_idx"], False)
         dst_attr = _TIERS[dst][0]
         lst = getattr(self, dst_attr)
         limit = getattr(self, f"max_{dst_attr[:-6]}_pages")
@@ -494,6 +511,7 @@ class PagedDynamicKVCache:
             lst.sort(key=lambda p: p.get("importance_score", 0.0))
             next_demote(lst.pop(0))
         idx = self._get_free_pool_idx(lst, limit)
+        self._slot(dst, idx, True)
         paged.requant_page(self.arenas[src], old["pool_idx"], self.arenas[dst], idx)
         entry = self._page_views(dst, idx)
         entry.update({"key_out_indices": old["key_out_indices"], "key_out_values": old["key_out_values"],
@@ -532,7 +550,7 @@ class PagedDynamicKVCache:
 
     def _demote_one_bit_to_jl(self, old):
         """1-bit page -> fp16 (sidecars applied) -> sequence projection W @ X (memory_manager.py:1125-1155)."""
-        self._invalidate()
+        self._slot("one_bit", old["pool_idx"], False)
         k_full, v_full = self._dequant_with_sidecars("one_bit", old)
         W = self.get_jl_projection_matrix(k_full.device, k_full.dtype)
         entry = {"key_proj": _jl.apply_left(W, k_full), "value_proj": _jl.apply_left(W, v_full)}
@@ -546,11 +564,12 @@ class PagedDynamicKVCache:
 
     def _resurrect_page(self, page, tier):
         """Dequantize a compressed page back into the FP16 active pool (memory_manager.py:832-917)."""
-        self._invalidate()
         t0 = time.perf_counter()
         if tier not in _TIERS and tier != "jl":
             return
         k, v = self._dequant_with_sidecars(tier, page)
+        if tier in _TIERS:
+            self._slot(tier, page["pool_idx"], False)
         attr = "jl_pages" if tier == "jl" else _TIERS[tier][0]
         setattr(self, attr, [p for p in getattr(self, attr) if p is not page])
         dt = (time.perf_counter() - t0) * 1000
@@ -569,6 +588,7 @@ class PagedDynamicKVCache:
             self.active_pages.sort(key=lambda x: x.get("importance_score", 0.0))
             self._demote_active_to_fp8(self.active_pages.pop(0))
         idx = self._get_free_pool_idx(self.active_pages, self.max_active_pages)
+        self._slot("fp16", idx, True)
         self.arenas["fp16"].view("k", idx).copy_(k)
         self.arenas["fp16"].view("v", idx).copy_(v)
         views = self._page_views("fp16", idx)
@@ -641,40 +661,80 @@ class PagedDynamicKVCache:
         return K, V
 
     def _attention_plan(self, q, tail=0):
-        """Fused-kernel tables for the current cache.  What depends on the pages (a scratch fp16
-        arena for the sinks, anchors and JL pages the fused JL kernel does not take; the pages'
-        outlier corrections; the JL operands) is rebuilt only when pages change.  The staging
-        buffer is an fp16 arena of its own over the static buffer, so a decode step that only
-        appends a token patches the token count of the buffer's last tile in place; the tables are
-        rebuilt when the buffer starts a new 16-token tile.  The newest `tail` tokens of the
-        staging buffer are left out (a causal step attends to them separately)."""
+        """Fused-kernel tables for the current cache, kept current at the cache's mutation points
+        rather than rebuilt.  The chunk list covers every slot of the FP16 pool and of each tier's
+        pool, and every 16-token block of the staging buffer's capacity (one chunk per block); which
+        slots hold live pages is a per-arena device occupancy array (argus_kv_arena.slot_live) that
+        page moves update a byte at a time (_slot), and the buffer's last live block gets its token
+        count patched in the chunk table.  So a decode step across a page formation, a demotion or a
+        resurrection uploads a few bytes and rebuilds nothing; the tables are rebuilt only when the
+        cache's structure changes: the pools or the staging buffer are reallocated (first push, swap,
+        buffer growth), the sinks or anchors change, or JL pages come or go.  The newest `tail`
+        tokens of the staging buffer are left out (a causal step attends to them separately)."""
         B, Hq, qlen, D = q.shape
         nbuf = max(0, self.buffer_length - tail) if self.k_buffer is not None else 0
-        base_key = (B, Hq, qlen, D, len(self.active_pages), tuple(len(lst) for _, lst in self._compressed_order()),
-                    self._scratch_version())
-        key = (base_key, self.static_k_buffer.data_ptr() if nbuf else 0, (nbuf + 15) // 16)
+        cap = self.static_k_buffer.shape[-2] if self._pools_allocated else 0
+        fused_jl = self._fused_jl(q)
+        base_key = (B, Hq, qlen, D, tuple((n, a.slots) for n, a in self.arenas.items()) if self._pools_allocated else (),
+                    self._scratch_version(fused_jl), fused_jl)
+        key = (base_key, self.static_k_buffer.data_ptr() if cap else 0, cap)
         plan = self._plan
-        if plan is not None and self._plan_key == key:
-            if plan.buffer_tokens != nbuf:
-                self._patch_buffer_tokens(plan, nbuf)
-            return plan
-        base = self._plan_base(q, base_key)
+        if plan is None or self._plan_key != key:
+            plan = self._build_plan(q, base_key, cap, fused_jl)
+            self._plan, self._plan_key = plan, key
+            self.plan_builds += 1
+        self._sync_live(plan)
+        self._sync_buffer(plan, nbuf)
+        plan.jl = self._jl_operands(q) if fused_jl else None
+        return plan
+
+    def _fused_jl(self, q):
+        """Whether JL pages are attended by the fused JL kernel (128-row blocks, i.e. 512-token pages,
+        head_dim 128, <= 8 queries per kv head) rather than rebuilt into the scratch arena."""
+        B, Hq, qlen, D = q.shape
+        if not (self.fused_jl_attention and self.jl_pages) or self.page_size // 4 != 128 or D != 128:
+            return False
+        Hkv = self.H if self._pools_allocated else self.sink_k.shape[1]
+        return (Hq // Hkv) * qlen <= 8 and self._pools_allocated
+
+    def _jl_operands(self, q):
+        """The fused JL kernel's operands (stacked Yk / Yv of the JL pages), rebuilt only when the JL
+        pages change."""
+        key = tuple(id(p) for p in self.jl_pages)
+        if self._jl_ops is None or self._jl_ops[0] != key:
+            R = self.get_jl_reconstruction_operator(q.device, torch.float16)
+            if self._jl_attention is None or self._jl_attention[0] is not R:
+                self._jl_attention = (R, _jl.JLAttention(R))
+            ops = {"att": self._jl_attention[1], "pages": list(self.jl_pages),
+                   "yk": torch.stack([pg["key_proj"] for pg in self.jl_pages], dim=2).contiguous(),
+                   "yv": torch.stack([pg["value_proj"] for pg in self.jl_pages], dim=2).contiguous()}
+            self._jl_ops = (key, ops)
+        return self._jl_ops[1]
+
+    def _build_plan(self, q, base_key, cap, fused_jl):
+        B, Hq, qlen, D = q.shape
+        base = self._plan_base(q, base_key, fused_jl)
         arenas, pages, page_seg = list(base["arenas"]), list(base["pages"]), list(base["page_seg"])
         segments = list(base["order"])
         buf_ai = -1
-        if nbuf:
+        nblk = (cap + 15) // 16
+        if cap:
             buf_ai = len(arenas)
-            arenas.append(A.KVArena.from_fp16(self.static_k_buffer, self.static_v_buffer))
+            buf = A.KVArena.from_fp16(self.static_k_buffer, self.static_v_buffer)
+            self._buf_live = torch.zeros(nblk, dtype=torch.uint8, device=q.device)
+            self._buf_live_host = np.zeros(nblk, np.uint8)
+            buf.slot_live = self._buf_live
+            arenas.append(buf)
             seg = len(segments)
-            segments.append(("buffer", None, nbuf))
-            for t0 in range(0, nbuf, 16):
-                pages.append((buf_ai, t0 // 16, min(16, nbuf - t0)))
+            segments.append(("buffer", None, 0))
+            for b in range(nblk):
+                pages.append((buf_ai, b, min(16, cap - 16 * b)))
                 page_seg.append(seg)
         Hkv = base["Hkv"]
         # attention is order-free: give each arena's pages in slot order so runs merge into chunks
         perm = sorted(range(len(pages)), key=lambda i: (pages[i][0], pages[i][1]))
         plan = A.AttentionPlan(arenas, [pages[i] for i in perm], batch=B, heads_kv=Hkv, group=Hq // Hkv,
-                               head_dim=D, q_len=qlen)
+                               head_dim=D, q_len=qlen, single_tile=(buf_ai,) if cap else ())
         # map (chunk, tile) of the launch -> segment
         cmap = torch.full((max(1, plan.n_chunks), 16), -1, dtype=torch.long)
         for c, src in enumerate(plan.chunk_pages):
@@ -682,56 +742,86 @@ class PagedDynamicKVCache:
                 cmap[c, i] = page_seg[perm[pi]]
         plan.tile_segment = cmap.to(q.device)
         plan.segments = segments
-        plan.jl = base["jl"]
-        plan.buffer_tokens = nbuf
-        plan.buffer_chunk = -1
-        if nbuf:
-            last = (nbuf - 1) // 16
-            plan.buffer_chunk = next(c for c, (slot, _, ai, nt, _) in enumerate(plan.chunks)
-                                     if ai == buf_ai and slot <= last < slot + nt)
-        self._plan, self._plan_key = plan, key
+        plan.buf_ai = buf_ai
+        # chunk of each buffer block, and the token count each block's chunk holds now
+        plan.buffer_chunks = [-1] * nblk
+        plan.buffer_ntok = [0] * nblk
+        for c, (slot, _, ai, nt, last) in enumerate(plan.chunks):
+            if ai == buf_ai:
+                plan.buffer_chunks[slot] = c
+                plan.buffer_ntok[slot] = last
+        plan.buffer_tokens = -1
+        self._live_dirty = True  # a fresh plan reads the occupancy of every arena
         return plan
 
-    def _patch_buffer_tokens(self, plan, nbuf):
-        """The staging buffer grew within its last 16-token tile: update that tile's token count in
-        the plan's device chunk table (one byte) and the buffer segment's length."""
-        c = plan.buffer_chunk
-        slot, tok0, ai, nt, _ = plan.chunks[c]
-        last = nbuf - 16 * ((nbuf - 1) // 16)
-        plan.chunks[c] = (slot, tok0, ai, nt, last)
-        # ntok_last is byte 8 of the 12-byte argus_kv_chunk
-        plan.chunks_dev[c * ctypes.sizeof(A.ChunkC) + 8] = last
-        plan.n_tokens += nbuf - plan.buffer_tokens
+    def _sync_buffer(self, plan, nbuf):
+        """The staging buffer holds nbuf tokens: blocks below ceil(nbuf/16) live, the last one patched
+        to its token count (a byte of the device chunk table), the others back to 16."""
+        if plan.buf_ai < 0 or plan.buffer_tokens == nbuf:
+            return
+        nb = (nbuf + 15) // 16
+        live = self._buf_live_host
+        changed = False
+        for b in range(len(live)):
+            want = 1 if b < nb else 0
+            if live[b] != want:
+                live[b] = want
+                changed = True
+            if b < nb:
+                ntok = 16 if b < nb - 1 else nbuf - 16 * (nb - 1)
+                if plan.buffer_ntok[b] != ntok:
+                    plan.patch_tokens(plan.buffer_chunks[b], ntok)
+                    plan.buffer_ntok[b] = ntok
+        if changed:
+            self._buf_live.copy_(torch.from_numpy(live))
         plan.segments[-1] = ("buffer", None, nbuf)
         plan.buffer_tokens = nbuf
 
-    def _plan_base(self, q, base_key):
-        """The page-dependent part of the attention tables (see _attention_plan), cached by key."""
+    def _slot(self, name, idx, live):
+        """Page moves: slot idx of pool `name` ("fp16" or a tier) now holds a live page (or not)."""
+        h = self._live_host.get(name)
+        if h is None:
+            return
+        h[idx] = 1 if live else 0
+        self._live_dirty = True
+        self._tiers_dirty.add(name)
+
+    def _sync_live(self, plan):
+        """Uploads the pools' occupancy after page moves, refreshes the outlier directories of the
+        tiers whose pages changed, and lets the plan re-read the arenas' pointers."""
+        if not self._live_dirty:
+            return
+        for name, h in self._live_host.items():
+            self.arenas[name].slot_live.copy_(torch.from_numpy(h))
+        for name in self._tiers_dirty | (set(_TIERS) if self._tiers_dirty_all else set()):
+            if name in _TIERS:
+                self._attach_outliers(name)
+        self._tiers_dirty = set()
+        self._tiers_dirty_all = False
+        plan.refresh_arenas()
+        self._live_dirty = False
+
+    def _plan_base(self, q, base_key, fused_jl):
+        """The structure-dependent part of the attention tables (see _attention_plan), cached by key:
+        the scratch fp16 arena (sinks, anchors, JL pages the fused JL kernel does not take) and every
+        slot of the FP16 and tier pools."""
         if self._plan_base_cache is not None and self._plan_base_cache[0] == base_key:
             return self._plan_base_cache[1]
         B, Hq, qlen, D = q.shape
         P = self.page_size
-        order = []  # (segment kind, page or None, tokens) in the reference's attention order
+        order = []  # (segment kind, page / (pool, slot) / None, tokens)
         if self.sink_k is not None:
             order.append(("sinks", None, self.sink_k.shape[-2]))
         if self.anchor_k is not None:
             order.append(("anchors", None, self.anchor_k.shape[-2]))
-        for page in self.active_pages:
-            order.append(("fp16", page, P))
-        others = (self.sink_k is not None or self.anchor_k is not None or bool(self.active_pages)
-                  or (self.k_buffer is not None and self.k_buffer.shape[-2] > 0)
-                  or any(lst for name, lst in self._compressed_order() if name != "jl"))
         Hkv = self.H if self._pools_allocated else (self.sink_k.shape[1])
-        fused_jl = (self.fused_jl_attention and len(self.jl_pages) > 0 and others and P // 4 == 128 and D == 128
-                    and (Hq // Hkv) * qlen <= 8)
-        for name, lst in self._compressed_order():
-            for page in lst:
-                if name == "jl" and fused_jl:
-                    order.append(("jl_fused", page, P))
-                    continue
-                # JL pages not taken by the fused JL kernel are rebuilt into the scratch arena; pages
-                # with outlier sidecars are read compressed, their sidecars applied by the kernel
-                order.append(("scratch:jl" if name == "jl" else name, page, P))
+        if not fused_jl:
+            for page in self.jl_pages:
+                order.append(("scratch:jl", page, P))
+        if self._pools_allocated:
+            for name in ["fp16"] + list(_TIERS):
+                for slot in range(self.arenas[name].slots):
+                    order.append(("slot", (name, slot), P))
         # scratch fp16 tensor: sinks, anchors and rebuilt JL pages, each padded to 16 tokens
         scratch_len = sum(-(-n // 16) * 16 for kind, _, n in order if kind in ("sinks", "anchors", "scratch:jl"))
         dev = q.device
@@ -745,11 +835,7 @@ class PagedDynamicKVCache:
             arenas.append(A.KVArena.from_fp16(sk, sv))
         pos = 0
         page_seg = []  # per entry of `pages`: its segment
-        jl_segs = []
         for seg, (kind, page, n) in enumerate(order):
-            if kind == "jl_fused":
-                jl_segs.append(seg)
-                continue
             if kind in ("sinks", "anchors", "scratch:jl"):
                 sk, sv = scratch
                 if kind == "sinks":
@@ -767,24 +853,14 @@ class PagedDynamicKVCache:
                     page_seg.append(seg)
                 pos += -(-n // 16) * 16
             else:
-                if kind not in index:
-                    index[kind] = len(arenas)
-                    arenas.append(self.arenas[kind])
-                pages.append((index[kind], page["pool_idx"], n))
+                name, slot = page
+                if name not in index:
+                    index[name] = len(arenas)
+                    arenas.append(self.arenas[name])
+                pages.append((index[name], slot, n))
                 page_seg.append(seg)
-        for name in _TIERS:
-            if name in index:
-                self._attach_outliers(name)
-        jl = None
-        if jl_segs:
-            R = self.get_jl_reconstruction_operator(dev, torch.float16)
-            if self._jl_attention is None or self._jl_attention[0] is not R:
-                self._jl_attention = (R, _jl.JLAttention(R))
-            pages_jl = [order[i][1] for i in jl_segs]
-            jl = {"att": self._jl_attention[1], "segs": jl_segs,
-                  "yk": torch.stack([pg["key_proj"] for pg in pages_jl], dim=2).contiguous(),
-                  "yv": torch.stack([pg["value_proj"] for pg in pages_jl], dim=2).contiguous()}
-        base = {"order": order, "arenas": arenas, "pages": pages, "page_seg": page_seg, "jl": jl, "Hkv": Hkv,
+        self._tiers_dirty_all = True  # the directories are rebuilt for the new plan
+        base = {"order": order, "arenas": arenas, "pages": pages, "page_seg": page_seg, "Hkv": Hkv,
                 "scratch": scratch}
         self._plan_base_cache = (base_key, base)
         return base
@@ -808,10 +884,12 @@ class PagedDynamicKVCache:
                 page["_outlier_blocks"] = cached
             arena.set_outliers(page["pool_idx"], cached[1], cached[2])
 
-    def _scratch_version(self):
+    def _scratch_version(self, fused_jl):
+        """What the scratch arena is built from: the sinks, the anchors and (when the fused JL kernel
+        does not take them) the JL pages.  Page moves between the pools do not change it."""
         return (self.sink_k.data_ptr() if self.sink_k is not None else 0,
-                self.anchor_k.shape[-2] if self.anchor_k is not None else 0, self._page_counter, self.num_resurrections,
-                self.total_demotions)
+                self.anchor_k.shape[-2] if self.anchor_k is not None else 0,
+                () if fused_jl else tuple(id(p) for p in self.jl_pages))
 
     def attend(self, q, scale=None, causal=False):
         """softmax(q K^T * scale) V over every tier straight from the compressed pages, without the
@@ -927,16 +1005,29 @@ class PagedDynamicKVCache:
         tile_mass = w.sum(dim=(0, 1, 2, 5)) / float(B * Hq * qlen)
         seg_mass = torch.zeros(len(plan.segments), device=q.device, dtype=torch.float32)
         seg_mass.index_add_(0, plan.tile_segment[valid], tile_mass[valid])
+        jl_masses = []
         if block_lse is not None:
             nq = G * qlen
             wj = torch.exp(block_lse[:, :, :nq] - lse.view(B * plan.Hkv, 1, nq))
-            jl_mass = wj.sum(dim=(0, 2)) / float(B * Hq * qlen)
-            seg_mass.index_add_(0, torch.tensor(plan.jl["segs"], device=q.device), jl_mass)
+            jl_masses = (wj.sum(dim=(0, 2)) / float(B * Hq * qlen)).tolist()
         masses = seg_mass.tolist()
+        # each page's mass from its pool slot (or, for JL pages, its own segment), in the reference's
+        # page order: active pages, then JL, 1-bit, INT2, INT4, INT8, FP8
+        by_seg = {}
+        for (kind, where, n), m in zip(plan.segments, masses):
+            if kind == "slot":
+                by_seg[where] = m
+            elif kind == "scratch:jl":
+                by_seg[id(where)] = m
+        if plan.jl is not None:
+            for page, m in zip(plan.jl["pages"], jl_masses):
+                by_seg[id(page)] = m
         resurrect = []
         compressed = {id(p): name for name, lst in self._compressed_order() for p in lst}
-        for (kind, page, n), block_w in zip(plan.segments, masses):
-            if page is None:
+        ordered = [("fp16", p) for p in self.active_pages] + [(n, p) for n, lst in self._compressed_order() for p in lst]
+        for name, page in ordered:
+            block_w = by_seg.get(id(page) if name == "jl" else (name, page["pool_idx"]))
+            if block_w is None:
                 continue
             page["attention_sum"] = page.get("attention_sum", 0.0) + block_w
             if block_w > 0.0:
@@ -1029,6 +1120,7 @@ class PagedDynamicKVCache:
         if self._pools_allocated and self._host_arenas:
             dev_arenas = spill.arenas_to_device(self._host_arenas, target)
             for name, a in zip(_TIERS, dev_arenas):
+                a.slot_live = torch.from_numpy(self._live_host[name]).to(target)
                 self.arenas[name] = a
                 for page in getattr(self, _TIERS[name][0]):
                     page.update(self._page_views(name, page["pool_idx"]))

@@ -953,6 +953,14 @@ __device__ __forceinline__ OutlierTile outlier_tile(unsigned long long blk, int 
     return ot;
 }
 
+// A tile of a slot that holds no live page: nothing attends to it; its per-tile mass reads -inf.
+template <bool MASS>
+__device__ __forceinline__ void skip_tile(float* mass_out) {
+    if constexpr (MASS) {
+        if ((threadIdx.x & 31) < kQ) mass_out[threadIdx.x & 31] = -INFINITY;
+    }
+}
+
 // Processes one staged tile: scores, online softmax, PV (OUT: with the page's outlier corrections).
 template <int D, int TIER, bool PRECISE, bool MASS, bool OUT>
 __device__ __forceinline__ void process_tile(const TilePtr& tp, int g4, int t4, uint32_t qs, float scale_log2, float2 qsum,
@@ -1247,6 +1255,17 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
                 }
             }
         }
+        // tiles of slots that hold no live page (slot_live) are skipped: bit i of live_mask is tile i
+        unsigned live_mask = 0xffffffffu;
+        {
+            const argus_kv_arena& la = p.arenas[ch.arena];
+            if (la.slot_live) {
+                const bool wr = whole_records(la.layout, la.page_tokens);
+                const bool mine = wr ? lane < ch.ntiles : lane == 0;
+                const bool alive = mine && __ldg(la.slot_live + ch.slot0 + (wr ? lane : 0)) != 0;
+                live_mask = wr ? __ballot_sync(0xffffffffu, alive) : (__any_sync(0xffffffffu, alive) ? 0xffffffffu : 0u);
+            }
+        }
         {
             // bounded: chunk j is issued by whichever warp finishes chunk j - kStages.  Both waits are
             // voted over the warp, so its lanes leave the loop together.
@@ -1275,6 +1294,10 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
             /* one full 16-token page per record: compile-time offsets */                                        \
             constexpr int RB = record_bytes(T, 16, D), PB = payload_bytes(T, 16, D);                              \
             for (int i = 0; i < n; ++i) {                                                                         \
+                if (!((live_mask >> i) & 1u)) {                                                                   \
+                    skip_tile<MASS>(mass_base ? mass_base + i * kQ : nullptr);                                    \
+                    continue;                                                                                     \
+                }                                                                                                 \
                 const unsigned char* r = sb + i * RB;                                                             \
                 TilePtr tp;                                                                                       \
                 tp.k = r;                                                                                         \
@@ -1292,6 +1315,10 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
         } else {                                                                                                  \
             const ChunkView cv = chunk_view<D>(ar, n);                                                            \
             for (int i = 0; i < n; ++i) {                                                                         \
+                if (!((live_mask >> i) & 1u)) {                                                                   \
+                    skip_tile<MASS>(mass_base ? mass_base + i * kQ : nullptr);                                    \
+                    continue;                                                                                     \
+                }                                                                                                 \
                 TilePtr tp;                                                                                       \
                 const int po = i * cv.pstride, so = i * cv.sstride;                                               \
                 tp.k = sb + cv.k_off + po;                                                                        \

@@ -281,6 +281,15 @@ typedef struct argus_kv_arena {
     const uint64_t* outlier_dir;
     int32_t dir_slots;
     int32_t reserved;
+    /* Occupancy of the arena's slots (null = every slot the chunk list names holds a page): a device
+     * array of one byte per slot (per 16-token slot in the split layout), nonzero where the slot holds
+     * live tokens.  Tiles of dead slots are skipped (their tile_lse entries read -inf); a chunk of a
+     * record page longer than 16 tokens, or of the split layout, is live or dead as a whole (its first
+     * slot's byte).  So a chunk list covering a whole pool
+     * stays valid while pages come and go: the cache updates one byte per page move (demotion,
+     * resurrection, a new page: core/memory_manager.py:383-489, 832-917, 944-1155) instead of rebuilding
+     * its tables. */
+    const uint8_t* slot_live;
 } argus_kv_arena;
 
 /* A run of up to 16 consecutive 16-token tiles of one arena, staged as one unit:

@@ -199,3 +199,45 @@ def test_fused_steps_of_several_tokens_match_materializing_adapter(tmp_path, mon
     assert fused_cache.get_seq_length(0) == ref_cache.get_seq_length(0) == 144
     assert fused_steps >= 4, fused_steps
     assert worst <= 1e-2, worst
+
+
+
+def test_decode_steps_across_demotions_keep_the_launch_tables(tmp_path, monkeypatch):
+    """The launch tables cover every pool slot and the staging buffer's capacity: single-token decode
+    steps that cross new 16-token tiles, page formations, demotions down the cascade (no JL) and
+    resurrections only update the device occupancy and a token count, so after the first step no
+    table is rebuilt; attention stays within the bar of float64 attention over the rebuilt K/V and
+    inplace_paged_attention keeps taking its per-page masses from the same launch."""
+    import time
+
+    import oracle
+    from argus_b200.core.memory_manager import PagedDynamicKVCache
+    monkeypatch.setenv("ARGUS_LOG_LEVEL", "quiet")
+    monkeypatch.chdir(tmp_path)
+    B, H, G, D = 1, 2, 4, 64
+    cache = PagedDynamicKVCache(page_size=16, max_active_pages=2, max_fp8_pages=2, max_int8_pages=2,
+                                max_int4_pages=2, max_int2_pages=2, max_one_bit_pages=8, sink_tokens=4)
+    g = torch.Generator().manual_seed(13)
+    kv = lambda n: (torch.randn(B, H, n, D, generator=g) * 1.5).half().cuda()  # noqa: E731
+    cache.push_new_tokens(kv(100), kv(100))
+    q0 = (torch.randn(B, H * G, 1, D, generator=g) / 8).half().cuda()
+    cache.attend(q0)
+    builds = cache.plan_builds
+    demotions = cache.total_demotions
+    times = []
+    for step in range(60):
+        cache.push_new_tokens(kv(1), kv(1))
+        q = (torch.randn(B, H * G, 1, D, generator=g) / 8).half()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = cache.attend(q.cuda()) if step % 2 else cache.inplace_paged_attention(q.cuda())
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+        got = host(out).astype(np.float64)
+        K, V = cache.get_all_keys_values()
+        ref = oracle.sdpa_f64(q.numpy(), host(K), host(V), 1.0 / math.sqrt(D))
+        bar = 2e-3 + np.abs(ref) * 2.0 ** -11
+        assert (np.abs(got - ref) <= bar).all(), (step, np.abs(got - ref).max())
+    assert not cache.jl_pages
+    assert cache.total_demotions - demotions >= 3  # pages formed and moved down the cascade meanwhile
+    assert cache.plan_builds == builds, (cache.plan_builds, builds)
