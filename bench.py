@@ -34,6 +34,8 @@ Further workloads (not the headline line) are measured by the same script:
                                                    # pinned host memory, streamed under the resident tiers
     python bench.py --workload tinyllama-sidecars  # TinyLlama-shaped layer: H_q 32, H_kv 4, D 64, 4096
                                                    # tokens, 3840 in INT8 pages with outlier sidecars
+    python bench.py --workload llama3-8b-sidecars  # the Llama-3-8B layer with sigma-3 outlier sidecars on
+                                                   # every quantized page, with and without the corrections
     python bench.py --workload cascade             # pack/unpack of every tier, 1M tokens x 8 heads x 128
 
 --impl reference times the CPU restatement of the reference's path (dequantize every page, then
@@ -699,6 +701,70 @@ def _tinyllama_cpu(k, v, q, Pt, HQt, min_seconds=10.0):
                       f"({n * dt:.1f} s of CPU work)"}
 
 
+def run_8b_sidecars(args):
+    """The Llama-3-8B mixed-tier layer (B 8, 32 q / 8 KV heads, D 128, 32K context, every tier) with
+    the reference's outlier isolation (sigma 3, core/memory_manager.py:89-113) applied to every
+    quantized page before it is quantized, its COO sidecars attached as correction blocks that the
+    fused kernel applies while reading the pages compressed.  Timed with and without the
+    corrections; bytes = compressed pages + correction blocks."""
+    import torch
+
+    from argus_b200 import attention as A
+    from argus_b200 import paged
+    from argus_b200.core.memory_manager import isolate_outliers
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    arenas, pages, entries, block_bytes = [], [], 0, 0
+    for tier, ntok in SPLIT:
+        n = ntok // P
+        k = torch.randn(n, B, HKV, P, D, device=dev, generator=g).half()
+        v = torch.randn(n, B, HKV, P, D, device=dev, generator=g).half()
+        a = A.KVArena.allocate(A.TIER_NAMES[tier], B, HKV, n, P, D, dev)
+        if tier == "fp16":
+            a.write_pages(0, k, v)
+        else:
+            for j in range(n):
+                kn, ko, km = isolate_outliers(k[j], 3.0)
+                vn, vo, vm = isolate_outliers(v[j], 3.0)
+                paged.quantize_page(a, j, kn, vn)
+                ki, kv_ = paged.outliers_to_coo(km, ko)
+                vi, vv_ = paged.outliers_to_coo(vm, vo)
+                paged.attach_outliers(a, j, ki, kv_, vi, vv_)
+                entries += ki.shape[0] + vi.shape[0]
+                block_bytes += a._outlier_blocks[j].numel()
+        del k, v
+        arenas.append(a)
+        pages += [(len(arenas) - 1, j, P) for j in range(n)]
+    torch.cuda.synchronize()
+    plan = A.AttentionPlan(arenas, pages, batch=B, heads_kv=HKV, group=HQ // HKV, head_dim=D)
+    bare_arenas = [A.KVArena(a.tier, a.layout, a.k, a.v, bh_stride=a.bh_stride, record_bytes=a.record_bytes,
+                             page_tokens=P, head_dim=D, batch=B, heads=HKV, slots=a.slots) for a in arenas]
+    bare = A.AttentionPlan(bare_arenas, pages, batch=B, heads_kv=HKV, group=HQ // HKV, head_dim=D)
+    q = (torch.randn(B, HQ, 1, D, device=dev, generator=g) / math.sqrt(D)).half()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    with ClockSampler(vis.split(",")[0] if vis else "0") as clk:
+        ms = statistics.median(_windows(lambda: plan.run(q), args.steps, 1, dev, min_seconds=args.min_seconds))
+        ms_bare = statistics.median(_windows(lambda: bare.run(q), args.steps, 1, dev, min_seconds=0.3))
+    hbm, peak_kind = peaks()
+    nbytes = plan.compressed_bytes + block_bytes
+    values = sum(2 * B * HKV * n * D for t, n in SPLIT if t != "fp16")
+    print(json.dumps({"metric": "Llama-3-8B layer decode with outlier sidecars (sigma 3) on every quantized page, "
+                                "KV tokens/s", "value": B * L / (ms * 1e-3), "unit": "KV tokens/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "dtype": "fp16", "data": "synthetic",
+                      "config": {"workload": "llama3-8b-sidecars", "batch": B, "q_heads": HQ, "kv_heads": HKV,
+                                 "head_dim": D, "context": L, "page_size": P, "tiers_oldest_first": dict(SPLIT),
+                                 "sigma": 3.0, "outlier_entries": entries,
+                                 "outlier_density": entries / max(1, values), "correction_block_bytes": block_bytes},
+                      "without_sidecars_ms": ms_bare, "sidecar_cost": ms / ms_bare,
+                      "fp16_rebuild_equivalent_ms": 2 * B * HKV * L * D * 2 / (hbm * 1e9) * 1e3,
+                      "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": hbm,
+                                   "unit": "GB/s", "frac": nbytes / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
+                                   "algorithmic_bytes_per_launch": nbytes},
+                      "clocks": clk.summary()}), flush=True)
+
+
 def run_70b(args, rank, world, local_rank):
     """Llama-3-70B layer: B 64, H_q 64, H_kv 8, D 128, context 131072 with the 8B tier ratios x4
     (8.98 GB compressed).  Sharded by KV head over the ranks (rank r holds heads [8r/N, 8(r+1)/N) of
@@ -882,7 +948,7 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the K-step timed window until this much device time has passed")
     ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b", "tinyllama-sidecars",
-                                           "cascade"), default="llama3-8b-layer")
+                                           "llama3-8b-sidecars", "cascade"), default="llama3-8b-layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "jl-archive":
@@ -890,6 +956,9 @@ def main():
         return
     if args.workload == "tinyllama-sidecars":
         run_tinyllama_sidecars(args)
+        return
+    if args.workload == "llama3-8b-sidecars":
+        run_8b_sidecars(args)
         return
     if args.workload == "cascade":
         run_cascade(args)
