@@ -228,14 +228,15 @@ def test_decode_steps_across_demotions_keep_the_launch_tables(tmp_path, monkeypa
     for step in range(60):
         cache.push_new_tokens(kv(1), kv(1))
         q = (torch.randn(B, H * G, 1, D, generator=g) / 8).half()
+        # the reference K/V before the call: inplace_paged_attention may resurrect pages afterwards
+        K, V = cache.get_all_keys_values()
+        ref = oracle.sdpa_f64(q.numpy(), host(K), host(V), 1.0 / math.sqrt(D))
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         out = cache.attend(q.cuda()) if step % 2 else cache.inplace_paged_attention(q.cuda())
         torch.cuda.synchronize()
         times.append(time.perf_counter() - t0)
         got = host(out).astype(np.float64)
-        K, V = cache.get_all_keys_values()
-        ref = oracle.sdpa_f64(q.numpy(), host(K), host(V), 1.0 / math.sqrt(D))
         bar = 2e-3 + np.abs(ref) * 2.0 ** -11
         assert (np.abs(got - ref) <= bar).all(), (step, np.abs(got - ref).max())
     assert not cache.jl_pages
