@@ -568,9 +568,11 @@ class PagedDynamicKVCache:
         if tier not in _TIERS and tier != "jl":
             return
         k, v = self._dequant_with_sidecars(tier, page)
-        if tier in _TIERS:
-            self._slot(tier, page["pool_idx"], False)
         attr = "jl_pages" if tier == "jl" else _TIERS[tier][0]
+        # a page listed for resurrection may have been moved by an earlier resurrection's cascade in the
+        # same call (the reference resurrects it anyway); its old slot then holds another page
+        if tier in _TIERS and any(p is page for p in getattr(self, attr)):
+            self._slot(tier, page["pool_idx"], False)
         setattr(self, attr, [p for p in getattr(self, attr) if p is not page])
         dt = (time.perf_counter() - t0) * 1000
         self.total_dequant_time += dt

@@ -215,8 +215,10 @@ def test_decode_steps_across_demotions_keep_the_launch_tables(tmp_path, monkeypa
     monkeypatch.setenv("ARGUS_LOG_LEVEL", "quiet")
     monkeypatch.chdir(tmp_path)
     B, H, G, D = 1, 2, 4, 64
-    cache = PagedDynamicKVCache(page_size=16, max_active_pages=2, max_fp8_pages=2, max_int8_pages=2,
-                                max_int4_pages=2, max_int2_pages=2, max_one_bit_pages=8, sink_tokens=4)
+    # tiers with room enough that the cascade (and the resurrections' churn) stays above the JL archive,
+    # which 16-token pages attend through the scratch arena and so would rebuild the tables
+    cache = PagedDynamicKVCache(page_size=16, max_active_pages=4, max_fp8_pages=4, max_int8_pages=4,
+                                max_int4_pages=4, max_int2_pages=4, max_one_bit_pages=16, sink_tokens=4)
     g = torch.Generator().manual_seed(13)
     kv = lambda n: (torch.randn(B, H, n, D, generator=g) * 1.5).half().cuda()  # noqa: E731
     cache.push_new_tokens(kv(100), kv(100))
@@ -241,4 +243,5 @@ def test_decode_steps_across_demotions_keep_the_launch_tables(tmp_path, monkeypa
         assert (np.abs(got - ref) <= bar).all(), (step, np.abs(got - ref).max())
     assert not cache.jl_pages
     assert cache.total_demotions - demotions >= 3  # pages formed and moved down the cascade meanwhile
+    assert cache.num_resurrections > 0
     assert cache.plan_builds == builds, (cache.plan_builds, builds)
