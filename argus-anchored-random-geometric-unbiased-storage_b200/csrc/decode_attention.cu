@@ -681,10 +681,8 @@ __device__ __forceinline__ void softmax_update(const float (&x)[NT][4], SoftmaxS
 //
 // Head dims up to 128 scatter the tile's deltas into a dense fp16 16 x D tile in the warp's shared
 // memory (zero between uses, stored in MMA fragment order) and run it through the same tensor-core
-// MMAs as the tile itself, so the cost hardly depends on how many outliers a tile has.  Each delta
-// enters as fp16(delta): the corrected key or value is the dequantized one plus the delta rounded to
-// fp16 once more, a relative 2^-12 of the outlier's value (the reference holds the sidecar value
-// exactly; the attention tests bound the difference).  These kernels run 3 CTAs per SM to make room
+// MMAs as the tile itself, so the cost hardly depends on how many outliers a tile has; deltas that
+// fp16 does not hold exactly take a second pass with the remainder.  These kernels run 3 CTAs per SM to make room
 // for the tiles.  Head dim 256 walks each lane's own entries (keys by the token pair whose scores
 // the lane holds, values by the dims of the outputs it holds), using a 512-byte buffer per warp.
 __host__ __device__ constexpr bool side_dense(int D) { return D <= 128; }
@@ -739,49 +737,62 @@ __device__ __forceinline__ void load_delta_frags(const unsigned char* buf, uint3
 }
 
 // This lane's share of a tile's key or value entries, ready to store: positions (halves of the
-// fragment-ordered tile, -1 = none) and fp16(delta) of each.
+// fragment-ordered tile, -1 = none) and fp16 hi | lo << 16 of each delta.
 struct DeltaSlots {
     int pos[2];
-    unsigned short h[2];
+    uint32_t hl[2];
 };
 
 template <int D>
-__device__ __forceinline__ void delta_slot(uint2 raw, bool key, int tb, int ntok, int& pos, unsigned short& h) {
+__device__ __forceinline__ void delta_slot(uint2 raw, bool key, int tb, int ntok, int& pos, uint32_t& hl) {
     const int tok = (int)(raw.x & 0xffffu) - tb, d = (int)(raw.x >> 16);
     pos = -1;
-    h = 0;
+    hl = 0u;
     if (tok < 0 || tok >= ntok || d >= D) return;
+    const float delta = __uint_as_float(raw.y);
+    const __half hi = __float2half_rn(delta);
+    const __half lo = __float2half_rn(delta - __half2float(hi));
     pos = key ? k_half<D>(tok, d) : v_half<D>(tok, d);
-    h = __half_as_ushort(__float2half_rn(__uint_as_float(raw.y)));
+    hl = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
 }
 
-// Prepares this lane's slots for its first two entries (loaded as the tile starts).
+// Prepares this lane's slots; returns (warp-uniform) whether any delta has a nonzero fp16 remainder.
 template <int D>
-__device__ __forceinline__ void delta_slots(const OutlierTile& ot, bool key, int ntok, DeltaSlots& ds) {
+__device__ __forceinline__ bool delta_slots(const OutlierTile& ot, bool key, int ntok, DeltaSlots& ds) {
     const int lane = threadIdx.x & 31;
     const int e0 = key ? ot.k0 : ot.v0, e1 = key ? ot.k1 : ot.v1;
+    bool rem = false;
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
         ds.pos[u] = -1;
-        ds.h[u] = 0;
-        if (e0 + 32 * u + lane < e1) delta_slot<D>(key ? ot.ke[u] : ot.ve[u], key, 16 * ot.ti, ntok, ds.pos[u], ds.h[u]);
+        ds.hl[u] = 0u;
+        if (e0 + 32 * u + lane < e1) {
+            delta_slot<D>(key ? ot.ke[u] : ot.ve[u], key, 16 * ot.ti, ntok, ds.pos[u], ds.hl[u]);
+            rem |= (ds.hl[u] >> 16) != 0u;
+        }
     }
+    for (int e = e0 + 64 + lane; e < e1; e += 32) {  // tiles with more than 64 entries
+        int pos;
+        uint32_t hl;
+        delta_slot<D>(__ldg(ot.ent + e), key, 16 * ot.ti, ntok, pos, hl);
+        rem |= (hl >> 16) != 0u;
+    }
+    return __any_sync(0xffffffffu, rem);
 }
 
-// Stores the slots' deltas (clear: zeros) into the dense tile, and those of any entries past the
-// first 64.
+// Stores pass 0: hi, 1: lo, 2: zero of the slots (and of any entries past the first 64).
 template <int D>
-__device__ __forceinline__ void store_deltas(const OutlierTile& ot, bool key, int ntok, const DeltaSlots& ds, bool clear) {
+__device__ __forceinline__ void store_deltas(const OutlierTile& ot, bool key, int ntok, const DeltaSlots& ds, int pass) {
     unsigned short* buf = reinterpret_cast<unsigned short*>(ot.buf);
 #pragma unroll
     for (int u = 0; u < 2; ++u)
-        if (ds.pos[u] >= 0) buf[ds.pos[u]] = clear ? (unsigned short)0 : ds.h[u];
+        if (ds.pos[u] >= 0) buf[ds.pos[u]] = pass == 2 ? (unsigned short)0 : (unsigned short)(ds.hl[u] >> (16 * pass));
     const int e0 = key ? ot.k0 : ot.v0, e1 = key ? ot.k1 : ot.v1;
-    for (int e = e0 + 64 + (threadIdx.x & 31); e < e1; e += 32) {  // tiles with more than 64 entries
+    for (int e = e0 + 64 + (threadIdx.x & 31); e < e1; e += 32) {
         int pos;
-        unsigned short h;
-        delta_slot<D>(__ldg(ot.ent + e), key, 16 * ot.ti, ntok, pos, h);
-        if (pos >= 0) buf[pos] = clear ? (unsigned short)0 : h;
+        uint32_t hl;
+        delta_slot<D>(__ldg(ot.ent + e), key, 16 * ot.ti, ntok, pos, hl);
+        if (pos >= 0) buf[pos] = pass == 2 ? (unsigned short)0 : (unsigned short)(hl >> (16 * pass));
     }
     __syncwarp();
 }
@@ -793,19 +804,20 @@ __device__ __forceinline__ void dense_k_outliers(const OutlierTile& ot, uint32_t
     if (ot.k0 >= ot.k1) return;
     constexpr int KC = D / 16;
     DeltaSlots ds;
-    delta_slots<D>(ot, true, ntok, ds);
+    const bool rem = delta_slots<D>(ot, true, ntok, ds);
     uint32_t qf[KC][2];
     load_qfrags<D>(qs, threadIdx.x & 31, qf);
     float s[4] = {0.f, 0.f, 0.f, 0.f};
-    store_deltas<D>(ot, true, ntok, ds, false);
-    {
+    for (int pass = 0; pass < 2; ++pass) {
+        store_deltas<D>(ot, true, ntok, ds, pass);
         uint32_t a[KC][4];
         load_delta_frags<D>(ot.buf, a);
 #pragma unroll
         for (int c = 0; c < KC; ++c) mma16816(s, a[c], qf[c][0], qf[c][1]);
+        __syncwarp();  // every lane has its fragments before the tile is rewritten
+        if (!rem) break;
     }
-    __syncwarp();  // every lane has its fragments before the tile is cleared
-    store_deltas<D>(ot, true, ntok, ds, true);
+    store_deltas<D>(ot, true, ntok, ds, 2);
     x[0] += s[0] * scale_log2;
     x[1] += s[1] * scale_log2;
     x[2] += s[2] * scale_log2;
@@ -819,9 +831,9 @@ __device__ __forceinline__ void dense_v_outliers(const OutlierTile& ot, int ntok
     if (ot.v0 >= ot.v1) return;
     constexpr int KC = D / 16;
     DeltaSlots ds;
-    delta_slots<D>(ot, false, ntok, ds);
-    store_deltas<D>(ot, false, ntok, ds, false);
-    {
+    const bool rem = delta_slots<D>(ot, false, ntok, ds);
+    for (int pass = 0; pass < 2; ++pass) {
+        store_deltas<D>(ot, false, ntok, ds, pass);
         uint32_t av[KC][4];
         load_delta_frags<D>(ot.buf, av);
 #pragma unroll
@@ -829,9 +841,10 @@ __device__ __forceinline__ void dense_v_outliers(const OutlierTile& ot, int ntok
             mma16816(o[t], av[t], b01, b23);
             if constexpr (PRECISE) mma16816(o[t], av[t], c01, c23);
         }
+        __syncwarp();
+        if (!rem) break;
     }
-    __syncwarp();
-    store_deltas<D>(ot, false, ntok, ds, true);
+    store_deltas<D>(ot, false, ntok, ds, 2);
 }
 
 // q[n][d] of the CTA's query group from the Q^T fragments in shared memory (load_qfrags layout:
