@@ -213,6 +213,7 @@ class PagedDynamicKVCache:
         self._buf_live_host = None
         self._jl_ops = None
         self.plan_builds = 0
+        self.fused_causal_page_steps = 0  # causal steps whose masked tail reached into the active pages
         # attend JL pages without rebuilding them (argus_b200.core.jl.JLAttention) when their shape
         # allows it (128-row blocks, i.e. 512-token pages, head_dim 128, <= 8 queries per kv head)
         self.fused_jl_attention = True
@@ -925,31 +926,68 @@ class PagedDynamicKVCache:
         return _jl.merge_attention(out, lse, out_j, lse_j)
 
     def newest_in_buffer(self, n):
-        """True when the newest n cached tokens all sit in the fp16 staging buffer, which is what
-        attend(causal=True) reads them from without rebuilding the compressed pages."""
+        """True when the newest n cached tokens all sit in the fp16 staging buffer."""
         return self.k_buffer is not None and self.buffer_length >= n
 
-    def _attend_causal(self, q, scale):
-        """attend(causal=True): the newest q_len tokens (in the staging buffer) under the causal
-        mask, everything older through the fused kernel, joined by LSE.  When the newest tokens
-        are not all in the buffer (a page was just formed from them), the full K/V is rebuilt."""
-        B, Hq, qlen, D = q.shape
+    def causal_tail_pages(self, n):
+        """The causal mask of a step of n tokens is bottom-right over the reference's concatenation
+        order (..., FP8, active pages in list order, staging buffer): its last n entries are the
+        masked ones.  Returns how many of the last active pages those entries reach into past the
+        staging buffer (0: all in the buffer), or None when they reach past the active pages."""
         nbuf = self.buffer_length if self.k_buffer is not None else 0
-        if nbuf < qlen:
+        if nbuf >= n:
+            return 0
+        m = -(-(n - nbuf) // self.page_size)
+        return m if m <= len(self.active_pages) else None
+
+    def fused_causal_ok(self, n):
+        """attend(q, causal=True) with n queries runs the fused kernel (no K/V rebuild)."""
+        return self.causal_tail_pages(n) is not None
+
+    def _attend_causal(self, q, scale):
+        """attend(causal=True): the masked tail of the concatenation (the newest q_len entries, see
+        causal_tail_pages) under the causal mask, everything before it through the fused kernel,
+        joined by LSE.  The tail is the end of the staging buffer, or, when a page has just formed
+        from the step's tokens, the last m active pages plus the whole buffer: those pages' slots
+        are marked dead for the fused launch (slot occupancy) and attended with the tail instead.
+        When the tail reaches past the active pages (a prefill into a fresh cache), K/V are rebuilt."""
+        B, Hq, qlen, D = q.shape
+        m = self.causal_tail_pages(qlen)
+        if m is None:
             K, V = self.get_all_keys_values()
             return _causal_sdpa(q, K, V, scale)
-        k_new = self.static_k_buffer[..., nbuf - qlen:nbuf, :]
-        v_new = self.static_v_buffer[..., nbuf - qlen:nbuf, :]
+        nbuf = self.buffer_length if self.k_buffer is not None else 0
+        P = self.page_size
+        tail_pages = self.active_pages[len(self.active_pages) - m:] if m else []
+        if m:
+            k_new = torch.cat([p["key"] for p in tail_pages] + [self.static_k_buffer[..., :nbuf, :]], dim=-2)
+            v_new = torch.cat([p["value"] for p in tail_pages] + [self.static_v_buffer[..., :nbuf, :]], dim=-2)
+        else:
+            k_new = self.static_k_buffer[..., nbuf - qlen:nbuf, :]
+            v_new = self.static_v_buffer[..., nbuf - qlen:nbuf, :]
         out_n, lse_n = _causal_sdpa(q, k_new, v_new, scale, with_lse=True)
-        older = nbuf - qlen + self.page_size * (len(self.active_pages) +
-                                                sum(len(lst) for _, lst in self._compressed_order()))
+        older = P * (len(self.active_pages) - m + sum(len(lst) for _, lst in self._compressed_order()))
+        older += (nbuf - qlen) if not m else 0
         older += self.sink_k.shape[-2] if self.sink_k is not None else 0
         older += self.anchor_k.shape[-2] if self.anchor_k is not None else 0
         if older == 0:
             return out_n
-        plan = self._attention_plan(q, tail=qlen)
+        plan = self._attention_plan(q, tail=nbuf if m else qlen)
         lse = torch.empty(B, Hq, qlen, dtype=torch.float32, device=q.device)
-        out = plan.run(q, scale=scale, lse=lse)
+        if m:
+            self.fused_causal_page_steps += 1
+            live = self._live_host["fp16"]
+            saved = live.copy()
+            for p in tail_pages:
+                live[p["pool_idx"]] = 0
+            self.arenas["fp16"].slot_live.copy_(torch.from_numpy(live))
+            try:
+                out = plan.run(q, scale=scale, lse=lse)
+            finally:
+                live[:] = saved
+                self.arenas["fp16"].slot_live.copy_(torch.from_numpy(live))
+        else:
+            out = plan.run(q, scale=scale, lse=lse)
         if plan.jl is not None:
             out_j, lse_j = plan.jl["att"].run(q, plan.jl["yk"], plan.jl["yv"], scale=scale)
             lse_t = torch.empty_like(lse)

@@ -13,8 +13,9 @@ the compressed pages, so the full K/V is never rebuilt (JL pages the fused JL ke
 take pass through the manager's fp16 scratch arena).  A step of several new tokens (speculative
 or chunked decoding) takes the same route when those tokens are still in the staging buffer: the
 kernel attends to everything older and the new tokens attend to one another under the causal
-mask, joined by LSE.  A prefill into an empty cache, a step whose tokens just formed a page, and
-padded batches rebuild K/V and run transformers' SDPA.
+mask, joined by LSE; a step whose tokens just formed a page takes the same route, the newest active
+pages joining the causal part.  A prefill whose tokens reach past the active pages (into tiers
+compressed during the prefill itself) and padded batches rebuild K/V and run transformers' SDPA.
 """
 import torch
 
@@ -147,7 +148,7 @@ def argus_attention_forward(module, query, key, value, attention_mask, dropout=0
         return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
                                       is_causal=is_causal, **kwargs)
     if attention_mask is None and dropout == 0.0 and query.dtype == torch.float16 and \
-            (ql == 1 or (causal and cache.newest_in_buffer(ql))):
+            (ql == 1 or (causal and cache.fused_causal_ok(ql))):
         out = cache.attend(query.contiguous(), scale=scaling, causal=ql > 1)
         return out.transpose(1, 2).contiguous(), None
     K, V = cache.get_all_keys_values()

@@ -245,3 +245,40 @@ def test_decode_steps_across_demotions_keep_the_launch_tables(tmp_path, monkeypa
     assert cache.total_demotions - demotions >= 3  # pages formed and moved down the cascade meanwhile
     assert cache.num_resurrections > 0
     assert cache.plan_builds == builds, (cache.plan_builds, builds)
+
+
+def test_causal_steps_that_form_pages_run_fused(tmp_path, monkeypatch):
+    """A step of several tokens whose tokens just formed a page (the masked tail of the concatenation
+    reaches one or two active pages past the staging buffer): attend(causal=True) runs the fused kernel
+    with those pages' slots left out and attends them with the step's causal part, matching float64
+    attention over the rebuilt K/V under the bottom-right causal mask."""
+    import oracle
+    from argus_b200.core.memory_manager import PagedDynamicKVCache
+    monkeypatch.setenv("ARGUS_LOG_LEVEL", "quiet")
+    monkeypatch.chdir(tmp_path)
+    B, H, G, D = 2, 2, 4, 64
+    cache = PagedDynamicKVCache(page_size=16, max_active_pages=4, max_fp8_pages=2, max_int8_pages=2,
+                                max_int4_pages=2, max_int2_pages=2, max_one_bit_pages=8, sink_tokens=4)
+    g = torch.Generator().manual_seed(17)
+    kv = lambda n: (torch.randn(B, H, n, D, generator=g) * 1.5).half().cuda()  # noqa: E731
+    scale = 1.0 / math.sqrt(D)
+    cache.push_new_tokens(kv(4 + 16 * 6 + 14), kv(4 + 16 * 6 + 14))  # sinks, 6 pages, 14 in the buffer
+    fused_before = cache.fused_causal_page_steps
+    for ql, want_pages in ((3, 1), (40, 2), (5, 0)):
+        cache.push_new_tokens(kv(ql), kv(ql))
+        assert cache.causal_tail_pages(ql) == want_pages, (ql, cache.buffer_length)
+        q = (torch.randn(B, H * G, ql, D, generator=g) / 8).half()
+        K, V = (host(t) for t in cache.get_all_keys_values())
+        out = host(cache.attend(q.cuda(), causal=True)).astype(np.float64)
+        L = K.shape[-2]
+        ref = np.stack([oracle.sdpa_f64(q.numpy()[:, :, i:i + 1], K[:, :, :L - ql + i + 1], V[:, :, :L - ql + i + 1],
+                                        scale)[:, :, 0] for i in range(ql)], axis=2)
+        bar = 2e-3 + np.abs(ref) * 2.0 ** -10
+        assert (np.abs(out - ref) <= bar).all(), (ql, np.abs(out - ref).max())
+    assert cache.fused_causal_page_steps - fused_before == 2
+    # the occupancy the launch borrowed is back: a decode step sees every cached token
+    q1 = (torch.randn(B, H * G, 1, D, generator=g) / 8).half()
+    K, V = (host(t) for t in cache.get_all_keys_values())
+    out1 = host(cache.attend(q1.cuda())).astype(np.float64)
+    ref1 = oracle.sdpa_f64(q1.numpy(), K, V, scale)
+    assert (np.abs(out1 - ref1) <= 2e-3 + np.abs(ref1) * 2.0 ** -11).all()
