@@ -137,9 +137,8 @@ class JLAttention:
             n_splits = 1
         n_ctas = int(n_ctas or 0)
         if n_splits is None:
-            # one CTA per SM (each holds two 64 KB block pairs) sharing all heads' block pairs evenly
-            pack = 2 if (Hq // Hkv) * qlen <= 4 else 1
-            n_ctas = min(148, B * Hkv * ((nb + pack - 1) // pack))
+            # one CTA per SM, sharing all heads' blocks in equal contiguous ranges
+            n_ctas = min(148, B * Hkv * nb)
             n_splits = 1
         n_splits = max(1, min(int(n_splits), max(1, nb)))
         return JLShapeC(B, Hkv, Hq // Hkv, qlen, D, MJ, self.N, nb, n_splits, n_ctas,

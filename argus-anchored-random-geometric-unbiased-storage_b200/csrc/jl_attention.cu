@@ -2,25 +2,32 @@
 //
 // The reference rebuilds each archived block as K = R . Yk, V = R . Yv (R = A^-1 W^T (W A^-1 W^T)^-1,
 // core/memory_manager.py:241-282, 1176-1178) and runs softmax attention over the rebuilt tokens.
-// Because the reconstruction is linear, the same attention is
-//     s = R . (Yk . q^T)          scores of the block's N tokens      (N x MJ) . (MJ x Q)
-//     w = R^T . p                 softmax weights folded back         (MJ x N) . (N x Q)
-//     o += Yv^T . w               output contribution                 (D x MJ) . (MJ x Q)
-// which costs 2*N*MJ*Q + 2*MJ*D*Q multiply-adds per block instead of 2*N*MJ*D (K and V rebuilt)
-// plus the attention itself.  All contractions run on the tensor cores (mma.sync m16n8k16, fp32
-// accumulation; u, p and w enter as fp16 hi + lo pairs).  R and R^T are stored once in MMA fragment
-// order so every operand load is one coalesced 16-byte read per lane from L2.
+// Because the reconstruction is linear, the same attention is, per block and query,
+//     u = Yk . q^T                 (MJ)        the query seen through the block's key rows
+//     s = R . u                    (N)         scores of the block's N tokens
+//     w = R^T . softmax(s)         (MJ)        softmax weights folded back onto the rows
+//     o = Yv^T . w                 (D)         output contribution
+// and every block of a kv head shares the one operator R [N x MJ].  So one CTA stacks the (block,
+// query) pairs of its blocks as the 128 rows of a tensor-memory tile and streams R past them once:
 //
-// The CTAs (8 warps each) share the block pairs of all (batch, kv_head) in equal contiguous ranges,
-// so every SM gets the same work whatever the head count; a range that spans two heads yields a
-// partial for each, and the last CTA to finish a head merges its partials.  With at most 4 queries
-// per kv head two archive blocks share the 8 query columns of every MMA.  Per block pair: warp w forms u rows 16w..16w+15,
-// then streams token tiles w, w+8, ... through scores, online softmax (per column, log2 domain)
-// and w accumulation; the warps' partial w merge in shared memory; warp w then adds Yv^T . w for
-// dims 16w..16w+15.  Yk / Yv blocks arrive by TMA tensor copies in 128-byte swizzle (two 64-column
-// halves of 128 rows x 128 bytes, 16-byte chunk c of row r stored at chunk c ^ (r % 8)) so the
-// ldmatrix reads of both contractions are free of bank conflicts; each buffer is refilled as soon as
-// it is consumed.
+//   U phase   Yk blocks arrive by TMA (128-byte swizzle); the warps form u with mma.sync, stage U^T
+//             (rows = block-query pairs, fp16 hi + lo) in shared memory, and warps 0-3 move their
+//             rows into tensor memory (the A operand of the scores).
+//   SW phase  for each 64-token chunk c of R: S_c = U^T . R_c^T (tcgen05.mma, A from tensor memory,
+//             M 128, N 64, fp32); warps 0-3 (one row per thread) run the online softmax of their row
+//             in the log2 domain and write P_c (fp16) over the first half of S_c; W += P_c . R_c
+//             (tcgen05.mma, A = P_c from tensor memory, M 128, N = MJ, fp32).  One thread issues the
+//             MMAs and the copies of the operator chunks (16 KB of R, 16 KB of R^T, laid out as
+//             K-major operands in 128-byte swizzle by argus_jl_operator_fragments); the first Yv
+//             blocks stream in meanwhile.
+//   O phase   the W rows, scaled to a common max per (kv head, query), go to shared memory (hi + lo);
+//             Yv blocks arrive by TMA and the warps add Yv^T . w with mma.sync.
+//
+// R is read from L2 once per CTA and round instead of once per block pair, the two large
+// contractions run on the 5th-generation tensor cores, and their A operands never leave tensor
+// memory.  CTAs take equal contiguous ranges of all (batch, kv_head) blocks; a range is processed
+// in rounds of at most 128 / (queries per kv head) blocks; a range that spans heads yields one
+// partial per head and the last CTA to finish a head merges its partials.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -33,22 +40,32 @@ namespace jla {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kD = 128;   // head_dim
-constexpr int kMJ = 128;  // rows per archived block
-constexpr int kCols = 8;  // query columns per MMA
+constexpr int kD = 128;      // head_dim
+constexpr int kMJ = 128;     // rows per archived block
+constexpr int kRows = 128;   // (block, query) rows per round = tensor-memory lanes
+constexpr int kChunk = 64;   // operator tokens per SW step
+constexpr int kCols = 8;     // query columns of the CUDA-core MMAs (queries per kv head <= 8)
+constexpr int kSlots = 4;    // 32 KB shared-memory slots
+constexpr uint32_t kSlotBytes = (uint32_t)kMJ * kD * 2;          // one Yk / Yv block
+constexpr uint32_t kOpChunkBytes = (uint32_t)kChunk * kMJ * 2;   // R_c or R^T_c
 constexpr long long kSpinLimit = 1ll << 26;
 constexpr float kNoMax = -1.0e30f;
-constexpr float kSlack = 8.0f;
+constexpr float kSlack = 8.0f;  // a row's reference max is raised only when a score passes it by 2^8
+// tensor memory: three S / P buffers (64 columns each; P, fp16, overwrites the first 32 of its S),
+// W (128 fp32 columns), U^T hi and lo (64 columns each: two fp16 per column)
+constexpr int kSBufs = 3;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemW = kSBufs * kChunk;        // 192
+constexpr uint32_t kTmemUhi = kTmemW + kMJ;         // 320
+constexpr uint32_t kTmemUlo = kTmemUhi + kMJ / 2;   // 384
 
 __device__ int g_status = 0;
 
 struct Params {
     CUtensorMap tmk;    // Yk as [B*Hkv][n_blocks][MJ][D], box 64 x MJ, 128-byte swizzle
     CUtensorMap tmv;    // Yv, same
-    const __half* yk;   // block j of (b, h) at yk + bh * bh_stride + j * block_stride
-    const __half* yv;
-    const uint4* rf;    // R [N x MJ] in A-fragment order: [N/16][MJ/16][32 lanes]
-    const uint4* rtf;   // R^T [MJ x N] in A-fragment order: [MJ/16][N/16][32 lanes]
+    const unsigned char* rop;   // R chunks: [N/64][16 KB], B operand of S (N = tokens, K = MJ)
+    const unsigned char* rtop;  // R^T chunks: [N/64][16 KB], B operand of W (N = MJ, K = tokens)
     const __half* q;    // [B, Hkv*G, qlen, D]
     __half* out;
     float* lse;
@@ -56,20 +73,30 @@ struct Params {
     float* part_o;      // [B*Hkv][S][8][D]  (S: partial slots per (b, h))
     float* part_lse;    // [B*Hkv][S][8]
     int* counters;      // [B*Hkv]
-    int64_t bh_stride, block_stride;  // elements
     int B, Hkv, G, qlen, n_blocks, N, S;
     float scale_log2;
 };
 
-constexpr int kRowPad = kMJ + 8;  // u^T / w^T row stride in halves (272 bytes: conflict-free reads)
+// Shared memory (offsets from a 1024-byte aligned base)
+constexpr uint32_t kOffU = 0;                                   // U^T staging hi | lo (64 KB) = slots 4, 5
+constexpr uint32_t kOffSlot = 65536;                            // slots 0 .. 3 (32 KB each)
+constexpr uint32_t kOffRow = kOffSlot + kSlots * kSlotBytes;    // mrow, lrow, frow [128] fp32
+constexpr uint32_t kOffSeg = kOffRow + 3 * kRows * 4;           // segM, segL, segA [128] fp32
+constexpr uint32_t kOffOpen = kOffSeg + 3 * kRows * 4;          // openM, openL [8] fp32
+constexpr uint32_t kOffBar = kOffOpen + 2 * kCols * 4;          // mbarriers
+// slot full (6), operator chunk full / empty (4 + 4), S full (3), P full (3), W done (2)
+// and, for rounds of at most 64 rows, lo scores shipped (3)
+constexpr int kBarFull = 0, kBarRF = 6, kBarRE = 10, kBarS = 14, kBarP = 17, kBarW = 20, kBarX = 22, kNumBars = 25;
+constexpr uint32_t kOffCnt = kOffBar + kNumBars * 8;            // per-slot release counters [6]
+constexpr uint32_t kOffMisc = kOffCnt + 8 * 4;                  // tensor-memory base, last flag, chunk counts
+constexpr size_t kSmemBytes = 1024 + kOffMisc + 16;
+static_assert(kSmemBytes <= 232448, "shared memory");
 
-__host__ __device__ constexpr size_t smem_bytes(int pack) {
-    return 1024                                 // alignment of the swizzled tiles
-           + (size_t)2 * pack * kMJ * kD * 2    // Yk, Yv blocks
-           + (size_t)2 * 2 * kCols * kRowPad * 2  // u^T and w^T, fp16 hi / lo
-           + (size_t)kWarps * 32 * 33 * 4       // per-warp partial w (lane stride 33)
-           + (size_t)(2 * kWarps * kCols + kWarps * kCols + 4 * kCols) * 4 + 64;
-}
+// Slot roles.  U phase: Yk block i in slot i % 4, U^T staged in slots 4-5.  SW phase: operator chunk
+// c in slot c % 4 while the first two Yv blocks come into slots 4 and 5.  O phase: W' hi | lo in
+// slots 0-1, Yv block i in slot oslot(i % 4) (4, 5, 2, 3).
+__host__ __device__ constexpr uint32_t oslot(int k) { return k < 2 ? 4u + (uint32_t)k : (uint32_t)k; }
+constexpr int kNumSlots = 6;
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return smem_u32(p); }
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -78,11 +105,6 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
-    uint32_t y;
-    asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
-    return y;
 }
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&a)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -94,19 +116,26 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&a)[4]) {
                  : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
                  : "r"(addr));
 }
-__device__ __forceinline__ uint32_t h2pack(float lo, float hi) {
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
 __device__ __forceinline__ void split_hl(float v, __half& hi, __half& lo) {
     hi = __float2half_rn(v);
     lo = __float2half_rn(v - __half2float(hi));
 }
-__device__ __forceinline__ void mbar_init(uint32_t bar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar));
+// two fp32 -> fp16x2 (hi) and the fp16x2 of their remainders (lo)
+__device__ __forceinline__ void split_hl2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - f.x, b - f.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
     for (long long i = 0; i < kSpinLimit; ++i) {
@@ -120,17 +149,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
     }
     return false;
 }
+// the same wait, decided for the whole warp (tensor-memory accesses that follow are warp-collective)
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t phase) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, phase));
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
 }
-__device__ __forceinline__ uint4 ldg_nc(const uint4* p) {
-    uint4 r;
-    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint32_t bar) {
     asm volatile(
@@ -139,417 +166,655 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// Copies blocks j .. j+nb-1 of (b, h) into `dst` (per block two swizzled 64-column halves) and arms
-// `bar` for the bytes.
-__device__ __forceinline__ void issue_blocks(const CUtensorMap* map, int64_t bh, int j, int nb, __half* dst, uint32_t bar) {
-    constexpr uint32_t bytes = kMJ * kD * 2;
+// Copies block j of (b, h) into `dst` (two swizzled 64-column halves) and arms `bar` for its bytes.
+__device__ __forceinline__ void issue_block(const CUtensorMap* map, int64_t bh, int j, uint32_t dst, uint32_t bar) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, bytes * nb);
-    for (int i = 0; i < nb; ++i) {
-        const uint32_t d = su32(dst + (size_t)i * kMJ * kD);
-        tma_load_4d(d, map, 0, 0, j + i, (int)bh, bar);
-        tma_load_4d(d + kMJ * 128, map, 64, 0, j + i, (int)bh, bar);
-    }
+    mbar_expect_tx(bar, kSlotBytes);
+    tma_load_4d(dst, map, 0, 0, j, (int)bh, bar);
+    tma_load_4d(dst + kMJ * 128, map, 64, 0, j, (int)bh, bar);
+}
+// Copies operator chunk c (R_c then R^T_c, 16 KB each) into `dst` and arms `bar`.
+__device__ __forceinline__ void issue_op_chunk(const Params& p, int c, uint32_t dst, uint32_t bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, 2 * kOpChunkBytes);
+    bulk_g2s(dst, p.rop + (size_t)c * kOpChunkBytes, kOpChunkBytes, bar);
+    bulk_g2s(dst + kOpChunkBytes, p.rtop + (size_t)c * kOpChunkBytes, kOpChunkBytes, bar);
 }
 
-// Shared-memory address of element (row r, column c) of a swizzled [MJ][D] block.
+// Shared-memory address of element (row r, column c) of a swizzled [MJ][D] Y block.
 __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) {
     return base + (uint32_t)((c >> 6) * (kMJ * 128) + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
 }
+// K-major operand in 128-byte swizzle (the layout a TMA copy with SWIZZLE_128B writes): K in blocks of
+// 64 fp16, each block `rows` x 128 bytes, 16-byte chunk c of row r at chunk c ^ (r % 8), 8-row groups
+// 1024 bytes apart.  Byte offset of element (row, k) of a tile with `rows` rows.
+__host__ __device__ __forceinline__ uint32_t sw128(int row, int k, int rows) {
+    return (uint32_t)((k >> 6) * rows * 128 + row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
+}
+// Row-major [row][128] fp16 staging (U^T, W'): 256-byte rows, 16-byte chunk c of row r at c ^ (r % 8).
+__device__ __forceinline__ uint32_t rowsw(int r, int k) {
+    return (uint32_t)(r * 256 + ((((k >> 3) ^ (r & 7))) << 4) + (k & 7) * 2);
+}
 
-template <int PACK>
-__global__ void __launch_bounds__(kThreads, 1) jl_attn_kernel(const __grid_constant__ Params p) {
-    constexpr int KD = kD / 16, KM = kMJ / 16;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    __half* ykbuf = reinterpret_cast<__half*>(smem);               // [PACK][MJ][D] swizzled
-    __half* yvbuf = ykbuf + PACK * kMJ * kD;                        // [PACK][MJ][D]
-    __half* uT = yvbuf + PACK * kMJ * kD;                           // [2][8][MJ + pad]
-    __half* wt = uT + 2 * kCols * kRowPad;                          // [2][8][MJ + pad]
-    float* wpart = reinterpret_cast<float*>(wt + 2 * kCols * kRowPad);  // [warps][32 lanes][33]
-    float* mw = wpart + kWarps * 32 * 33;                           // [warps][8]
-    float* lw = mw + kWarps * kCols;                                // [warps][8]
-    float* fw = lw + kWarps * kCols;                                // [warps][8] merge factors
-    float* mrun = fw + kWarps * kCols;                              // [8]
-    float* lrun = mrun + kCols;                                     // [8]
-    float* alpha = lrun + kCols;                                    // [8]
-    float* beta = alpha + kCols;                                    // [8]
-    uint64_t* bars = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(beta + kCols) + 15) & ~(uintptr_t)15);
+// tcgen05 shared-memory matrix descriptor of a K-major 128-byte-swizzled operand (version 1, stride
+// 1024 bytes between 8-row groups; a K step of 16 fp16 advances the start address by 32 bytes inside
+// the 1024-byte aligned swizzle atom) and kind::f16 instruction descriptor (fp32 accumulator, fp16 A
+// and B, both K-major).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)((1024u >> 4) & 0x3FFFu) << 32) |
+           (1ull << 46) | (2ull << 61);
+}
+__host__ __device__ constexpr uint32_t idesc(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+// the same with A (M 128 x K 16, two fp16 per column) in tensor memory
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+        "r"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+#define JLA_TMEM_LD32(addr, v)                                                                                   \
+    asm volatile(                                                                                                \
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"         \
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                               \
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),         \
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),  \
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),             \
+          "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),             \
+          "=r"(v[30]), "=r"(v[31])                                                                               \
+        : "r"(addr))
+#define JLA_TMEM_ST32(addr, v)                                                                                   \
+    asm volatile(                                                                                                \
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"  \
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(addr),                         \
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),      \
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),          \
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),         \
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])                       \
+        : "memory")
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_constant__ Params p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = su32(sm);
+    float* mrow = reinterpret_cast<float*>(sm + kOffRow);
+    float* lrow = mrow + kRows;
+    float* frow = lrow + kRows;
+    float* segM = reinterpret_cast<float*>(sm + kOffSeg);
+    float* segL = segM + kRows;
+    float* segA = segL + kRows;
+    float* openM = reinterpret_cast<float*>(sm + kOffOpen);
+    float* openL = openM + kCols;
+    int* cnt = reinterpret_cast<int*>(sm + kOffCnt);              // slot release counters
+    uint32_t* misc = reinterpret_cast<uint32_t*>(sm + kOffMisc);  // [0] tensor-memory base, [1] last flag, [2] [3] chunk counts
+    auto bar = [&](int i) { return sbase + kOffBar + 8u * (uint32_t)i; };
+    auto slot = [&](uint32_t s) { return s < 4 ? sbase + kOffSlot + s * kSlotBytes : sbase + kOffU + (s - 4) * kSlotBytes; };
+    const uint32_t uhi = slot(4), ulo = slot(5);  // U^T staging
+    const uint32_t whi = slot(0), wlo = slot(1);  // W' (O phase)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int NQ = p.G * p.qlen;
-    const int qpb = PACK == 2 ? 4 : 8;  // query columns per block
-    const uint32_t ykbar = su32(&bars[0]), yvbar = su32(&bars[1]);
+    const int bpr = kRows / NQ;  // blocks per round
+    const int nchunks = p.N / kChunk;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(misc)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
     if (tid == 0) {
-        mbar_init(ykbar);
-        mbar_init(yvbar);
+        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), (i >= kBarP && i < kBarW) ? 4u : (i >= kBarX ? 2u : 1u));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    __shared__ int last;
-
-    // The block pairs of all (batch, kv_head) groups, group after group, are dealt to the CTAs in
-    // equal contiguous ranges: pair x goes to CTA floor(x C / T).  A CTA whose range crosses groups
-    // finishes one group's segment (a partial) and starts the next.
-    const int64_t groups = (int64_t)p.B * p.Hkv;
-    const int64_t PP = (p.n_blocks + PACK - 1) / PACK, T = groups * PP;
-    const int64_t C = gridDim.x, c = blockIdx.x;
-    const int64_t x_end = ((c + 1) * T + C - 1) / C;
-    bool ok = true;
-    int it = 0;
-    // parity of each buffer's issued copy not yet seen complete (-1: none); kept alike by every
-    // thread, so that after a timed-out wait the CTA waits (bounded) for exactly the copies in flight
-    int yk_pend = -1, yv_pend = -1;
-    for (int64_t xs = (c * T + C - 1) / C; xs < x_end && ok;) {
-    const int64_t bh = xs / PP;
-    const int64_t xe = (x_end < (bh + 1) * PP) ? x_end : (bh + 1) * PP;
-    const int j0 = (int)((xs - bh * PP) * PACK);
-    const int j1 = (int)(((xe - bh * PP) * PACK < p.n_blocks) ? (xe - bh * PP) * PACK : p.n_blocks);
-    const int64_t first_c = bh * PP * C / T, last_c = ((bh + 1) * PP - 1) * C / T;
-    const int n_seg = (int)(last_c - first_c + 1), split = (int)(c - first_c);  // this group's partials
-    xs = xe;
-    const int b = (int)(bh / p.Hkv), h = (int)(bh - (int64_t)b * p.Hkv);
-
-    // query fragments: column n of the U contraction is query n (block A) or n - 4 (block B)
-    uint32_t qa[KD][2], qb[KD][2];
-    {
-        const int na = g, nb_ = g - 4;
-        const bool la = na < (PACK == 2 ? 4 : 8) && na < NQ, lb = PACK == 2 && nb_ >= 0 && nb_ < NQ;
-        const __half* qbase = p.q + (((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G) * p.qlen) * kD;
-#pragma unroll
-        for (int kk = 0; kk < KD; ++kk) {
-            const int d = 16 * kk + 2 * t;
-            qa[kk][0] = la ? *reinterpret_cast<const uint32_t*>(qbase + (int64_t)na * kD + d) : 0u;
-            qa[kk][1] = la ? *reinterpret_cast<const uint32_t*>(qbase + (int64_t)na * kD + d + 8) : 0u;
-            qb[kk][0] = lb ? *reinterpret_cast<const uint32_t*>(qbase + (int64_t)nb_ * kD + d) : 0u;
-            qb[kk][1] = lb ? *reinterpret_cast<const uint32_t*>(qbase + (int64_t)nb_ * kD + d + 8) : 0u;
-        }
-    }
-    if (tid < kCols) {
-        mrun[tid] = kNoMax;
-        lrun[tid] = 0.f;
-    }
+    if (tid < kCols) { openM[tid] = kNoMax; openL[tid] = 0.f; }
+    if (tid < kNumSlots) cnt[tid] = 0;
+    tc_fence_before();
     __syncthreads();
-    if (j0 < j1) {
-        if (tid == 0) {
-            const int nb = (j1 - j0) < PACK ? (j1 - j0) : PACK;
-            issue_blocks(&p.tmk, bh, j0, nb, ykbuf, ykbar);
-            issue_blocks(&p.tmv, bh, j0, nb, yvbuf, yvbar);
-        }
-        yk_pend = yv_pend = it & 1;
-    }
+    tc_fence_after();
+    const uint32_t tmem = misc[0];
+    const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's lane quarter
 
-    float oacc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 16*warp + g (+8), columns 2t, 2t+1
-    for (int j = j0; j < j1 && ok; j += PACK, ++it) {
-        const bool hasB = PACK == 2 && j + 1 < j1;
-        ok = __syncthreads_and(mbar_wait(ykbar, (uint32_t)(it & 1)));
-        if (!ok) break;
-        yk_pend = -1;
-        // ---- u = Yk . q^T: rows 16*warp .. +15, block A in columns 0..3 (or 0..7), block B in 4..7
-        {
-            float u[4] = {0.f, 0.f, 0.f, 0.f}, u2[4] = {0.f, 0.f, 0.f, 0.f};  // two independent chains
-            const int row = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
-            const int colo = 8 * (lane >> 4);
-            const uint32_t ka = su32(ykbuf), kb = su32(ykbuf + (size_t)kMJ * kD);
-#pragma unroll
-            for (int kk = 0; kk < KD; ++kk) {
-                uint32_t a[4];
-                ldsm_x4(swz(ka, row, 16 * kk + colo), a);
-                mma16816((kk & 1) ? u2 : u, a, qa[kk][0], qa[kk][1]);
-                if (hasB) {
-                    ldsm_x4(swz(kb, row, 16 * kk + colo), a);
-                    mma16816((kk & 1) ? u : u2, a, qb[kk][0], qb[kk][1]);
-                }
+    // Equal contiguous ranges of all (b, h) blocks: block x goes to CTA floor(x C / T).
+    const int64_t T = (int64_t)p.B * p.Hkv * p.n_blocks, C = gridDim.x, c = blockIdx.x;
+    const int64_t x_begin = (c * T + C - 1) / C, x_end = ((c + 1) * T + C - 1) / C;
+
+    // Slot loads in flight, kept alike by every thread: pend bit s = a copy into slot s not yet seen
+    // complete, whose completion has parity (ph >> s) & 1.
+    uint32_t ph = 0, pend = 0;
+    bool ok = true;
+    int64_t gchunk = 0;    // operator chunks of earlier rounds (phases of the chunk, S, P, W barriers)
+    int64_t gxchunk = 0;   // the same over stacked rounds only (phases of the lo-score barriers)
+    int64_t cur_bh = -1;   // the (b, h) whose partial output the o accumulators hold
+    float oacc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 16*warp + g (+8), query columns 2t, 2t+1
+
+    // A warp done with slot s: the last of the eight to get here copies block x of `map` into it.
+    auto release = [&](int s, bool refill, const CUtensorMap* map, int64_t x) {
+        if (!refill) return;
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            if (atomicAdd(&cnt[s], 1) == kWarps - 1) {
+                cnt[s] = 0;
+                issue_block(map, x / p.n_blocks, (int)(x % p.n_blocks), slot((uint32_t)s), bar(kBarFull + s));
             }
+        }
+        pend |= 1u << s;
+    };
+    // waits for the copy into slot s (decided for the whole warp)
+    auto arrive_slot = [&](int s) {
+        const bool r = mbar_wait_warp(bar(kBarFull + s), (ph >> s) & 1u);
+        if (r) {
+            ph ^= 1u << s;
+            pend &= ~(1u << s);
+        }
+        return r;
+    };
+
+    // Writes the partial of (b, h) `bh` (openM / openL: its max and normalizer per query) and, in
+    // the last CTA to finish it, merges all its partials into out / lse.
+    auto flush = [&](int64_t bh) {
+        const int64_t first_c = bh * p.n_blocks * C / T, last_c = ((bh + 1) * p.n_blocks - 1) * C / T;
+        const int n_seg = (int)(last_c - first_c + 1), split = (int)(c - first_c);
+        const int d0 = 16 * warp + g;
+        float* po = p.part_o + ((bh * p.S + split) * kCols) * kD;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) u[c] += u2[c];
-            const int m0 = 16 * warp + g;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int m = m0 + 8 * (c >> 1), n = 2 * t + (c & 1);
-                __half hi, lo;
-                split_hl(u[c], hi, lo);
-                uT[n * kRowPad + m] = hi;
-                uT[kCols * kRowPad + n * kRowPad + m] = lo;
+        for (int k = 0; k < 2; ++k) {
+            const int n = 2 * t + k;
+            if (n < NQ) {
+                const float L = openL[n];
+                po[n * kD + d0] = L > 0.f ? oacc[k] / L : 0.f;
+                po[n * kD + d0 + 8] = L > 0.f ? oacc[2 + k] / L : 0.f;
+                if (warp == 0 && g == 0)
+                    p.part_lse[(bh * p.S + split) * kCols + n] = L > 0.f ? openM[n] + log2f(L) : -INFINITY;
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const int prev = atomicAdd(&p.counters[bh], 1);
+            misc[1] = prev == n_seg - 1;
+            if (prev == n_seg - 1) p.counters[bh] = 0;
+        }
+        __syncthreads();
+        if (misc[1]) {
+            __threadfence();
+            const int64_t b = bh / p.Hkv, h = bh - b * p.Hkv;
+            for (int e = tid; e < NQ * kD; e += kThreads) {
+                const int n = e / kD, d = e - n * kD;
+                const float* pl = p.part_lse + bh * p.S * kCols + n;
+                float M = -INFINITY;
+                for (int s = 0; s < n_seg; ++s) M = fmaxf(M, __ldcg(pl + s * kCols));
+                float W = 0.f, acc = 0.f;
+                if (M != -INFINITY) {
+                    for (int s = 0; s < n_seg; ++s) {
+                        const float wgt = exp2f(__ldcg(pl + s * kCols) - M);
+                        W += wgt;
+                        acc += wgt * __ldcg(p.part_o + ((bh * p.S + s) * kCols + n) * kD + d);
+                    }
+                }
+                const int gi = n / p.qlen, qi = n - gi * p.qlen;
+                const int64_t row = ((b * p.Hkv + h) * p.G + gi) * p.qlen + qi;
+                p.out[row * kD + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
+                if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
             }
         }
         __syncthreads();
-        if (j + PACK < j1) {  // Yk buffer consumed: bring the next pair
-            if (tid == 0) {
-                const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
-                issue_blocks(&p.tmk, bh, j + PACK, nb, ykbuf, ykbar);
-            }
-            yk_pend = (it + 1) & 1;
+    };
+
+    for (int64_t xr = x_begin; xr < x_end && ok; xr += bpr) {
+        const int nb = (int)((x_end - xr) < bpr ? (x_end - xr) : bpr);
+        const int rows = nb * NQ;
+        // ================================================================ U phase
+        for (int i = 0; i < nb && i < 4; ++i) {
+            const int64_t x = xr + i;
+            if (tid == 0) issue_block(&p.tmk, x / p.n_blocks, (int)(x % p.n_blocks), slot(i), bar(kBarFull + i));
+            pend |= 1u << i;
         }
-        // ---- scores, softmax and w over this warp's token tiles
-        uint32_t ub[KM][2][2];
+        bool wok = true;
+        {
+            int64_t qbh = -1;
+            uint32_t qa[kD / 16][2];
+            for (int i = 0; i < nb; ++i) {
+                const int s = i % 4;
+                wok = arrive_slot(s);
+                if (!wok) break;
+                const int64_t x = xr + i, bh = x / p.n_blocks;
+                if (bh != qbh) {  // query fragments of this (b, h): column n = query n
+                    qbh = bh;
+                    const int64_t b = bh / p.Hkv, h = bh - b * p.Hkv;
+                    const __half* qb = p.q + ((b * p.Hkv + h) * p.G) * p.qlen * kD;
 #pragma unroll
-        for (int kk = 0; kk < KM; ++kk)
+                    for (int kk = 0; kk < kD / 16; ++kk) {
+                        const int d = 16 * kk + 2 * t;
+                        qa[kk][0] = g < NQ ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * kD + d) : 0u;
+                        qa[kk][1] = g < NQ ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * kD + d + 8) : 0u;
+                    }
+                }
+                // u = Yk . q^T for block rows 16*warp .. +15 -> U^T rows i*NQ + n
+                float u[4] = {0.f, 0.f, 0.f, 0.f}, u2[4] = {0.f, 0.f, 0.f, 0.f};
+                const int row = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1), colo = 8 * (lane >> 4);
+#pragma unroll
+                for (int kk = 0; kk < kD / 16; ++kk) {
+                    uint32_t a[4];
+                    ldsm_x4(swz(slot((uint32_t)s), row, 16 * kk + colo), a);
+                    mma16816((kk & 1) ? u2 : u, a, qa[kk][0], qa[kk][1]);
+                }
+                release(s, i + 4 < nb, &p.tmk, x + 4);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int mj = 16 * warp + g + 8 * (k >> 1), n = 2 * t + (k & 1);
+                    if (n < NQ) {
+                        __half hi, lo;
+                        split_hl(u[k] + u2[k], hi, lo);
+                        const uint32_t off = rowsw(i * NQ + n, mj);
+                        asm volatile("st.shared.b16 [%0], %1;" ::"r"(uhi + off), "h"(__half_as_ushort(hi)) : "memory");
+                        asm volatile("st.shared.b16 [%0], %1;" ::"r"(ulo + off), "h"(__half_as_ushort(lo)) : "memory");
+                    }
+                }
+            }
+        }
+        ok = __syncthreads_and(wok) != 0;
+        if (!ok) break;
+        // U^T rows -> tensor memory (the A operand of the scores); rows past this round's (block,
+        // query) pairs are zero, so their scores stay finite.  A round of at most 64 rows is
+        // stacked: lane r holds U^T_hi row r and lane 64 + r U^T_lo row r, so one MMA forms both
+        // parts of the scores (lanes 64.. then hold the lo parts, shipped to the softmax warps).
+        const bool stacked = rows <= 64;
+        if (warp < 4) {
+            const int r = 32 * warp + lane;
 #pragma unroll
             for (int hl = 0; hl < 2; ++hl) {
-                const __half* r = uT + hl * kCols * kRowPad + g * kRowPad + 16 * kk + 2 * t;
-                ub[kk][hl][0] = *reinterpret_cast<const uint32_t*>(r);
-                ub[kk][hl][1] = *reinterpret_cast<const uint32_t*>(r + 8);
-            }
-        // columns this thread's scores belong to: 2t, 2t+1; dead when the block or query is absent
-        const int qn0 = (2 * t) % qpb, qn1 = (2 * t + 1) % qpb;
-        const bool colB = PACK == 2 && t >= 2;
-        const bool live0 = qn0 < NQ && (!colB || hasB), live1 = qn1 < NQ && (!colB || hasB);
-        float ms[2] = {kNoMax, kNoMax}, ls[2] = {0.f, 0.f};
-        float wacc[KM][4];
+                if (stacked && hl) break;
+                const int src = stacked ? (r & 63) : r;
+                const uint32_t sbase_u = (stacked ? r >= 64 : hl) ? ulo : uhi;
 #pragma unroll
-        for (int mt = 0; mt < KM; ++mt) wacc[mt][0] = wacc[mt][1] = wacc[mt][2] = wacc[mt][3] = 0.f;
-        const int ntiles = p.N / 16;
-        uint4 rcur[KM];  // R fragments of the current tile, loaded one tile ahead
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    uint32_t v[32];
 #pragma unroll
-        for (int kk = 0; kk < KM; ++kk) rcur[kk] = ldg_nc(p.rf + ((size_t)warp * KM + kk) * 32 + lane);
-        for (int tt = warp; tt < ntiles; tt += kWarps) {
-            uint4 rt[KM];  // R^T fragments of this tile: in flight while the scores and softmax run
-            const uint4* rtf = p.rtf + (size_t)tt * 32 + lane;
-#pragma unroll
-            for (int mt = 0; mt < KM; ++mt) rt[mt] = ldg_nc(rtf + (size_t)mt * ntiles * 32);
-            float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-            float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
-#pragma unroll
-            for (int kk = 0; kk < KM; ++kk) {
-                const uint32_t a[4] = {rcur[kk].x, rcur[kk].y, rcur[kk].z, rcur[kk].w};
-                mma16816((kk & 1) ? sc : sa, a, ub[kk][0][0], ub[kk][0][1]);
-                mma16816((kk & 1) ? sd : sb, a, ub[kk][1][0], ub[kk][1][1]);
-            }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) { sa[c] += sc[c]; sb[c] += sd[c]; }
-            if (tt + kWarps < ntiles) {
-#pragma unroll
-                for (int kk = 0; kk < KM; ++kk) rcur[kk] = ldg_nc(p.rf + ((size_t)(tt + kWarps) * KM + kk) * 32 + lane);
-            }
-            float x[4];
-            x[0] = live0 ? (sa[0] + sb[0]) * p.scale_log2 : -INFINITY;
-            x[1] = live1 ? (sa[1] + sb[1]) * p.scale_log2 : -INFINITY;
-            x[2] = live0 ? (sa[2] + sb[2]) * p.scale_log2 : -INFINITY;
-            x[3] = live1 ? (sa[3] + sb[3]) * p.scale_log2 : -INFINITY;
-            const bool over = (fmaxf(x[0], x[2]) > ms[0] + kSlack) | (fmaxf(x[1], x[3]) > ms[1] + kSlack);
-            if (__any_sync(0xffffffffu, over)) {
-                float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
-#pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
-                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                    for (int kc = 0; kc < 8; ++kc) {
+                        uint4 x = make_uint4(0u, 0u, 0u, 0u);
+                        if (src < rows)
+                            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                                         : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w)
+                                         : "r"(sbase_u + rowsw(src, 64 * h2 + 8 * kc)));
+                        v[4 * kc] = x.x; v[4 * kc + 1] = x.y; v[4 * kc + 2] = x.z; v[4 * kc + 3] = x.w;
+                    }
+                    JLA_TMEM_ST32(trow + (hl ? kTmemUlo : kTmemUhi) + 32 * h2, v);
                 }
-                const float n0 = fmaxf(ms[0], mx0), n1 = fmaxf(ms[1], mx1);
-                const float f0 = exp2f(ms[0] - n0), f1 = exp2f(ms[1] - n1);
-                // w rows are MJ, columns are the score columns: c0/c2 -> column 2t, c1/c3 -> 2t+1
-#pragma unroll
-                for (int mt = 0; mt < KM; ++mt) { wacc[mt][0] *= f0; wacc[mt][2] *= f0; wacc[mt][1] *= f1; wacc[mt][3] *= f1; }
-                ls[0] *= f0; ls[1] *= f1;
-                ms[0] = n0; ms[1] = n1;
             }
-            const float p0 = exp2f(x[0] - ms[0]), p1 = exp2f(x[1] - ms[1]);
-            const float p2 = exp2f(x[2] - ms[0]), p3 = exp2f(x[3] - ms[1]);
-            ls[0] += p0 + p2;
-            ls[1] += p1 + p3;
-            const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
-            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-            const uint32_t b01 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&h01));
-            const uint32_t b23 = movmatrix_t(*reinterpret_cast<const uint32_t*>(&h23));
-            const uint32_t c01 = movmatrix_t(h2pack(p0 - f01.x, p1 - f01.y));
-            const uint32_t c23 = movmatrix_t(h2pack(p2 - f23.x, p3 - f23.y));
-#pragma unroll
-            for (int mt = 0; mt < KM; ++mt) {
-                const uint32_t a[4] = {rt[mt].x, rt[mt].y, rt[mt].z, rt[mt].w};
-                mma16816(wacc[mt], a, b01, b23);
-            }
-#pragma unroll
-            for (int mt = 0; mt < KM; ++mt) {
-                const uint32_t a[4] = {rt[mt].x, rt[mt].y, rt[mt].z, rt[mt].w};
-                mma16816(wacc[mt], a, c01, c23);
-            }
+            tmem_wait_st();
         }
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            ls[0] += __shfl_xor_sync(0xffffffffu, ls[0], off);
-            ls[1] += __shfl_xor_sync(0xffffffffu, ls[1], off);
-        }
-        if (g == 0) {
-            mw[warp * kCols + 2 * t] = ms[0];
-            mw[warp * kCols + 2 * t + 1] = ms[1];
-            lw[warp * kCols + 2 * t] = ls[0];
-            lw[warp * kCols + 2 * t + 1] = ls[1];
-        }
-        {
-            float* wp = wpart + ((size_t)warp * 32 + lane) * 33;
-#pragma unroll
-            for (int mt = 0; mt < KM; ++mt)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) wp[4 * mt + c] = wacc[mt][c];
-        }
+        tc_fence_before();
         __syncthreads();
-        // ---- merge the warps' w, fold into the running (per column) softmax state
-        if (tid < kCols) {
-            const int n = tid;
-            float mb = kNoMax;
-            for (int w = 0; w < kWarps; ++w) mb = fmaxf(mb, mw[w * kCols + n]);
-            float lb = 0.f;
-            for (int w = 0; w < kWarps; ++w) lb += exp2f(mw[w * kCols + n] - mb) * lw[w * kCols + n];
-            if (p.block_lse) {  // column n belongs to block j (+1 for the upper columns when packed)
-                const int blk = j + ((PACK == 2 && n >= 4) ? 1 : 0), qn = n % qpb;
-                if (qn < NQ && blk < j1)
-                    p.block_lse[(bh * p.n_blocks + blk) * kCols + qn] =
-                        lb > 0.f ? (mb + log2f(lb)) * 0.69314718055994530942f : -INFINITY;
+        tc_fence_after();
+
+        // ================================================================ SW phase
+        // the first two Yv blocks come in while the scores run (slots 4, 5: the staging is done;
+        // a stacked round ships its lo scores through them instead)
+        for (int i = 0; i < nb && i < 2 && !stacked; ++i) {
+            const int64_t x = xr + i;
+            const uint32_t sl = oslot(i);
+            if (tid == 0) issue_block(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
+            pend |= 1u << sl;
+        }
+        // Warps 0-3 run the softmax of the lane quarters that hold this round's rows (the others
+        // sit out); warp 6 issues the MMAs and warp 7 copies the operator chunks, on the schedulers
+        // of the quarters that sit out when the round has at most 64 rows.
+        const int nact = rows >= 96 ? 4 : (rows + 31) / 32;
+        if (warp == 7) {
+            if (lane == 0) {  // copies the operator chunks: chunk c+4 into the slot of chunk c once W_c is done
+                int loaded = 0;
+                auto load = [&](int cc) {
+                    const int k = (int)((gchunk + cc) & 3);
+                    issue_op_chunk(p, cc, slot((uint32_t)k), bar(kBarRF + k));
+                    loaded = cc + 1;
+                };
+                for (int cc = 0; cc < 4 && cc < nchunks; ++cc) load(cc);
+                for (int cc = 0; cc + 4 < nchunks; ++cc) {
+                    const int64_t gc = gchunk + cc;
+                    wok = mbar_wait(bar(kBarRE + (int)(gc & 3)), (uint32_t)((gc >> 2) & 1));
+                    if (!wok) break;
+                    load(cc + 4);
+                }
+                misc[3] = (uint32_t)loaded;
             }
-            const float mo = mrun[n], mn = fmaxf(mo, mb);
-            const float a = exp2f(mo - mn), be = exp2f(mb - mn);
-            lrun[n] = a * lrun[n] + be * lb;
-            mrun[n] = mn;
-            alpha[n] = a;
-            for (int w = 0; w < kWarps; ++w) fw[w * kCols + n] = exp2f(mw[w * kCols + n] - mb) * be;
-        }
-        __syncthreads();
-        for (int pos = tid; pos < kMJ * kCols; pos += kThreads) {
-            const int ln = pos & 31, idx = pos >> 5;  // (lane, value index) of the per-warp fragments
-            const int mt = idx >> 2, c = idx & 3;
-            const int m = 16 * mt + (ln >> 2) + 8 * (c >> 1), n = 2 * (ln & 3) + (c & 1);
-            float wv = 0.f;
+            __syncwarp();
+        } else if (warp == 6) {
+            if (lane == 0) {  // issues the MMAs
+                tc_fence_after();
+                const uint32_t id_s = idesc(kRows, kChunk), id_w = idesc(kRows, kMJ);
+                int last_bar = -1;
+                uint32_t last_par = 0;
+                int landed = 0;  // operator chunks seen arrived
+                auto s_mma = [&](int cc) {  // S_cc = U^T . R_cc^T into S buffer gc % 3
+                    const int64_t gc = gchunk + cc;
+                    if (!mbar_wait(bar(kBarRF + (int)(gc & 3)), (uint32_t)((gc >> 2) & 1))) return false;
+                    landed = cc + 1;
+                    tc_fence_after();
+                    const uint32_t d = tmem + (uint32_t)(gc % kSBufs) * kChunk, rsm = slot((uint32_t)(gc & 3));
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) wv += fw[w * kCols + n] * wpart[((size_t)w * 32 + ln) * 33 + idx];
-            __half hi, lo;
-            split_hl(wv, hi, lo);
-            wt[n * kRowPad + m] = hi;
-            wt[kCols * kRowPad + n * kRowPad + m] = lo;
+                    for (int ks = 0; ks < kMJ / 16; ++ks) {
+                        const uint64_t bd = sdesc(rsm + (uint32_t)(ks >> 2) * (kChunk * 128) + (uint32_t)(ks & 3) * 32);
+                        umma_ts(d, tmem + kTmemUhi + 8 * ks, bd, id_s, ks > 0 ? 1u : 0u);
+                        if (!stacked) umma_ts(d, tmem + kTmemUlo + 8 * ks, bd, id_s, 1u);
+                    }
+                    umma_commit(bar(kBarS + (int)(gc % kSBufs)));
+                    last_bar = kBarS + (int)(gc % kSBufs);
+                    last_par = (uint32_t)((gc / kSBufs) & 1);
+                    return true;
+                };
+                for (int cc = 0; cc < 2 && cc < nchunks && wok; ++cc) wok = s_mma(cc);
+                for (int cc = 0; cc < nchunks && wok; ++cc) {
+                    const int64_t gc = gchunk + cc;
+                    if (cc + 2 < nchunks) {
+                        wok = s_mma(cc + 2);
+                        if (!wok) break;
+                    }
+                    wok = mbar_wait(bar(kBarP + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
+                    if (!wok) break;
+                    tc_fence_after();
+                    // W += P_cc . R_cc  (A = P_cc in tensor memory; B = R^T_cc, K-major: rows MJ, K = tokens)
+                    const uint32_t rtsm = slot((uint32_t)(gc & 3)) + kOpChunkBytes;
+                    const uint32_t pt = tmem + (uint32_t)(gc % kSBufs) * kChunk;
+#pragma unroll
+                    for (int ks = 0; ks < kChunk / 16; ++ks)
+                        umma_ts(tmem + kTmemW, pt + 8 * ks, sdesc(rtsm + (uint32_t)ks * 32), id_w,
+                                (cc > 0 || ks > 0) ? 1u : 0u);
+                    umma_commit(bar(kBarW + (int)(gc & 1)));
+                    umma_commit(bar(kBarRE + (int)(gc & 3)));
+                    last_bar = kBarW + (int)(gc & 1);
+                    last_par = (uint32_t)((gc >> 1) & 1);
+                }
+                if (!wok && last_bar >= 0) (void)mbar_wait(bar(last_bar), last_par);  // MMAs in flight finish
+                misc[2] = (uint32_t)landed;
+            }
+            __syncwarp();
+        } else if (stacked && warp >= 2 && warp < 2 + nact) {  // ships the lo scores of rows 32(w-2) ..
+            const int r = 32 * (warp - 2) + lane;
+            for (int cc = 0; cc < nchunks; ++cc) {
+                const int64_t gc = gchunk + cc;
+                wok = mbar_wait_warp(bar(kBarS + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
+                if (!wok) break;
+                tc_fence_after();
+                const uint32_t sb = trow + (uint32_t)(gc % kSBufs) * kChunk;
+                uint32_t v[kChunk];
+                JLA_TMEM_LD32(sb, v);
+                JLA_TMEM_LD32(sb + 32, (v + 32));
+                tmem_wait_ld();
+                // 3 x 16 KB exchange buffers in slots 4, 5: row r of buffer b at 256 r, 16-byte
+                // chunks XOR-swizzled by row
+                const int64_t gx = gxchunk + cc;
+                const uint32_t xrow = slot(4) + (uint32_t)(gx % kSBufs) * 16384u + (uint32_t)r * 256u;
+#pragma unroll
+                for (int k = 0; k < kChunk / 4; ++k)
+                    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xrow + (uint32_t)((k ^ (r & 7)) << 4)),
+                                 "r"(v[4 * k]), "r"(v[4 * k + 1]), "r"(v[4 * k + 2]), "r"(v[4 * k + 3])
+                                 : "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarX + (int)(gx % kSBufs)), warp == 2 ? 1u + 2u - (uint32_t)nact : 1u);
+            }
+        } else if (warp < nact) {  // online softmax of row r
+            const int r = 32 * warp + lane;
+            float m = kNoMax, l = 0.f;
+            for (int cc = 0; cc < nchunks; ++cc) {
+                const int64_t gc = gchunk + cc;
+                // S_cc complete; it was issued after W_{cc-3}, the last reader of the P this buffer held
+                wok = mbar_wait_warp(bar(kBarS + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
+                if (!wok) break;
+                tc_fence_after();
+                const uint32_t sb = trow + (uint32_t)(gc % kSBufs) * kChunk;
+                uint32_t v[kChunk];
+                JLA_TMEM_LD32(sb, v);
+                JLA_TMEM_LD32(sb + 32, (v + 32));
+                tmem_wait_ld();
+                if (stacked) {  // add the lo parts shipped by the warp of lanes 64 + r
+                    const int64_t gx = gxchunk + cc;
+                    wok = mbar_wait_warp(bar(kBarX + (int)(gx % kSBufs)), (uint32_t)((gx / kSBufs) & 1));
+                    if (!wok) break;
+                    const uint32_t xrow = slot(4) + (uint32_t)(gx % kSBufs) * 16384u + (uint32_t)r * 256u;
+#pragma unroll
+                    for (int k = 0; k < kChunk / 4; ++k) {
+                        float4 lo;
+                        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                                     : "=f"(lo.x), "=f"(lo.y), "=f"(lo.z), "=f"(lo.w)
+                                     : "r"(xrow + (uint32_t)((k ^ (r & 7)) << 4)));
+                        v[4 * k] = __float_as_uint(__uint_as_float(v[4 * k]) + lo.x);
+                        v[4 * k + 1] = __float_as_uint(__uint_as_float(v[4 * k + 1]) + lo.y);
+                        v[4 * k + 2] = __float_as_uint(__uint_as_float(v[4 * k + 2]) + lo.z);
+                        v[4 * k + 3] = __float_as_uint(__uint_as_float(v[4 * k + 3]) + lo.w);
+                    }
+                }
+                float cm = kNoMax;
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    const float x = __uint_as_float(v[j]) * p.scale_log2;
+                    v[j] = __float_as_uint(x);
+                    cm = fmaxf(cm, x);
+                }
+                const bool bump = cm > m + kSlack;
+                const float mnew = bump ? cm : m;
+                const float alpha = ex2(m - mnew);  // 0 on the first chunk (m = kNoMax)
+                l *= alpha;
+                m = mnew;
+                uint32_t pp[kChunk / 2];
+#pragma unroll
+                for (int j = 0; j < kChunk / 2; ++j) {
+                    const float e0 = ex2(__uint_as_float(v[2 * j]) - m), e1 = ex2(__uint_as_float(v[2 * j + 1]) - m);
+                    l += e0 + e1;
+                    const __half2 h = __floats2half2_rn(e0, e1);
+                    pp[j] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                if (cc > 0 && __any_sync(0xffffffffu, bump)) {  // W_{cc-1} done, then rescaled to the new max
+                    wok = mbar_wait_warp(bar(kBarW + (int)((gc - 1) & 1)), (uint32_t)(((gc - 1) >> 1) & 1));
+                    if (!wok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int j0 = 0; j0 < kMJ; j0 += 32) {
+                        uint32_t w[32];
+                        JLA_TMEM_LD32(trow + kTmemW + j0, w);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(__uint_as_float(w[j]) * alpha);
+                        JLA_TMEM_ST32(trow + kTmemW + j0, w);
+                    }
+                }
+                JLA_TMEM_ST32(sb, pp);  // P_cc (fp16) over the first 32 columns of its S
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarP + (int)(gc % kSBufs)), warp == 0 ? 1u + 4u - (uint32_t)nact : 1u);
+            }
+            mrow[r] = m;
+            lrow[r] = l;
         }
-        __syncthreads();
-        ok = __syncthreads_and(mbar_wait(yvbar, (uint32_t)(it & 1)));
+        ok = __syncthreads_and(wok) != 0;
+        if (!ok && tid == 7 * 32) {  // operator copies still in flight land before the CTA goes on (bounded)
+            for (int cc = (int)misc[2]; cc < (int)misc[3]; ++cc) {
+                const int64_t gc = gchunk + cc;
+                (void)mbar_wait(bar(kBarRF + (int)(gc & 3)), (uint32_t)((gc >> 2) & 1));
+            }
+        }
+        if (ok) {  // the last W (and with it every MMA of the round)
+            const int64_t gl = gchunk + nchunks - 1;
+            ok = __syncthreads_and(mbar_wait(bar(kBarW + (int)(gl & 1)), (uint32_t)((gl >> 1) & 1))) != 0;
+        }
+        gchunk += nchunks;
+        if (stacked) gxchunk += nchunks;
         if (!ok) break;
-        yv_pend = -1;
-        // ---- o += Yv^T . w for dims 16*warp .. +15
-        {
-            const float a0 = alpha[2 * t], a1 = alpha[2 * t + 1];
-            oacc[0] *= a0; oacc[2] *= a0; oacc[1] *= a1; oacc[3] *= a1;
-            float olo[4] = {0.f, 0.f, 0.f, 0.f};  // the lo parts of w: an independent chain
-            const int mrow = (lane & 7) + 8 * (lane >> 4), dcol = 16 * warp + 8 * ((lane >> 3) & 1);
-            const bool inA = PACK == 1 || g < 4;
-#pragma unroll
-            for (int kk = 0; kk < KM; ++kk) {
-                const __half* wr = wt + g * kRowPad + 16 * kk + 2 * t;
-                const uint32_t wh0 = *reinterpret_cast<const uint32_t*>(wr), wh1 = *reinterpret_cast<const uint32_t*>(wr + 8);
-                const uint32_t wl0 = *reinterpret_cast<const uint32_t*>(wr + kCols * kRowPad);
-                const uint32_t wl1 = *reinterpret_cast<const uint32_t*>(wr + kCols * kRowPad + 8);
-                uint32_t a[4];
-                ldsm_x4_t(swz(su32(yvbuf), 16 * kk + mrow, dcol), a);
-                mma16816(oacc, a, inA ? wh0 : 0u, inA ? wh1 : 0u);
-                mma16816(olo, a, inA ? wl0 : 0u, inA ? wl1 : 0u);
-                if (hasB) {
-                    ldsm_x4_t(swz(su32(yvbuf + (size_t)kMJ * kD), 16 * kk + mrow, dcol), a);
-                    mma16816(oacc, a, inA ? 0u : wh0, inA ? 0u : wh1);
-                    mma16816(olo, a, inA ? 0u : wl0, inA ? 0u : wl1);
-                }
+        tc_fence_after();
+        // the operator slots are free again: slots 2, 3 take the third and fourth Yv blocks (a
+        // stacked round also the first two, in slots 4, 5)
+        for (int i = stacked ? 0 : 2; i < nb && i < 4; ++i) {
+            const int64_t x = xr + i;
+            const uint32_t sl = oslot(i);
+            if (tid == 0) issue_block(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
+            pend |= 1u << sl;
+        }
+
+        // ================================================================ O phase
+        // per (segment = run of one (b, h)'s blocks, query): the common max, the normalizer and the
+        // factor of each row; the first segment continues the open head when it is the same (b, h)
+        const int64_t bh0 = xr / p.n_blocks;
+        const int nseg = (int)((xr + nb - 1) / p.n_blocks - bh0) + 1;
+        const bool cont = bh0 == cur_bh;
+        if (tid < nseg * NQ) {
+            const int s = tid / NQ, n = tid - s * NQ;
+            const int64_t hb = (bh0 + s) * p.n_blocks;
+            const int i0 = (int)(hb - xr > 0 ? hb - xr : 0);
+            const int i1 = (int)(hb + p.n_blocks - xr < nb ? hb + p.n_blocks - xr : nb);
+            float M = kNoMax, prevM = kNoMax, prevL = 0.f;
+            for (int i = i0; i < i1; ++i) M = fmaxf(M, mrow[i * NQ + n]);
+            if (s == 0 && cont) {
+                prevM = openM[n];
+                prevL = openL[n];
+                M = fmaxf(M, prevM);
             }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) oacc[c] += olo[c];
+            const float a = exp2f(prevM - M);
+            float L = a * prevL;
+            for (int i = i0; i < i1; ++i) {
+                const float f = exp2f(mrow[i * NQ + n] - M);
+                frow[i * NQ + n] = f;
+                L += f * lrow[i * NQ + n];
+            }
+            segM[tid] = M;
+            segL[tid] = L;
+            segA[tid] = a;
         }
         __syncthreads();
-        if (j + PACK < j1) {  // Yv buffer consumed
-            if (tid == 0) {
-                const int nb = (j1 - j - PACK) < PACK ? (j1 - j - PACK) : PACK;
-                issue_blocks(&p.tmv, bh, j + PACK, nb, yvbuf, yvbar);
+        if (warp < 4) {  // W rows, scaled, -> W' [row][MJ] fp16 hi | lo (16-byte chunks XOR-swizzled by row)
+            const int r = 32 * warp + lane;
+            const bool live = r < rows;
+            const float f = live ? frow[r] : 0.f;
+#pragma unroll
+            for (int j0 = 0; j0 < kMJ; j0 += 32) {
+                uint32_t w[32];
+                JLA_TMEM_LD32(trow + kTmemW + j0, w);
+                tmem_wait_ld();
+                if (live) {
+#pragma unroll
+                    for (int kc = 0; kc < 4; ++kc) {
+                        uint32_t h[4], lo[4];
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj)
+                            split_hl2(f * __uint_as_float(w[8 * kc + 2 * jj]), f * __uint_as_float(w[8 * kc + 2 * jj + 1]),
+                                      h[jj], lo[jj]);
+                        const uint32_t off = rowsw(r, j0 + 8 * kc);
+                        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(whi + off), "r"(h[0]), "r"(h[1]),
+                                     "r"(h[2]), "r"(h[3])
+                                     : "memory");
+                        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(wlo + off), "r"(lo[0]), "r"(lo[1]),
+                                     "r"(lo[2]), "r"(lo[3])
+                                     : "memory");
+                    }
+                }
             }
-            yv_pend = (it + 1) & 1;
+            if (live && p.block_lse) {
+                const int i = r / NQ, n = r - i * NQ;
+                p.block_lse[(xr + i) * kCols + n] =
+                    lrow[r] > 0.f ? (mrow[r] + log2f(lrow[r])) * 0.69314718055994530942f : -INFINITY;
+            }
         }
+        tc_fence_before();
+        __syncthreads();
+        wok = true;
+        for (int i = 0; i < nb; ++i) {
+            const int s = (int)oslot(i % 4);
+            wok = arrive_slot(s);
+            if (!wok) break;
+            const int64_t x = xr + i, bh = x / p.n_blocks;
+            if (bh != cur_bh || i == 0) {  // every warp reaches this block: a CTA-wide step
+                const int seg = (int)(bh - bh0);
+                if (bh != cur_bh) {
+                    if (cur_bh >= 0) flush(cur_bh);
+                    oacc[0] = oacc[1] = oacc[2] = oacc[3] = 0.f;
+                    cur_bh = bh;
+                } else {  // the open head goes on: rescale its running output to the new max
+                    const float a0 = 2 * t < NQ ? segA[2 * t] : 0.f, a1 = 2 * t + 1 < NQ ? segA[2 * t + 1] : 0.f;
+                    oacc[0] *= a0; oacc[2] *= a0; oacc[1] *= a1; oacc[3] *= a1;
+                }
+                __syncthreads();
+                if (tid < NQ) {
+                    openM[tid] = segM[seg * NQ + tid];
+                    openL[tid] = segL[seg * NQ + tid];
+                }
+                __syncthreads();
+            }
+            // o += Yv^T . w' for dims 16*warp .. +15 (columns: the block's queries)
+            {
+                const int mr = (lane & 7) + 8 * (lane >> 4), dcol = 16 * warp + 8 * ((lane >> 3) & 1);
+                const bool lq = g < NQ;
+                const int r = i * NQ + g;
+                float olo[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int kk = 0; kk < kMJ / 16; ++kk) {
+                    uint32_t wh0 = 0u, wh1 = 0u, wl0 = 0u, wl1 = 0u;
+                    if (lq) {
+                        const uint32_t o0 = rowsw(r, 16 * kk + 2 * t), o1 = rowsw(r, 16 * kk + 8 + 2 * t);
+                        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wh0) : "r"(whi + o0));
+                        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wh1) : "r"(whi + o1));
+                        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wl0) : "r"(wlo + o0));
+                        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wl1) : "r"(wlo + o1));
+                    }
+                    uint32_t a[4];
+                    ldsm_x4_t(swz(slot((uint32_t)s), 16 * kk + mr, dcol), a);
+                    mma16816(oacc, a, wh0, wh1);
+                    mma16816(olo, a, wl0, wl1);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) oacc[k] += olo[k];
+            }
+            release(s, i + 4 < nb, &p.tmv, x + 4);
+        }
+        ok = __syncthreads_and(wok) != 0;
     }
+    if (ok && cur_bh >= 0) flush(cur_bh);
     if (!ok) {
         if (tid == 0) atomicExch(&g_status, (int)ARGUS_ERR_TIMEOUT);
-        // let copies in flight land before the CTA exits (bounded)
-        if (yk_pend >= 0) (void)mbar_wait(ykbar, (uint32_t)yk_pend);
-        if (yv_pend >= 0) (void)mbar_wait(yvbar, (uint32_t)yv_pend);
-        break;
+        // copies in flight land before the CTA exits (bounded)
+        for (int s = 0; s < kNumSlots; ++s)
+            if (pend >> s & 1) (void)mbar_wait(bar(kBarFull + s), (ph >> s) & 1u);
     }
+    tc_fence_before();
     __syncthreads();
-
-    // ---- per query: merge block columns (n and n + 4 when two blocks share the MMA), write partials
-    float o0 = oacc[0], o1 = oacc[1], o2 = oacc[2], o3 = oacc[3];
-    float M0 = mrun[2 * t], M1 = mrun[2 * t + 1], L0 = lrun[2 * t], L1 = lrun[2 * t + 1];
-    if (PACK == 2) {
-        const float po0 = __shfl_xor_sync(0xffffffffu, o0, 2), po1 = __shfl_xor_sync(0xffffffffu, o1, 2);
-        const float po2 = __shfl_xor_sync(0xffffffffu, o2, 2), po3 = __shfl_xor_sync(0xffffffffu, o3, 2);
-        const int pt = t ^ 2;
-        const float PM0 = mrun[2 * pt], PM1 = mrun[2 * pt + 1], PL0 = lrun[2 * pt], PL1 = lrun[2 * pt + 1];
-        const float N0 = fmaxf(M0, PM0), N1 = fmaxf(M1, PM1);
-        const float x0 = exp2f(M0 - N0), y0 = exp2f(PM0 - N0), x1 = exp2f(M1 - N1), y1 = exp2f(PM1 - N1);
-        o0 = x0 * o0 + y0 * po0; o2 = x0 * o2 + y0 * po2;
-        o1 = x1 * o1 + y1 * po1; o3 = x1 * o3 + y1 * po3;
-        L0 = x0 * L0 + y0 * PL0; L1 = x1 * L1 + y1 * PL1;
-        M0 = N0; M1 = N1;
-    }
-    const bool writer = PACK == 1 || t < 2;
-    const int d0 = 16 * warp + g;
-    if (writer) {
-        const int n0 = 2 * t, n1 = 2 * t + 1;  // query index (t < 2 when packed)
-        float* po = p.part_o + ((bh * p.S + split) * kCols) * kD;  // p.S: partial slots per group
-        po[n0 * kD + d0] = L0 > 0.f ? o0 / L0 : 0.f;
-        po[n0 * kD + d0 + 8] = L0 > 0.f ? o2 / L0 : 0.f;
-        po[n1 * kD + d0] = L1 > 0.f ? o1 / L1 : 0.f;
-        po[n1 * kD + d0 + 8] = L1 > 0.f ? o3 / L1 : 0.f;
-        if (warp == 0 && g == 0) {
-            p.part_lse[(bh * p.S + split) * kCols + n0] = L0 > 0.f ? M0 + log2f(L0) : -INFINITY;
-            p.part_lse[(bh * p.S + split) * kCols + n1] = L1 > 0.f ? M1 + log2f(L1) : -INFINITY;
-        }
-    }
-    // ---- the last segment CTA of this (b, h) merges its partials
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const int prev = atomicAdd(&p.counters[bh], 1);
-        last = prev == n_seg - 1;
-        if (last) p.counters[bh] = 0;
-    }
-    __syncthreads();
-    if (last) {
-    __threadfence();
-    for (int e = tid; e < NQ * kD; e += kThreads) {
-        const int n = e / kD, d = e - n * kD;
-        const float* pl = p.part_lse + bh * p.S * kCols + n;
-        float M = -INFINITY;
-        for (int s = 0; s < n_seg; ++s) M = fmaxf(M, __ldcg(pl + s * kCols));
-        float W = 0.f, acc = 0.f;
-        if (M != -INFINITY) {
-            for (int s = 0; s < n_seg; ++s) {
-                const float wgt = exp2f(__ldcg(pl + s * kCols) - M);
-                W += wgt;
-                acc += wgt * __ldcg(p.part_o + ((bh * p.S + s) * kCols + n) * kD + d);
-            }
-        }
-        const int gi = n / p.qlen, qi = n - gi * p.qlen;
-        const int64_t row = ((int64_t)b * p.Hkv * p.G + (int64_t)h * p.G + gi) * p.qlen + qi;
-        p.out[row * kD + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
-        if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
-    }
-    }
-    __syncthreads();  // shared state is reset for the next segment
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
 }
 
-// R [N x MJ] fp16 row-major -> A-fragment orders of R (tokens x MJ) and R^T (MJ x tokens).
-__global__ void operator_fragments_kernel(const __half* __restrict__ R, int N, int MJ, uint4* __restrict__ rf,
-                                          uint4* __restrict__ rtf) {
-    const int64_t total = (int64_t)(N / 16) * (MJ / 16) * 32;
+// R [N x MJ] fp16 row-major -> the operator chunks the kernel copies: for each 64-token chunk c,
+// R_c (rows = tokens, K = MJ) and R^T_c (rows = MJ, K = the chunk's tokens), each a K-major operand in
+// 128-byte swizzle, ready for a plain bulk copy into a 1024-byte aligned shared-memory slot.
+__global__ void operator_chunks_kernel(const __half* __restrict__ R, int N, int MJ, __half* __restrict__ rop,
+                                       __half* __restrict__ rtop) {
+    const int64_t total = (int64_t)N * MJ;
+    const uint32_t chunk_elems = (uint32_t)kChunk * MJ;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int lane = (int)(i & 31);
-        const int64_t tile = i >> 5;
-        const int g = lane >> 2, t = lane & 3;
-        auto at = [&](int r, int c) { return R[(int64_t)r * MJ + c]; };
-        auto pk = [](__half lo, __half hi) {
-            return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-        };
-        {  // R: tile (tt, kk) row-major over [N/16][MJ/16]
-            const int tt = (int)(tile / (MJ / 16)), kk = (int)(tile % (MJ / 16));
-            const int r0 = 16 * tt + g, c0 = 16 * kk + 2 * t;
-            rf[i] = make_uint4(pk(at(r0, c0), at(r0, c0 + 1)), pk(at(r0 + 8, c0), at(r0 + 8, c0 + 1)),
-                               pk(at(r0, c0 + 8), at(r0, c0 + 9)), pk(at(r0 + 8, c0 + 8), at(r0 + 8, c0 + 9)));
-        }
-        {  // R^T: tile (mt, tt) over [MJ/16][N/16]; element (row m, col token) = R[token][m]
-            const int mt = (int)(tile / (N / 16)), tt = (int)(tile % (N / 16));
-            const int m0 = 16 * mt + g, k0 = 16 * tt + 2 * t;
-            rtf[i] = make_uint4(pk(at(k0, m0), at(k0 + 1, m0)), pk(at(k0, m0 + 8), at(k0 + 1, m0 + 8)),
-                                pk(at(k0 + 8, m0), at(k0 + 9, m0)), pk(at(k0 + 8, m0 + 8), at(k0 + 9, m0 + 8)));
-        }
+        const int tok = (int)(i / MJ), m = (int)(i - (int64_t)tok * MJ);
+        const int cidx = tok / kChunk, tl = tok - cidx * kChunk;
+        const __half v = R[i];
+        rop[(int64_t)cidx * chunk_elems + sw128(tl, m, kChunk) / 2] = v;
+        rtop[(int64_t)cidx * chunk_elems + sw128(m, tl, MJ) / 2] = v;
     }
 }
 
@@ -607,13 +872,14 @@ extern "C" {
 int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, void* r_frag, void* rt_frag,
                                 argus_stream_t stream) {
     if (!R || !r_frag || !rt_frag) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
-    if (n_tokens <= 0 || n_rows <= 0 || n_tokens % 16 || n_rows % 16)
-        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "block tokens and rows must be positive multiples of 16");
+    if (n_tokens <= 0 || n_rows <= 0 || n_tokens % jla::kChunk || n_rows % 64)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT,
+                               "block tokens and rows must be positive multiples of 64");
     if (!argus_aligned(r_frag, 16) || !argus_aligned(rt_frag, 16))
-        return argus_set_error(ARGUS_ERR_MISALIGNED, "fragment buffers must be 16-byte aligned");
-    const int64_t total = (int64_t)(n_tokens / 16) * (n_rows / 16) * 32;
-    jla::operator_fragments_kernel<<<argus_grid_cap((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const __half*>(R), n_tokens, n_rows, static_cast<uint4*>(r_frag), static_cast<uint4*>(rt_frag));
+        return argus_set_error(ARGUS_ERR_MISALIGNED, "operator buffers must be 16-byte aligned");
+    const int64_t total = (int64_t)n_tokens * n_rows;
+    jla::operator_chunks_kernel<<<argus_grid_cap((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const __half*>(R), n_tokens, n_rows, static_cast<__half*>(r_frag), static_cast<__half*>(rt_frag));
     ARGUS_CHECK_LAUNCH();
     return ARGUS_OK;
 }
@@ -674,8 +940,8 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "non-positive size");
     if (s->head_dim != jla::kD || s->block_rows != jla::kMJ)
         return argus_set_error(ARGUS_ERR_UNSUPPORTED, "JL attention supports head_dim 128 and 128-row blocks");
-    if (s->block_tokens <= 0 || s->block_tokens % (16 * jla::kWarps))
-        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "block tokens must be a multiple of 128");
+    if (s->block_tokens <= 0 || s->block_tokens % jla::kChunk)
+        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "block tokens must be a multiple of 64");
     const int NQ = s->group * s->q_len;
     if (NQ > jla::kCols) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "at most 8 queries per kv head");
     if (s->n_splits > (s->n_blocks > 0 ? s->n_blocks : 1))
@@ -689,10 +955,8 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     int rc = make_block_map(&p.tmk, yk, s);
     if (rc == ARGUS_OK) rc = make_block_map(&p.tmv, yv, s);
     if (rc != ARGUS_OK) return rc;
-    p.yk = reinterpret_cast<const __half*>(yk);
-    p.yv = reinterpret_cast<const __half*>(yv);
-    p.rf = static_cast<const uint4*>(r_frag);
-    p.rtf = static_cast<const uint4*>(rt_frag);
+    p.rop = static_cast<const unsigned char*>(r_frag);
+    p.rtop = static_cast<const unsigned char*>(rt_frag);
     p.q = reinterpret_cast<const __half*>(q);
     p.out = reinterpret_cast<__half*>(out);
     p.lse = lse;
@@ -701,19 +965,16 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     p.counters = static_cast<int*>(workspace);
     p.part_lse = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + ((groups * 4 + 255) & ~255LL));
     p.part_o = p.part_lse + groups * jl_slots(s) * jla::kCols;
-    p.bh_stride = s->bh_stride;
-    p.block_stride = s->block_stride;
     p.B = s->batch; p.Hkv = s->heads_kv; p.G = s->group; p.qlen = s->q_len;
     p.n_blocks = s->n_blocks; p.N = s->block_tokens; p.S = (int)jl_slots(s);
     p.scale_log2 = s->scale * 1.4426950408889634f;
     cudaStream_t st = (cudaStream_t)stream;
-    const bool pack = NQ <= 4;
-    const int64_t pairs = groups * ((s->n_blocks + (pack ? 1 : 0)) / (pack ? 2 : 1));
+    const int64_t blocks = groups * s->n_blocks;
     const int64_t ctas = jl_ctas(s);
-    if (ctas > pairs || ctas > 0x7fffffff)
-        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "more CTAs than block pairs");
-    const size_t smem = jla::smem_bytes(pack ? 2 : 1);
-    auto kern = pack ? jla::jl_attn_kernel<2> : jla::jl_attn_kernel<1>;
+    if (ctas > blocks || ctas > 0x7fffffff)
+        return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "more CTAs than blocks");
+    const size_t smem = jla::kSmemBytes;
+    auto kern = jla::jl_attn_tc_kernel;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
     kern<<<(unsigned)ctas, jla::kThreads, smem, st>>>(p);

@@ -206,9 +206,9 @@ typedef struct argus_jl_attn_shape {
     int32_t block_tokens;  /* tokens a block stands for (N) */
     int32_t n_blocks;
     int32_t n_splits;      /* split-K partitions of each (batch, kv_head)'s blocks (<= n_blocks) */
-    int32_t n_ctas;        /* > 0: this many CTAs share the block pairs of all (batch, kv_head) in equal
-                              contiguous ranges (a range may span two heads), instead of n_splits per
-                              (batch, kv_head); at most the number of block pairs */
+    int32_t n_ctas;        /* > 0: this many CTAs share the blocks of all (batch, kv_head) in equal
+                              contiguous ranges (a range may span heads), instead of n_splits per
+                              (batch, kv_head); at most the number of blocks */
     float scale;
     int32_t reserved;
     int64_t bh_stride;     /* elements */
@@ -216,8 +216,9 @@ typedef struct argus_jl_attn_shape {
 } argus_jl_attn_shape;
 
 /* Writes R [n_tokens][n_rows] (fp16, the reconstruction operator of core/memory_manager.py:241-282)
- * into the MMA fragment orders the JL attention reads: r_frag and rt_frag, n_tokens*n_rows*2 bytes
- * each, 16-byte aligned.  Done once per operator. */
+ * into the operator chunks the JL attention copies: for every 64 tokens, R and R^T as K-major
+ * tensor-core operands in 128-byte swizzle (r_frag and rt_frag, n_tokens*n_rows*2 bytes each,
+ * 16-byte aligned; n_tokens and n_rows multiples of 64).  Done once per operator. */
 int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, void* r_frag, void* rt_frag,
                                 argus_stream_t stream);
 /* Workspace bytes of argus_jl_attention: one arrival counter per (batch, kv_head) at the front

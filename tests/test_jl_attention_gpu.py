@@ -102,15 +102,18 @@ def test_jl_attention_matches_rebuilt_attention(B, Hkv, G, ql, N, ratio, nb, spl
 
 
 @pytest.mark.parametrize("B,Hkv,G,nb,n_ctas", [
-    (2, 2, 4, 7, 5),      # CTA ranges of block pairs that span two heads
+    (2, 2, 4, 7, 5),      # CTA ranges that span two heads
     (1, 3, 4, 9, 4),
-    (2, 2, 8, 3, 5),      # 8 queries per head: one block per MMA, ranges of single blocks
-    (1, 2, 4, 6, None),   # the default: one CTA per block pair here
+    (2, 2, 8, 3, 5),      # 8 queries per head
+    (1, 2, 4, 6, None),   # the default: one CTA per block here
+    (1, 1, 4, 40, 1),     # one CTA, two rounds: 32 blocks (128 rows, hi and lo MMAs) then 8 (stacked)
+    (1, 2, 8, 20, 2),     # 8 queries: rounds of 16 blocks, a head continued across rounds
+    (1, 2, 4, 20, 2),     # 80 rows in one round (hi and lo MMAs, three softmax warps)
 ])
 def test_jl_attention_ctas_span_heads(B, Hkv, G, nb, n_ctas):
-    """CTAs that take a contiguous range of all heads' block pairs (crossing from one head to the
-    next) give the same attention and per-block LSE as the rebuilt K/V, on two launches in a row
-    (the arrival counters are left at zero)."""
+    """CTAs that take a contiguous range of all heads' blocks (crossing from one head to the next,
+    in rounds of at most 128 (block, query) rows) give the same attention and per-block LSE as the
+    rebuilt K/V, on two launches in a row (the arrival counters are left at zero)."""
     from argus_b200 import attention as A
     from argus_b200.core import jl
     N, ratio, D, ql = 512, 4, 128, 1
