@@ -48,7 +48,8 @@ constexpr int kCols = 8;     // query columns of the CUDA-core MMAs (queries per
 constexpr int kSlots = 4;    // 32 KB shared-memory slots
 constexpr uint32_t kSlotBytes = (uint32_t)kMJ * kD * 2;          // one Yk / Yv block
 constexpr uint32_t kOpChunkBytes = (uint32_t)kChunk * kMJ * 2;   // R_c or R^T_c
-constexpr long long kSpinLimit = 1ll << 26;
+constexpr long long kWaitTries = 1ll << 21;  // x kWaitHintNs: about two seconds
+constexpr uint32_t kWaitHintNs = 1000;
 constexpr float kNoMax = -1.0e30f;
 constexpr float kSlack = 8.0f;  // a row's reference max is raised only when a score passes it by 2^8
 // tensor memory: three S / P buffers (64 columns each; P, fp16, overwrites the first 32 of its S),
@@ -137,13 +138,15 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
+// Bounded wait: each try_wait suspends the thread (up to kWaitHintNs) until the phase completes, so
+// waiting warps leave the issue slots to the warps that share their scheduler.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
-    for (long long i = 0; i < kSpinLimit; ++i) {
+    for (long long i = 0; i < kWaitTries; ++i) {
         uint32_t ok;
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(ok)
-            : "r"(bar), "r"(phase)
+            : "r"(bar), "r"(phase), "n"(kWaitHintNs)
             : "memory");
         if (ok) return true;
     }
