@@ -692,10 +692,11 @@ class PagedDynamicKVCache:
         return plan
 
     def _fused_jl(self, q):
-        """Whether JL pages are attended by the fused JL kernel (128-row blocks, i.e. 512-token pages,
-        head_dim 128, <= 8 queries per kv head) rather than rebuilt into the scratch arena."""
+        """Whether JL pages are attended by the fused JL kernel (64- or 128-row blocks, i.e. 256- or
+        512-token pages at the projection ratio 4, head_dim 64 or 128, <= 8 queries per kv head)
+        rather than rebuilt into the scratch arena."""
         B, Hq, qlen, D = q.shape
-        if not (self.fused_jl_attention and self.jl_pages) or self.page_size // 4 != 128 or D != 128:
+        if not (self.fused_jl_attention and self.jl_pages) or self.page_size not in (256, 512) or D not in (64, 128):
             return False
         Hkv = self.H if self._pools_allocated else self.sink_k.shape[1]
         return (Hq // Hkv) * qlen <= 8 and self._pools_allocated

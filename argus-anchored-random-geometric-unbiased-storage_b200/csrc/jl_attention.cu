@@ -40,14 +40,13 @@ namespace jla {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kD = 128;      // head_dim
-constexpr int kMJ = 128;     // rows per archived block
+constexpr int kD = 128;      // largest head_dim (64 or 128); strides of the partial outputs
+constexpr int kMJ = 128;     // largest rows per archived block (64 or 128)
 constexpr int kRows = 128;   // (block, query) rows per round = tensor-memory lanes
 constexpr int kChunk = 64;   // operator tokens per SW step
 constexpr int kCols = 8;     // query columns of the CUDA-core MMAs (queries per kv head <= 8)
 constexpr int kSlots = 4;    // 32 KB shared-memory slots
-constexpr uint32_t kSlotBytes = (uint32_t)kMJ * kD * 2;          // one Yk / Yv block
-constexpr uint32_t kOpChunkBytes = (uint32_t)kChunk * kMJ * 2;   // R_c or R^T_c
+constexpr uint32_t kSlotBytes = (uint32_t)kMJ * kD * 2;          // room for one Yk / Yv block
 constexpr long long kWaitTries = 1ll << 21;  // x kWaitHintNs: about two seconds
 constexpr uint32_t kWaitHintNs = 1000;
 constexpr float kNoMax = -1.0e30f;
@@ -169,24 +168,31 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// Copies block j of (b, h) into `dst` (two swizzled 64-column halves) and arms `bar` for its bytes.
+// Copies block j of (b, h) into `dst` (D / 64 swizzled 64-column halves of MJ rows) and arms `bar`.
+template <int D, int MJ>
 __device__ __forceinline__ void issue_block(const CUtensorMap* map, int64_t bh, int j, uint32_t dst, uint32_t bar) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, kSlotBytes);
+    mbar_expect_tx(bar, (uint32_t)MJ * D * 2);
     tma_load_4d(dst, map, 0, 0, j, (int)bh, bar);
-    tma_load_4d(dst + kMJ * 128, map, 64, 0, j, (int)bh, bar);
+    if (D > 64) tma_load_4d(dst + MJ * 128, map, 64, 0, j, (int)bh, bar);
 }
-// Copies operator chunk c (R_c then R^T_c, 16 KB each) into `dst` and arms `bar`.
+// bytes of R_c or R^T_c (64 operator tokens x MJ rows)
+template <int MJ>
+__host__ __device__ constexpr uint32_t op_chunk_bytes() { return (uint32_t)kChunk * MJ * 2; }
+// Copies operator chunk c (R_c then R^T_c) into `dst` and arms `bar`.
+template <int MJ>
 __device__ __forceinline__ void issue_op_chunk(const Params& p, int c, uint32_t dst, uint32_t bar) {
+    constexpr uint32_t B = op_chunk_bytes<MJ>();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, 2 * kOpChunkBytes);
-    bulk_g2s(dst, p.rop + (size_t)c * kOpChunkBytes, kOpChunkBytes, bar);
-    bulk_g2s(dst + kOpChunkBytes, p.rtop + (size_t)c * kOpChunkBytes, kOpChunkBytes, bar);
+    mbar_expect_tx(bar, 2 * B);
+    bulk_g2s(dst, p.rop + (size_t)c * B, B, bar);
+    bulk_g2s(dst + B, p.rtop + (size_t)c * B, B, bar);
 }
 
 // Shared-memory address of element (row r, column c) of a swizzled [MJ][D] Y block.
+template <int MJ>
 __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) {
-    return base + (uint32_t)((c >> 6) * (kMJ * 128) + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
+    return base + (uint32_t)((c >> 6) * (MJ * 128) + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
 }
 // K-major operand in 128-byte swizzle (the layout a TMA copy with SWIZZLE_128B writes): K in blocks of
 // 64 fp16, each block `rows` x 128 bytes, 16-byte chunk c of row r at chunk c ^ (r % 8), 8-row groups
@@ -255,6 +261,7 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+template <int D, int MJ>
 __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -317,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
             __threadfence_block();
             if (atomicAdd(&cnt[s], 1) == kWarps - 1) {
                 cnt[s] = 0;
-                issue_block(map, x / p.n_blocks, (int)(x % p.n_blocks), slot((uint32_t)s), bar(kBarFull + s));
+                issue_block<D, MJ>(map, x / p.n_blocks, (int)(x % p.n_blocks), slot((uint32_t)s), bar(kBarFull + s));
             }
         }
         pend |= 1u << s;
@@ -342,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int n = 2 * t + k;
-            if (n < NQ) {
+            if (n < NQ && d0 < D) {
                 const float L = openL[n];
                 po[n * kD + d0] = L > 0.f ? oacc[k] / L : 0.f;
                 po[n * kD + d0 + 8] = L > 0.f ? oacc[2 + k] / L : 0.f;
@@ -361,8 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         if (misc[1]) {
             __threadfence();
             const int64_t b = bh / p.Hkv, h = bh - b * p.Hkv;
-            for (int e = tid; e < NQ * kD; e += kThreads) {
-                const int n = e / kD, d = e - n * kD;
+            for (int e = tid; e < NQ * D; e += kThreads) {
+                const int n = e / D, d = e - n * D;
                 const float* pl = p.part_lse + bh * p.S * kCols + n;
                 float M = -INFINITY;
                 for (int s = 0; s < n_seg; ++s) M = fmaxf(M, __ldcg(pl + s * kCols));
@@ -376,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 }
                 const int gi = n / p.qlen, qi = n - gi * p.qlen;
                 const int64_t row = ((b * p.Hkv + h) * p.G + gi) * p.qlen + qi;
-                p.out[row * kD + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
+                p.out[row * D + d] = __float2half_rn(W > 0.f ? acc / W : 0.f);
                 if (p.lse && d == 0) p.lse[row] = (W > 0.f) ? (M + log2f(W)) * 0.69314718055994530942f : -INFINITY;
             }
         }
@@ -389,13 +396,13 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         // ================================================================ U phase
         for (int i = 0; i < nb && i < 4; ++i) {
             const int64_t x = xr + i;
-            if (tid == 0) issue_block(&p.tmk, x / p.n_blocks, (int)(x % p.n_blocks), slot(i), bar(kBarFull + i));
+            if (tid == 0) issue_block<D, MJ>(&p.tmk, x / p.n_blocks, (int)(x % p.n_blocks), slot(i), bar(kBarFull + i));
             pend |= 1u << i;
         }
         bool wok = true;
         {
             int64_t qbh = -1;
-            uint32_t qa[kD / 16][2];
+            uint32_t qa[D / 16][2];
             for (int i = 0; i < nb; ++i) {
                 const int s = i % 4;
                 wok = arrive_slot(s);
@@ -404,28 +411,32 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 if (bh != qbh) {  // query fragments of this (b, h): column n = query n
                     qbh = bh;
                     const int64_t b = bh / p.Hkv, h = bh - b * p.Hkv;
-                    const __half* qb = p.q + ((b * p.Hkv + h) * p.G) * p.qlen * kD;
+                    const __half* qb = p.q + ((b * p.Hkv + h) * p.G) * p.qlen * D;
 #pragma unroll
-                    for (int kk = 0; kk < kD / 16; ++kk) {
+                    for (int kk = 0; kk < D / 16; ++kk) {
                         const int d = 16 * kk + 2 * t;
-                        qa[kk][0] = g < NQ ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * kD + d) : 0u;
-                        qa[kk][1] = g < NQ ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * kD + d + 8) : 0u;
+                        qa[kk][0] = g < NQ ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * D + d) : 0u;
+                        qa[kk][1] = g < NQ ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * D + d + 8) : 0u;
                     }
                 }
-                // u = Yk . q^T for block rows 16*warp .. +15 -> U^T rows i*NQ + n
+                // u = Yk . q^T for block rows 16*warp .. +15 -> U^T rows i*NQ + n (warps past the
+                // block's MJ rows only pass the slot on)
+                const bool urows = 16 * warp < MJ;
                 float u[4] = {0.f, 0.f, 0.f, 0.f}, u2[4] = {0.f, 0.f, 0.f, 0.f};
                 const int row = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1), colo = 8 * (lane >> 4);
+                if (urows) {
 #pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk) {
-                    uint32_t a[4];
-                    ldsm_x4(swz(slot((uint32_t)s), row, 16 * kk + colo), a);
-                    mma16816((kk & 1) ? u2 : u, a, qa[kk][0], qa[kk][1]);
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        uint32_t a[4];
+                        ldsm_x4(swz<MJ>(slot((uint32_t)s), row, 16 * kk + colo), a);
+                        mma16816((kk & 1) ? u2 : u, a, qa[kk][0], qa[kk][1]);
+                    }
                 }
                 release(s, i + 4 < nb, &p.tmk, x + 4);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const int mj = 16 * warp + g + 8 * (k >> 1), n = 2 * t + (k & 1);
-                    if (n < NQ) {
+                    if (urows && n < NQ) {
                         __half hi, lo;
                         split_hl(u[k] + u2[k], hi, lo);
                         const uint32_t off = rowsw(i * NQ + n, mj);
@@ -450,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 const int src = stacked ? (r & 63) : r;
                 const uint32_t sbase_u = (stacked ? r >= 64 : hl) ? ulo : uhi;
 #pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {
+                for (int h2 = 0; h2 < MJ / 64; ++h2) {
                     uint32_t v[32];
 #pragma unroll
                     for (int kc = 0; kc < 8; ++kc) {
@@ -476,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         for (int i = 0; i < nb && i < 2 && !stacked; ++i) {
             const int64_t x = xr + i;
             const uint32_t sl = oslot(i);
-            if (tid == 0) issue_block(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
+            if (tid == 0) issue_block<D, MJ>(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
             pend |= 1u << sl;
         }
         // Warps 0-3 run the softmax of the lane quarters that hold this round's rows (the others
@@ -488,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 int loaded = 0;
                 auto load = [&](int cc) {
                     const int k = (int)((gchunk + cc) & 3);
-                    issue_op_chunk(p, cc, slot((uint32_t)k), bar(kBarRF + k));
+                    issue_op_chunk<MJ>(p, cc, slot((uint32_t)k), bar(kBarRF + k));
                     loaded = cc + 1;
                 };
                 for (int cc = 0; cc < 4 && cc < nchunks; ++cc) load(cc);
@@ -504,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         } else if (warp == 6) {
             if (lane == 0) {  // issues the MMAs
                 tc_fence_after();
-                const uint32_t id_s = idesc(kRows, kChunk), id_w = idesc(kRows, kMJ);
+                const uint32_t id_s = idesc(kRows, kChunk), id_w = idesc(kRows, MJ);
                 int last_bar = -1;
                 uint32_t last_par = 0;
                 int landed = 0;  // operator chunks seen arrived
@@ -515,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                     tc_fence_after();
                     const uint32_t d = tmem + (uint32_t)(gc % kSBufs) * kChunk, rsm = slot((uint32_t)(gc & 3));
 #pragma unroll
-                    for (int ks = 0; ks < kMJ / 16; ++ks) {
+                    for (int ks = 0; ks < MJ / 16; ++ks) {
                         const uint64_t bd = sdesc(rsm + (uint32_t)(ks >> 2) * (kChunk * 128) + (uint32_t)(ks & 3) * 32);
                         umma_ts(d, tmem + kTmemUhi + 8 * ks, bd, id_s, ks > 0 ? 1u : 0u);
                         if (!stacked) umma_ts(d, tmem + kTmemUlo + 8 * ks, bd, id_s, 1u);
@@ -536,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                     if (!wok) break;
                     tc_fence_after();
                     // W += P_cc . R_cc  (A = P_cc in tensor memory; B = R^T_cc, K-major: rows MJ, K = tokens)
-                    const uint32_t rtsm = slot((uint32_t)(gc & 3)) + kOpChunkBytes;
+                    const uint32_t rtsm = slot((uint32_t)(gc & 3)) + op_chunk_bytes<MJ>();
                     const uint32_t pt = tmem + (uint32_t)(gc % kSBufs) * kChunk;
 #pragma unroll
                     for (int ks = 0; ks < kChunk / 16; ++ks)
@@ -632,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                     if (!wok) break;
                     tc_fence_after();
 #pragma unroll
-                    for (int j0 = 0; j0 < kMJ; j0 += 32) {
+                    for (int j0 = 0; j0 < MJ; j0 += 32) {
                         uint32_t w[32];
                         JLA_TMEM_LD32(trow + kTmemW + j0, w);
                         tmem_wait_ld();
@@ -670,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         for (int i = stacked ? 0 : 2; i < nb && i < 4; ++i) {
             const int64_t x = xr + i;
             const uint32_t sl = oslot(i);
-            if (tid == 0) issue_block(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
+            if (tid == 0) issue_block<D, MJ>(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
             pend |= 1u << sl;
         }
 
@@ -709,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
             const bool live = r < rows;
             const float f = live ? frow[r] : 0.f;
 #pragma unroll
-            for (int j0 = 0; j0 < kMJ; j0 += 32) {
+            for (int j0 = 0; j0 < MJ; j0 += 32) {
                 uint32_t w[32];
                 JLA_TMEM_LD32(trow + kTmemW + j0, w);
                 tmem_wait_ld();
@@ -763,13 +774,13 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 __syncthreads();
             }
             // o += Yv^T . w' for dims 16*warp .. +15 (columns: the block's queries)
-            {
+            if (16 * warp < D) {
                 const int mr = (lane & 7) + 8 * (lane >> 4), dcol = 16 * warp + 8 * ((lane >> 3) & 1);
                 const bool lq = g < NQ;
                 const int r = i * NQ + g;
                 float olo[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int kk = 0; kk < kMJ / 16; ++kk) {
+                for (int kk = 0; kk < MJ / 16; ++kk) {
                     uint32_t wh0 = 0u, wh1 = 0u, wl0 = 0u, wl1 = 0u;
                     if (lq) {
                         const uint32_t o0 = rowsw(r, 16 * kk + 2 * t), o1 = rowsw(r, 16 * kk + 8 + 2 * t);
@@ -779,7 +790,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                         asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wl1) : "r"(wlo + o1));
                     }
                     uint32_t a[4];
-                    ldsm_x4_t(swz(slot((uint32_t)s), 16 * kk + mr, dcol), a);
+                    ldsm_x4_t(swz<MJ>(slot((uint32_t)s), 16 * kk + mr, dcol), a);
                     mma16816(oacc, a, wh0, wh1);
                     mma16816(olo, a, wl0, wl1);
                 }
@@ -941,8 +952,8 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
     if (s->batch <= 0 || s->heads_kv <= 0 || s->group <= 0 || s->q_len <= 0 || s->n_blocks < 0 || s->n_splits <= 0)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "non-positive size");
-    if (s->head_dim != jla::kD || s->block_rows != jla::kMJ)
-        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "JL attention supports head_dim 128 and 128-row blocks");
+    if ((s->head_dim != 64 && s->head_dim != 128) || (s->block_rows != 64 && s->block_rows != 128))
+        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "JL attention supports head_dim 64 or 128 and 64- or 128-row blocks");
     if (s->block_tokens <= 0 || s->block_tokens % jla::kChunk)
         return argus_set_error(ARGUS_ERR_UNSUPPORTED, "block tokens must be a multiple of 64");
     const int NQ = s->group * s->q_len;
@@ -977,7 +988,8 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
     if (ctas > blocks || ctas > 0x7fffffff)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "more CTAs than blocks");
     const size_t smem = jla::kSmemBytes;
-    auto kern = jla::jl_attn_tc_kernel;
+    auto kern = s->head_dim == 128 ? (s->block_rows == 128 ? jla::jl_attn_tc_kernel<128, 128> : jla::jl_attn_tc_kernel<128, 64>)
+                                   : (s->block_rows == 128 ? jla::jl_attn_tc_kernel<64, 128> : jla::jl_attn_tc_kernel<64, 64>);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return argus_set_cuda_error(e);
     kern<<<(unsigned)ctas, jla::kThreads, smem, st>>>(p);

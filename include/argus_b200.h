@@ -225,7 +225,8 @@ int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, voi
  * (zero before the first use with a shape; every completed launch leaves them zero) and the split
  * partials. */
 int64_t argus_jl_attention_workspace_size(const argus_jl_attn_shape* shape);
-/* q [B, heads_kv*group, q_len, 128] fp16 -> out (same shape, fp16) and optional lse (natural log,
+/* q [B, heads_kv*group, q_len, D] fp16 (D 64 or 128; blocks of 64 or 128 rows) -> out (same shape,
+ * fp16) and optional lse (natural log,
  * [B, heads_kv*group, q_len] fp32) over the archived tokens only.  Optional block_lse
  * [B*heads_kv][n_blocks][8] fp32 receives each block's natural-log LSE per query (group*q_len
  * queries used): the per-page attention mass of the importance policy

@@ -141,6 +141,44 @@ def test_jl_attention_ctas_span_heads(B, Hkv, G, nb, n_ctas):
         assert np.allclose(block_lse.cpu().numpy()[:, :, :G * ql], ref_blk, rtol=0, atol=2e-3)
 
 
+@pytest.mark.parametrize("D,N,ratio,G,nb,n_ctas", [
+    (64, 512, 4, 4, 5, 3),     # head_dim 64, 128-row blocks
+    (128, 256, 4, 4, 5, 3),    # 64-row blocks
+    (64, 256, 4, 4, 5, 3),     # both
+    (64, 256, 4, 8, 20, 2),    # 64-row blocks, 8 queries: rounds of 16 blocks (128 rows), then 4
+    (64, 1024, 16, 4, 40, 1),  # one CTA over two rounds
+])
+def test_jl_attention_head_dims_and_block_rows(D, N, ratio, G, nb, n_ctas):
+    """head_dim 64 and 64-row blocks (256-token pages at the reference's ratio 4) through the same
+    kernel: attention and per-block LSE as the rebuilt K/V."""
+    from argus_b200 import attention as A
+    from argus_b200.core import jl
+    B, Hkv, ql = 1, 2, 1
+    MJ = N // ratio
+    R = operator(N, ratio)
+    g = torch.Generator().manual_seed(D + N + nb)
+    yk = torch.randn(B, Hkv, nb, MJ, D, generator=g).half()
+    yv = torch.randn(B, Hkv, nb, MJ, D, generator=g).half()
+    q = (torch.randn(B, Hkv * G, ql, D, generator=g) / math.sqrt(D) * 2.0).half()
+    att = jl.JLAttention(R.cuda())
+    block_lse = torch.empty(B * Hkv, nb, 8, dtype=torch.float32, device="cuda")
+    out, lse = att.run(q.cuda(), yk.cuda(), yv.cuda(), block_lse=block_lse, n_ctas=n_ctas)
+    torch.cuda.synchronize()
+    assert A.device_status() == 0
+    K, V = rebuild(R, yk), rebuild(R, yv)
+    ref, _ = f64_attention(q.numpy(), K, V, 1.0 / math.sqrt(D))
+    got = out.cpu().numpy().astype(np.float64)
+    assert within(got, ref).all(), np.abs(got - ref).max()
+    Kx = np.repeat(K.astype(np.float64), G, axis=1)
+    s = np.einsum("bhqd,bhkd->bhqk", q.numpy().astype(np.float64), Kx) / math.sqrt(D)
+    mx = s.max(-1)
+    assert np.allclose(lse.cpu().numpy(), mx + np.log(np.exp(s - mx[..., None]).sum(-1)), rtol=0, atol=2e-3)
+    sb = s.reshape(B, Hkv, G, ql, nb, N)
+    mb = sb.max(-1)
+    ref_blk = (mb + np.log(np.exp(sb - mb[..., None]).sum(-1))).reshape(B * Hkv, G * ql, nb).transpose(0, 2, 1)
+    assert np.allclose(block_lse.cpu().numpy()[:, :, :G * ql], ref_blk, rtol=0, atol=2e-3)
+
+
 def test_merge_joins_jl_archive_with_other_tiers():
     from argus_b200 import attention as A
     from argus_b200.core import jl

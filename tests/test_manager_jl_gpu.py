@@ -1,5 +1,5 @@
-"""PagedDynamicKVCache with 512-token pages (128-row JL blocks): inplace_paged_attention attends the
-JL pages without rebuilding them (JLAttention + LSE merge) and gives the same output (attention bar
+"""PagedDynamicKVCache with 512- and 256-token pages (128- and 64-row JL blocks) at head_dim 128 and
+64: inplace_paged_attention attends the JL pages without rebuilding them (JLAttention + LSE merge) and gives the same output (attention bar
 plus the JL slack of the other manager tests), per-page attention mass and tier moves as the path
 that rebuilds them into the fp16 scratch arena."""
 import math
@@ -14,13 +14,13 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-def run_cache(fused, tmp_path, pushes, q):
+def run_cache(fused, tmp_path, pushes, q, page=512):
     from argus_b200.core.memory_manager import PagedDynamicKVCache
     os.environ["ARGUS_LOG_LEVEL"] = "quiet"
     cwd = os.getcwd()
     os.chdir(tmp_path)
     try:
-        c = PagedDynamicKVCache(page_size=512, max_active_pages=1, max_fp8_pages=1, max_int8_pages=1,
+        c = PagedDynamicKVCache(page_size=page, max_active_pages=1, max_fp8_pages=1, max_int8_pages=1,
                                 max_int4_pages=1, max_int2_pages=1, max_one_bit_pages=1, sink_tokens=16,
                                 threshold_sigma=0.0)
         c.fused_jl_attention = fused
@@ -34,15 +34,16 @@ def run_cache(fused, tmp_path, pushes, q):
     return c, out, K, V
 
 
-def test_fused_jl_pages_match_rebuilt_pages(tmp_path):
+@pytest.mark.parametrize("page,D", [(512, 128), (256, 128), (512, 64), (256, 64)])
+def test_fused_jl_pages_match_rebuilt_pages(tmp_path, page, D):
     from argus_b200 import attention as A
     g = torch.Generator().manual_seed(9)
-    B, H, D = 1, 2, 128
-    pushes = [(torch.randn(B, H, 512, D, generator=g).half(), torch.randn(B, H, 512, D, generator=g).half())
+    B, H = 1, 2
+    pushes = [(torch.randn(B, H, page, D, generator=g).half(), torch.randn(B, H, page, D, generator=g).half())
               for _ in range(10)]
     q = (torch.randn(B, H * 4, 1, D, generator=g) * 2.0 / math.sqrt(D)).half()
-    c1, out1, K1, V1 = run_cache(True, tmp_path, pushes, q)
-    c0, out0, K0, V0 = run_cache(False, tmp_path, pushes, q)
+    c1, out1, K1, V1 = run_cache(True, tmp_path, pushes, q, page)
+    c0, out0, K0, V0 = run_cache(False, tmp_path, pushes, q, page)
     assert A.device_status() == 0
     # the fused path built its JL attention; the other rebuilt the pages instead
     assert len(c1.jl_pages) >= 2 and c1._jl_attention is not None and c0._jl_attention is None
