@@ -30,6 +30,8 @@ SIGNATURES = {
     "argus_dequant_int8": [_p, _p, _i64, _i32, _p, _p],
     "argus_quant_fp8sim": [_p, _i64, _i32, _p, _p, _p],
     "argus_dequant_fp8sim": [_p, _p, _i64, _i32, _p, _p],
+    "argus_quant_e4m3": [_p, _i64, _i32, _p, _p, _p],
+    "argus_dequant_e4m3": [_p, _p, _i64, _i32, _p, _p],
     "argus_quant_int4": [_p, _i64, _i32, _p, _p, _p, _p],
     "argus_dequant_int4": [_p, _p, _p, _i64, _i32, _p, _p],
     "argus_quant_int2": [_p, _i64, _i32, _p, _p, _p, _p],

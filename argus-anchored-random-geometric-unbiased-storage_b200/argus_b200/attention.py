@@ -21,14 +21,17 @@ import torch
 
 from . import _lib
 
-TIER_FP16, TIER_FP8SIM, TIER_INT8, TIER_INT4, TIER_INT2, TIER_1BIT = range(6)
+TIER_FP16, TIER_FP8SIM, TIER_INT8, TIER_INT4, TIER_INT2, TIER_1BIT, TIER_E4M3 = range(7)
 LAYOUT_RECORD, LAYOUT_SPLIT_FP16 = 0, 1
+# TIER_E4M3 is the true-e4m3 storage mode (codes of OCP FP8 E4M3 with an fp16 scale per token), a
+# separately named non-parity tier: the reference's "fp8" tier is the int8-with-wrap simulation.
 TIER_NAMES = {"fp16": TIER_FP16, "fp8": TIER_FP8SIM, "int8": TIER_INT8, "int4": TIER_INT4, "int2": TIER_INT2,
-              "one_bit": TIER_1BIT}
-TIER_BITS = {TIER_FP16: 16, TIER_FP8SIM: 8, TIER_INT8: 8, TIER_INT4: 4, TIER_INT2: 2, TIER_1BIT: 1}
-TIER_PER = {TIER_FP16: 1, TIER_FP8SIM: 1, TIER_INT8: 1, TIER_INT4: 2, TIER_INT2: 4, TIER_1BIT: 8}
+              "one_bit": TIER_1BIT, "e4m3": TIER_E4M3}
+TIER_BITS = {TIER_FP16: 16, TIER_FP8SIM: 8, TIER_INT8: 8, TIER_INT4: 4, TIER_INT2: 2, TIER_1BIT: 1, TIER_E4M3: 8}
+TIER_PER = {TIER_FP16: 1, TIER_FP8SIM: 1, TIER_INT8: 1, TIER_INT4: 2, TIER_INT2: 4, TIER_1BIT: 8, TIER_E4M3: 1}
 TIER_PAYLOAD_DTYPE = {TIER_FP16: torch.float16, TIER_FP8SIM: torch.int8, TIER_INT8: torch.int8,
-                      TIER_INT4: torch.uint8, TIER_INT2: torch.uint8, TIER_1BIT: torch.uint8}
+                      TIER_INT4: torch.uint8, TIER_INT2: torch.uint8, TIER_1BIT: torch.uint8,
+                      TIER_E4M3: torch.uint8}
 MAX_ARENAS = 8
 NUM_SMS = 148
 
@@ -221,7 +224,7 @@ def chunk_capacity(arena, head_dim):
 # whatever its bytes (the low-bit tiers are bound by instruction latency), except fp16, whose
 # tiles stream at the HBM rate.
 TIER_TOKEN_COST = {TIER_1BIT: 0.69, TIER_INT2: 0.93, TIER_INT4: 0.96, TIER_INT8: 1.06, TIER_FP8SIM: 1.06,
-                   TIER_FP16: 2.0}
+                   TIER_FP16: 2.0, TIER_E4M3: 1.06}
 
 # CUDA graphs AttentionPlan.run_host keeps (one per pair of host buffers and scale).
 RUN_HOST_GRAPHS = 4

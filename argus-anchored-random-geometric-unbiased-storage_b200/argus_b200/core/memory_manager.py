@@ -149,7 +149,14 @@ class PagedDynamicKVCache:
     """Seven-tier paged KV cache (core/memory_manager.py:115-1824)."""
 
     def __init__(self, page_size=4096, max_active_pages=2, max_fp8_pages=2, max_int8_pages=2, max_int4_pages=2,
-                 max_int2_pages=2, max_one_bit_pages=2, sink_tokens=4, threshold_sigma=3.0, config=None):
+                 max_int2_pages=2, max_one_bit_pages=2, sink_tokens=4, threshold_sigma=3.0, config=None,
+                 fp8_format="simulated"):
+        # "simulated": the reference's FP8 tier (int8 codes with wraparound, quantization.py:203-216);
+        # "e4m3": true OCP E4M3 codes with an fp16 scale per token, a non-parity storage mode.  Fixed
+        # once the pools are allocated (the first push).
+        if fp8_format not in ("simulated", "e4m3"):
+            raise ValueError("fp8_format must be 'simulated' or 'e4m3'")
+        self.fp8_format = fp8_format
         if config is None:
             config = ArgusConfig(page_size=page_size, max_active_pages=max_active_pages, max_fp8_pages=max_fp8_pages,
                                  max_int8_pages=max_int8_pages, max_int4_pages=max_int4_pages,
@@ -278,8 +285,12 @@ class PagedDynamicKVCache:
         self.buffer_length = 0
         self.B, self.H, self.D = B, H, D
         self.arenas = {"fp16": A.KVArena.allocate(A.TIER_FP16, B, H, self.max_active_pages, P, D, dev)}
+        if self.fp8_format not in ("simulated", "e4m3"):
+            raise ValueError("fp8_format must be 'simulated' or 'e4m3'")
         for name, (attr, tier) in _TIERS.items():
             slots = getattr(self, f"max_{attr[:-6]}_pages")
+            if name == "fp8" and self.fp8_format == "e4m3":
+                tier = A.TIER_E4M3
             self.arenas[name] = A.KVArena.allocate(tier, B, H, max(1, slots), P, D, dev)
         # per pool: which slots hold live pages (host mirror, device array read by the kernel)
         self._live_host = {}

@@ -98,6 +98,19 @@ def dequantize_from_fp8_simulated(quantized: torch.Tensor, scales: torch.Tensor)
     return _dequant_sym8("argus_dequant_fp8sim", quantized, scales)
 
 
+def quantize_to_e4m3(tensor: torch.Tensor, dim: int = -1):
+    """True e4m3 (a separately named non-parity mode; the reference's FP8 tier is the simulation
+    above): s = fp16(amax / 448) per token, codes = e4m3(x / s) (nearest even, saturating, NaN -> 0),
+    returned as uint8 codes and fp16 scales [..., 1]."""
+    q, s = _quant_sym8("argus_quant_e4m3", tensor, dim)
+    return q.view(torch.uint8), s
+
+
+def dequantize_from_e4m3(quantized: torch.Tensor, scales: torch.Tensor):
+    """fp16(e4m3(code) * s)."""
+    return _dequant_sym8("argus_dequant_e4m3", quantized, scales)
+
+
 # --------------------------------------------------------------- sequence-packed low bits
 def _quant_packed(fn, per, tensor, seq_dim, quant_dim, with_min):
     _check(tensor)

@@ -15,11 +15,16 @@
 // group in shared memory (decoded from any tier), reduce each row with 8 lanes, then emit 4 output
 // bytes per thread, so one kernel both quantizes fp16 and re-quantizes a page from one tier into
 // another (the fused demotion of the cascade).
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace argus {
 
-enum QuantMode { Q_INT8 = 0, Q_FP8SIM = 1, Q_INT4 = 2, Q_INT2 = 3, Q_SIGN1 = 4, Q_OUTLIER = 5, Q_FP16 = 6 };
+// Q_E4M3 is the true-e4m3 storage mode, a separately named non-parity tier (the reference's FP8 is
+// the int8-with-wrap simulation, Q_FP8SIM): s = fp16(amax / 448), code = e4m3(x / s) from the IEEE
+// fp32 quotient (round to nearest even, saturating at 448, NaN -> 0), value = fp16(e4m3(code) * s).
+enum QuantMode { Q_INT8 = 0, Q_FP8SIM = 1, Q_INT4 = 2, Q_INT2 = 3, Q_SIGN1 = 4, Q_OUTLIER = 5, Q_FP16 = 6, Q_E4M3 = 7 };
 
 __host__ __device__ constexpr int mode_per(int m) { return m == Q_INT4 ? 2 : (m == Q_INT2 ? 4 : (m == Q_SIGN1 ? 8 : 1)); }
 __host__ __device__ constexpr int tier_mode(int tier) {
@@ -27,7 +32,8 @@ __host__ __device__ constexpr int tier_mode(int tier) {
          : tier == ARGUS_TIER_FP8SIM ? Q_FP8SIM
          : tier == ARGUS_TIER_INT8 ? Q_INT8
          : tier == ARGUS_TIER_INT4 ? Q_INT4
-         : tier == ARGUS_TIER_INT2 ? Q_INT2 : Q_SIGN1;
+         : tier == ARGUS_TIER_INT2 ? Q_INT2
+         : tier == ARGUS_TIER_E4M3 ? Q_E4M3 : Q_SIGN1;
 }
 
 // Addressing of one operand: row t of group g sits at
@@ -153,6 +159,17 @@ __device__ __forceinline__ void decode8(const Rows& s, int64_t g, int pr, int c8
                 out[0][2 * e] = __low2half(v);
                 out[0][2 * e + 1] = __high2half(v);
             }
+        } else if constexpr (SRC == Q_E4M3) {
+            // e4m3 pairs to fp16 (exact), then fp16(v * s)
+            const __half2 s2 = __half2half2(sp[0]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)(((e < 2) ? raw.x : raw.y) >> (16 * (e & 1)));
+                const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
+                const __half2 v = __hmul2_rn(*reinterpret_cast<const __half2*>(&hr), s2);
+                out[0][2 * e] = __low2half(v);
+                out[0][2 * e + 1] = __high2half(v);
+            }
         } else if constexpr (SRC == Q_INT4 || SRC == Q_INT2) {
             constexpr int BITS = 8 / per;
             constexpr uint32_t m = (1u << BITS) - 1u;
@@ -230,7 +247,7 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
             const bool live = rb < rows;
             const __half* row = tile + (live ? rb : 0) * stride;
             float a = 0.0f, b = 0.0f;
-            if (MODE == Q_INT8 || MODE == Q_FP8SIM) {
+            if (MODE == Q_INT8 || MODE == Q_FP8SIM || MODE == Q_E4M3) {
                 bool nan = false;
                 float m = 0.0f;
                 for (int c = lane8; c < D; c += 8) {
@@ -243,7 +260,7 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
                     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
                     nan |= __shfl_xor_sync(0xffffffffu, (int)nan, o) != 0;
                 }
-                const float div = (MODE == Q_INT8) ? 127.0f : 240.0f;
+                const float div = (MODE == Q_INT8) ? 127.0f : (MODE == Q_E4M3 ? 448.0f : 240.0f);
                 a = nan ? __int_as_float(0x7fc00000) : rh(__fdiv_rn(m, div));  // s = fp16(amax / div)
             } else if (MODE == Q_INT4 || MODE == Q_INT2) {
                 bool nan = false;
@@ -305,6 +322,10 @@ quant_kernel(Rows src, Rows dst, int64_t n_groups, int group_rows, int D, int ti
                         const float lo = (MODE == Q_INT8) ? -128.0f : -240.0f;
                         const float hi = (MODE == Q_INT8) ? 127.0f : 240.0f;
                         code = w8(clamp_nan(round_even(rh(quot(v, a, ra))), lo, hi));
+                        word |= code << (8 * e);
+                    } else if (MODE == Q_E4M3) {
+                        const float qv = __fdiv_rn(v, a);  // keeps the sign of -0
+                        code = (qv != qv) ? 0u : (uint32_t)__nv_cvt_float_to_fp8(qv, __NV_SATFINITE, __NV_E4M3);
                         word |= code << (8 * e);
                     } else if (MODE == Q_INT4 || MODE == Q_INT2) {
                         const float qmax = (MODE == Q_INT4) ? 15.0f : 3.0f;
@@ -769,6 +790,7 @@ int quant_dispatch(int mode, int src_mode, const Rows& src, const Rows& dst, int
         case Q_INT4: return launch_quant<M, Q_INT4>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
         case Q_INT2: return launch_quant<M, Q_INT2>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
         case Q_SIGN1: return launch_quant<M, Q_SIGN1>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
+        case Q_E4M3: return launch_quant<M, Q_E4M3>(src, dst, n_groups, group_rows, D, 0.f, nullptr, nullptr, st); \
         default: return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad source tier");                       \
     }
     switch (mode) {
@@ -778,6 +800,7 @@ int quant_dispatch(int mode, int src_mode, const Rows& src, const Rows& dst, int
         case Q_INT2: ARGUS_Q(Q_INT2)
         case Q_SIGN1: ARGUS_Q(Q_SIGN1)
         case Q_FP16: ARGUS_Q(Q_FP16)
+        case Q_E4M3: ARGUS_Q(Q_E4M3)
         default: return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad destination tier");
     }
 #undef ARGUS_Q
@@ -796,6 +819,7 @@ int dequant_dispatch(int src_mode, const Rows& src, const Rows& dst, int64_t n_g
         case Q_INT4: dequant_kernel<Q_INT4><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
         case Q_INT2: dequant_kernel<Q_INT2><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
         case Q_SIGN1: dequant_kernel<Q_SIGN1><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
+        case Q_E4M3: dequant_kernel<Q_E4M3><<<dq_blocks(items), 256, 0, st>>>(src, dst, n_groups, group_rows, D); break;
         default: return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad source tier");
     }
     ARGUS_CHECK_LAUNCH();
@@ -821,7 +845,7 @@ Rows page_rows(const argus_kv_arena* a, int slot, int which, int D) {
 int check_arena(const argus_kv_arena* a, int D) {
     if (!a || !a->k) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null arena");
     if (a->layout != ARGUS_LAYOUT_RECORD) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "page codecs need a record arena");
-    if (a->tier < ARGUS_TIER_FP16 || a->tier > ARGUS_TIER_1BIT) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad tier");
+    if (a->tier < ARGUS_TIER_FP16 || a->tier > ARGUS_TIER_E4M3) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad tier");
     if (D % 8 || D <= 0) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "head dim must be a multiple of 8");
     if (a->page_tokens <= 0 || a->page_tokens % 8) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "page size must be a multiple of 8");
     if (!argus_aligned(a->k, 16) || a->bh_stride % 16 || a->record_bytes % 16)
@@ -989,6 +1013,19 @@ int argus_dequant_int8(const int8_t* q, const uint16_t* scales, int64_t n_rows, 
 int argus_dequant_fp8sim(const int8_t* q, const uint16_t* scales, int64_t n_rows, int D, uint16_t* out,
                          argus_stream_t stream) {
     return argus_dequant_int8(q, scales, n_rows, D, out, stream);
+}
+
+int argus_quant_e4m3(const uint16_t* x, int64_t n_rows, int D, uint8_t* q, uint16_t* scales, argus_stream_t stream) {
+    int rc = check_rows(x, q, n_rows, D, 1);
+    if (rc || !scales) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
+    return flat_quant(Q_E4M3, x, n_rows, D, q, scales, nullptr, (cudaStream_t)stream);
+}
+
+int argus_dequant_e4m3(const uint8_t* q, const uint16_t* scales, int64_t n_rows, int D, uint16_t* out,
+                       argus_stream_t stream) {
+    int rc = check_rows(q, out, n_rows, D, 1);
+    if (rc || !scales) return rc ? rc : argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null scales");
+    return flat_dequant(Q_E4M3, q, scales, nullptr, n_rows, D, out, (cudaStream_t)stream);
 }
 
 int argus_dequant_int4(const uint8_t* packed, const uint16_t* scales, const uint16_t* mins, int64_t n_rows, int D,

@@ -26,6 +26,8 @@
 // kv_head, query group) to finish merges the split-K partials by log-sum-exp inside this kernel.
 #include <mutex>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace argus {
@@ -172,6 +174,11 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
     return y;
 }
+// two e4m3 codes (low 16 bits of x, low byte first) -> their exact fp16 values as an f16x2
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t x) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(x & 0xffffu), __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t r;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
@@ -317,6 +324,19 @@ __device__ __forceinline__ void k_frags(const unsigned char* kp, int g4, int t4,
             a[c][1] = prmt(wb, kMagic1024, 0x7270);
             a[c][3] = prmt(wb, kMagic1024, 0x7371);
         }
+    } else if constexpr (TIER == ARGUS_TIER_E4M3) {
+        // e4m3 code pairs (bytes 0, 2 and 1, 3) to their exact fp16 values; the token's scale is
+        // applied to the score tile
+        uint32_t ra[KC], rb[KC];
+        lds<D / 4>(kp + (2 * g4) * D + t4 * (D / 4), ra);
+        lds<D / 4>(kp + (2 * g4 + 1) * D + t4 * (D / 4), rb);
+#pragma unroll
+        for (int c = 0; c < KC; ++c) {
+            a[c][0] = e4m3x2_f16x2(prmt(ra[c], 0u, 0x3120));
+            a[c][2] = e4m3x2_f16x2(prmt(ra[c], 0u, 0x3120) >> 16);
+            a[c][1] = e4m3x2_f16x2(prmt(rb[c], 0u, 0x3120));
+            a[c][3] = e4m3x2_f16x2(prmt(rb[c], 0u, 0x3120) >> 16);
+        }
     } else if constexpr (TIER == ARGUS_TIER_INT4 || TIER == ARGUS_TIER_INT2) {
         // codes of token 2g at mantissa bit pA of each byte, of token 2g+1 at pB
         uint32_t r[KC], mA, mB, gA, gB;
@@ -395,6 +415,24 @@ __device__ __forceinline__ void v_frags(const unsigned char* vp, int g4, int t4,
             a[t][1] = h2u(__hmul2_rn(u2h(hsub2u(prmt(y02, kMagic1024, 0x7372), kMagic1152)), ts.s[0]));
             a[t][2] = h2u(__hmul2_rn(u2h(hsub2u(prmt(y13, kMagic1024, 0x7170), kMagic1152)), ts.s[1]));
             a[t][3] = h2u(__hmul2_rn(u2h(hsub2u(prmt(y13, kMagic1024, 0x7372), kMagic1152)), ts.s[1]));
+        }
+    } else if constexpr (TIER == ARGUS_TIER_E4M3) {
+        uint32_t r0[W], r1[W], r2[W], r3[W];
+        const unsigned char* base = vp + (4 * t4) * D + g4 * (D / 8);
+        lds_small<D / 8>(base, r0);
+        lds_small<D / 8>(base + D, r1);
+        lds_small<D / 8>(base + 2 * D, r2);
+        lds_small<D / 8>(base + 3 * D, r3);
+#pragma unroll
+        for (int t = 0; t < KC; ++t) {
+            const int w = t >> 1, e0 = 2 * (t & 1);
+            const uint32_t sel = e0 | ((4 + e0) << 4) | ((e0 + 1) << 8) | ((5 + e0) << 12);
+            const uint32_t y02 = prmt(r0[w], r2[w], sel);  // (tok 4u d0, tok 4u+2 d0, .. d1, .. d1)
+            const uint32_t y13 = prmt(r1[w], r3[w], sel);
+            a[t][0] = h2u(__hmul2_rn(u2h(e4m3x2_f16x2(y02)), ts.s[0]));
+            a[t][1] = h2u(__hmul2_rn(u2h(e4m3x2_f16x2(y02 >> 16)), ts.s[0]));
+            a[t][2] = h2u(__hmul2_rn(u2h(e4m3x2_f16x2(y13)), ts.s[1]));
+            a[t][3] = h2u(__hmul2_rn(u2h(e4m3x2_f16x2(y13 >> 16)), ts.s[1]));
         }
     } else if constexpr (TIER == ARGUS_TIER_INT4) {
         uint32_t ra[W], rb[W];
@@ -488,6 +526,9 @@ __device__ __forceinline__ void load_tok_scales(const TilePtr& tp, int g4, int t
         if constexpr (TIER == ARGUS_TIER_INT8 || TIER == ARGUS_TIER_FP8SIM) {
             // codes 1152 + q: score = s * (S - 1152 * sum(q))
             tk.kz[0] = tk.kz[1] = -1152.f;
+            tk.kw[0] = __low2float(k2);
+            tk.kw[1] = __high2float(k2);
+        } else if constexpr (TIER == ARGUS_TIER_E4M3) {  // e4m3 values: score = s * S
             tk.kw[0] = __low2float(k2);
             tk.kw[1] = __high2float(k2);
         }
@@ -1353,6 +1394,7 @@ __global__ void __launch_bounds__(kThreads, SIDE ? side_ctas_per_sm(D) : ctas_pe
             ARGUS_TILE_CASE(ARGUS_TIER_INT4)
             ARGUS_TILE_CASE(ARGUS_TIER_INT2)
             ARGUS_TILE_CASE(ARGUS_TIER_1BIT)
+            ARGUS_TILE_CASE(ARGUS_TIER_E4M3)
 #undef ARGUS_TILE_CASE
 #undef ARGUS_TILE_LOOPS
             default: break;
@@ -1534,12 +1576,12 @@ bool valid_head_dim(int D) { return D == 16 || D == 32 || D == 64 || D == 128 ||
 extern "C" {
 
 int argus_record_bytes(int tier, int page_tokens, int head_dim) {
-    if (tier < ARGUS_TIER_FP16 || tier > ARGUS_TIER_1BIT || page_tokens <= 0 || head_dim <= 0) return 0;
+    if (tier < ARGUS_TIER_FP16 || tier > ARGUS_TIER_E4M3 || page_tokens <= 0 || head_dim <= 0) return 0;
     return da::record_bytes(tier, page_tokens, head_dim);
 }
 
 int argus_decode_attention_chunk_tiles(int tier, int layout, int page_tokens, int head_dim) {
-    if (tier < ARGUS_TIER_FP16 || tier > ARGUS_TIER_1BIT || !valid_head_dim(head_dim) || page_tokens <= 0) return 0;
+    if (tier < ARGUS_TIER_FP16 || tier > ARGUS_TIER_E4M3 || !valid_head_dim(head_dim) || page_tokens <= 0) return 0;
     if (layout != ARGUS_LAYOUT_RECORD && layout != ARGUS_LAYOUT_SPLIT_FP16) return 0;
     return da::chunk_tiles(tier, layout, page_tokens, head_dim);
 }
@@ -1576,7 +1618,7 @@ int prepare_attention(const argus_attn_shape* s, const argus_kv_arena* arenas, c
     memset(&prm, 0, sizeof(prm));
     for (int i = 0; i < s->n_arenas; ++i) {
         const argus_kv_arena& a = arenas[i];
-        if (a.tier < ARGUS_TIER_FP16 || a.tier > ARGUS_TIER_1BIT)
+        if (a.tier < ARGUS_TIER_FP16 || a.tier > ARGUS_TIER_E4M3)
             return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "bad arena tier");
         if (!a.k || !argus_aligned(a.k, 16) || (a.bh_stride % 16))
             return argus_set_error(ARGUS_ERR_MISALIGNED, "arena base and (b,h) stride must be 16-byte aligned");

@@ -72,6 +72,13 @@ int argus_quant_fp8sim(const uint16_t* x, int64_t n_rows, int D, int8_t* q, uint
 /* Replaces dequantize_from_fp8_simulated, core/quantization.py:218-222. */
 int argus_dequant_fp8sim(const int8_t* q, const uint16_t* scales, int64_t n_rows, int D, uint16_t* out,
                          argus_stream_t stream);
+/* True e4m3 per token (ARGUS_TIER_E4M3; no reference counterpart: a separately named non-parity
+ * mode beside the simulated FP8 above).  x:[n_rows][D] -> codes:[n_rows][D], s:[n_rows]. */
+int argus_quant_e4m3(const uint16_t* x, int64_t n_rows, int D, uint8_t* q, uint16_t* scales,
+                     argus_stream_t stream);
+/* fp16(e4m3(code) * s). */
+int argus_dequant_e4m3(const uint8_t* q, const uint16_t* scales, int64_t n_rows, int D, uint16_t* out,
+                       argus_stream_t stream);
 
 /* Asymmetric INT4, 2 tokens per byte along the sequence (low nibble = even token).
  * s = fp16(fp16(max-min)/15), u = uint8(clamp(round(fp16(fp16(x-min)/s)), 0, 15)).
@@ -254,7 +261,11 @@ enum argus_tier {
     ARGUS_TIER_INT8 = 2,   /* int8 codes, fp16 scale per token */
     ARGUS_TIER_INT4 = 3,   /* 2 tokens per byte, fp16 scale + min per token */
     ARGUS_TIER_INT2 = 4,   /* 4 tokens per byte, fp16 scale + min per token */
-    ARGUS_TIER_1BIT = 5    /* 8 tokens per byte (sign), fp16 scale per token */
+    ARGUS_TIER_1BIT = 5,   /* 8 tokens per byte (sign), fp16 scale per token */
+    ARGUS_TIER_E4M3 = 6    /* true e4m3 codes (OCP FP8 E4M3), fp16 scale per token: a separately named
+                              non-parity tier (the reference's FP8 tier is ARGUS_TIER_FP8SIM);
+                              s = fp16(amax / 448), code = e4m3(x / s) from the fp32 quotient (nearest
+                              even, saturating at 448, NaN -> 0), value = fp16(e4m3(code) * s) */
 };
 
 /* Arena layouts. */

@@ -58,6 +58,9 @@ def lib():
         L.oracle_isolate_outliers.argtypes = [_u16p, _i64, _int, _flt, _u16p, _u16p, _u8p]
         L.oracle_f32_to_f16.argtypes = [_f32p, _i64, _u16p]
         L.oracle_torch_mean_abs.argtypes = [_u16p, _int]
+        L.oracle_quant_e4m3.argtypes = [_u16p, _i64, _int, _u8p, _u16p]
+        L.oracle_dequant_e4m3.argtypes = [_u8p, _u16p, _i64, _int, _u16p]
+        L.oracle_e4m3_encode.argtypes = [_f32p, _i64, _u8p]
         L.oracle_torch_mean_abs.restype = ctypes.c_float
         _lib = L
     return _lib
@@ -109,6 +112,36 @@ def dequantize_from_int8(q, s):
 
 
 dequantize_from_fp8_simulated = dequantize_from_int8
+
+
+# ------------------------------------------------------------- true e4m3 (non-parity tier)
+def quantize_to_e4m3(x):
+    """Per-row e4m3 codes (uint8) and fp16 scales (last dim): s = fp16(amax / 448),
+    code = e4m3(x / s) rounded to nearest even, saturating at 448, NaN -> 0."""
+    x, xb = _h(x)
+    D = x.shape[-1]
+    q = np.empty(x.shape, np.uint8)
+    s = np.empty(x.shape[:-1] + (1,), np.float16)
+    lib().oracle_quant_e4m3(_p(xb, _u16p), x.size // D, D, _p(q, _u8p), _p(s.view(np.uint16), _u16p))
+    return q, s
+
+
+def dequantize_from_e4m3(q, s):
+    q = np.ascontiguousarray(q, np.uint8)
+    s = np.ascontiguousarray(np.broadcast_to(s, q.shape[:-1] + (1,)), np.float16)
+    D = q.shape[-1]
+    out = np.empty(q.shape, np.float16)
+    lib().oracle_dequant_e4m3(_p(q, _u8p), _p(s.view(np.uint16), _u16p), q.size // D, D,
+                              _p(out.view(np.uint16), _u16p))
+    return out
+
+
+def e4m3_encode(v):
+    """The e4m3 encoder alone on fp32 values (uint8 codes)."""
+    v = np.ascontiguousarray(v, np.float32)
+    q = np.empty(v.shape, np.uint8)
+    lib().oracle_e4m3_encode(_p(v, _f32p), v.size, _p(q, _u8p))
+    return q
 
 
 # ------------------------------------------------------------- sequence-packed codes

@@ -26,6 +26,9 @@
  *   oracle_quant_1bit     quantization.py:173-194; pack fallback triton_kernels.py:264-278
  *   oracle_dequant_1bit   quantization.py:196-201; unpack fallback triton_kernels.py:334-386
  *   oracle_isolate_outliers memory_manager.py:89-113
+ *   oracle_quant_e4m3 / oracle_dequant_e4m3: the true-e4m3 storage mode, a separately named
+ *                         non-parity tier (the reference's "FP8" is the int8-with-wrap simulation of
+ *                         quantization.py:203-216); its arithmetic is defined in the comment below
  *
  * Layout convention: a tensor is [rows][T][D] with D contiguous; packing runs along T.
  */
@@ -230,6 +233,61 @@ void oracle_dequant_sym8(const int8_t* q, const uint16_t* s, int64_t n_rows, int
         float sc = h2f(s[r]);
         for (int d = 0; d < D; ++d) out[r * D + d] = f2h((float)q[r * D + d] * sc);
     }
+}
+
+/* ------------------------------------------------------------ true e4m3 (non-parity) */
+/* OCP FP8 E4M3 ("e4m3fn"): sign, 4 exponent bits (bias 7), 3 mantissa bits, no infinities, NaN =
+ * S.1111.111, largest finite 448, smallest subnormal 2^-9.  Encoding: round to nearest even,
+ * magnitudes from 448 up (and infinities) saturate to +-448; NaN stores code 0 (the tier's rule,
+ * as the int8 tiers store 0 for NaN). */
+static uint8_t e4m3_encode(float v) {
+    if (isnan(v)) return 0;
+    const uint8_t sign = signbit(v) ? 0x80u : 0u;
+    const float a = fabsf(v);
+    if (a >= 448.0f) return (uint8_t)(sign | 0x7eu);
+    if (a < 0.015625f) { /* below 2^-6: subnormal grid of 2^-9 (a * 512 is exact) */
+        const float q = rintf(a * 512.0f);   /* 8 is the smallest normal, code 0x08 */
+        return (uint8_t)(sign | (uint8_t)q);
+    }
+    int e2;
+    (void)frexpf(a, &e2);                    /* a = f * 2^e2, f in [0.5, 1) */
+    int E = e2 - 1;                          /* a = 1.m * 2^E, E in [-6, 8] */
+    float q = rintf(ldexpf(a, 3 - E));       /* 1.m * 8 rounded: [8, 16] */
+    if (q >= 16.0f) { q = 8.0f; E += 1; }
+    if (E > 8 || (E == 8 && q > 14.0f)) return (uint8_t)(sign | 0x7eu);
+    return (uint8_t)(sign | (uint8_t)((E + 7) << 3) | (uint8_t)((int)q - 8));
+}
+
+static float e4m3_decode(uint8_t c) {
+    const float sign = (c & 0x80u) ? -1.0f : 1.0f;
+    const int E = (c >> 3) & 0xf, m = c & 7;
+    if (E == 0xf && m == 7) return NAN;
+    if (E == 0) return sign * ldexpf((float)m, -9);
+    return sign * ldexpf((float)(8 + m), E - 10);
+}
+
+/* The e4m3 tier: s = rh(amax|x| / 448) per row, code = e4m3(x / s) from the fp32 quotient (one
+ * rounding), value = rh(e4m3(code) * s).  A zero row has s = 0, its quotients are NaN and store 0.
+ * x: [n_rows][D] fp16 bits -> q: [n_rows][D] codes, s: [n_rows] fp16 bits. */
+void oracle_quant_e4m3(const uint16_t* x, int64_t n_rows, int D, uint8_t* q, uint16_t* s) {
+    for (int64_t r = 0; r < n_rows; ++r) {
+        const uint16_t* row = x + r * D;
+        const float sc = rh(row_amax_abs(row, D) / 448.0f);
+        s[r] = f2h(sc);
+        for (int d = 0; d < D; ++d) q[r * D + d] = e4m3_encode(h2f(row[d]) / sc);
+    }
+}
+
+void oracle_dequant_e4m3(const uint8_t* q, const uint16_t* s, int64_t n_rows, int D, uint16_t* out) {
+    for (int64_t r = 0; r < n_rows; ++r) {
+        const float sc = h2f(s[r]);
+        for (int d = 0; d < D; ++d) out[r * D + d] = f2h(e4m3_decode(q[r * D + d]) * sc);
+    }
+}
+
+/* e4m3 codes of n fp32 values (the encoder alone). */
+void oracle_e4m3_encode(const float* v, int64_t n, uint8_t* q) {
+    for (int64_t i = 0; i < n; ++i) q[i] = e4m3_encode(v[i]);
 }
 
 /* Asymmetric quantization with sequence packing.  bits = 4 (2 codes/byte) or 2 (4 codes/byte).
