@@ -537,12 +537,11 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                     return true;
                 };
                 for (int cc = 0; cc < 2 && cc < nchunks && wok; ++cc) wok = s_mma(cc);
+                // W_cc goes in as soon as P_cc is written, then S_{cc+2} (two chunks ahead of the
+                // softmax); an MMA issue waits for room in the tensor pipe, so issuing S first would
+                // hold W back
                 for (int cc = 0; cc < nchunks && wok; ++cc) {
                     const int64_t gc = gchunk + cc;
-                    if (cc + 2 < nchunks) {
-                        wok = s_mma(cc + 2);
-                        if (!wok) break;
-                    }
                     wok = mbar_wait(bar(kBarP + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
                     if (!wok) break;
                     tc_fence_after();
@@ -557,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                     umma_commit(bar(kBarRE + (int)(gc & 3)));
                     last_bar = kBarW + (int)(gc & 1);
                     last_par = (uint32_t)((gc >> 1) & 1);
+                    if (cc + 2 < nchunks) wok = s_mma(cc + 2);
                 }
                 if (!wok && last_bar >= 0) (void)mbar_wait(bar(last_bar), last_par);  // MMAs in flight finish
                 misc[2] = (uint32_t)landed;
@@ -592,7 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
             float m = kNoMax, l = 0.f;
             for (int cc = 0; cc < nchunks; ++cc) {
                 const int64_t gc = gchunk + cc;
-                // S_cc complete; it was issued after W_{cc-3}, the last reader of the P this buffer held
+                // S_cc complete; it was issued after W_{cc-2}, so after W_{cc-3}, the last reader of the P
+                // this buffer held
                 wok = mbar_wait_warp(bar(kBarS + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
                 if (!wok) break;
                 tc_fence_after();

@@ -120,8 +120,8 @@ def build_cache(device, seed, batch=None, heads_kv=None, sample=None):
         a = A.KVArena.allocate(A.TIER_NAMES[tier], Bc, Hc, n, P, D, device)
         if tier == "fp16":
             a.write_pages(0, k, v)
-        elif tier in ("int8", "fp8"):
-            f = Q.quantize_to_int8 if tier == "int8" else Q.quantize_to_fp8_simulated
+        elif tier in ("int8", "fp8", "e4m3"):
+            f = {"int8": Q.quantize_to_int8, "fp8": Q.quantize_to_fp8_simulated, "e4m3": Q.quantize_to_e4m3}[tier]
             (kq, ks), (vq, vs) = f(k), f(v)
             a.write_pages(0, kq, vq, ks, vs)
         elif tier in ("int4", "int2"):
@@ -701,6 +701,39 @@ def _tinyllama_cpu(k, v, q, Pt, HQt, min_seconds=10.0):
                       f"({n * dt:.1f} s of CPU work)"}
 
 
+def run_tier_sweep(args):
+    """The Llama-3-8B layer (B 8, 32 q / 8 KV heads, D 128) with every token in one tier, for each
+    tier: 32K tokens (16K for fp16, which would not be a compressed layer), the fused kernel timed
+    alone (no CPU leg); one JSON line per tier with its share of the HBM roof."""
+    import torch
+
+    global SPLIT
+    dev = torch.device("cuda", 0)
+    hbm, peak_kind = peaks()
+    saved = SPLIT
+    try:
+        for tier in ("fp16", "fp8", "int8", "int4", "int2", "one_bit", "e4m3"):
+            SPLIT = [(tier, 16384 if tier == "fp16" else 32768)]
+            plan, q = build_cache(dev, seed=1234)
+            for _ in range(args.warmup):
+                plan.run(q)
+            ms = statistics.median(_windows(lambda: plan.run(q), args.steps, 1, dev, min_seconds=args.min_seconds))
+            tokens = B * HKV * SPLIT[0][1]
+            gbs = plan.compressed_bytes / (ms * 1e-3) / 1e9
+            print(json.dumps({"metric": "decode-attn KV tokens/s, one tier", "value": tokens / (ms * 1e-3),
+                              "unit": "KV tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": ms, "higher_is_better": True, "dtype": "fp16", "data": "synthetic",
+                              "config": {"workload": "tier-sweep", "tier": tier, "batch": B, "q_heads": HQ,
+                                         "kv_heads": HKV, "head_dim": D, "context": SPLIT[0][1], "page_size": P},
+                              "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                           "frac": gbs / hbm, "peak_kind": peak_kind,
+                                           "algorithmic_bytes_per_launch": plan.compressed_bytes}}), flush=True)
+            del plan, q
+            torch.cuda.empty_cache()
+    finally:
+        SPLIT = saved
+
+
 def run_8b_sidecars(args):
     """The Llama-3-8B mixed-tier layer (B 8, 32 q / 8 KV heads, D 128, 32K context, every tier) with
     the reference's outlier isolation (sigma 3, core/memory_manager.py:89-113) applied to every
@@ -948,7 +981,7 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the K-step timed window until this much device time has passed")
     ap.add_argument("--workload", choices=("llama3-8b-layer", "jl-archive", "llama3-70b", "tinyllama-sidecars",
-                                           "llama3-8b-sidecars", "cascade"), default="llama3-8b-layer")
+                                           "llama3-8b-sidecars", "cascade", "tier-sweep"), default="llama3-8b-layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "jl-archive":
@@ -962,6 +995,9 @@ def main():
         return
     if args.workload == "cascade":
         run_cascade(args)
+        return
+    if args.workload == "tier-sweep":
+        run_tier_sweep(args)
         return
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
