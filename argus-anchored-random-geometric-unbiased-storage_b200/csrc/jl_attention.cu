@@ -13,13 +13,14 @@
 //   U phase   Yk blocks arrive by TMA (128-byte swizzle); the warps form u with mma.sync, stage U^T
 //             (rows = block-query pairs, fp16 hi + lo) in shared memory, and warps 0-3 move their
 //             rows into tensor memory (the A operand of the scores).
-//   SW phase  for each 64-token chunk c of R: S_c = U^T . R_c^T (tcgen05.mma, A from tensor memory,
-//             M 128, N 64, fp32); warps 0-3 (one row per thread) run the online softmax of their row
-//             in the log2 domain and write P_c (fp16) over the first half of S_c; W += P_c . R_c
-//             (tcgen05.mma, A = P_c from tensor memory, M 128, N = MJ, fp32).  One thread issues the
-//             MMAs and the copies of the operator chunks (16 KB of R, 16 KB of R^T, laid out as
-//             K-major operands in 128-byte swizzle by argus_jl_operator_fragments); the first Yv
-//             blocks stream in meanwhile.
+//   SW phase  for each pair of 64-token chunks of R: S = U^T . R_pair^T (tcgen05.mma, A from tensor
+//             memory, M 128, N 128, fp32: one MMA group forms the scores of both chunks, since an
+//             MMA costs about the same at N 64 as at N 128); per chunk c, warps 0-3 (one row per
+//             thread) run the online softmax of their row in the log2 domain and write P_c (fp16)
+//             over the first half of S_c; W += P_c . R_c (tcgen05.mma, A = P_c from tensor memory,
+//             M 128, N = MJ, fp32).  One thread issues the MMAs and the copies of the operator
+//             pairs (R of 128 tokens, R^T of both chunks, laid out as K-major operands in 128-byte
+//             swizzle by argus_jl_operator_fragments); the first Yv blocks stream in meanwhile.
 //   O phase   the W rows, scaled to a common max per (kv head, query), go to shared memory (hi + lo);
 //             Yv blocks arrive by TMA and the warps add Yv^T . w with mma.sync.
 //
@@ -43,7 +44,8 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kD = 128;      // largest head_dim (64 or 128); strides of the partial outputs
 constexpr int kMJ = 128;     // largest rows per archived block (64 or 128)
 constexpr int kRows = 128;   // (block, query) rows per round = tensor-memory lanes
-constexpr int kChunk = 64;   // operator tokens per SW step
+constexpr int kChunk = 64;   // operator tokens per softmax step
+constexpr int kPairTok = 2 * kChunk;  // operator tokens per score MMA group and operator copy
 constexpr int kCols = 8;     // query columns of the CUDA-core MMAs (queries per kv head <= 8)
 constexpr int kSlots = 4;    // 32 KB shared-memory slots
 constexpr uint32_t kSlotBytes = (uint32_t)kMJ * kD * 2;          // room for one Yk / Yv block
@@ -51,21 +53,23 @@ constexpr long long kWaitTries = 1ll << 21;  // x kWaitHintNs: about two seconds
 constexpr uint32_t kWaitHintNs = 1000;
 constexpr float kNoMax = -1.0e30f;
 constexpr float kSlack = 8.0f;  // a row's reference max is raised only when a score passes it by 2^8
-// tensor memory: three S / P buffers (64 columns each; P, fp16, overwrites the first 32 of its S),
-// W (128 fp32 columns), U^T hi and lo (64 columns each: two fp16 per column)
-constexpr int kSBufs = 3;
+// tensor memory: four S / P buffers (64 columns each, filled in pairs; P, fp16, overwrites the
+// first 32 columns of its S), W (128 fp32 columns), U^T hi and lo (64 columns each: two fp16 per
+// column)
+constexpr int kSBufs = 4;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemW = kSBufs * kChunk;        // 192
-constexpr uint32_t kTmemUhi = kTmemW + kMJ;         // 320
-constexpr uint32_t kTmemUlo = kTmemUhi + kMJ / 2;   // 384
+constexpr uint32_t kTmemW = kSBufs * kChunk;        // 256
+constexpr uint32_t kTmemUhi = kTmemW + kMJ;         // 384
+constexpr uint32_t kTmemUlo = kTmemUhi + kMJ / 2;   // 448
+static_assert(kTmemUlo + kMJ / 2 <= kTmemCols, "tensor memory");
 
 __device__ int g_status = 0;
 
 struct Params {
     CUtensorMap tmk;    // Yk as [B*Hkv][n_blocks][MJ][D], box 64 x MJ, 128-byte swizzle
     CUtensorMap tmv;    // Yv, same
-    const unsigned char* rop;   // R chunks: [N/64][16 KB], B operand of S (N = tokens, K = MJ)
-    const unsigned char* rtop;  // R^T chunks: [N/64][16 KB], B operand of W (N = MJ, K = tokens)
+    const unsigned char* rop;   // R pairs: [N/128][128 x MJ fp16], B operand of S (N = tokens, K = MJ)
+    const unsigned char* rtop;  // R^T chunks: [N/64][64 x MJ fp16], B operand of W (N = MJ, K = tokens)
     const __half* q;    // [B, Hkv*G, qlen, D]
     __half* out;
     float* lse;
@@ -84,16 +88,16 @@ constexpr uint32_t kOffRow = kOffSlot + kSlots * kSlotBytes;    // mrow, lrow, f
 constexpr uint32_t kOffSeg = kOffRow + 3 * kRows * 4;           // segM, segL, segA [128] fp32
 constexpr uint32_t kOffOpen = kOffSeg + 3 * kRows * 4;          // openM, openL [8] fp32
 constexpr uint32_t kOffBar = kOffOpen + 2 * kCols * 4;          // mbarriers
-// slot full (6), operator chunk full / empty (4 + 4), S full (3), P full (3), W done (2)
-// and, for rounds of at most 64 rows, lo scores shipped (3)
-constexpr int kBarFull = 0, kBarRF = 6, kBarRE = 10, kBarS = 14, kBarP = 17, kBarW = 20, kBarX = 22, kNumBars = 25;
+// slot full (6), operator pair full / empty (2 + 2), S full (4), P full (4), W done (2) and, for
+// rounds of at most 64 rows, lo scores shipped (4)
+constexpr int kBarFull = 0, kBarRF = 6, kBarRE = 8, kBarS = 10, kBarP = 14, kBarW = 18, kBarX = 20, kNumBars = 24;
 constexpr uint32_t kOffCnt = kOffBar + kNumBars * 8;            // per-slot release counters [6]
 constexpr uint32_t kOffMisc = kOffCnt + 8 * 4;                  // tensor-memory base, last flag, chunk counts
 constexpr size_t kSmemBytes = 1024 + kOffMisc + 16;
 static_assert(kSmemBytes <= 232448, "shared memory");
 
-// Slot roles.  U phase: Yk block i in slot i % 4, U^T staged in slots 4-5.  SW phase: operator chunk
-// c in slot c % 4 while the first two Yv blocks come into slots 4 and 5.  O phase: W' hi | lo in
+// Slot roles.  U phase: Yk block i in slot i % 4, U^T staged in slots 4-5.  SW phase: operator pair
+// k in slots 2 (k % 2), +1 while the first two Yv blocks come into slots 4 and 5.  O phase: W' hi | lo in
 // slots 0-1, Yv block i in slot oslot(i % 4) (4, 5, 2, 3).
 __host__ __device__ constexpr uint32_t oslot(int k) { return k < 2 ? 4u + (uint32_t)k : (uint32_t)k; }
 constexpr int kNumSlots = 6;
@@ -176,17 +180,19 @@ __device__ __forceinline__ void issue_block(const CUtensorMap* map, int64_t bh, 
     tma_load_4d(dst, map, 0, 0, j, (int)bh, bar);
     if (D > 64) tma_load_4d(dst + MJ * 128, map, 64, 0, j, (int)bh, bar);
 }
-// bytes of R_c or R^T_c (64 operator tokens x MJ rows)
+// bytes of R^T_c (64 operator tokens x MJ rows) and of an R pair (128 tokens x MJ rows)
 template <int MJ>
 __host__ __device__ constexpr uint32_t op_chunk_bytes() { return (uint32_t)kChunk * MJ * 2; }
-// Copies operator chunk c (R_c then R^T_c) into `dst` and arms `bar`.
 template <int MJ>
-__device__ __forceinline__ void issue_op_chunk(const Params& p, int c, uint32_t dst, uint32_t bar) {
-    constexpr uint32_t B = op_chunk_bytes<MJ>();
+__host__ __device__ constexpr uint32_t op_pair_bytes() { return (uint32_t)kPairTok * MJ * 2; }
+// Copies operator pair k (R of chunks 2k, 2k+1, then R^T of both) into `dst` and arms `bar`.
+template <int MJ>
+__device__ __forceinline__ void issue_op_pair(const Params& p, int k, uint32_t dst, uint32_t bar) {
+    constexpr uint32_t RB = op_pair_bytes<MJ>(), TB = 2 * op_chunk_bytes<MJ>();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(bar, 2 * B);
-    bulk_g2s(dst, p.rop + (size_t)c * B, B, bar);
-    bulk_g2s(dst + B, p.rtop + (size_t)c * B, B, bar);
+    mbar_expect_tx(bar, RB + TB);
+    bulk_g2s(dst, p.rop + (size_t)k * RB, RB, bar);
+    bulk_g2s(dst + RB, p.rtop + (size_t)k * TB, TB, bar);
 }
 
 // Shared-memory address of element (row r, column c) of a swizzled [MJ][D] Y block.
@@ -285,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
     const int NQ = p.G * p.qlen;
     const int bpr = kRows / NQ;  // blocks per round
     const int nchunks = p.N / kChunk;
+    const int npairs = nchunks / 2;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(misc)),
@@ -311,7 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
     // complete, whose completion has parity (ph >> s) & 1.
     uint32_t ph = 0, pend = 0;
     bool ok = true;
-    int64_t gchunk = 0;    // operator chunks of earlier rounds (phases of the chunk, S, P, W barriers)
+    int64_t gchunk = 0;    // operator chunks of earlier rounds (phases of the S, P, W barriers)
+    int64_t gpair = 0;     // operator pairs of earlier rounds (phases of the pair barriers)
     int64_t gxchunk = 0;   // the same over stacked rounds only (phases of the lo-score barriers)
     int64_t cur_bh = -1;   // the (b, h) whose partial output the o accumulators hold
     float oacc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 16*warp + g (+8), query columns 2t, 2t+1
@@ -495,19 +503,19 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         // of the quarters that sit out when the round has at most 64 rows.
         const int nact = rows >= 96 ? 4 : (rows + 31) / 32;
         if (warp == 7) {
-            if (lane == 0) {  // copies the operator chunks: chunk c+4 into the slot of chunk c once W_c is done
+            if (lane == 0) {  // copies the operator pairs: pair k+2 into the slots of pair k once its Ws are done
                 int loaded = 0;
-                auto load = [&](int cc) {
-                    const int k = (int)((gchunk + cc) & 3);
-                    issue_op_chunk<MJ>(p, cc, slot((uint32_t)k), bar(kBarRF + k));
-                    loaded = cc + 1;
+                auto load = [&](int k) {
+                    const int e = (int)((gpair + k) & 1);
+                    issue_op_pair<MJ>(p, k, slot(2u * (uint32_t)e), bar(kBarRF + e));
+                    loaded = k + 1;
                 };
-                for (int cc = 0; cc < 4 && cc < nchunks; ++cc) load(cc);
-                for (int cc = 0; cc + 4 < nchunks; ++cc) {
-                    const int64_t gc = gchunk + cc;
-                    wok = mbar_wait(bar(kBarRE + (int)(gc & 3)), (uint32_t)((gc >> 2) & 1));
+                for (int k = 0; k < 2 && k < npairs; ++k) load(k);
+                for (int k = 0; k + 2 < npairs; ++k) {
+                    const int64_t gp = gpair + k;
+                    wok = mbar_wait(bar(kBarRE + (int)(gp & 1)), (uint32_t)((gp >> 1) & 1));
                     if (!wok) break;
-                    load(cc + 4);
+                    load(k + 2);
                 }
                 misc[3] = (uint32_t)loaded;
             }
@@ -515,48 +523,53 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         } else if (warp == 6) {
             if (lane == 0) {  // issues the MMAs
                 tc_fence_after();
-                const uint32_t id_s = idesc(kRows, kChunk), id_w = idesc(kRows, MJ);
+                const uint32_t id_s = idesc(kRows, kPairTok), id_w = idesc(kRows, MJ);
                 int last_bar = -1;
                 uint32_t last_par = 0;
-                int landed = 0;  // operator chunks seen arrived
-                auto s_mma = [&](int cc) {  // S_cc = U^T . R_cc^T into S buffer gc % 3
-                    const int64_t gc = gchunk + cc;
-                    if (!mbar_wait(bar(kBarRF + (int)(gc & 3)), (uint32_t)((gc >> 2) & 1))) return false;
-                    landed = cc + 1;
+                int landed = 0;  // operator pairs seen arrived
+                // S of chunks 2k, 2k+1 = U^T . R_pair^T into the adjacent S buffers gc % 4, +1 (gc even)
+                auto s_mma = [&](int k) {
+                    const int64_t gp = gpair + k, gc = gchunk + 2 * k;
+                    if (!mbar_wait(bar(kBarRF + (int)(gp & 1)), (uint32_t)((gp >> 1) & 1))) return false;
+                    landed = k + 1;
                     tc_fence_after();
-                    const uint32_t d = tmem + (uint32_t)(gc % kSBufs) * kChunk, rsm = slot((uint32_t)(gc & 3));
+                    const uint32_t d = tmem + (uint32_t)(gc % kSBufs) * kChunk, rsm = slot(2u * (uint32_t)(gp & 1));
 #pragma unroll
                     for (int ks = 0; ks < MJ / 16; ++ks) {
-                        const uint64_t bd = sdesc(rsm + (uint32_t)(ks >> 2) * (kChunk * 128) + (uint32_t)(ks & 3) * 32);
+                        const uint64_t bd = sdesc(rsm + (uint32_t)(ks >> 2) * (kPairTok * 128) + (uint32_t)(ks & 3) * 32);
                         umma_ts(d, tmem + kTmemUhi + 8 * ks, bd, id_s, ks > 0 ? 1u : 0u);
                         if (!stacked) umma_ts(d, tmem + kTmemUlo + 8 * ks, bd, id_s, 1u);
                     }
                     umma_commit(bar(kBarS + (int)(gc % kSBufs)));
-                    last_bar = kBarS + (int)(gc % kSBufs);
-                    last_par = (uint32_t)((gc / kSBufs) & 1);
+                    umma_commit(bar(kBarS + (int)((gc + 1) % kSBufs)));
+                    last_bar = kBarS + (int)((gc + 1) % kSBufs);
+                    last_par = (uint32_t)(((gc + 1) / kSBufs) & 1);
                     return true;
                 };
-                for (int cc = 0; cc < 2 && cc < nchunks && wok; ++cc) wok = s_mma(cc);
-                // W_cc goes in as soon as P_cc is written, then S_{cc+2} (two chunks ahead of the
-                // softmax); an MMA issue waits for room in the tensor pipe, so issuing S first would
-                // hold W back
+                for (int k = 0; k < 2 && k < npairs && wok; ++k) wok = s_mma(k);
+                // W_cc goes in as soon as P_cc is written; after the second W of pair k the S of
+                // pair k+2 goes into the same two buffers (the MMAs run in issue order, so the
+                // scores overwrite P_{2k}, P_{2k+1} after both W have read them)
                 for (int cc = 0; cc < nchunks && wok; ++cc) {
-                    const int64_t gc = gchunk + cc;
+                    const int64_t gc = gchunk + cc, gp = gpair + cc / 2;
                     wok = mbar_wait(bar(kBarP + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
                     if (!wok) break;
                     tc_fence_after();
                     // W += P_cc . R_cc  (A = P_cc in tensor memory; B = R^T_cc, K-major: rows MJ, K = tokens)
-                    const uint32_t rtsm = slot((uint32_t)(gc & 3)) + op_chunk_bytes<MJ>();
+                    const uint32_t rtsm = slot(2u * (uint32_t)(gp & 1)) + op_pair_bytes<MJ>() +
+                                          (uint32_t)(cc & 1) * op_chunk_bytes<MJ>();
                     const uint32_t pt = tmem + (uint32_t)(gc % kSBufs) * kChunk;
 #pragma unroll
                     for (int ks = 0; ks < kChunk / 16; ++ks)
                         umma_ts(tmem + kTmemW, pt + 8 * ks, sdesc(rtsm + (uint32_t)ks * 32), id_w,
                                 (cc > 0 || ks > 0) ? 1u : 0u);
                     umma_commit(bar(kBarW + (int)(gc & 1)));
-                    umma_commit(bar(kBarRE + (int)(gc & 3)));
                     last_bar = kBarW + (int)(gc & 1);
                     last_par = (uint32_t)((gc >> 1) & 1);
-                    if (cc + 2 < nchunks) wok = s_mma(cc + 2);
+                    if (cc & 1) {
+                        umma_commit(bar(kBarRE + (int)(gp & 1)));
+                        if (cc / 2 + 2 < npairs) wok = s_mma(cc / 2 + 2);
+                    }
                 }
                 if (!wok && last_bar >= 0) (void)mbar_wait(bar(last_bar), last_par);  // MMAs in flight finish
                 misc[2] = (uint32_t)landed;
@@ -574,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 JLA_TMEM_LD32(sb, v);
                 JLA_TMEM_LD32(sb + 32, (v + 32));
                 tmem_wait_ld();
-                // 3 x 16 KB exchange buffers in slots 4, 5: row r of buffer b at 256 r, 16-byte
+                // 4 x 16 KB exchange buffers in slots 4, 5: row r of buffer b at 256 r, 16-byte
                 // chunks XOR-swizzled by row
                 const int64_t gx = gxchunk + cc;
                 const uint32_t xrow = slot(4) + (uint32_t)(gx % kSBufs) * 16384u + (uint32_t)r * 256u;
@@ -592,8 +605,8 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
             float m = kNoMax, l = 0.f;
             for (int cc = 0; cc < nchunks; ++cc) {
                 const int64_t gc = gchunk + cc;
-                // S_cc complete; it was issued after W_{cc-2}, so after W_{cc-3}, the last reader of the P
-                // this buffer held
+                // S_cc complete; its pair was issued after W_{cc-4} and W_{cc-3}, so after the last
+                // reader of the P this buffer held
                 wok = mbar_wait_warp(bar(kBarS + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
                 if (!wok) break;
                 tc_fence_after();
@@ -664,9 +677,9 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         }
         ok = __syncthreads_and(wok) != 0;
         if (!ok && tid == 7 * 32) {  // operator copies still in flight land before the CTA goes on (bounded)
-            for (int cc = (int)misc[2]; cc < (int)misc[3]; ++cc) {
-                const int64_t gc = gchunk + cc;
-                (void)mbar_wait(bar(kBarRF + (int)(gc & 3)), (uint32_t)((gc >> 2) & 1));
+            for (int k = (int)misc[2]; k < (int)misc[3]; ++k) {
+                const int64_t gp = gpair + k;
+                (void)mbar_wait(bar(kBarRF + (int)(gp & 1)), (uint32_t)((gp >> 1) & 1));
             }
         }
         if (ok) {  // the last W (and with it every MMA of the round)
@@ -674,6 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
             ok = __syncthreads_and(mbar_wait(bar(kBarW + (int)(gl & 1)), (uint32_t)((gl >> 1) & 1))) != 0;
         }
         gchunk += nchunks;
+        gpair += npairs;
         if (stacked) gxchunk += nchunks;
         if (!ok) break;
         tc_fence_after();
@@ -817,18 +831,20 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
     }
 }
 
-// R [N x MJ] fp16 row-major -> the operator chunks the kernel copies: for each 64-token chunk c,
-// R_c (rows = tokens, K = MJ) and R^T_c (rows = MJ, K = the chunk's tokens), each a K-major operand in
-// 128-byte swizzle, ready for a plain bulk copy into a 1024-byte aligned shared-memory slot.
+// R [N x MJ] fp16 row-major -> the operator pieces the kernel copies: for each 128-token pair R_pair
+// (rows = tokens, K = MJ) and for each 64-token chunk c R^T_c (rows = MJ, K = the chunk's tokens),
+// each a K-major operand in 128-byte swizzle, ready for a plain bulk copy into a 1024-byte aligned
+// shared-memory slot.
 __global__ void operator_chunks_kernel(const __half* __restrict__ R, int N, int MJ, __half* __restrict__ rop,
                                        __half* __restrict__ rtop) {
     const int64_t total = (int64_t)N * MJ;
-    const uint32_t chunk_elems = (uint32_t)kChunk * MJ;
+    const uint32_t chunk_elems = (uint32_t)kChunk * MJ, pair_elems = (uint32_t)kPairTok * MJ;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int tok = (int)(i / MJ), m = (int)(i - (int64_t)tok * MJ);
         const int cidx = tok / kChunk, tl = tok - cidx * kChunk;
+        const int pidx = tok / kPairTok, tp = tok - pidx * kPairTok;
         const __half v = R[i];
-        rop[(int64_t)cidx * chunk_elems + sw128(tl, m, kChunk) / 2] = v;
+        rop[(int64_t)pidx * pair_elems + sw128(tp, m, kPairTok) / 2] = v;
         rtop[(int64_t)cidx * chunk_elems + sw128(m, tl, MJ) / 2] = v;
     }
 }
@@ -887,9 +903,9 @@ extern "C" {
 int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, void* r_frag, void* rt_frag,
                                 argus_stream_t stream) {
     if (!R || !r_frag || !rt_frag) return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "null pointer");
-    if (n_tokens <= 0 || n_rows <= 0 || n_tokens % jla::kChunk || n_rows % 64)
+    if (n_tokens <= 0 || n_rows <= 0 || n_tokens % jla::kPairTok || n_rows % 64)
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT,
-                               "block tokens and rows must be positive multiples of 64");
+                               "block tokens must be a positive multiple of 128 and rows of 64");
     if (!argus_aligned(r_frag, 16) || !argus_aligned(rt_frag, 16))
         return argus_set_error(ARGUS_ERR_MISALIGNED, "operator buffers must be 16-byte aligned");
     const int64_t total = (int64_t)n_tokens * n_rows;
@@ -955,8 +971,8 @@ int argus_jl_attention(const argus_jl_attn_shape* s, const uint16_t* yk, const u
         return argus_set_error(ARGUS_ERR_INVALID_ARGUMENT, "non-positive size");
     if ((s->head_dim != 64 && s->head_dim != 128) || (s->block_rows != 64 && s->block_rows != 128))
         return argus_set_error(ARGUS_ERR_UNSUPPORTED, "JL attention supports head_dim 64 or 128 and 64- or 128-row blocks");
-    if (s->block_tokens <= 0 || s->block_tokens % jla::kChunk)
-        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "block tokens must be a multiple of 64");
+    if (s->block_tokens <= 0 || s->block_tokens % jla::kPairTok)
+        return argus_set_error(ARGUS_ERR_UNSUPPORTED, "block tokens must be a multiple of 128");
     const int NQ = s->group * s->q_len;
     if (NQ > jla::kCols) return argus_set_error(ARGUS_ERR_UNSUPPORTED, "at most 8 queries per kv head");
     if (s->n_splits > (s->n_blocks > 0 ? s->n_blocks : 1))

@@ -202,7 +202,7 @@ int argus_jl_apply(const uint16_t* A, const uint16_t* X, int64_t batch, int M, i
  * R . Yk, R . Yv before softmax attention (core/memory_manager.py:1176-1178, 1317-1447).  The kernel
  * computes the same attention without rebuilding K and V: s = R (Yk q^T), w = R^T p, o = Yv^T w.
  * Block j of (b, h) is at yk + (b*heads_kv + h)*bh_stride + j*block_stride (elements); supported:
- * head_dim 128, block_rows 128, block_tokens a multiple of 128, group*q_len <= 8. */
+ * head_dim 64 or 128, block_rows 64 or 128, block_tokens a multiple of 128, group*q_len <= 8. */
 typedef struct argus_jl_attn_shape {
     int32_t batch;
     int32_t heads_kv;
@@ -223,9 +223,10 @@ typedef struct argus_jl_attn_shape {
 } argus_jl_attn_shape;
 
 /* Writes R [n_tokens][n_rows] (fp16, the reconstruction operator of core/memory_manager.py:241-282)
- * into the operator chunks the JL attention copies: for every 64 tokens, R and R^T as K-major
- * tensor-core operands in 128-byte swizzle (r_frag and rt_frag, n_tokens*n_rows*2 bytes each,
- * 16-byte aligned; n_tokens and n_rows multiples of 64).  Done once per operator. */
+ * into the operator pieces the JL attention copies: R for every 128 tokens and R^T for every 64
+ * tokens, as K-major tensor-core operands in 128-byte swizzle (r_frag and rt_frag,
+ * n_tokens*n_rows*2 bytes each, 16-byte aligned; n_tokens a multiple of 128, n_rows of 64).  Done
+ * once per operator. */
 int argus_jl_operator_fragments(const uint16_t* R, int n_tokens, int n_rows, void* r_frag, void* rt_frag,
                                 argus_stream_t stream);
 /* Workspace bytes of argus_jl_attention: one arrival counter per (batch, kv_head) at the front
