@@ -88,9 +88,8 @@ constexpr uint32_t kOffRow = kOffSlot + kSlots * kSlotBytes;    // mrow, lrow, f
 constexpr uint32_t kOffSeg = kOffRow + 3 * kRows * 4;           // segM, segL, segA [128] fp32
 constexpr uint32_t kOffOpen = kOffSeg + 3 * kRows * 4;          // openM, openL [8] fp32
 constexpr uint32_t kOffBar = kOffOpen + 2 * kCols * 4;          // mbarriers
-// slot full (6), operator pair full / empty (2 + 2), S full (4), P full (4), W done (2) and, for
-// rounds of at most 64 rows, lo scores shipped (4)
-constexpr int kBarFull = 0, kBarRF = 6, kBarRE = 8, kBarS = 10, kBarP = 14, kBarW = 18, kBarX = 20, kNumBars = 24;
+// slot full (6), operator pair full / empty (2 + 2), S full (4), P full (4), W done (2)
+constexpr int kBarFull = 0, kBarRF = 6, kBarRE = 8, kBarS = 10, kBarP = 14, kBarW = 18, kNumBars = 20;
 constexpr uint32_t kOffCnt = kOffBar + kNumBars * 8;            // per-slot release counters [6]
 constexpr uint32_t kOffMisc = kOffCnt + 8 * 4;                  // tensor-memory base, last flag, chunk counts
 constexpr size_t kSmemBytes = 1024 + kOffMisc + 16;
@@ -299,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (tid == 0) {
-        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), (i >= kBarP && i < kBarW) ? 4u : (i >= kBarX ? 2u : 1u));
+        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), (i >= kBarP && i < kBarW) ? 4u : 1u);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (tid < kCols) { openM[tid] = kNoMax; openL[tid] = 0.f; }
@@ -320,7 +319,6 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
     bool ok = true;
     int64_t gchunk = 0;    // operator chunks of earlier rounds (phases of the S, P, W barriers)
     int64_t gpair = 0;     // operator pairs of earlier rounds (phases of the pair barriers)
-    int64_t gxchunk = 0;   // the same over stacked rounds only (phases of the lo-score barriers)
     int64_t cur_bh = -1;   // the (b, h) whose partial output the o accumulators hold
     float oacc[4] = {0.f, 0.f, 0.f, 0.f};  // dims 16*warp + g (+8), query columns 2t, 2t+1
 
@@ -456,18 +454,17 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         }
         ok = __syncthreads_and(wok) != 0;
         if (!ok) break;
-        // U^T rows -> tensor memory (the A operand of the scores); rows past this round's (block,
-        // query) pairs are zero, so their scores stay finite.  A round of at most 64 rows is
-        // stacked: lane r holds U^T_hi row r and lane 64 + r U^T_lo row r, so one MMA forms both
-        // parts of the scores (lanes 64.. then hold the lo parts, shipped to the softmax warps).
-        const bool stacked = rows <= 64;
+        // U^T rows -> tensor memory (the A operands of the scores: hi and lo, one MMA each); rows
+        // past this round's (block, query) pairs are zero, so their scores stay finite.  (Stacking
+        // hi and lo of a round of at most 64 rows in the two lane halves, for one MMA per K step,
+        // measured slower: its lo scores have to cross to the softmax warps through the shared
+        // memory that otherwise takes the first Yv blocks during the scores.)
         if (warp < 4) {
             const int r = 32 * warp + lane;
 #pragma unroll
             for (int hl = 0; hl < 2; ++hl) {
-                if (stacked && hl) break;
-                const int src = stacked ? (r & 63) : r;
-                const uint32_t sbase_u = (stacked ? r >= 64 : hl) ? ulo : uhi;
+                const int src = r;
+                const uint32_t sbase_u = hl ? ulo : uhi;
 #pragma unroll
                 for (int h2 = 0; h2 < MJ / 64; ++h2) {
                     uint32_t v[32];
@@ -490,17 +487,15 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         tc_fence_after();
 
         // ================================================================ SW phase
-        // the first two Yv blocks come in while the scores run (slots 4, 5: the staging is done;
-        // a stacked round ships its lo scores through them instead)
-        for (int i = 0; i < nb && i < 2 && !stacked; ++i) {
+        // the first two Yv blocks come in while the scores run (slots 4, 5: the staging is done)
+        for (int i = 0; i < nb && i < 2; ++i) {
             const int64_t x = xr + i;
             const uint32_t sl = oslot(i);
             if (tid == 0) issue_block<D, MJ>(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
             pend |= 1u << sl;
         }
         // Warps 0-3 run the softmax of the lane quarters that hold this round's rows (the others
-        // sit out); warp 6 issues the MMAs and warp 7 copies the operator chunks, on the schedulers
-        // of the quarters that sit out when the round has at most 64 rows.
+        // sit out); warp 6 issues the MMAs and warp 7 copies the operator pairs.
         const int nact = rows >= 96 ? 4 : (rows + 31) / 32;
         if (warp == 7) {
             if (lane == 0) {  // copies the operator pairs: pair k+2 into the slots of pair k once its Ws are done
@@ -538,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                     for (int ks = 0; ks < MJ / 16; ++ks) {
                         const uint64_t bd = sdesc(rsm + (uint32_t)(ks >> 2) * (kPairTok * 128) + (uint32_t)(ks & 3) * 32);
                         umma_ts(d, tmem + kTmemUhi + 8 * ks, bd, id_s, ks > 0 ? 1u : 0u);
-                        if (!stacked) umma_ts(d, tmem + kTmemUlo + 8 * ks, bd, id_s, 1u);
+                        umma_ts(d, tmem + kTmemUlo + 8 * ks, bd, id_s, 1u);
                     }
                     umma_commit(bar(kBarS + (int)(gc % kSBufs)));
                     umma_commit(bar(kBarS + (int)((gc + 1) % kSBufs)));
@@ -575,31 +570,6 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 misc[2] = (uint32_t)landed;
             }
             __syncwarp();
-        } else if (stacked && warp >= 2 && warp < 2 + nact) {  // ships the lo scores of rows 32(w-2) ..
-            const int r = 32 * (warp - 2) + lane;
-            for (int cc = 0; cc < nchunks; ++cc) {
-                const int64_t gc = gchunk + cc;
-                wok = mbar_wait_warp(bar(kBarS + (int)(gc % kSBufs)), (uint32_t)((gc / kSBufs) & 1));
-                if (!wok) break;
-                tc_fence_after();
-                const uint32_t sb = trow + (uint32_t)(gc % kSBufs) * kChunk;
-                uint32_t v[kChunk];
-                JLA_TMEM_LD32(sb, v);
-                JLA_TMEM_LD32(sb + 32, (v + 32));
-                tmem_wait_ld();
-                // 4 x 16 KB exchange buffers in slots 4, 5: row r of buffer b at 256 r, 16-byte
-                // chunks XOR-swizzled by row
-                const int64_t gx = gxchunk + cc;
-                const uint32_t xrow = slot(4) + (uint32_t)(gx % kSBufs) * 16384u + (uint32_t)r * 256u;
-#pragma unroll
-                for (int k = 0; k < kChunk / 4; ++k)
-                    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(xrow + (uint32_t)((k ^ (r & 7)) << 4)),
-                                 "r"(v[4 * k]), "r"(v[4 * k + 1]), "r"(v[4 * k + 2]), "r"(v[4 * k + 3])
-                                 : "memory");
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kBarX + (int)(gx % kSBufs)), warp == 2 ? 1u + 2u - (uint32_t)nact : 1u);
-            }
         } else if (warp < nact) {  // online softmax of row r
             const int r = 32 * warp + lane;
             float m = kNoMax, l = 0.f;
@@ -615,23 +585,6 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                 JLA_TMEM_LD32(sb, v);
                 JLA_TMEM_LD32(sb + 32, (v + 32));
                 tmem_wait_ld();
-                if (stacked) {  // add the lo parts shipped by the warp of lanes 64 + r
-                    const int64_t gx = gxchunk + cc;
-                    wok = mbar_wait_warp(bar(kBarX + (int)(gx % kSBufs)), (uint32_t)((gx / kSBufs) & 1));
-                    if (!wok) break;
-                    const uint32_t xrow = slot(4) + (uint32_t)(gx % kSBufs) * 16384u + (uint32_t)r * 256u;
-#pragma unroll
-                    for (int k = 0; k < kChunk / 4; ++k) {
-                        float4 lo;
-                        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                                     : "=f"(lo.x), "=f"(lo.y), "=f"(lo.z), "=f"(lo.w)
-                                     : "r"(xrow + (uint32_t)((k ^ (r & 7)) << 4)));
-                        v[4 * k] = __float_as_uint(__uint_as_float(v[4 * k]) + lo.x);
-                        v[4 * k + 1] = __float_as_uint(__uint_as_float(v[4 * k + 1]) + lo.y);
-                        v[4 * k + 2] = __float_as_uint(__uint_as_float(v[4 * k + 2]) + lo.z);
-                        v[4 * k + 3] = __float_as_uint(__uint_as_float(v[4 * k + 3]) + lo.w);
-                    }
-                }
                 float cm = kNoMax;
 #pragma unroll
                 for (int j = 0; j < kChunk; ++j) {
@@ -688,12 +641,10 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         }
         gchunk += nchunks;
         gpair += npairs;
-        if (stacked) gxchunk += nchunks;
         if (!ok) break;
         tc_fence_after();
-        // the operator slots are free again: slots 2, 3 take the third and fourth Yv blocks (a
-        // stacked round also the first two, in slots 4, 5)
-        for (int i = stacked ? 0 : 2; i < nb && i < 4; ++i) {
+        // the operator slots are free again: slots 2, 3 take the third and fourth Yv blocks
+        for (int i = 2; i < nb && i < 4; ++i) {
             const int64_t x = xr + i;
             const uint32_t sl = oslot(i);
             if (tid == 0) issue_block<D, MJ>(&p.tmv, x / p.n_blocks, (int)(x % p.n_blocks), slot(sl), bar(kBarFull + (int)sl));
