@@ -652,41 +652,50 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
         }
 
         // ================================================================ O phase
-        // per (segment = run of one (b, h)'s blocks, query): the common max, the normalizer and the
-        // factor of each row; the first segment continues the open head when it is the same (b, h)
+        // per (segment = run of one (b, h)'s blocks, query), one warp each with its lanes over the
+        // segment's blocks: the common max, the normalizer and the factor of each row; the first
+        // segment continues the open head when it is the same (b, h)
         const int64_t bh0 = xr / p.n_blocks;
         const int nseg = (int)((xr + nb - 1) / p.n_blocks - bh0) + 1;
         const bool cont = bh0 == cur_bh;
-        if (tid < nseg * NQ) {
-            const int s = tid / NQ, n = tid - s * NQ;
+        for (int sq = warp; sq < nseg * NQ; sq += kWarps) {
+            const int s = sq / NQ, n = sq - s * NQ;
             const int64_t hb = (bh0 + s) * p.n_blocks;
             const int i0 = (int)(hb - xr > 0 ? hb - xr : 0);
             const int i1 = (int)(hb + p.n_blocks - xr < nb ? hb + p.n_blocks - xr : nb);
             float M = kNoMax, prevM = kNoMax, prevL = 0.f;
-            for (int i = i0; i < i1; ++i) M = fmaxf(M, mrow[i * NQ + n]);
+            for (int i = i0 + lane; i < i1; i += 32) M = fmaxf(M, mrow[i * NQ + n]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
             if (s == 0 && cont) {
                 prevM = openM[n];
                 prevL = openL[n];
                 M = fmaxf(M, prevM);
             }
             const float a = exp2f(prevM - M);
-            float L = a * prevL;
-            for (int i = i0; i < i1; ++i) {
+            float L = 0.f;
+            for (int i = i0 + lane; i < i1; i += 32) {
                 const float f = exp2f(mrow[i * NQ + n] - M);
                 frow[i * NQ + n] = f;
                 L += f * lrow[i * NQ + n];
             }
-            segM[tid] = M;
-            segL[tid] = L;
-            segA[tid] = a;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+            if (lane == 0) {
+                segM[sq] = M;
+                segL[sq] = a * prevL + L;
+                segA[sq] = a;
+            }
         }
         __syncthreads();
-        if (warp < 4) {  // W rows, scaled, -> W' [row][MJ] fp16 hi | lo (16-byte chunks XOR-swizzled by row)
-            const int r = 32 * warp + lane;
+        {  // W rows, scaled, -> W' [row][MJ] fp16 hi | lo (16-byte chunks XOR-swizzled by row); warps
+           // w and w + 4 share lane quarter w, each half of the columns
+            const int r = 32 * (warp & 3) + lane;
             const bool live = r < rows;
             const float f = live ? frow[r] : 0.f;
+            const int jb = (warp >> 2) * (MJ / 2);
 #pragma unroll
-            for (int j0 = 0; j0 < MJ; j0 += 32) {
+            for (int j0 = jb; j0 < jb + MJ / 2; j0 += 32) {
                 uint32_t w[32];
                 JLA_TMEM_LD32(trow + kTmemW + j0, w);
                 tmem_wait_ld();
@@ -708,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1) jl_attn_tc_kernel(const __grid_co
                     }
                 }
             }
-            if (live && p.block_lse) {
+            if (live && p.block_lse && warp < 4) {
                 const int i = r / NQ, n = r - i * NQ;
                 p.block_lse[(xr + i) * kCols + n] =
                     lrow[r] > 0.f ? (mrow[r] + log2f(lrow[r])) * 0.69314718055994530942f : -INFINITY;
