@@ -106,3 +106,38 @@ def test_wait_timeout_selftest_refuses_bad_arguments():
     assert L.argus_selftest_wait_timeout(0, ctypes.byref(g), None) == _lib.ERR_INVALID_ARGUMENT
     assert L.argus_selftest_wait_timeout((1 << 20) + 1, ctypes.byref(g), None) == _lib.ERR_INVALID_ARGUMENT
     assert L.argus_selftest_wait_timeout(10, None, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_jl_entry_points_refuse_bad_shapes_before_any_launch():
+    """The JL operator layout is R in 128-token pairs and R^T in 64-token chunks, so both JL entry
+    points refuse block token counts that are not a multiple of 128, and the attention refuses
+    unsupported head dims, block rows, query groups and misaligned blocks, on the host."""
+    from argus_b200 import _lib
+    from argus_b200.core import jl
+
+    L = jl._jl_bind()
+    buf = (ctypes.c_uint8 * 4096)()
+    p = ctypes.addressof(buf)
+    p16 = (p + 15) & ~15
+    assert L.argus_jl_operator_fragments(p16, 192, 64, p16, p16, None) == _lib.ERR_INVALID_ARGUMENT
+    assert "multiple of 128" in L.argus_last_error().decode()
+    assert L.argus_jl_operator_fragments(p16, 256, 48, p16, p16, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.argus_jl_operator_fragments(None, 256, 64, p16, p16, None) == _lib.ERR_INVALID_ARGUMENT
+
+    def shape(**kw):
+        s = dict(batch=1, heads_kv=2, group=4, q_len=1, head_dim=128, block_rows=128, block_tokens=512,
+                 n_blocks=3, n_splits=1, n_ctas=0, scale=0.1, reserved=0, bh_stride=3 * 128 * 128,
+                 block_stride=128 * 128)
+        s.update(kw)
+        return jl.JLShapeC(**s)
+
+    def call(s, yk=p16):
+        return L.argus_jl_attention(ctypes.byref(s), yk, p16, p16, p16, p16, p16, None, None, p16, None)
+
+    assert call(shape(block_tokens=192)) == _lib.ERR_UNSUPPORTED
+    assert "multiple of 128" in L.argus_last_error().decode()
+    assert call(shape(head_dim=96)) == _lib.ERR_UNSUPPORTED
+    assert call(shape(block_rows=32)) == _lib.ERR_UNSUPPORTED
+    assert call(shape(group=9)) == _lib.ERR_UNSUPPORTED
+    assert call(shape(n_splits=4)) == _lib.ERR_INVALID_ARGUMENT
+    assert call(shape(), yk=p16 + 2) == _lib.ERR_MISALIGNED
