@@ -94,10 +94,12 @@ constexpr uint32_t kOffCnt = kOffBar + kNumBars * 8;            // per-slot rele
 constexpr uint32_t kOffMisc = kOffCnt + 8 * 4;                  // tensor-memory base, last flag, chunk counts
 constexpr size_t kSmemBytes = 1024 + kOffMisc + 16;
 static_assert(kSmemBytes <= 232448, "shared memory");
+// a CTA allocates all 512 tensor-memory columns, so no second CTA may share its SM
+static_assert(kSmemBytes > 232448 / 2, "one CTA per SM");
 
 // Slot roles.  U phase: Yk block i in slot i % 4, U^T staged in slots 4-5.  SW phase: operator pair
-// k in slots 2 (k % 2), +1 while the first two Yv blocks come into slots 4 and 5.  O phase: W' hi | lo in
-// slots 0-1, Yv block i in slot oslot(i % 4) (4, 5, 2, 3).
+// k in slots 2 (k % 2) and 2 (k % 2) + 1 while the first two Yv blocks come into slots 4 and 5.
+// O phase: W' hi | lo in slots 0-1, Yv block i in slot oslot(i % 4) (4, 5, 2, 3).
 __host__ __device__ constexpr uint32_t oslot(int k) { return k < 2 ? 4u + (uint32_t)k : (uint32_t)k; }
 constexpr int kNumSlots = 6;
 
